@@ -1,0 +1,187 @@
+/*
+ * p100/b200.h — C ABI of the B200 (sm_100a) decode hot path.
+ *
+ * This is the drop-in boundary for the quantised mat-vec, FlashAttention-vec
+ * decode and tensor-parallel paths of Frostbite1536/P100.  Each entry point
+ * names the reference interface it replaces.  Plain pointers, sizes and a
+ * CUDA stream only: no C++ or PyTorch types cross this boundary, so the same
+ * header serves C, C++ (include/p100/b200.hpp wraps it with exceptions),
+ * ctypes, cgo or JNI callers.
+ *
+ * Conventions
+ *   - The caller owns every device buffer.  All work is ordered on the given
+ *     stream; no entry point synchronises the device or the stream.
+ *   - Status codes never throw.  On failure p100_last_error() returns a
+ *     thread-local description; shape errors use the reference's wording.
+ *   - Entry points act on the calling thread's current device and leave it
+ *     current.  They are thread-safe across distinct streams.
+ *   - There is no CPU fallback.  Without an sm_100 device every compute entry
+ *     point returns P100_ERR_UNSUPPORTED.
+ *   - Every wait inside a kernel is bounded (about one second).  A wait that
+ *     runs out sets a per-device flag that p100_device_error() reports as
+ *     P100_ERR_TIMEOUT; the kernel returns instead of hanging.
+ */
+#ifndef P100_B200_H
+#define P100_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define P100_B200_ABI_VERSION 1
+
+typedef enum p100_status {
+    P100_OK = 0,
+    P100_ERR_INVALID = 1,      /* bad shape or argument (reference: std::invalid_argument)   */
+    P100_ERR_CUDA = 2,         /* CUDA runtime error (reference: P100_CUDA_CHECK, check.h:7-17) */
+    P100_ERR_NCCL = 3,         /* NCCL error in the tensor-parallel layer                     */
+    P100_ERR_TIMEOUT = 4,      /* a bounded device-side wait ran out                          */
+    P100_ERR_UNSUPPORTED = 5   /* no sm_100 device, or a shape this build does not handle     */
+} p100_status;
+
+/* Weight formats in the order of p100::qmv::Type (include/p100/qmv.h:20). */
+typedef enum p100_qtype { P100_Q4_0 = 0, P100_Q8_0 = 1, P100_Q4_K = 2 } p100_qtype;
+
+/* Same type as cudaStream_t; 0 is the legacy default stream. */
+typedef struct CUstream_st* p100_stream_t;
+
+/* ------------------------------------------------------------------ library */
+int p100_abi_version(void);
+/* Thread-local text of the last failure on this thread ("" after success). */
+const char* p100_last_error(void);
+const char* p100_status_name(p100_status status);
+/* P100_OK if `device` is an sm_100 GPU this build has code for. */
+p100_status p100_device_check(int device);
+/* Reads, and with clear != 0 resets, the current device's bounded-wait flag:
+ * P100_ERR_TIMEOUT if any kernel gave up waiting since the last clear.
+ * Synchronises the current device. */
+p100_status p100_device_error(int clear);
+
+/* --------------------------------------------------------- quantised mat-vec */
+/* Elements and bytes per weight block (qmv_model.cpp:12-13); -1 if unknown. */
+int p100_block_elems(int type);
+int p100_block_bytes(int type);
+/* Bytes of a rows x k matrix of `type` blocks, row-major along k. */
+size_t p100_weight_bytes(int type, int rows, int k);
+/* Bytes of batch rows of k activations in block_q8_1 layout: per 32 values
+ * {fp16 d, fp16 sum, int8 q[32]} = 36 bytes. */
+size_t p100_q8_1_bytes(int k, int batch);
+
+/* Q8_1 activation quantisation; replaces p100::qmv::prepare's q8_1 fields
+ * (include/p100/qmv.h:34, qmv_model.cpp:53-71) and llama.cpp's
+ * quantize_row_q8_1.  x is batch rows of k fp32 (k % 32 == 0).  Bit-exact with
+ * prepare(): d = fp16(max|x|/127), q = round-half-away(x/(max|x|/127)),
+ * sum = fp16 of the XOR-butterfly sum of the original x. */
+p100_status p100_q8_1_quantize(const float* x, void* x_q8_1, int k, int batch,
+                               p100_stream_t stream);
+
+/* Dequantise a rows x k weight matrix to fp32, out[r*k + i].  Bit-exact with
+ * float(double(d)*sc*q - double(dmin)*mn) of qmv_model.cpp:143. */
+p100_status p100_dequantize(int type, const void* w, int rows, int k, float* out,
+                            p100_stream_t stream);
+
+/* y[c*rows + r] = sum_i W[r][i] * x_c[i] for c < batch (1..16), the q81 path
+ * of p100::qmv::evaluate (qmv_model.cpp:147-180) over whole matrices; the
+ * device counterpart of llama.cpp's mul_mat_vec_q and of the reference's
+ * prototype mmv_h2_<type>_b<B> (bench/micro/h2_mmv.cu:151-176, same output
+ * layout).  w: rows x k blocks of `type` (2-byte alignment suffices; 16-byte
+ * aligned rows take the bulk-copy path).  x_q8_1: p100_q8_1_bytes(k, batch).
+ * Integer block dots are exact; FP32 accumulation order differs from the
+ * sequential CPU model within 1e-3 * ||w|| * ||x||. */
+p100_status p100_qmv(int type, const void* w, int rows, int k, const void* x_q8_1,
+                     int batch, float* y, p100_stream_t stream);
+
+/* Flags for p100_qmv_ex. */
+#define P100_QMV_PDL 1u  /* launch as a programmatic dependent of the previous
+                            kernel in the stream: weights are prefetched before
+                            that kernel finishes, so they must not be written
+                            by it.  Activations are read only after it ends. */
+p100_status p100_qmv_ex(int type, const void* w, int rows, int k, const void* x_q8_1,
+                        int batch, float* y, unsigned flags, p100_stream_t stream);
+
+/* ---------------------------------------------------- FlashAttention decode */
+/* AttnParams (include/p100/attention.h:27-41) plus the split and the strides of
+ * a KV cache whose capacity exceeds seq_kv.  Layouts (attention.h:8-14):
+ *   q   fp32 [batch][n_head_q][seq_q][d_qk]
+ *   k   fp16 [batch][n_head_kv][seq_kv][d_qk]   (rows of kv_head_stride)
+ *   v   fp16 [batch][n_head_kv][seq_kv][d_v]
+ *   o   fp32 [batch][n_head_q][seq_q][d_v]
+ *   lse fp32 [batch][n_head_q][seq_q]  (natural log; -inf for a fully masked row)
+ *   mask fp32 [seq_q][seq_kv], additive, optional.
+ * Query head h reads kv head h / (n_head_q / n_head_kv). */
+typedef struct p100_attn_desc {
+    int batch, n_head_q, n_head_kv, seq_q, seq_kv, d_qk, d_v;
+    float scale;      /* 0 means 1/sqrt(d_qk)          */
+    float softcap;    /* 0 means off                   */
+    int causal;       /* bottom-right alignment        */
+    int kv_splits;    /* split-K parts per head, 0 = chosen for the device */
+    long long kv_head_stride;   /* elements between kv heads, 0 = seq_kv * d */
+    long long kv_batch_stride;  /* elements between batches,  0 = n_head_kv * head stride */
+} p100_attn_desc;
+
+/* validate (attention_reference.cpp:18-32): P100_OK, or P100_ERR_INVALID with
+ * the reference's reason copied into why. */
+p100_status p100_attn_validate(const p100_attn_desc* desc, char* why, size_t why_len);
+/* Workspace bytes p100_fa_decode needs for desc on the current device. */
+size_t p100_fa_workspace_size(const p100_attn_desc* desc);
+/* Zero a workspace before its first use (the kernel leaves it zeroed). */
+p100_status p100_fa_workspace_init(void* ws, size_t ws_bytes, p100_stream_t stream);
+/* Split-K FlashAttention-vec decode; replaces attention_reference /
+ * attention_tiled_model (attention_reference.cpp:87-135,
+ * attention_tiled_model.cpp:52-227) and llama.cpp's FA VEC kernel with its
+ * parallel_blocks combine.  seq_q == 1; d_qk == d_v in {64, 128, 256};
+ * n_head_q / n_head_kv <= 8.  FP32 logits, online softmax and accumulation;
+ * parts merged by the rebased combine of attention_tiled_model.cpp:183-222.
+ * lse and mask may be NULL. */
+p100_status p100_fa_decode(const p100_attn_desc* desc, const float* q, const void* k,
+                           const void* v, const float* mask, float* o, float* lse,
+                           void* ws, size_t ws_bytes, p100_stream_t stream);
+
+/* ------------------------------------------------- tensor-parallel (NCCL) */
+/* Row-split tensor parallelism over the GPUs of one box; replaces the
+ * reference's two-GPU PCIe layer (src/p2p/p2p.cpp) for the per-layer
+ * partial-sum exchange.  One handle per rank. */
+typedef struct p100_tp p100_tp;
+#define P100_TP_ID_BYTES 128
+/* A fresh communicator id (ncclGetUniqueId) for rank 0 to share. */
+p100_status p100_tp_unique_id(void* id /* P100_TP_ID_BYTES */);
+/* One rank of a multi-process group: binds `device` and joins the group. */
+p100_status p100_tp_init_rank(const void* id, int nranks, int rank, int device, p100_tp** out);
+/* All ranks of a single-process group (ncclCommInitAll): out[i] for devs[i]. */
+p100_status p100_tp_create(int ngpu, const int* devs, p100_tp** out);
+int p100_tp_rank(const p100_tp* tp);
+int p100_tp_size(const p100_tp* tp);
+int p100_tp_device(const p100_tp* tp);
+/* In-place fp32 sum over ranks, ordered on stream (which belongs to the
+ * rank's device). */
+p100_status p100_tp_allreduce_sum(p100_tp* tp, float* buf, size_t count, p100_stream_t stream);
+/* The same for every rank of a single-process group, as one NCCL group call. */
+p100_status p100_tp_allreduce_sum_group(p100_tp* const* tps, int n, float* const* bufs,
+                                        size_t count, const p100_stream_t* streams);
+/* Gather `count` fp32 from each rank into out[rank*count ...] on every rank. */
+p100_status p100_tp_allgather(p100_tp* tp, const float* in, float* out, size_t count,
+                              p100_stream_t stream);
+/* Aborts the communicator if it reports an asynchronous error; then frees it. */
+p100_status p100_tp_destroy(p100_tp* tp);
+
+/* ------------------------------------------------------ peer copies (p2p) */
+/* C view of p100::p2p (include/p100/p2p.h of the reference, src/p2p/p2p.cpp),
+ * which this library also exports with its C++ signatures. */
+typedef struct p100_peer_link p100_peer_link;
+enum { P100_PATH_PEER = 0, P100_PATH_STAGED = 1 };
+/* Topology text as p100::p2p::describe(probe()); returns bytes needed. */
+size_t p100_p2p_describe(char* out, size_t out_len);
+int p100_p2p_disabled_by_env(void);
+p100_status p100_peer_link_create(int src_dev, int dst_dev, size_t chunk_bytes, p100_peer_link** out);
+int p100_peer_link_path(const p100_peer_link* link);
+p100_status p100_peer_link_copy(p100_peer_link* link, void* dst, const void* src, size_t bytes,
+                                p100_stream_t stream);
+p100_status p100_peer_link_destroy(p100_peer_link* link);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* P100_B200_H */

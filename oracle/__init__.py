@@ -1,0 +1,331 @@
+"""CPU oracle for the p100_b200 hot path — TEST INFRASTRUCTURE ONLY.
+
+Only tests/, ``__graft_entry__.smoke()`` and ``bench.py``'s cpu_baseline leg
+import this package.  The product (``p100_b200``) never imports it.
+
+Two ctypes-loaded libraries (built by ``oracle/Makefile``):
+
+* ``lib/libp100_oracle.so`` — the restatement of the reference's CPU contract
+  (``p100_oracle.cpp``), always available once built;
+* ``_ref/libp100_ref.so`` — the reference's own ``src/reference/*.cpp``
+  compiled where they lie, available where the reference sources were present
+  at build time (``Ref.available()``).
+
+The numpy-facing helpers below mirror ``p100::qmv::{prepare,evaluate}`` and
+``p100::attention_{reference,tiled_model}`` (include/p100/qmv.h:17-49,
+include/p100/attention.h:27-80).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import pathlib
+import subprocess
+
+import numpy as np
+
+HERE = pathlib.Path(__file__).resolve().parent
+LIB = HERE / "lib" / "libp100_oracle.so"
+REF_LIB = HERE / "_ref" / "libp100_ref.so"
+
+Q4_0, Q8_0, Q4_K = 0, 1, 2
+TYPE_NAMES = {Q4_0: "q4_0", Q8_0: "q8_0", Q4_K: "q4_K"}
+BLOCK_ELEMS = {Q4_0: 32, Q8_0: 32, Q4_K: 256}
+BLOCK_BYTES = {Q4_0: 18, Q8_0: 34, Q4_K: 144}
+
+# p100o_act / qmv::ActivationBlock: 68 four-byte fields.
+ACT_DTYPE = np.dtype([("scale", "<f4"), ("sum", "<f4"), ("h", "<f4", (32,)),
+                      ("qd", "<f4"), ("qsum", "<f4"), ("q", "<i4", (32,))])
+assert ACT_DTYPE.itemsize == 272
+
+
+class Attn(C.Structure):
+    """AttnParams (include/p100/attention.h:27-41)."""
+    _fields_ = [("batch", C.c_int), ("n_head_q", C.c_int), ("n_head_kv", C.c_int),
+                ("seq_q", C.c_int), ("seq_kv", C.c_int), ("d_qk", C.c_int), ("d_v", C.c_int),
+                ("scale", C.c_float), ("softcap", C.c_float), ("causal", C.c_int)]
+
+    def __init__(self, batch=1, n_head_q=1, n_head_kv=1, seq_q=1, seq_kv=1, d_qk=128, d_v=128,
+                 scale=0.0, softcap=0.0, causal=False):
+        super().__init__(batch, n_head_q, n_head_kv, seq_q, seq_kv, d_qk, d_v, scale, softcap,
+                         int(bool(causal)))
+
+    def shapes(self):
+        b, hq, hk, sq, sk = self.batch, self.n_head_q, self.n_head_kv, self.seq_q, self.seq_kv
+        return ((b, hq, sq, self.d_qk), (b, hk, sk, self.d_qk), (b, hk, sk, self.d_v),
+                (b, hq, sq, self.d_v), (b, hq, sq))
+
+
+class Tiled(C.Structure):
+    """TiledModelConfig (include/p100/attention.h:54-71), same defaults."""
+    _fields_ = [("br", C.c_int), ("bc", C.c_int), ("qk_accum_fp16", C.c_int), ("p_fp16", C.c_int),
+                ("o_fp16_out", C.c_int), ("qk_scale_in_q", C.c_int), ("qk_q_prescale", C.c_float),
+                ("qk_products_fp16", C.c_int), ("qk_half2_chain", C.c_int),
+                ("kq_max_offset", C.c_float), ("l_from_unrounded_p", C.c_int),
+                ("o_accum_fp16", C.c_int), ("kv_parallel_blocks", C.c_int), ("o_accum_np", C.c_int),
+                ("o_accum_fp16_tile_flush", C.c_int)]
+
+    def __init__(self, br=64, bc=64, qk_accum_fp16=False, p_fp16=True, o_fp16_out=True, **kw):
+        vals = dict(qk_scale_in_q=0, qk_q_prescale=1.0, qk_products_fp16=0, qk_half2_chain=0,
+                    kq_max_offset=0.0, l_from_unrounded_p=0, o_accum_fp16=0, kv_parallel_blocks=1,
+                    o_accum_np=1, o_accum_fp16_tile_flush=0)
+        vals.update(kw)
+        super().__init__(br, bc, int(qk_accum_fp16), int(p_fp16), int(o_fp16_out), **{
+            k: (float(v) if k in ("qk_q_prescale", "kq_max_offset") else int(v)) for k, v in vals.items()})
+
+
+def _ptr(a):
+    return a.ctypes.data_as(C.c_void_p) if a is not None else None
+
+
+def build():
+    """Compile the oracle (and, where the reference is present, oracle/_ref)."""
+    subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
+
+
+def _load(path, prefix):
+    if not path.exists():
+        raise FileNotFoundError(f"{path} is not built; run make -C {HERE}")
+    lib = C.CDLL(str(path))
+    return lib
+
+
+class _Base:
+    prefix = ""
+
+    def _f(self, name, restype, *argtypes):
+        fn = getattr(self.lib, self.prefix + name)
+        fn.restype = restype
+        fn.argtypes = list(argtypes)
+        return fn
+
+    def _check(self, status):
+        if status != 0:
+            raise ValueError(self.last_error())
+        return status
+
+
+class Oracle(_Base):
+    """The restated CPU contract (p100_oracle.cpp)."""
+    prefix = "p100o_"
+
+    def __init__(self, path=LIB):
+        self.lib = _load(path, self.prefix)
+        f = self._f
+        vp, ip, fp = C.c_void_p, C.c_int, C.c_float
+        self.last_error = lambda: f("last_error", C.c_char_p)().decode()
+        self.fp16_round = f("fp16_round", fp, fp)
+        self.fp16_round_d = f("fp16_round_d", fp, C.c_double)
+        self.fp16_bits = f("fp16_bits", C.c_uint16, fp)
+        self.fp16_value = f("fp16_value", fp, C.c_uint16)
+        self._prepare = f("prepare", ip, vp, ip, vp)
+        self._pack = f("pack_q8_1", None, vp, ip, vp)
+        self._quantize = f("quantize_q8_1", ip, vp, ip, ip, vp)
+        self._rng_new = f("rng_new", vp, C.c_uint32)
+        self._rng_free = f("rng_free", None, vp)
+        self._random_row = f("random_row", ip, ip, ip, vp, vp)
+        self._dequantize = f("dequantize", ip, ip, vp, ip, ip, vp)
+        self._evaluate = f("evaluate", ip, ip, vp, vp, ip, vp, vp)
+        self._qmv = f("qmv_q81", ip, ip, vp, ip, ip, vp, ip, vp)
+        self._qmv_mt = f("qmv_q81_threaded", C.c_double, ip, vp, ip, ip, vp, ip, vp, ip)
+        self._validate = f("attn_validate", ip, vp, C.c_char_p, ip)
+        self._attn_ref = f("attention_reference", ip, vp, vp, vp, vp, vp, vp, vp)
+        self._attn_ref_mt = f("attention_reference_threaded", C.c_double, vp, vp, vp, vp, vp, vp, ip)
+        self._attn_tiled = f("attention_tiled", ip, vp, vp, vp, vp, vp, vp, vp, vp)
+        self._eff_scale = f("attn_effective_scale", fp, vp)
+        self._fill_normal = f("fill_normal", None, C.c_uint32, fp, fp, ip, C.c_size_t, vp)
+        self._fill_uniform = f("fill_uniform", None, C.c_uint32, fp, fp, ip, C.c_size_t, vp)
+
+    # ------------------------------------------------------------ seeded inputs
+    def fill_normal(self, seed, n, mean=0.0, stddev=1.0, round_fp16=False):
+        out = np.zeros(n, dtype=np.float32)
+        self._fill_normal(seed, mean, stddev, int(round_fp16), n, _ptr(out))
+        return out
+
+    def fill_uniform(self, seed, n, lo, hi, round_fp16=False):
+        out = np.zeros(n, dtype=np.float32)
+        self._fill_uniform(seed, lo, hi, int(round_fp16), n, _ptr(out))
+        return out
+
+    # ------------------------------------------------------------ quantised mat-vec
+    def prepare(self, x):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        out = np.zeros(x.size // 32, dtype=ACT_DTYPE)
+        self._check(self._prepare(_ptr(x), x.size, _ptr(out)))
+        return out
+
+    def pack_q8_1(self, acts):
+        out = np.zeros(acts.size * 36, dtype=np.uint8)
+        self._pack(_ptr(acts), acts.size, _ptr(out))
+        return out
+
+    def quantize_q8_1(self, x, k):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        batch = x.size // k
+        out = np.zeros(batch * (k // 32) * 36, dtype=np.uint8)
+        self._check(self._quantize(_ptr(x), k, batch, _ptr(out)))
+        return out
+
+    def random_rows(self, type_, k, rows, seed):
+        """rows weight rows from one generator seeded once (qmv_model.cpp:30-43)."""
+        rb = k // BLOCK_ELEMS[type_] * BLOCK_BYTES[type_]
+        out = np.zeros(rows * rb, dtype=np.uint8)
+        rng = self._rng_new(seed)
+        try:
+            for r in range(rows):
+                self._check(self._random_row(type_, k, rng, out[r * rb:].ctypes.data_as(C.c_void_p)))
+        finally:
+            self._rng_free(rng)
+        return out
+
+    def dequantize(self, type_, w, rows, k):
+        out = np.zeros(rows * k, dtype=np.float32)
+        self._check(self._dequantize(type_, _ptr(np.ascontiguousarray(w)), rows, k, _ptr(out)))
+        return out.reshape(rows, k)
+
+    def evaluate(self, type_, w_row, x, acts):
+        """All paths of qmv::evaluate for one row: dict of exact/h16_exact/weight_norm/q81/h8/h16."""
+        r = np.zeros(1, dtype=[("exact", "<f8"), ("h16_exact", "<f8"), ("weight_norm", "<f8"),
+                               ("q81", "<f4"), ("h8", "<f4"), ("h16", "<f4")])
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        self._check(self._evaluate(type_, _ptr(np.ascontiguousarray(w_row)), _ptr(x), x.size,
+                                   _ptr(acts), _ptr(r)))
+        return {n: r[n][0] for n in r.dtype.names}
+
+    def qmv_q81(self, type_, w, rows, k, acts, batch):
+        y = np.zeros(batch * rows, dtype=np.float32)
+        self._check(self._qmv(type_, _ptr(np.ascontiguousarray(w)), rows, k, _ptr(acts), batch, _ptr(y)))
+        return y.reshape(batch, rows)
+
+    def qmv_q81_threaded(self, type_, w, rows, k, acts, batch, nthreads):
+        y = np.zeros(batch * rows, dtype=np.float32)
+        secs = self._qmv_mt(type_, _ptr(np.ascontiguousarray(w)), rows, k, _ptr(acts), batch, _ptr(y),
+                            nthreads)
+        if secs < 0:
+            raise ValueError(self.last_error())
+        return y.reshape(batch, rows), secs
+
+    # ------------------------------------------------------------ attention
+    def effective_scale(self, p):
+        return self._eff_scale(C.byref(p))
+
+    def validate(self, p):
+        buf = C.create_string_buffer(256)
+        ok = self._validate(C.byref(p), buf, 256)
+        return bool(ok), buf.value.decode()
+
+    def attention_reference(self, p, q, k, v, mask=None, want_lse=True):
+        qs, ks, vs, os_, ls = p.shapes()
+        o = np.zeros(os_, dtype=np.float32)
+        lse = np.zeros(ls, dtype=np.float32) if want_lse else None
+        args = [np.ascontiguousarray(a, dtype=np.float32) if a is not None else None for a in (q, k, v, mask)]
+        self._check(self._attn_ref(C.byref(p), *[_ptr(a) for a in args], _ptr(o), _ptr(lse)))
+        return o, lse
+
+    def attention_reference_threaded(self, p, q, k, v, nthreads):
+        qs, ks, vs, os_, ls = p.shapes()
+        o = np.zeros(os_, dtype=np.float32)
+        lse = np.zeros(ls, dtype=np.float32)
+        args = [np.ascontiguousarray(a, dtype=np.float32) for a in (q, k, v)]
+        secs = self._attn_ref_mt(C.byref(p), *[_ptr(a) for a in args], _ptr(o), _ptr(lse), nthreads)
+        if secs < 0:
+            raise ValueError(self.last_error())
+        return o, lse, secs
+
+    def attention_tiled(self, p, cfg, q, k, v, mask=None, want_lse=True):
+        qs, ks, vs, os_, ls = p.shapes()
+        o = np.zeros(os_, dtype=np.float32)
+        lse = np.zeros(ls, dtype=np.float32) if want_lse else None
+        args = [np.ascontiguousarray(a, dtype=np.float32) if a is not None else None for a in (q, k, v, mask)]
+        self._check(self._attn_tiled(C.byref(p), C.byref(cfg), *[_ptr(a) for a in args], _ptr(o), _ptr(lse)))
+        return o, lse
+
+
+class Ref(_Base):
+    """The reference's own CPU contract, compiled into oracle/_ref (ref_shim.cpp)."""
+    prefix = "p100r_"
+
+    @staticmethod
+    def available():
+        return REF_LIB.exists()
+
+    def __init__(self, path=REF_LIB):
+        self.lib = _load(path, self.prefix)
+        f = self._f
+        vp, ip, fp = C.c_void_p, C.c_int, C.c_float
+        self.last_error = lambda: f("last_error", C.c_char_p)().decode()
+        self.round_to_fp16 = f("round_to_fp16", fp, fp)
+        self.round_to_fp16_d = f("round_to_fp16_d", fp, C.c_double)
+        self.half_bits = f("half_bits", C.c_uint16, fp)
+        self.half_value = f("half_value", fp, C.c_uint16)
+        self._rng_new = f("rng_new", vp, C.c_uint32)
+        self._rng_free = f("rng_free", None, vp)
+        self._random_row = f("random_row", ip, ip, ip, vp, vp)
+        self._prepare = f("prepare", ip, vp, ip, vp)
+        self._evaluate = f("evaluate", ip, ip, vp, vp, ip, vp, vp, vp)
+        self._validate = f("validate", ip, vp, C.c_char_p, ip)
+        self._attn_ref = f("attention_reference", ip, vp, vp, vp, vp, vp, vp, vp)
+        self._attn_tiled = f("attention_tiled", ip, vp, vp, vp, vp, vp, vp, vp, vp)
+
+    def random_rows(self, type_, k, rows, seed):
+        rb = k // BLOCK_ELEMS[type_] * BLOCK_BYTES[type_]
+        out = np.zeros(rows * rb, dtype=np.uint8)
+        rng = self._rng_new(seed)
+        try:
+            for r in range(rows):
+                self._check(self._random_row(type_, k, rng, out[r * rb:].ctypes.data_as(C.c_void_p)))
+        finally:
+            self._rng_free(rng)
+        return out
+
+    def prepare(self, x):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        out = np.zeros(x.size // 32, dtype=ACT_DTYPE)
+        self._check(self._prepare(_ptr(x), x.size, _ptr(out)))
+        return out
+
+    def evaluate(self, type_, w_row, x, acts):
+        d3 = np.zeros(3, dtype=np.float64)
+        f3 = np.zeros(3, dtype=np.float32)
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        self._check(self._evaluate(type_, _ptr(np.ascontiguousarray(w_row)), _ptr(x), x.size, _ptr(acts),
+                                   _ptr(d3), _ptr(f3)))
+        return dict(exact=d3[0], h16_exact=d3[1], weight_norm=d3[2], q81=f3[0], h8=f3[1], h16=f3[2])
+
+    def validate(self, p):
+        buf = C.create_string_buffer(256)
+        ok = self._validate(C.byref(p), buf, 256)
+        return bool(ok), buf.value.decode()
+
+    def attention_reference(self, p, q, k, v, mask=None, want_lse=True):
+        qs, ks, vs, os_, ls = p.shapes()
+        o = np.zeros(os_, dtype=np.float32)
+        lse = np.zeros(ls, dtype=np.float32) if want_lse else None
+        args = [np.ascontiguousarray(a, dtype=np.float32) if a is not None else None for a in (q, k, v, mask)]
+        self._check(self._attn_ref(C.byref(p), *[_ptr(a) for a in args], _ptr(o), _ptr(lse)))
+        return o, lse
+
+    def attention_tiled(self, p, cfg, q, k, v, mask=None, want_lse=True):
+        qs, ks, vs, os_, ls = p.shapes()
+        o = np.zeros(os_, dtype=np.float32)
+        lse = np.zeros(ls, dtype=np.float32) if want_lse else None
+        args = [np.ascontiguousarray(a, dtype=np.float32) if a is not None else None for a in (q, k, v, mask)]
+        self._check(self._attn_tiled(C.byref(p), C.byref(cfg), *[_ptr(a) for a in args], _ptr(o), _ptr(lse)))
+        return o, lse
+
+
+_oracle = None
+
+
+def oracle():
+    """Process-wide Oracle instance (building the library on first use if needed)."""
+    global _oracle
+    if _oracle is None:
+        if not LIB.exists():
+            build()
+        _oracle = Oracle()
+    return _oracle
+
+
+def host_cores():
+    return len(os.sched_getaffinity(0))

@@ -1,0 +1,317 @@
+"""p100_b200 — B200 (sm_100a) decode hot path of the P100 numerics contract.
+
+The product is the C-ABI shared library ``p100_b200/lib/libp100_b200.so``
+declared in ``include/p100/b200.h``.  This module is a thin ctypes view of it
+for Python callers, tests and ``bench.py``: torch supplies device memory and
+streams, every computation happens in the library's CUDA kernels, and there is
+no CPU path — calls raise ``P100Error`` when the library or an sm_100 device
+is missing.
+
+Names follow the reference's contract (include/p100/qmv.h:17-49,
+include/p100/attention.h:27-80): ``Q4_0/Q8_0/Q4_K`` block formats, Q8_1
+activation blocks, ``AttnDesc`` mirroring ``AttnParams``.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import pathlib
+import subprocess
+import threading
+
+HERE = pathlib.Path(__file__).resolve().parent
+LIB_PATH = HERE / "lib" / "libp100_b200.so"
+CSRC = HERE / "csrc"
+
+Q4_0, Q8_0, Q4_K = 0, 1, 2
+TYPE_NAMES = {Q4_0: "q4_0", Q8_0: "q8_0", Q4_K: "q4_K"}
+TYPES = {v: k for k, v in TYPE_NAMES.items()}
+BLOCK_ELEMS = {Q4_0: 32, Q8_0: 32, Q4_K: 256}
+BLOCK_BYTES = {Q4_0: 18, Q8_0: 34, Q4_K: 144}
+Q8_1_BLOCK_BYTES = 36
+QMV_PDL = 1
+
+STATUS = {0: "P100_OK", 1: "P100_ERR_INVALID", 2: "P100_ERR_CUDA", 3: "P100_ERR_NCCL",
+          4: "P100_ERR_TIMEOUT", 5: "P100_ERR_UNSUPPORTED"}
+OK, ERR_INVALID, ERR_CUDA, ERR_NCCL, ERR_TIMEOUT, ERR_UNSUPPORTED = range(6)
+PATH_PEER, PATH_STAGED = 0, 1
+TP_ID_BYTES = 128
+
+
+class P100Error(RuntimeError):
+    """A non-OK p100_status, with p100_last_error()'s text."""
+
+    def __init__(self, status, message):
+        super().__init__(f"{STATUS.get(status, status)}: {message}")
+        self.status = status
+        self.message = message
+
+
+class InvalidArgument(P100Error, ValueError):
+    """P100_ERR_INVALID — the reference raises std::invalid_argument here."""
+
+
+class AttnDesc(C.Structure):
+    """p100_attn_desc: AttnParams (include/p100/attention.h:27-41) + split/strides."""
+    _fields_ = [("batch", C.c_int), ("n_head_q", C.c_int), ("n_head_kv", C.c_int), ("seq_q", C.c_int),
+                ("seq_kv", C.c_int), ("d_qk", C.c_int), ("d_v", C.c_int), ("scale", C.c_float),
+                ("softcap", C.c_float), ("causal", C.c_int), ("kv_splits", C.c_int),
+                ("kv_head_stride", C.c_longlong), ("kv_batch_stride", C.c_longlong)]
+
+    def __init__(self, batch=1, n_head_q=1, n_head_kv=1, seq_q=1, seq_kv=1, d_qk=128, d_v=128, scale=0.0,
+                 softcap=0.0, causal=False, kv_splits=0, kv_head_stride=0, kv_batch_stride=0):
+        super().__init__(batch, n_head_q, n_head_kv, seq_q, seq_kv, d_qk, d_v, scale, softcap, int(bool(causal)),
+                         kv_splits, kv_head_stride, kv_batch_stride)
+
+
+_lib = None
+_lock = threading.Lock()
+
+
+def build(verbose=False):
+    """Compile the CUDA library for sm_100a (nvcc cross-compiles without a GPU)."""
+    out = None if verbose else subprocess.DEVNULL
+    subprocess.run(["make", "-s", "-C", str(CSRC)], check=True, stdout=out)
+
+
+def _bind(lib):
+    vp, ip, sz, st = C.c_void_p, C.c_int, C.c_size_t, C.c_void_p
+    sigs = {
+        "p100_abi_version": (ip, []),
+        "p100_last_error": (C.c_char_p, []),
+        "p100_status_name": (C.c_char_p, [ip]),
+        "p100_device_check": (ip, [ip]),
+        "p100_device_error": (ip, [ip]),
+        "p100_block_elems": (ip, [ip]),
+        "p100_block_bytes": (ip, [ip]),
+        "p100_weight_bytes": (sz, [ip, ip, ip]),
+        "p100_q8_1_bytes": (sz, [ip, ip]),
+        "p100_q8_1_quantize": (ip, [vp, vp, ip, ip, st]),
+        "p100_dequantize": (ip, [ip, vp, ip, ip, vp, st]),
+        "p100_qmv": (ip, [ip, vp, ip, ip, vp, ip, vp, st]),
+        "p100_qmv_ex": (ip, [ip, vp, ip, ip, vp, ip, vp, C.c_uint, st]),
+        "p100_attn_validate": (ip, [vp, C.c_char_p, sz]),
+        "p100_fa_workspace_size": (sz, [vp]),
+        "p100_fa_workspace_init": (ip, [vp, sz, st]),
+        "p100_fa_decode": (ip, [vp, vp, vp, vp, vp, vp, vp, vp, sz, st]),
+        "p100_tp_unique_id": (ip, [vp]),
+        "p100_tp_init_rank": (ip, [vp, ip, ip, ip, C.POINTER(vp)]),
+        "p100_tp_create": (ip, [ip, C.POINTER(ip), C.POINTER(vp)]),
+        "p100_tp_rank": (ip, [vp]),
+        "p100_tp_size": (ip, [vp]),
+        "p100_tp_device": (ip, [vp]),
+        "p100_tp_allreduce_sum": (ip, [vp, vp, sz, st]),
+        "p100_tp_allreduce_sum_group": (ip, [C.POINTER(vp), ip, C.POINTER(vp), sz, C.POINTER(vp)]),
+        "p100_tp_allgather": (ip, [vp, vp, vp, sz, st]),
+        "p100_tp_destroy": (ip, [vp]),
+        "p100_p2p_describe": (sz, [C.c_char_p, sz]),
+        "p100_p2p_disabled_by_env": (ip, []),
+        "p100_peer_link_create": (ip, [ip, ip, sz, C.POINTER(vp)]),
+        "p100_peer_link_path": (ip, [vp]),
+        "p100_peer_link_copy": (ip, [vp, vp, vp, sz, st]),
+        "p100_peer_link_destroy": (ip, [vp]),
+    }
+    for name, (res, args) in sigs.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    return lib
+
+
+def lib():
+    """The loaded C-ABI library.  Raises P100Error when it is not built."""
+    global _lib
+    if _lib is None:
+        with _lock:
+            if _lib is None:
+                if not LIB_PATH.exists():
+                    raise P100Error(ERR_UNSUPPORTED, f"{LIB_PATH} is not built (python -c 'import p100_b200; "
+                                                     "p100_b200.build()')")
+                _lib = _bind(C.CDLL(str(LIB_PATH)))
+    return _lib
+
+
+def symbols():
+    """Every symbol include/p100/b200.h declares, in header order."""
+    import re
+    text = (HERE.parent / "include" / "p100" / "b200.h").read_text()
+    return re.findall(r"^\s*(?:const\s+)?[a-z_0-9]+\*?\s+\**(p100_[a-z0-9_]+)\(", text, re.M)
+
+
+def last_error():
+    return lib().p100_last_error().decode()
+
+
+def check(status):
+    if status != OK:
+        cls = InvalidArgument if status == ERR_INVALID else P100Error
+        raise cls(status, last_error())
+    return status
+
+
+# ---------------------------------------------------------------- torch glue
+def _torch():
+    import torch
+    return torch
+
+
+def _ptr(t):
+    return C.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def _stream(stream):
+    torch = _torch()
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return C.c_void_p(s.cuda_stream)
+
+
+def device_check(device=0):
+    return lib().p100_device_check(device)
+
+
+def device_error(clear=True):
+    """P100_ERR_TIMEOUT if a kernel gave up a bounded wait (synchronises)."""
+    return lib().p100_device_error(int(clear))
+
+
+def weight_bytes(qtype, rows, k):
+    return lib().p100_weight_bytes(qtype, rows, k)
+
+
+def q8_1_bytes(k, batch=1):
+    return lib().p100_q8_1_bytes(k, batch)
+
+
+def q8_1_quantize(x, out=None, stream=None):
+    """Q8_1 blocks of x (fp32 [batch, k] on the GPU) -> uint8 [batch * k/32 * 36]."""
+    torch = _torch()
+    x = x.contiguous()
+    k = x.shape[-1]
+    batch = x.numel() // k
+    if out is None:
+        out = torch.empty(batch * (k // 32) * Q8_1_BLOCK_BYTES, dtype=torch.uint8, device=x.device)
+    check(lib().p100_q8_1_quantize(_ptr(x), _ptr(out), k, batch, _stream(stream)))
+    return out
+
+
+def dequantize(qtype, w, rows, k, out=None, stream=None):
+    torch = _torch()
+    if out is None:
+        out = torch.empty(rows, k, dtype=torch.float32, device=w.device)
+    check(lib().p100_dequantize(qtype, _ptr(w), rows, k, _ptr(out), _stream(stream)))
+    return out
+
+
+def qmv(qtype, w, rows, k, x_q8_1, batch=1, y=None, flags=0, stream=None):
+    """y[batch, rows] = W x for Q8_1 activations (p100_qmv / p100_qmv_ex)."""
+    torch = _torch()
+    if y is None:
+        y = torch.empty(batch, rows, dtype=torch.float32, device=w.device)
+    check(lib().p100_qmv_ex(qtype, _ptr(w), rows, k, _ptr(x_q8_1), batch, _ptr(y), flags, _stream(stream)))
+    return y
+
+
+def attn_validate(desc):
+    buf = C.create_string_buffer(256)
+    st = lib().p100_attn_validate(C.byref(desc), buf, 256)
+    return st == OK, buf.value.decode()
+
+
+def fa_workspace_size(desc):
+    return lib().p100_fa_workspace_size(C.byref(desc))
+
+
+def fa_workspace(desc, device=None, stream=None):
+    """A zero-initialised workspace for desc (None if none is needed)."""
+    torch = _torch()
+    n = fa_workspace_size(desc)
+    if n == 0:
+        msg = last_error()
+        if msg:
+            raise P100Error(ERR_INVALID, msg)
+        return None
+    return torch.zeros(n, dtype=torch.uint8, device=device or "cuda")
+
+
+def fa_decode(desc, q, k, v, mask=None, o=None, lse=None, ws=None, stream=None):
+    """Split-K FA-vec decode: q fp32 [B,Hq,1,D], k/v fp16 [B,Hkv,S,D] -> o fp32, lse fp32."""
+    torch = _torch()
+    if o is None:
+        o = torch.empty(desc.batch, desc.n_head_q, desc.seq_q, desc.d_v, dtype=torch.float32, device=q.device)
+    if lse is None:
+        lse = torch.empty(desc.batch, desc.n_head_q, desc.seq_q, dtype=torch.float32, device=q.device)
+    if ws is None:
+        ws = fa_workspace(desc, q.device)
+    nbytes = ws.numel() if ws is not None else 0
+    check(lib().p100_fa_decode(C.byref(desc), _ptr(q), _ptr(k), _ptr(v), _ptr(mask), _ptr(o), _ptr(lse),
+                               _ptr(ws), nbytes, _stream(stream)))
+    return o, lse
+
+
+# ---------------------------------------------------------------- tensor parallel
+def tp_unique_id():
+    buf = (C.c_ubyte * TP_ID_BYTES)()
+    check(lib().p100_tp_unique_id(buf))
+    return bytes(buf)
+
+
+class TP:
+    """One rank of a row-split tensor-parallel group (p100_tp_*)."""
+
+    def __init__(self, uid: bytes, nranks: int, rank: int, device: int):
+        h = C.c_void_p()
+        buf = (C.c_ubyte * TP_ID_BYTES).from_buffer_copy(uid)
+        check(lib().p100_tp_init_rank(buf, nranks, rank, device, C.byref(h)))
+        self.handle = h
+
+    @property
+    def rank(self):
+        return lib().p100_tp_rank(self.handle)
+
+    @property
+    def size(self):
+        return lib().p100_tp_size(self.handle)
+
+    def allreduce_sum(self, buf, stream=None):
+        check(lib().p100_tp_allreduce_sum(self.handle, _ptr(buf), buf.numel(), _stream(stream)))
+        return buf
+
+    def allgather(self, inp, out, stream=None):
+        check(lib().p100_tp_allgather(self.handle, _ptr(inp), _ptr(out), inp.numel(), _stream(stream)))
+        return out
+
+    def close(self):
+        if self.handle:
+            h, self.handle = self.handle, None
+            check(lib().p100_tp_destroy(h))
+
+
+# ---------------------------------------------------------------- peer copies
+def p2p_describe():
+    n = lib().p100_p2p_describe(None, 0)
+    if n == 0:
+        raise P100Error(ERR_CUDA, last_error())
+    buf = C.create_string_buffer(n)
+    lib().p100_p2p_describe(buf, n)
+    return buf.value.decode()
+
+
+class PeerLink:
+    """p100::p2p::PeerLink (include/p100/p2p.h) through the C view."""
+
+    def __init__(self, src_dev, dst_dev, chunk_bytes=4 << 20):
+        h = C.c_void_p()
+        check(lib().p100_peer_link_create(src_dev, dst_dev, chunk_bytes, C.byref(h)))
+        self.handle = h
+
+    @property
+    def path(self):
+        return lib().p100_peer_link_path(self.handle)
+
+    def copy_async(self, dst_ptr, src_ptr, nbytes, stream=None):
+        check(lib().p100_peer_link_copy(self.handle, C.c_void_p(dst_ptr), C.c_void_p(src_ptr), nbytes,
+                                        _stream(stream)))
+
+    def close(self):
+        if self.handle:
+            h, self.handle = self.handle, None
+            check(lib().p100_peer_link_destroy(h))

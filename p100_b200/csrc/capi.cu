@@ -1,0 +1,461 @@
+// capi.cu — the extern "C" entry points of include/p100/b200.h for the
+// quantised mat-vec and FlashAttention decode paths, plus library plumbing
+// (status text, device checks, the bounded-wait flag).
+//
+// Single CUDA translation unit: every kernel header is included here so the
+// library has one device module and one g_device_error word per device.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "common.cuh"
+#include "fa_decode.cuh"
+#include "qmv.cuh"
+#include "quant.cuh"
+
+namespace p100b {
+
+namespace {
+thread_local std::string t_error;
+std::mutex g_dev_mutex;
+int g_dev_sm100[64];     // 0 unknown, 1 sm_100, -1 other
+int g_dev_sms[64];
+}  // namespace
+
+p100_status set_error(p100_status status, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    std::vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    t_error = buf;
+    return status;
+}
+
+void clear_error() { t_error.clear(); }
+
+p100_status cuda_status(cudaError_t err, const char* what) {
+    if (err == cudaSuccess) return P100_OK;
+    return set_error(P100_ERR_CUDA, "%s: %s", what, cudaGetErrorString(err));
+}
+
+p100_status require_sm100(int* device_out, int* sm_count_out) {
+    int dev = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err != cudaSuccess) {
+        (void)cudaGetLastError();
+        return set_error(P100_ERR_UNSUPPORTED, "no CUDA device: %s", cudaGetErrorString(err));
+    }
+    if (dev < 0 || dev >= 64) return set_error(P100_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
+    std::lock_guard<std::mutex> lock(g_dev_mutex);
+    if (g_dev_sm100[dev] == 0) {
+        int major = 0, minor = 0, sms = 0;
+        if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+            (void)cudaGetLastError();
+            return set_error(P100_ERR_UNSUPPORTED, "cannot query device %d", dev);
+        }
+        g_dev_sm100[dev] = (major == 10 && minor == 0) ? 1 : -1;
+        g_dev_sms[dev] = sms;
+    }
+    if (g_dev_sm100[dev] != 1)
+        return set_error(P100_ERR_UNSUPPORTED, "device %d is not sm_100; this build has sm_100a code only", dev);
+    if (device_out) *device_out = dev;
+    if (sm_count_out) *sm_count_out = g_dev_sms[dev];
+    return P100_OK;
+}
+
+namespace {
+
+bool known_type(int t) { return t == P100_Q4_0 || t == P100_Q8_0 || t == P100_Q4_K; }
+int elems_of(int t) { return t == P100_Q4_K ? 256 : 32; }
+int bytes_of(int t) { return t == P100_Q4_0 ? 18 : t == P100_Q8_0 ? 34 : 144; }
+
+p100_status launch_status(const char* what) { return cuda_status(cudaGetLastError(), what); }
+
+// ------------------------------------------------------------------ qmv plan
+struct QmvPlan {
+    qmv::Params p;
+    int ipt = 0, bmax = 0, grid = 0;
+    size_t smem = 0;
+};
+
+// Fills plan for the bulk path; false if the shape or alignment needs the
+// generic kernel.
+bool plan_bulk(int type, const void* w, int rows, int k, int sms, QmvPlan& plan) {
+    const size_t row_bytes = size_t(k / elems_of(type)) * bytes_of(type);
+    if (reinterpret_cast<uintptr_t>(w) % 16 || row_bytes % 16 || k % 256) return false;
+    const int ipr = k / 64;
+    const int ipt = (ipr + qmv::kThreads - 1) / qmv::kThreads;
+    if (ipt > 2) return false;
+    const int per = (ipr + ipt - 1) / ipt;
+    const int tpr = (per + 31) / 32 * 32;
+    const int groups = qmv::kThreads / tpr;
+    const int bmax = ipt == 1 ? 4 : 2;
+    int rps = groups * std::max(1, int(qmv::kStageCap / (row_bytes * groups)));
+    if (rps * bmax > qmv::kThreads) rps = (qmv::kThreads / bmax) / groups * groups;
+    if (rps < 1) return false;
+    const size_t stage = size_t(rps) * row_bytes;
+    const int slot = int((stage + 127) / 128 * 128);
+    const int part_floats = bmax * rps * (tpr / 32);
+    const size_t head = 128 + ((size_t(2) * part_floats * 4 + 127) & ~size_t(127));
+    int nstage = qmv::kMaxStages;
+    while (nstage > 1 && head + size_t(nstage) * slot > size_t(qmv::kSmemLimit)) --nstage;
+    if (nstage < 2) return false;
+    plan.p.rows = rows;
+    plan.p.k = k;
+    plan.p.row_bytes = int(row_bytes);
+    plan.p.ipr = ipr;
+    plan.p.tpr = tpr;
+    plan.p.groups = groups;
+    plan.p.rps = rps;
+    plan.p.nstage = nstage;
+    plan.p.slot_bytes = slot;
+    plan.p.part_floats = part_floats;
+    plan.ipt = ipt;
+    plan.bmax = bmax;
+    plan.smem = head + size_t(nstage) * slot;
+    const int want = (rows + rps - 1) / rps;   // no CTA with less than a stage of rows
+    plan.grid = std::max(1, std::min(sms, want));
+    return true;
+}
+
+template <int TYPE, int B, int IPT>
+p100_status launch_bulk_t(const QmvPlan& plan, bool pdl, cudaStream_t stream) {
+    auto kern = qmv::qmv_bulk_kernel<TYPE, B, IPT>;
+    static thread_local int configured_smem[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (configured_smem[dev] < int(plan.smem)) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(plan.smem));
+        if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(qmv)");
+        configured_smem[dev] = int(plan.smem);
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(plan.grid);
+    cfg.blockDim = dim3(qmv::kThreads);
+    cfg.dynamicSmemBytes = plan.smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cuda_status(cudaLaunchKernelEx(&cfg, kern, plan.p), "qmv_bulk_kernel launch");
+}
+
+template <int TYPE>
+p100_status launch_bulk_type(const QmvPlan& plan, int cols, bool pdl, cudaStream_t s) {
+    if (plan.ipt == 1) {
+        switch (cols) {
+            case 1: return launch_bulk_t<TYPE, 1, 1>(plan, pdl, s);
+            case 2: return launch_bulk_t<TYPE, 2, 1>(plan, pdl, s);
+            case 3: return launch_bulk_t<TYPE, 3, 1>(plan, pdl, s);
+            default: return launch_bulk_t<TYPE, 4, 1>(plan, pdl, s);
+        }
+    }
+    return cols == 1 ? launch_bulk_t<TYPE, 1, 2>(plan, pdl, s) : launch_bulk_t<TYPE, 2, 2>(plan, pdl, s);
+}
+
+p100_status run_qmv(int type, const void* w, int rows, int k, const void* xq, int batch, float* y, unsigned flags,
+                    cudaStream_t stream) {
+    if (!known_type(type)) return set_error(P100_ERR_INVALID, "unknown weight type %d", type);
+    if (k <= 0 || k % elems_of(type)) return set_error(P100_ERR_INVALID, "whole weight blocks required");
+    if (rows < 0) return set_error(P100_ERR_INVALID, "rows must be non-negative");
+    if (batch < 1 || batch > 16) return set_error(P100_ERR_INVALID, "batch must be in 1..16");
+    if (rows == 0) return P100_OK;
+    if (!w || !xq || !y) return set_error(P100_ERR_INVALID, "null buffer");
+    if (reinterpret_cast<uintptr_t>(xq) % 4) return set_error(P100_ERR_INVALID, "x_q8_1 must be 4-byte aligned");
+    if (reinterpret_cast<uintptr_t>(w) % 2) return set_error(P100_ERR_INVALID, "weights must be 2-byte aligned");
+    int sms = 0;
+    if (p100_status st = require_sm100(nullptr, &sms)) return st;
+    QmvPlan plan;
+    if (plan_bulk(type, w, rows, k, sms, plan)) {
+        plan.p.w = static_cast<const uint8_t*>(w);
+        plan.p.xq = static_cast<const uint8_t*>(xq);
+        plan.p.y = y;
+        for (int c0 = 0; c0 < batch; c0 += plan.bmax) {
+            const int cols = std::min(plan.bmax, batch - c0);
+            plan.p.col0 = c0;
+            p100_status st;
+            // Only the first launch may overlap the previous kernel; later
+            // column chunks follow this call's own launches.
+            const bool pdl = (flags & P100_QMV_PDL) && c0 == 0;
+            switch (type) {
+                case P100_Q4_0: st = launch_bulk_type<P100_Q4_0>(plan, cols, pdl, stream); break;
+                case P100_Q8_0: st = launch_bulk_type<P100_Q8_0>(plan, cols, pdl, stream); break;
+                default: st = launch_bulk_type<P100_Q4_K>(plan, cols, pdl, stream); break;
+            }
+            if (st) return st;
+        }
+        return P100_OK;
+    }
+    const size_t row_bytes = size_t(k / elems_of(type)) * bytes_of(type);
+    const dim3 grid((rows + 7) / 8);
+    const uint8_t* wb = static_cast<const uint8_t*>(w);
+    const uint8_t* xb = static_cast<const uint8_t*>(xq);
+    switch (type) {
+        case P100_Q4_0: qmv::qmv_generic_kernel<P100_Q4_0><<<grid, 256, 0, stream>>>(wb, xb, y, rows, k, batch, row_bytes); break;
+        case P100_Q8_0: qmv::qmv_generic_kernel<P100_Q8_0><<<grid, 256, 0, stream>>>(wb, xb, y, rows, k, batch, row_bytes); break;
+        default: qmv::qmv_generic_kernel<P100_Q4_K><<<grid, 256, 0, stream>>>(wb, xb, y, rows, k, batch, row_bytes); break;
+    }
+    return launch_status("qmv_generic_kernel launch");
+}
+
+// ------------------------------------------------------------------ attention
+const char* attn_reason(const p100_attn_desc& d) {
+    // attention_reference.cpp:18-32, same wording and order.
+    if (d.batch <= 0 || d.n_head_q <= 0 || d.n_head_kv <= 0 || d.seq_q <= 0 || d.seq_kv <= 0 || d.d_qk <= 0 ||
+        d.d_v <= 0)
+        return "all dimensions must be positive";
+    if (d.n_head_q % d.n_head_kv != 0) return "n_head_q must be divisible by n_head_kv";
+    if (d.softcap < 0.0f || !std::isfinite(d.softcap)) return "softcap must be finite and non-negative";
+    if (!std::isfinite(d.scale)) return "scale must be finite";
+    return nullptr;
+}
+
+struct FaPlan {
+    int D = 0, G = 0, gmax = 0, parts = 1, nstage = 0;
+    long long head_stride = 0, batch_stride = 0;
+    size_t smem = 0, ws_o = 0, ws_ml = 0, ws_tickets = 0, ws_total = 0;
+};
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+p100_status plan_fa(const p100_attn_desc& d, int sms, FaPlan& plan) {
+    if (const char* why = attn_reason(d)) return set_error(P100_ERR_INVALID, "%s", why);
+    if (d.seq_q != 1) return set_error(P100_ERR_UNSUPPORTED, "decode kernel handles seq_q == 1 only");
+    if (d.d_qk != d.d_v || (d.d_qk != 64 && d.d_qk != 128 && d.d_qk != 256))
+        return set_error(P100_ERR_UNSUPPORTED, "d_qk == d_v in {64, 128, 256} required");
+    const int G = d.n_head_q / d.n_head_kv;
+    if (G > 8) return set_error(P100_ERR_UNSUPPORTED, "GQA group of %d query heads exceeds 8", G);
+    plan.D = d.d_qk;
+    plan.G = G;
+    plan.gmax = G <= 1 ? 1 : G <= 2 ? 2 : G <= 4 ? 4 : 8;
+    plan.head_stride = d.kv_head_stride ? d.kv_head_stride : static_cast<long long>(d.seq_kv) * d.d_qk;
+    plan.batch_stride = d.kv_batch_stride ? d.kv_batch_stride : plan.head_stride * d.n_head_kv;
+    if (plan.head_stride < static_cast<long long>(d.seq_kv) * d.d_qk || plan.head_stride % 8 ||
+        plan.batch_stride % 8)
+        return set_error(P100_ERR_INVALID, "KV strides must cover seq_kv rows and be multiples of 8 elements");
+    const int heads = d.batch * d.n_head_kv;
+    const int max_parts = std::max(1, d.seq_kv / fa::kTile);
+    int parts = d.kv_splits;
+    if (parts <= 0) parts = std::max(1, sms / heads);
+    plan.parts = std::min(parts, max_parts);
+    plan.nstage = d.d_qk == 256 ? 2 : 4;
+    const size_t head = ((64 + (plan.gmax * fa::kTile + fa::kTile * 8 + 24 + plan.gmax * plan.D + 4) * 4) + 127) & ~size_t(127);
+    plan.smem = head + size_t(plan.nstage) * 2 * fa::kTile * plan.D * 2;
+    if (plan.parts > 1) {
+        plan.ws_o = align256(size_t(heads) * plan.parts * G * plan.D * 4);
+        plan.ws_ml = align256(size_t(heads) * plan.parts * G * 2 * 4);
+        plan.ws_tickets = align256(size_t(heads) * 4);
+    }
+    plan.ws_total = plan.ws_o + plan.ws_ml + plan.ws_tickets;
+    return P100_OK;
+}
+
+template <int D, int GMAX>
+p100_status launch_fa_t(const FaPlan& plan, const fa::Params& prm, int heads, cudaStream_t stream) {
+    auto kern = fa::fa_decode_kernel<D, GMAX>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(plan.smem));
+    if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(fa)");
+    kern<<<dim3(plan.parts, heads), fa::kThreads, plan.smem, stream>>>(prm);
+    return launch_status("fa_decode_kernel launch");
+}
+
+template <int D>
+p100_status launch_fa_d(const FaPlan& plan, const fa::Params& prm, int heads, cudaStream_t s) {
+    switch (plan.gmax) {
+        case 1: return launch_fa_t<D, 1>(plan, prm, heads, s);
+        case 2: return launch_fa_t<D, 2>(plan, prm, heads, s);
+        case 4: return launch_fa_t<D, 4>(plan, prm, heads, s);
+        default: return launch_fa_t<D, 8>(plan, prm, heads, s);
+    }
+}
+
+}  // namespace
+}  // namespace p100b
+
+using namespace p100b;
+
+extern "C" {
+
+int p100_abi_version(void) { return P100_B200_ABI_VERSION; }
+
+const char* p100_last_error(void) { return t_error.c_str(); }
+
+const char* p100_status_name(p100_status s) {
+    switch (s) {
+        case P100_OK: return "P100_OK";
+        case P100_ERR_INVALID: return "P100_ERR_INVALID";
+        case P100_ERR_CUDA: return "P100_ERR_CUDA";
+        case P100_ERR_NCCL: return "P100_ERR_NCCL";
+        case P100_ERR_TIMEOUT: return "P100_ERR_TIMEOUT";
+        case P100_ERR_UNSUPPORTED: return "P100_ERR_UNSUPPORTED";
+    }
+    return "P100_ERR_UNKNOWN";
+}
+
+p100_status p100_device_check(int device) {
+    clear_error();
+    int cur = 0;
+    if (cudaGetDevice(&cur) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return set_error(P100_ERR_UNSUPPORTED, "no CUDA device");
+    }
+    if (cudaSetDevice(device) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return set_error(P100_ERR_UNSUPPORTED, "no CUDA device %d", device);
+    }
+    p100_status st = require_sm100(nullptr, nullptr);
+    cudaSetDevice(cur);
+    return st;
+}
+
+p100_status p100_device_error(int clear) {
+    clear_error();
+    if (p100_status st = require_sm100(nullptr, nullptr)) return st;
+    int value = 0;
+    if (p100_status st = cuda_status(cudaDeviceSynchronize(), "cudaDeviceSynchronize")) return st;
+    if (p100_status st = cuda_status(cudaMemcpyFromSymbol(&value, g_device_error, sizeof value), "read device flag"))
+        return st;
+    if (clear && value) {
+        const int zero = 0;
+        if (p100_status st = cuda_status(cudaMemcpyToSymbol(g_device_error, &zero, sizeof zero), "clear device flag"))
+            return st;
+    }
+    return value ? set_error(P100_ERR_TIMEOUT, "a kernel gave up a bounded wait") : P100_OK;
+}
+
+int p100_block_elems(int type) { return known_type(type) ? elems_of(type) : -1; }
+int p100_block_bytes(int type) { return known_type(type) ? bytes_of(type) : -1; }
+
+size_t p100_weight_bytes(int type, int rows, int k) {
+    if (!known_type(type) || rows < 0 || k <= 0 || k % elems_of(type)) return 0;
+    return size_t(rows) * (k / elems_of(type)) * bytes_of(type);
+}
+
+size_t p100_q8_1_bytes(int k, int batch) {
+    if (k <= 0 || k % 32 || batch <= 0) return 0;
+    return size_t(batch) * (k / 32) * 36;
+}
+
+p100_status p100_q8_1_quantize(const float* x, void* x_q8_1, int k, int batch, p100_stream_t stream) {
+    clear_error();
+    if (k <= 0 || k % 32) return set_error(P100_ERR_INVALID, "whole activation blocks required");
+    if (batch <= 0 || batch > 65535) return set_error(P100_ERR_INVALID, "batch must be in 1..65535");
+    if (!x || !x_q8_1) return set_error(P100_ERR_INVALID, "null buffer");
+    if (reinterpret_cast<uintptr_t>(x_q8_1) % 4) return set_error(P100_ERR_INVALID, "x_q8_1 must be 4-byte aligned");
+    if (p100_status st = require_sm100(nullptr, nullptr)) return st;
+    const int blocks = k / 32;
+    q8_1_quantize_kernel<<<dim3((blocks + 7) / 8, batch), 256, 0, stream>>>(x, static_cast<uint8_t*>(x_q8_1), k,
+                                                                             blocks);
+    return launch_status("q8_1_quantize_kernel launch");
+}
+
+p100_status p100_dequantize(int type, const void* w, int rows, int k, float* out, p100_stream_t stream) {
+    clear_error();
+    if (!known_type(type)) return set_error(P100_ERR_INVALID, "unknown weight type %d", type);
+    if (k <= 0 || k % elems_of(type)) return set_error(P100_ERR_INVALID, "whole weight blocks required");
+    if (rows < 0) return set_error(P100_ERR_INVALID, "rows must be non-negative");
+    if (rows == 0) return P100_OK;
+    if (!w || !out) return set_error(P100_ERR_INVALID, "null buffer");
+    if (reinterpret_cast<uintptr_t>(out) % 16) return set_error(P100_ERR_INVALID, "out must be 16-byte aligned");
+    if (p100_status st = require_sm100(nullptr, nullptr)) return st;
+    const size_t row_bytes = size_t(k / elems_of(type)) * bytes_of(type);
+    const long long slabs = static_cast<long long>(rows) * (k / 32);
+    const dim3 grid(static_cast<unsigned>((slabs + 255) / 256));
+    const uint8_t* wb = static_cast<const uint8_t*>(w);
+    switch (type) {
+        case P100_Q4_0: dequantize_kernel<P100_Q4_0><<<grid, 256, 0, stream>>>(wb, out, rows, k, row_bytes); break;
+        case P100_Q8_0: dequantize_kernel<P100_Q8_0><<<grid, 256, 0, stream>>>(wb, out, rows, k, row_bytes); break;
+        default: dequantize_kernel<P100_Q4_K><<<grid, 256, 0, stream>>>(wb, out, rows, k, row_bytes); break;
+    }
+    return launch_status("dequantize_kernel launch");
+}
+
+p100_status p100_qmv(int type, const void* w, int rows, int k, const void* x_q8_1, int batch, float* y,
+                     p100_stream_t stream) {
+    clear_error();
+    return run_qmv(type, w, rows, k, x_q8_1, batch, y, 0u, stream);
+}
+
+p100_status p100_qmv_ex(int type, const void* w, int rows, int k, const void* x_q8_1, int batch, float* y,
+                        unsigned flags, p100_stream_t stream) {
+    clear_error();
+    if (flags & ~P100_QMV_PDL) return set_error(P100_ERR_INVALID, "unknown flags 0x%x", flags);
+    return run_qmv(type, w, rows, k, x_q8_1, batch, y, flags, stream);
+}
+
+p100_status p100_attn_validate(const p100_attn_desc* desc, char* why, size_t why_len) {
+    clear_error();
+    if (!desc) return set_error(P100_ERR_INVALID, "null descriptor");
+    const char* reason = attn_reason(*desc);
+    if (why && why_len) std::snprintf(why, why_len, "%s", reason ? reason : "");
+    return reason ? set_error(P100_ERR_INVALID, "%s", reason) : P100_OK;
+}
+
+size_t p100_fa_workspace_size(const p100_attn_desc* desc) {
+    clear_error();
+    if (!desc) return 0;
+    int sms = 0;
+    if (require_sm100(nullptr, &sms)) return 0;
+    FaPlan plan;
+    if (plan_fa(*desc, sms, plan)) return 0;
+    return plan.ws_total;
+}
+
+p100_status p100_fa_workspace_init(void* ws, size_t ws_bytes, p100_stream_t stream) {
+    clear_error();
+    if (!ws || !ws_bytes) return P100_OK;
+    return cuda_status(cudaMemsetAsync(ws, 0, ws_bytes, stream), "cudaMemsetAsync(workspace)");
+}
+
+p100_status p100_fa_decode(const p100_attn_desc* desc, const float* q, const void* k, const void* v,
+                           const float* mask, float* o, float* lse, void* ws, size_t ws_bytes,
+                           p100_stream_t stream) {
+    clear_error();
+    if (!desc) return set_error(P100_ERR_INVALID, "null descriptor");
+    int sms = 0;
+    if (const char* why = attn_reason(*desc)) return set_error(P100_ERR_INVALID, "%s", why);
+    if (p100_status st = require_sm100(nullptr, &sms)) return st;
+    FaPlan plan;
+    if (p100_status st = plan_fa(*desc, sms, plan)) return st;
+    if (!q || !k || !v || !o) return set_error(P100_ERR_INVALID, "null buffer");
+    if (reinterpret_cast<uintptr_t>(k) % 16 || reinterpret_cast<uintptr_t>(v) % 16)
+        return set_error(P100_ERR_INVALID, "K and V must be 16-byte aligned");
+    if (plan.ws_total > ws_bytes || (plan.ws_total && !ws))
+        return set_error(P100_ERR_INVALID, "workspace of %zu bytes needed, %zu given", plan.ws_total, ws_bytes);
+    if (reinterpret_cast<uintptr_t>(ws) % 256) return set_error(P100_ERR_INVALID, "workspace must be 256-byte aligned");
+    fa::Params prm = {};
+    prm.q = q;
+    prm.k = static_cast<const __half*>(k);
+    prm.v = static_cast<const __half*>(v);
+    prm.mask = mask;
+    prm.o = o;
+    prm.lse = lse;
+    uint8_t* wsb = static_cast<uint8_t*>(ws);
+    prm.ws_o = plan.parts > 1 ? reinterpret_cast<float*>(wsb) : nullptr;
+    prm.ws_ml = plan.parts > 1 ? reinterpret_cast<float*>(wsb + plan.ws_o) : nullptr;
+    prm.tickets = plan.parts > 1 ? reinterpret_cast<unsigned*>(wsb + plan.ws_o + plan.ws_ml) : nullptr;
+    prm.nkv = desc->n_head_kv;
+    prm.G = plan.G;
+    prm.seq = desc->seq_kv;
+    prm.parts = plan.parts;
+    prm.nstage = plan.nstage;
+    prm.head_stride = plan.head_stride;
+    prm.batch_stride = plan.batch_stride;
+    prm.scale = desc->scale == 0.0f ? 1.0f / std::sqrt(static_cast<float>(desc->d_qk)) : desc->scale;
+    prm.softcap = desc->softcap;
+    const int heads = desc->batch * desc->n_head_kv;
+    switch (plan.D) {
+        case 64: return launch_fa_d<64>(plan, prm, heads, stream);
+        case 128: return launch_fa_d<128>(plan, prm, heads, stream);
+        default: return launch_fa_d<256>(plan, prm, heads, stream);
+    }
+}
+
+}  // extern "C"
