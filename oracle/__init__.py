@@ -266,6 +266,16 @@ class Ref(_Base):
         self._validate = f("validate", ip, vp, C.c_char_p, ip)
         self._attn_ref = f("attention_reference", ip, vp, vp, vp, vp, vp, vp, vp)
         self._attn_tiled = f("attention_tiled", ip, vp, vp, vp, vp, vp, vp, vp, vp)
+        self._eval_rows_mt = f("evaluate_rows_threaded", C.c_double, ip, vp, ip, ip, vp, vp, ip)
+
+    def evaluate_rows_threaded(self, type_, w, rows, k, x, nthreads):
+        """prepare(x) + evaluate() of every row on nthreads threads -> (q81 [rows], seconds)."""
+        y = np.zeros(rows, dtype=np.float32)
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        secs = self._eval_rows_mt(type_, _ptr(np.ascontiguousarray(w)), rows, k, _ptr(x), _ptr(y), nthreads)
+        if secs < 0:
+            raise ValueError(self.last_error())
+        return y, secs
 
     def random_rows(self, type_, k, rows, seed):
         rb = k // BLOCK_ELEMS[type_] * BLOCK_BYTES[type_]

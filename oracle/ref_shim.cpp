@@ -12,7 +12,9 @@
 #include <cstring>
 #include <exception>
 #include <random>
+#include <chrono>
 #include <string>
+#include <thread>
 #include <vector>
 
 namespace {
@@ -93,6 +95,30 @@ int p100r_evaluate(int type, const void* w, const float* x, int k, const void* a
         d3[0] = r.exact; d3[1] = r.h16_exact; d3[2] = r.weight_norm;
         f3[0] = r.q81; f3[1] = r.h8; f3[2] = r.h16;
     });
+}
+
+// prepare() of one activation row, then evaluate() of rows weight rows split
+// over nthreads std::threads; q81 outputs to y.  Returns wall seconds
+// (negative on error).  Used as the timed CPU baseline: it is the reference's
+// own per-row CPU path, unmodified.
+double p100r_evaluate_rows_threaded(int type, const void* w, int rows, int k, const float* x, float* y,
+                                    int nthreads) {
+    const auto start = std::chrono::steady_clock::now();
+    std::vector<p100::qmv::ActivationBlock> acts;
+    if (guarded([&] { acts = p100::qmv::prepare(x, k); })) return -1.0;
+    const size_t row_bytes = size_t(k / p100::qmv::block_size(type_of(type))) *
+                             p100::qmv::block_bytes(type_of(type));
+    if (nthreads < 1) nthreads = 1;
+    std::vector<std::thread> pool;
+    for (int t = 0; t < nthreads; ++t) {
+        pool.emplace_back([&, t] {
+            for (int r = t; r < rows; r += nthreads)
+                y[r] = p100::qmv::evaluate(type_of(type), static_cast<const uint8_t*>(w) + r * row_bytes, x, k,
+                                           acts).q81;
+        });
+    }
+    for (auto& th : pool) th.join();
+    return std::chrono::duration<double>(std::chrono::steady_clock::now() - start).count();
 }
 
 int p100r_validate(const void* a, char* why, int why_len) {

@@ -237,10 +237,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_bulk_kernel(const Params p) {
     bool ok = true;
     for (int s = 0; s < nst; ++s) {
         const int slot = s % p.nstage;
-        if (!mbar_wait(&full[slot], (s / p.nstage) & 1)) {
-            ok = false;   // every thread waits on the same phase, so all leave here
-            break;
-        }
+        const bool timed_out = !mbar_wait(&full[slot], (s / p.nstage) & 1);
         const uint8_t* stage = ring + size_t(slot) * p.slot_bytes;
         const int first = r0 + s * p.rps;
         const int nr = min(p.rps, r1 - first);
@@ -270,7 +267,12 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_bulk_kernel(const Params p) {
                 }
             }
         }
-        __syncthreads();   // slot fully read; this stage's partials visible
+        // Slot fully read and this stage's partials visible.  A timed-out wait
+        // is decided for the whole CTA here, so every thread leaves together.
+        if (__syncthreads_or(timed_out)) {
+            ok = false;
+            break;
+        }
         if (tid == 0 && s + p.nstage < nst) issue(s + p.nstage);
         if (tid < nr * B) {
             const int c = tid / nr, rl = tid % nr;

@@ -1,0 +1,75 @@
+"""Seeded synthetic inputs in the distributions of the benchmark configurations.
+
+Host-side numpy generators (one seed per tensor) for the mat-vec and attention
+workloads: there is no dataset or checkpoint behind this path, so these stand
+in for model weights, activations and a prefilled KV cache.
+
+* Q4_0: per block d = fp16(|N(0,1)| * 0.02), 32 codes uniform in 0..15
+  (value d * (code - 8)); low nibble of byte i is element i, high nibble is
+  element i + 16 (include/p100/qmv.h:6, qmv_model.cpp:82).
+* Q8_0: d as above, codes uniform in -127..127.
+* Q4_K: d, dmin = fp16(|N(0,1)| * 0.02), 12 packed scale bytes uniform in
+  0..255 (so every 6-bit scale/min is uniform), 128 nibble bytes uniform.
+* activations ~ N(0,1) fp32; K/V cache fp16 N(0,1) * 0.5; q ~ N(0,1).
+"""
+from __future__ import annotations
+
+import numpy as np
+
+Q4_0, Q8_0, Q4_K = 0, 1, 2
+BLOCK_ELEMS = {Q4_0: 32, Q8_0: 32, Q4_K: 256}
+BLOCK_BYTES = {Q4_0: 18, Q8_0: 34, Q4_K: 144}
+
+# Llama-3-8B layer shapes of the mat-vec sweep, (name, k, rows).
+LLAMA3_8B_SHAPES = [("q/o", 4096, 4096), ("k/v", 4096, 1024), ("gate/up", 4096, 14336), ("down", 14336, 4096)]
+
+
+def _scales(rng, shape):
+    return (np.abs(rng.standard_normal(shape)) * 0.02).astype(np.float16)
+
+
+def weights(qtype, rows, k, seed):
+    """rows x k weight matrix of qtype as GGUF block bytes (uint8, row-major)."""
+    rng = np.random.default_rng(seed)
+    be = BLOCK_ELEMS[qtype]
+    if k % be:
+        raise ValueError("whole weight blocks required")
+    nb = k // be
+    if qtype == Q4_0:
+        out = np.empty((rows, nb, 18), np.uint8)
+        out[..., :2] = _scales(rng, (rows, nb)).view(np.uint8).reshape(rows, nb, 2)
+        codes = rng.integers(0, 16, (rows, nb, 32), dtype=np.uint8)
+        out[..., 2:] = codes[..., :16] | (codes[..., 16:] << 4)
+    elif qtype == Q8_0:
+        out = np.empty((rows, nb, 34), np.uint8)
+        out[..., :2] = _scales(rng, (rows, nb)).view(np.uint8).reshape(rows, nb, 2)
+        out[..., 2:] = rng.integers(-127, 128, (rows, nb, 32), dtype=np.int8).view(np.uint8)
+    else:
+        out = np.empty((rows, nb, 144), np.uint8)
+        out[..., 0:2] = _scales(rng, (rows, nb)).view(np.uint8).reshape(rows, nb, 2)
+        out[..., 2:4] = _scales(rng, (rows, nb)).view(np.uint8).reshape(rows, nb, 2)
+        out[..., 4:] = rng.integers(0, 256, (rows, nb, 140), dtype=np.uint8)
+    return out.reshape(-1)
+
+
+def activations(batch, k, seed):
+    return np.random.default_rng(seed).standard_normal((batch, k)).astype(np.float32)
+
+
+def attention_inputs(batch, n_head_q, n_head_kv, seq_kv, d, seed):
+    """q fp32 [B,Hq,1,D]; K, V fp16 [B,Hkv,S,D] ~ N(0,1)*0.5."""
+    rng = np.random.default_rng(seed)
+    q = rng.standard_normal((batch, n_head_q, 1, d)).astype(np.float32)
+    k = (rng.standard_normal((batch, n_head_kv, seq_kv, d), dtype=np.float32) * 0.5).astype(np.float16)
+    v = (rng.standard_normal((batch, n_head_kv, seq_kv, d), dtype=np.float32) * 0.5).astype(np.float16)
+    return q, k, v
+
+
+def qmv_algorithmic_bytes(qtype, rows, k, batch):
+    """Weight bytes + fp32 activations + fp32 outputs (bin/mm-gbps.py:51-57)."""
+    return rows * (k // BLOCK_ELEMS[qtype]) * BLOCK_BYTES[qtype] + batch * k * 4 + batch * rows * 4
+
+
+def fa_algorithmic_bytes(batch, n_head_q, n_head_kv, seq_kv, d):
+    """fp16 K and V read once + fp32 q and O (+ LSE)."""
+    return batch * n_head_kv * seq_kv * d * 2 * 2 + batch * n_head_q * d * 4 * 2 + batch * n_head_q * 4

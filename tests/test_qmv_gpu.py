@@ -1,0 +1,200 @@
+"""GPU parity of the quantised mat-vec path through the C-ABI.
+
+Bar: Q8_1 activation blocks and dequantised weights bit-exact with the CPU
+contract; mat-vec within 1e-3 * ||w|| * ||x|| of prepare()+evaluate().q81
+(tests/h2_mmv_gpu.cu:89,141 use the same normalisation)."""
+import numpy as np
+import pytest
+
+from conftest import QMV_NORM_TOL, golden
+
+import oracle
+import p100_b200 as P
+from p100_b200 import workloads as W
+
+pytestmark = pytest.mark.gpu
+
+
+def dev(torch, a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def q81_reference(orc, qtype, w, rows, k, x):
+    acts = np.concatenate([orc.prepare(xc) for xc in x])
+    y, _ = orc.qmv_q81_threaded(qtype, w, rows, k, acts, x.shape[0], oracle.host_cores())
+    return y
+
+
+def row_norms(orc, qtype, w, rows, k):
+    rb = w.size // rows
+    out = np.empty(rows)
+    for r0 in range(0, rows, 1024):
+        r1 = min(rows, r0 + 1024)
+        deq = orc.dequantize(qtype, w[r0 * rb:r1 * rb], r1 - r0, k).astype(np.float64)
+        out[r0:r1] = np.sqrt((deq * deq).sum(axis=1))
+    return out
+
+
+def assert_qmv_close(y, yref, wn, x, tol=QMV_NORM_TOL):
+    xn = np.sqrt((x.astype(np.float64) ** 2).sum(axis=1))
+    err = np.abs(y.astype(np.float64) - yref) / (wn[None, :] * xn[:, None] + 1e-30)
+    assert err.max() <= tol, f"max normalised error {err.max():.3e}"
+    return err.max()
+
+
+# ------------------------------------------------------------------ Q8_1
+def test_q8_1_bit_exact_golden(cuda, orc):
+    g = golden("q8_1.npz")
+    for i, x in enumerate(g["x"]):
+        got = P.q8_1_quantize(dev(cuda, x)).cpu().numpy()
+        blocks = got.reshape(-1, 36)
+        assert np.array_equal(blocks[:, 0:2].copy().view(np.uint16)[:, 0],
+                              g["qd"][i].astype(np.float16).view(np.uint16))
+        assert np.array_equal(blocks[:, 2:4].copy().view(np.uint16)[:, 0],
+                              g["qsum"][i].astype(np.float16).view(np.uint16))
+        assert np.array_equal(blocks[:, 4:].view(np.int8), g["q"][i])
+
+
+@pytest.mark.parametrize("k,batch", [(32, 1), (4096, 3), (14336, 16), (28672, 2)])
+def test_q8_1_bit_exact_random(cuda, orc, k, batch):
+    rng = np.random.default_rng(k + batch)
+    x = rng.standard_normal((batch, k)).astype(np.float32)
+    x[0, :32] = 0
+    x[-1] *= rng.standard_normal(k).astype(np.float32) * 3
+    if batch > 2:
+        x[1] *= 1e4
+        x[2] *= 1e-5
+    got = P.q8_1_quantize(dev(cuda, x)).cpu().numpy()
+    assert np.array_equal(got, orc.quantize_q8_1(x, k))
+
+
+# ------------------------------------------------------------------ dequant
+@pytest.mark.parametrize("qtype", [P.Q4_0, P.Q8_0, P.Q4_K])
+@pytest.mark.parametrize("k", [256, 4096])
+def test_dequantize_bit_exact(cuda, orc, qtype, k):
+    rows = 19
+    w = orc.random_rows(qtype, k, rows, 3 + qtype + k)
+    got = P.dequantize(qtype, dev(cuda, w), rows, k).cpu().numpy()
+    assert np.array_equal(got.view(np.uint32), orc.dequantize(qtype, w, rows, k).view(np.uint32))
+
+
+# ------------------------------------------------------------------ mat-vec
+def test_qmv_golden(cuda, orc):
+    g = golden("qmv.npz")
+    for qtype, name in oracle.TYPE_NAMES.items():
+        for k in (256, 4096, 14336):
+            key = f"{name}_{k}"
+            w, x = g[key + "_w"], g[key + "_x"]
+            rows = g[key + "_wnorm"].size
+            xq = P.q8_1_quantize(dev(cuda, x))
+            y = P.qmv(qtype, dev(cuda, w), rows, k, xq, batch=2).cpu().numpy()
+            assert_qmv_close(y, g[key + "_q81"].astype(np.float64), g[key + "_wnorm"], x)
+            # and it tracks the exact FP64 dot like the CPU q81 model does
+            xn = np.sqrt((x.astype(np.float64) ** 2).sum(axis=1))
+            e_gpu = np.abs(y - g[key + "_exact"]) / (g[key + "_wnorm"][None] * xn[:, None])
+            e_cpu = np.abs(g[key + "_q81"] - g[key + "_exact"]) / (g[key + "_wnorm"][None] * xn[:, None])
+            assert e_gpu.max() <= e_cpu.max() + QMV_NORM_TOL
+
+
+SHAPES = [(k, rows) for _, k, rows in W.LLAMA3_8B_SHAPES]
+
+
+@pytest.mark.parametrize("qtype", [P.Q4_0, P.Q8_0, P.Q4_K])
+@pytest.mark.parametrize("k,rows", SHAPES)
+def test_qmv_llama_shapes(cuda, orc, qtype, k, rows):
+    """Config-2 shapes at batch 1 and 4 against the sequential CPU model."""
+    w = W.weights(qtype, rows, k, seed=1000 + k + rows + qtype)
+    x = W.activations(4, k, seed=77 + k)
+    wd = dev(cuda, w)
+    wn = row_norms(orc, qtype, w, rows, k)
+    yref = q81_reference(orc, qtype, w, rows, k, x).astype(np.float64)
+    xq = P.q8_1_quantize(dev(cuda, x))
+    y4 = P.qmv(qtype, wd, rows, k, xq, batch=4).cpu().numpy()
+    assert_qmv_close(y4, yref, wn, x)
+    y1 = P.qmv(qtype, wd, rows, k, xq[: k // 32 * 36], batch=1).cpu().numpy()
+    assert_qmv_close(y1, yref[:1], wn, x[:1])
+
+
+@pytest.mark.parametrize("qtype", [P.Q4_0, P.Q8_0, P.Q4_K])
+def test_qmv_batch_columns_independent(cuda, qtype):
+    """Every batch size 1..16 gives each column bit-identical to a batch-1 call."""
+    k, rows = 4096, 1024
+    w = dev(cuda, W.weights(qtype, rows, k, seed=5 + qtype))
+    x = W.activations(16, k, seed=6)
+    xq = P.q8_1_quantize(dev(cuda, x))
+    nbytes = k // 32 * 36
+    singles = [P.qmv(qtype, w, rows, k, xq[c * nbytes:(c + 1) * nbytes], 1).cpu().numpy() for c in range(16)]
+    for batch in (2, 3, 5, 8, 13, 16):
+        y = P.qmv(qtype, w, rows, k, xq, batch).cpu().numpy()
+        for c in range(batch):
+            assert np.array_equal(y[c], singles[c][0]), (batch, c)
+
+
+def test_qmv_batch16_full_shape(cuda, orc):
+    """Batch 16 on the down projection against the CPU model."""
+    k, rows = 14336, 4096
+    w = W.weights(P.Q4_0, rows, k, seed=99)
+    x = W.activations(16, k, seed=98)
+    yref = q81_reference(orc, P.Q4_0, w, rows, k, x).astype(np.float64)
+    y = P.qmv(P.Q4_0, dev(cuda, w), rows, k, P.q8_1_quantize(dev(cuda, x)), 16).cpu().numpy()
+    assert_qmv_close(y, yref, row_norms(orc, P.Q4_0, w, rows, k), x)
+
+
+@pytest.mark.parametrize("qtype", [P.Q4_0, P.Q8_0, P.Q4_K])
+@pytest.mark.parametrize("k,rows,offset", [(256, 1, 0), (256, 17, 0), (512, 300, 2), (8192, 33, 0),
+                                            (28672, 40, 0), (1024, 5, 18)])
+def test_qmv_edge_shapes(cuda, orc, qtype, k, rows, offset):
+    """Tiny and ragged shapes, 2-byte-aligned weights (generic kernel), k up to 28672."""
+    if k % P.BLOCK_ELEMS[qtype]:
+        pytest.skip("not whole blocks")
+    w = W.weights(qtype, rows, k, seed=k + rows + qtype)
+    x = W.activations(3, k, seed=k)
+    x[1, :64] = 0
+    buf = cuda.zeros(w.size + offset, dtype=cuda.uint8, device="cuda")
+    buf[offset:] = dev(cuda, w)
+    y = P.qmv(qtype, buf[offset:], rows, k, P.q8_1_quantize(dev(cuda, x)), 3).cpu().numpy()
+    assert_qmv_close(y, q81_reference(orc, qtype, w, rows, k, x).astype(np.float64),
+                     row_norms(orc, qtype, w, rows, k), x)
+
+
+def test_qmv_k32_generic(cuda, orc):
+    for qtype in (P.Q4_0, P.Q8_0):
+        w = orc.random_rows(qtype, 32, 9, 4)
+        x = W.activations(2, 32, seed=3)
+        y = P.qmv(qtype, dev(cuda, w), 9, 32, P.q8_1_quantize(dev(cuda, x)), 2).cpu().numpy()
+        assert_qmv_close(y, q81_reference(orc, qtype, w, 9, 32, x).astype(np.float64),
+                         row_norms(orc, qtype, w, 9, 32), x)
+
+
+def test_qmv_zero_activation_and_rows(cuda):
+    k, rows = 4096, 64
+    w = dev(cuda, W.weights(P.Q4_0, rows, k, seed=1))
+    xq = P.q8_1_quantize(cuda.zeros(1, k, device="cuda"))
+    assert cuda.count_nonzero(P.qmv(P.Q4_0, w, rows, k, xq, 1)).item() == 0
+    y = cuda.full((1, 1), 7.0, device="cuda")
+    P.qmv(P.Q4_0, w, 0, k, xq, 1, y=y)   # rows == 0: nothing written
+    assert y.item() == 7.0
+
+
+def test_qmv_deterministic_and_pdl(cuda):
+    k, rows = 14336, 4096
+    w = dev(cuda, W.weights(P.Q4_K, rows, k, seed=2))
+    x = dev(cuda, W.activations(2, k, seed=3))
+    xq = P.q8_1_quantize(x)
+    a = P.qmv(P.Q4_K, w, rows, k, xq, 2).clone()
+    for _ in range(3):
+        xq = P.q8_1_quantize(x)                        # producer kernel right before
+        b = P.qmv(P.Q4_K, w, rows, k, xq, 2, flags=P.QMV_PDL)
+        assert cuda.equal(a, b)
+    assert P.device_error() == P.OK
+
+
+def test_qmv_invalid_arguments(cuda):
+    w = cuda.zeros(1000, dtype=cuda.uint8, device="cuda")
+    xq = cuda.zeros(1000, dtype=cuda.uint8, device="cuda")
+    with pytest.raises(P.InvalidArgument, match="whole weight blocks required"):
+        P.qmv(P.Q4_K, w, 1, 128, xq, 1)
+    with pytest.raises(P.InvalidArgument, match="batch"):
+        P.qmv(P.Q4_0, w, 1, 32, xq, 17)
+    with pytest.raises(P.InvalidArgument, match="unknown weight type"):
+        P.qmv(7, w, 1, 32, xq, 1)
