@@ -401,6 +401,10 @@ p100_status p100_attn_validate(const p100_attn_desc* desc, char* why, size_t why
 size_t p100_fa_workspace_size(const p100_attn_desc* desc) {
     clear_error();
     if (!desc) return 0;
+    if (const char* why = attn_reason(*desc)) {
+        set_error(P100_ERR_INVALID, "%s", why);
+        return 0;
+    }
     int sms = 0;
     if (require_sm100(nullptr, &sms)) return 0;
     FaPlan plan;

@@ -11,12 +11,21 @@
 // ncclGetErrorString text; destroy aborts a communicator that reports an
 // asynchronous error instead of waiting on it.  P100_FAULT=tp_init makes
 // init fail on the host (for tests of the error path; no GPU involvement).
+//
+// NCCL is bound at first use with dlopen rather than linked: a process that
+// already holds an NCCL (PyTorch loads its own libnccl.so.2) keeps that one,
+// so two NCCL builds never meet in one process.  P100_NCCL_LIB names a
+// specific library file.
 #include <cuda_runtime.h>
+#include <dlfcn.h>
 #include <nccl.h>
 
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 #include <new>
+#include <type_traits>
+#include <string>
 #include <vector>
 
 #include "p100/b200.h"
@@ -54,9 +63,62 @@ bool fault_injected(const char* name) {
 }  // namespace p100b
 
 namespace {
+// The NCCL entry points this layer uses, resolved from one library handle.
+struct Nccl {
+    decltype(&ncclGetUniqueId) getUniqueId = nullptr;
+    decltype(&ncclCommInitRank) commInitRank = nullptr;
+    decltype(&ncclCommInitAll) commInitAll = nullptr;
+    decltype(&ncclAllReduce) allReduce = nullptr;
+    decltype(&ncclAllGather) allGather = nullptr;
+    decltype(&ncclGroupStart) groupStart = nullptr;
+    decltype(&ncclGroupEnd) groupEnd = nullptr;
+    decltype(&ncclCommDestroy) commDestroy = nullptr;
+    decltype(&ncclCommAbort) commAbort = nullptr;
+    decltype(&ncclCommGetAsyncError) commGetAsyncError = nullptr;
+    decltype(&ncclGetErrorString) getErrorString = nullptr;
+    std::string error;
+};
+
+const Nccl& nccl() {
+    static Nccl api;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* h = nullptr;
+        if (const char* path = std::getenv("P100_NCCL_LIB")) h = dlopen(path, RTLD_NOW | RTLD_GLOBAL);
+        if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL | RTLD_NOLOAD);   // already in the process
+        if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) {
+            const char* why = dlerror();
+            api.error = std::string("cannot load libnccl.so.2: ") + (why ? why : "unknown");
+            return;
+        }
+        auto bind = [&](auto& fn, const char* name) {
+            fn = reinterpret_cast<std::remove_reference_t<decltype(fn)>>(dlsym(h, name));
+            if (!fn && api.error.empty()) api.error = std::string("libnccl.so.2 lacks ") + name;
+        };
+        bind(api.getUniqueId, "ncclGetUniqueId");
+        bind(api.commInitRank, "ncclCommInitRank");
+        bind(api.commInitAll, "ncclCommInitAll");
+        bind(api.allReduce, "ncclAllReduce");
+        bind(api.allGather, "ncclAllGather");
+        bind(api.groupStart, "ncclGroupStart");
+        bind(api.groupEnd, "ncclGroupEnd");
+        bind(api.commDestroy, "ncclCommDestroy");
+        bind(api.commAbort, "ncclCommAbort");
+        bind(api.commGetAsyncError, "ncclCommGetAsyncError");
+        bind(api.getErrorString, "ncclGetErrorString");
+    });
+    return api;
+}
+
+p100_status nccl_ready() {
+    const Nccl& api = nccl();
+    return api.error.empty() ? P100_OK : set_error(P100_ERR_NCCL, "%s", api.error.c_str());
+}
+
 p100_status nccl_status(ncclResult_t r, const char* what) {
     if (r == ncclSuccess) return P100_OK;
-    return set_error(P100_ERR_NCCL, "%s: %s", what, ncclGetErrorString(r));
+    return set_error(P100_ERR_NCCL, "%s: %s", what, nccl().getErrorString(r));
 }
 
 // Restores the caller's current device on scope exit.
@@ -80,8 +142,9 @@ p100_status p100_tp_unique_id(void* id) {
     clear_error();
     static_assert(sizeof(ncclUniqueId) == P100_TP_ID_BYTES, "ncclUniqueId size");
     if (!id) return set_error(P100_ERR_INVALID, "null id buffer");
+    if (p100_status st = nccl_ready()) return st;
     ncclUniqueId uid;
-    if (p100_status st = nccl_status(ncclGetUniqueId(&uid), "ncclGetUniqueId")) return st;
+    if (p100_status st = nccl_status(nccl().getUniqueId(&uid), "ncclGetUniqueId")) return st;
     std::memcpy(id, &uid, sizeof uid);
     return P100_OK;
 }
@@ -92,6 +155,7 @@ p100_status p100_tp_init_rank(const void* id, int nranks, int rank, int device, 
     if (nranks < 1 || rank < 0 || rank >= nranks) return set_error(P100_ERR_INVALID, "rank %d of %d", rank, nranks);
     *out = nullptr;
     if (fault_injected("tp_init")) return set_error(P100_ERR_NCCL, "injected fault: tp_init (P100_FAULT)");
+    if (p100_status st = nccl_ready()) return st;
     DeviceScope scope;
     if (p100_status st = cuda_status(cudaSetDevice(device), "cudaSetDevice")) return st;
     if (p100_status st = require_sm100(nullptr, nullptr)) return st;
@@ -99,7 +163,7 @@ p100_status p100_tp_init_rank(const void* id, int nranks, int rank, int device, 
     std::memcpy(&uid, id, sizeof uid);
     auto* tp = new (std::nothrow) p100_tp;
     if (!tp) return set_error(P100_ERR_INVALID, "out of host memory");
-    if (p100_status st = nccl_status(ncclCommInitRank(&tp->comm, nranks, uid, rank), "ncclCommInitRank")) {
+    if (p100_status st = nccl_status(nccl().commInitRank(&tp->comm, nranks, uid, rank), "ncclCommInitRank")) {
         delete tp;
         return st;
     }
@@ -114,13 +178,14 @@ p100_status p100_tp_create(int ngpu, const int* devs, p100_tp** out) {
     clear_error();
     if (ngpu < 1 || !devs || !out) return set_error(P100_ERR_INVALID, "bad arguments");
     if (fault_injected("tp_init")) return set_error(P100_ERR_NCCL, "injected fault: tp_init (P100_FAULT)");
+    if (p100_status st = nccl_ready()) return st;
     DeviceScope scope;
     for (int i = 0; i < ngpu; ++i) {
         if (p100_status st = cuda_status(cudaSetDevice(devs[i]), "cudaSetDevice")) return st;
         if (p100_status st = require_sm100(nullptr, nullptr)) return st;
     }
     std::vector<ncclComm_t> comms(ngpu);
-    if (p100_status st = nccl_status(ncclCommInitAll(comms.data(), ngpu, devs), "ncclCommInitAll")) return st;
+    if (p100_status st = nccl_status(nccl().commInitAll(comms.data(), ngpu, devs), "ncclCommInitAll")) return st;
     for (int i = 0; i < ngpu; ++i) {
         out[i] = new p100_tp;
         out[i]->comm = comms[i];
@@ -141,7 +206,7 @@ p100_status p100_tp_allreduce_sum(p100_tp* tp, float* buf, size_t count, p100_st
     if (count == 0) return P100_OK;
     DeviceScope scope;
     if (p100_status st = cuda_status(cudaSetDevice(tp->device), "cudaSetDevice")) return st;
-    return nccl_status(ncclAllReduce(buf, buf, count, ncclFloat32, ncclSum, tp->comm, stream), "ncclAllReduce");
+    return nccl_status(nccl().allReduce(buf, buf, count, ncclFloat32, ncclSum, tp->comm, stream), "ncclAllReduce");
 }
 
 p100_status p100_tp_allreduce_sum_group(p100_tp* const* tps, int n, float* const* bufs, size_t count,
@@ -150,15 +215,15 @@ p100_status p100_tp_allreduce_sum_group(p100_tp* const* tps, int n, float* const
     if (!tps || !bufs || !streams || n < 1) return set_error(P100_ERR_INVALID, "null argument");
     if (count == 0) return P100_OK;
     DeviceScope scope;
-    if (p100_status st = nccl_status(ncclGroupStart(), "ncclGroupStart")) return st;
+    if (p100_status st = nccl_status(nccl().groupStart(), "ncclGroupStart")) return st;
     p100_status first = P100_OK;
     for (int i = 0; i < n && !first; ++i) {
         first = cuda_status(cudaSetDevice(tps[i]->device), "cudaSetDevice");
         if (!first)
-            first = nccl_status(ncclAllReduce(bufs[i], bufs[i], count, ncclFloat32, ncclSum, tps[i]->comm, streams[i]),
+            first = nccl_status(nccl().allReduce(bufs[i], bufs[i], count, ncclFloat32, ncclSum, tps[i]->comm, streams[i]),
                                 "ncclAllReduce");
     }
-    p100_status end = nccl_status(ncclGroupEnd(), "ncclGroupEnd");
+    p100_status end = nccl_status(nccl().groupEnd(), "ncclGroupEnd");
     return first ? first : end;
 }
 
@@ -168,7 +233,7 @@ p100_status p100_tp_allgather(p100_tp* tp, const float* in, float* out, size_t c
     if (count == 0) return P100_OK;
     DeviceScope scope;
     if (p100_status st = cuda_status(cudaSetDevice(tp->device), "cudaSetDevice")) return st;
-    return nccl_status(ncclAllGather(in, out, count, ncclFloat32, tp->comm, stream), "ncclAllGather");
+    return nccl_status(nccl().allGather(in, out, count, ncclFloat32, tp->comm, stream), "ncclAllGather");
 }
 
 p100_status p100_tp_destroy(p100_tp* tp) {
@@ -179,12 +244,12 @@ p100_status p100_tp_destroy(p100_tp* tp) {
     p100_status st = P100_OK;
     if (tp->comm) {
         ncclResult_t async = ncclSuccess;
-        ncclCommGetAsyncError(tp->comm, &async);
+        nccl().commGetAsyncError(tp->comm, &async);
         if (async != ncclSuccess) {
             st = nccl_status(async, "communicator async error");
-            ncclCommAbort(tp->comm);
+            nccl().commAbort(tp->comm);
         } else {
-            st = nccl_status(ncclCommDestroy(tp->comm), "ncclCommDestroy");
+            st = nccl_status(nccl().commDestroy(tp->comm), "ncclCommDestroy");
         }
     }
     delete tp;
