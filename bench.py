@@ -93,7 +93,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True)
             self.reader = threading.Thread(target=self._read, daemon=True)
             self.reader.start()
         except OSError:
@@ -129,7 +129,7 @@ class ClockSampler:
                 if val.lower().startswith("active"):
                     reasons.add(name)
         if not sm:
-            return None
+            return {"error": (self.lines[:2] or ["nvidia-smi gave no samples"])[0][:200]}
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
                 "samples": len(sm)}
 
@@ -207,19 +207,109 @@ def cpu_baseline_sample():
 
 
 # ------------------------------------------------------------------ B200 arm
+def capture(torch, fn):
+    """A CUDA graph of fn()'s stream work (the C-ABI calls it makes), captured
+    after one eager call has configured every kernel."""
+    fn()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, capture_error_mode="thread_local"):
+        fn()
+    return g
+
+
+def time_graphs(torch, graphs, n, stream):
+    """Device ms of n replays cycling through graphs (events on the stream)."""
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    for i in range(n):
+        graphs[i % len(graphs)].replay()
+    e.record(stream)
+    torch.cuda.synchronize()
+    return s.elapsed_time(e)
+
+
+FA_CONTEXTS = (512, 4096, 16384, 32768)
+
+
+def fa_section(torch, P, stream):
+    """Config 3: FA-vec decode, 32 query / 8 KV heads, d 128, per context
+    length; K/V rotate over copies totalling more than 3x L2; a CUDA graph of
+    back-to-back calls, CUDA events around its replays."""
+    out = {}
+    peak, _ = peak_gbs()
+    for seq in FA_CONTEXTS:
+        q, k, v = W.attention_inputs(1, 32, 8, seq, 128, seed=seq)
+        copies = max(2, int(np.ceil(3 * L2_BYTES / (k.nbytes * 2))) + 1)
+        qd = torch.from_numpy(q).cuda()
+        kd = [torch.from_numpy(k).cuda() for _ in range(copies)]
+        vd = [torch.from_numpy(v).cuda() for _ in range(copies)]
+        desc = P.AttnDesc(n_head_q=32, n_head_kv=8, seq_kv=seq)
+        ws = P.fa_workspace(desc)
+        o = torch.empty(1, 32, 1, 128, device="cuda")
+        lse = torch.empty(1, 32, 1, device="cuda")
+        reps = max(4, 64 // copies)
+        g = capture(torch, lambda: [P.fa_decode(desc, qd, kd[r % copies], vd[r % copies], o=o, lse=lse, ws=ws)
+                                    for r in range(copies * reps)])
+        time_graphs(torch, [g], 2, stream)
+        n = 10
+        us = time_graphs(torch, [g], n, stream) / (n * copies * reps) * 1e3
+        nbytes = W.fa_algorithmic_bytes(1, 32, 8, seq, 128)
+        out[str(seq)] = {"us": round(us, 3), "GB/s": round(nbytes / (us / 1e6) / 1e9, 1),
+                         "frac": round(nbytes / (us / 1e6) / 1e9 / peak, 4)}
+        del kd, vd
+    return out
+
+
+def kernel_only(args):
+    """Eager launches of one kernel over rotating inputs larger than L2 — the
+    small cases for ncu captures: the target mat-vec (5 weight copies, 165 MB)
+    or FA decode at 32K context (2 K/V copies, 268 MB)."""
+    import torch
+    import p100_b200 as P
+    if args.kernel_only == "fa":
+        seq = 32768
+        q, k, v = W.attention_inputs(1, 32, 8, seq, 128, seed=seq)
+        qd = torch.from_numpy(q).cuda()
+        kd = [torch.from_numpy(k).cuda() for _ in range(2)]
+        vd = [torch.from_numpy(v).cuda() for _ in range(2)]
+        desc = P.AttnDesc(n_head_q=32, n_head_kv=8, seq_kv=seq)
+        ws = P.fa_workspace(desc)
+        for i in range(args.warmup + args.steps):
+            P.fa_decode(desc, qd, kd[i % 2], vd[i % 2], ws=ws)
+        torch.cuda.synchronize()
+        P.check(P.device_error())
+        print(json.dumps({"kernel_only": f"fa_decode 32/8 heads d128 ctx {seq}", "launches": args.warmup + args.steps}))
+        return 0
+    _, k, rows = TARGET
+    base = torch.from_numpy(W.weights(W.Q4_0, rows, k, seed=1)).cuda()
+    ws = [base] + [base.clone() for _ in range(4)]
+    xq = P.q8_1_quantize(torch.from_numpy(W.activations(1, k, seed=2)).cuda())
+    y = torch.empty(1, rows, device="cuda")
+    for i in range(args.warmup + args.steps):
+        P.qmv(W.Q4_0, ws[i % len(ws)], rows, k, xq, 1, y=y)
+    torch.cuda.synchronize()
+    P.check(P.device_error())
+    print(json.dumps({"kernel_only": f"qmv Q4_0 {k}x{rows}", "launches": args.warmup + args.steps}))
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
-    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=5000)
+    ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kernel-only", choices=["qmv", "fa"], help="one kernel's launches only (ncu cases)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         return run_reference(args, rank, world)
+    if args.kernel_only:
+        return kernel_only(args)
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
 
@@ -236,24 +326,25 @@ def main():
     stream = torch.cuda.current_stream()
 
     # Weights: one host-generated set per shape, replicated on the device into
-    # R copies so the steps rotate through more than 3x L2 of distinct bytes.
+    # `copies` copies so successive steps rotate through more than 3x L2.
     per_copy = sum(W.weights(W.Q4_0, 1, k, 0).size * rows for _, k, rows in SHAPES)
     copies = max(4, int(np.ceil(3 * L2_BYTES / per_copy)) + 1)
     wdev = []
     for si, (name, k, rows) in enumerate(SHAPES):
-        host = torch.from_numpy(W.weights(W.Q4_0, rows, k, seed=1000 + si + 17 * rank))
-        base = host.cuda()
+        base = torch.from_numpy(W.weights(W.Q4_0, rows, k, seed=1000 + si + 17 * rank)).cuda()
         wdev.append([base] + [base.clone() for _ in range(copies - 1)])
     xs = [torch.from_numpy(W.activations(1, k, seed=2000 + si)).cuda() for si, (_, k, _) in enumerate(SHAPES)]
     xqs = [torch.empty(P.q8_1_bytes(k, 1), dtype=torch.uint8, device="cuda") for _, k, _ in SHAPES]
     ys = [torch.empty(1, rows, dtype=torch.float32, device="cuda") for _, _, rows in SHAPES]
     launches_per_step = 2 * len(SHAPES)
 
-    def step(i):
-        c = i % copies
+    def step_body(c):
+        # Each mat-vec is a programmatic dependent of its quantise kernel: its
+        # weights stream in while the quantiser runs; its activations are read
+        # after the quantiser completes.
         for si, (name, k, rows) in enumerate(SHAPES):
-            P.q8_1_quantize(xs[si], out=xqs[si], stream=stream)
-            P.qmv(W.Q4_0, wdev[si][c], rows, k, xqs[si], 1, y=ys[si], stream=stream)
+            P.q8_1_quantize(xs[si], out=xqs[si])
+            P.qmv(W.Q4_0, wdev[si][c], rows, k, xqs[si], 1, y=ys[si], flags=P.QMV_PDL)
 
     def barrier():
         if dist is not None:
@@ -266,98 +357,120 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return t.item()
 
-    for i in range(args.warmup):
-        step(i)
-    torch.cuda.synchronize()
+    # One graph per weight copy: step i replays graph i % copies.
+    graphs = [capture(torch, lambda c=c: step_body(c)) for c in range(copies)]
+    time_graphs(torch, graphs, args.warmup, stream)
     barrier()
     torch.cuda.synchronize()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
-        start.record(stream)
-        for i in range(args.steps):
-            step(i)
-        end.record(stream)
-        torch.cuda.synchronize()
-    ms = max_over_ranks(start.elapsed_time(end))
+        ms = time_graphs(torch, graphs, args.steps, stream)
+    ms = max_over_ranks(ms)
     barrier()
     per_step = step_bytes()
     value = per_step * world * args.steps / (ms / 1e3) / 1e9
 
-    # Per-shape device time (same rotation, each shape alone) and the target kernel.
-    shape_gbs = {}
-    target_ms = None
-    reps = 8 * copies
+    # Each shape alone: a graph of 4*copies back-to-back launches over the
+    # rotating copies, chained with PDL (each launch's weights stream in while
+    # the previous one finishes) and, for comparison, isolated.
+    shape_gbs, target_us, target_us_isolated = {}, None, None
     for si, (name, k, rows) in enumerate(SHAPES):
-        P.q8_1_quantize(xs[si], out=xqs[si], stream=stream)
-        for r in range(copies):
-            P.qmv(W.Q4_0, wdev[si][r], rows, k, xqs[si], 1, y=ys[si], stream=stream)
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record(stream)
-        for r in range(reps):
-            P.qmv(W.Q4_0, wdev[si][r % copies], rows, k, xqs[si], 1, y=ys[si], stream=stream)
-        e.record(stream)
-        torch.cuda.synchronize()
-        t = s.elapsed_time(e) / reps
-        shape_gbs[f"{name} {k}x{rows}"] = {"us": round(t * 1e3, 3),
-                                           "GB/s": round(W.qmv_algorithmic_bytes(W.Q4_0, rows, k, 1) / (t / 1e3) / 1e9, 1)}
+        P.q8_1_quantize(xs[si], out=xqs[si])
+        n_in_graph = 4 * copies
+        per = {}
+        for mode, flags in (("chained", P.QMV_PDL), ("isolated", 0)):
+            g = capture(torch, lambda si=si, k=k, rows=rows, flags=flags: [
+                P.qmv(W.Q4_0, wdev[si][r % copies], rows, k, xqs[si], 1, y=ys[si], flags=flags)
+                for r in range(n_in_graph)])
+            time_graphs(torch, [g], 3, stream)
+            reps = 20
+            per[mode] = time_graphs(torch, [g], reps, stream) / (reps * n_in_graph) * 1e3
+        nbytes = W.qmv_algorithmic_bytes(W.Q4_0, rows, k, 1)
+        shape_gbs[f"{name} {k}x{rows}"] = {
+            "us": round(per["chained"], 3), "GB/s": round(nbytes / (per["chained"] / 1e6) / 1e9, 1),
+            "us_isolated": round(per["isolated"], 3),
+            "GB/s_isolated": round(nbytes / (per["isolated"] / 1e6) / 1e9, 1)}
         if (name, k, rows) == TARGET:
-            target_ms = t
+            target_us, target_us_isolated = per["chained"], per["isolated"]
 
-    # End to end through the C-ABI with host buffers.
+    # End to end through the C-ABI with host buffers: each step copies its
+    # activations in from pinned memory, runs, copies y out and synchronises
+    # before the host reads the result.  "graph": the calls captured once and
+    # replayed (a decode loop's form); "eager": the calls issued every step.
     xh = [torch.from_numpy(W.activations(1, k, seed=3000 + si)).pin_memory() for si, (_, k, _) in enumerate(SHAPES)]
     yh = [torch.empty(1, rows, dtype=torch.float32).pin_memory() for _, _, rows in SHAPES]
     xd = [torch.empty(1, k, dtype=torch.float32, device="cuda") for _, k, _ in SHAPES]
     h2d = sum(t.numel() * 4 for t in xh)
     d2h = sum(t.numel() * 4 for t in yh)
 
-    def e2e_step(i):
-        c = i % copies
+    def e2e_body(c):
         for si, (name, k, rows) in enumerate(SHAPES):
             xd[si].copy_(xh[si], non_blocking=True)
-            P.q8_1_quantize(xd[si], out=xqs[si], stream=stream)
-            P.qmv(W.Q4_0, wdev[si][c], rows, k, xqs[si], 1, y=ys[si], stream=stream)
+            P.q8_1_quantize(xd[si], out=xqs[si])
+            P.qmv(W.Q4_0, wdev[si][c], rows, k, xqs[si], 1, y=ys[si], flags=P.QMV_PDL)
             yh[si].copy_(ys[si], non_blocking=True)
-        stream.synchronize()   # the host reads this step's results
 
-    for i in range(args.warmup):
-        e2e_step(i)
+    e2e_graphs = [capture(torch, lambda c=c: e2e_body(c)) for c in range(copies)]
+    checksum = 0.0
+
+    def e2e_run(n, eager):
+        nonlocal checksum
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        for i in range(n):
+            if eager:
+                e2e_body(i % copies)
+            else:
+                e2e_graphs[i % copies].replay()
+            stream.synchronize()
+            checksum += float(yh[0][0, 0])      # the host reads the step's result
+        e.record(stream)
+        torch.cuda.synchronize()
+        return s.elapsed_time(e)
+
+    e2e_run(args.warmup, False)
+    e2e_run(args.warmup, True)
     barrier()
-    torch.cuda.synchronize()
-    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s.record(stream)
-    for i in range(args.steps):
-        e2e_step(i)
-    e.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = max_over_ranks(s.elapsed_time(e))
+    e2e_ms = max_over_ranks(e2e_run(args.steps, False))
+    e2e_eager_ms = max_over_ranks(e2e_run(args.steps, True))
     barrier()
     e2e_value = per_step * world * args.steps / (e2e_ms / 1e3) / 1e9
+    e2e_eager = per_step * world * args.steps / (e2e_eager_ms / 1e3) / 1e9
+    del e2e_graphs
+    fa = fa_section(torch, P, stream) if rank == 0 else None
     P.check(P.device_error())
 
     peak, peak_kind = peak_gbs()
     target_bytes = W.qmv_algorithmic_bytes(W.Q4_0, TARGET[2], TARGET[1], 1)
-    achieved = target_bytes / (target_ms / 1e3) / 1e9
-    traffic = ncu_traffic("qmv_q4_0_4096x14336")
+    achieved = target_bytes / (target_us / 1e6) / 1e9
     result = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "int8/fp32", "data": "synthetic",
         "config": {"workload": WORKLOAD, "global_batch": world, "seq_len": 1,
                    "parallelism": f"row-split shards x{world}, no data-path collective" if world > 1 else "1 GPU",
-                   "l2": f"inputs larger than L2: {copies} rotating weight copies ({copies * per_copy / 1e6:.0f} MB)"},
+                   "l2": f"inputs larger than L2: {copies} rotating weight copies ({copies * per_copy / 1e6:.0f} MB)",
+                   "launch": "C-ABI calls captured into one CUDA graph per weight copy, replayed per step"},
         "roofline": {"bound": "hbm", "kernel": "qmv_bulk_kernel<Q4_0,1,1> gate/up 4096x14336",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_source": peak_kind,
-                     "traffic": traffic, "algorithmic_bytes": target_bytes, "us_per_launch": round(target_ms * 1e3, 3)},
-        "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+                     "traffic": ncu_traffic("qmv_q4_0_4096x14336"), "algorithmic_bytes": target_bytes,
+                     "us_per_launch": round(target_us, 3),
+                     "timing": "CUDA events over graph replays of back-to-back launches chained with PDL",
+                     "isolated_us_per_launch": round(target_us_isolated, 3),
+                     "isolated_frac": round(target_bytes / (target_us_isolated / 1e6) / 1e9 / peak, 4)},
+        "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "form": "graph replay + stream sync + host read per step", "eager_value": round(e2e_eager, 2)},
         "gpu_launches": launches_per_step * args.steps,
         "shapes": shape_gbs,
+        "fa_decode": fa,
         "clocks": clocks.summary(),
+        "checksum": round(checksum, 3),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline_sample()
     if rank == 0:
         print(json.dumps(result), flush=True)
+    del graphs
     if dist is not None:
         dist.destroy_process_group()
     return 0

@@ -13,6 +13,7 @@
 #include "common.cuh"
 #include "fa_decode.cuh"
 #include "qmv.cuh"
+#include "qmv_team.cuh"
 #include "quant.cuh"
 
 namespace p100b {
@@ -79,64 +80,68 @@ p100_status launch_status(const char* what) { return cuda_status(cudaGetLastErro
 // ------------------------------------------------------------------ qmv plan
 struct QmvPlan {
     qmv::Params p;
-    int ipt = 0, bmax = 0, grid = 0;
+    int bmax = 0, grid = 0, threads = 0;
     size_t smem = 0;
 };
 
-// Fills plan for the bulk path; false if the shape or alignment needs the
-// generic kernel.
-bool plan_bulk(int type, const void* w, int rows, int k, int sms, QmvPlan& plan) {
+size_t round128(size_t x) { return (x + 127) & ~size_t(127); }
+
+// Fills plan for the bulk path with up to bmax activation columns per launch;
+// false if the shape or alignment needs the generic kernel.  Stages are whole
+// rows, about 16 KB; for one column the CTA keeps to half an SM's shared
+// memory so two launches of a chain are resident together.
+constexpr size_t kStageTarget = 16 * 1024;
+
+bool plan_bulk(int type, const void* w, int rows, int k, int batch, int sms, QmvPlan& plan) {
     const size_t row_bytes = size_t(k / elems_of(type)) * bytes_of(type);
     if (reinterpret_cast<uintptr_t>(w) % 16 || row_bytes % 16 || k % 256) return false;
-    const int ipr = k / 64;
-    const int ipt = (ipr + qmv::kThreads - 1) / qmv::kThreads;
-    if (ipt > 2) return false;
-    const int per = (ipr + ipt - 1) / ipt;
-    const int tpr = (per + 31) / 32 * 32;
-    const int groups = qmv::kThreads / tpr;
-    const int bmax = ipt == 1 ? 4 : 2;
-    int rps = groups * std::max(1, int(qmv::kStageCap / (row_bytes * groups)));
-    if (rps * bmax > qmv::kThreads) rps = (qmv::kThreads / bmax) / groups * groups;
-    if (rps < 1) return false;
-    const size_t stage = size_t(rps) * row_bytes;
-    const int slot = int((stage + 127) / 128 * 128);
-    const int part_floats = bmax * rps * (tpr / 32);
-    const size_t head = 128 + ((size_t(2) * part_floats * 4 + 127) & ~size_t(127));
-    int nstage = qmv::kMaxStages;
-    while (nstage > 1 && head + size_t(nstage) * slot > size_t(qmv::kSmemLimit)) --nstage;
-    if (nstage < 2) return false;
-    plan.p.rows = rows;
-    plan.p.k = k;
-    plan.p.row_bytes = int(row_bytes);
-    plan.p.ipr = ipr;
-    plan.p.tpr = tpr;
-    plan.p.groups = groups;
-    plan.p.rps = rps;
-    plan.p.nstage = nstage;
-    plan.p.slot_bytes = slot;
-    plan.p.part_floats = part_floats;
-    plan.ipt = ipt;
-    plan.bmax = bmax;
-    plan.smem = head + size_t(nstage) * slot;
-    const int want = (rows + rps - 1) / rps;   // no CTA with less than a stage of rows
-    plan.grid = std::max(1, std::min(sms, want));
-    return true;
+    const int rps = int(std::max<size_t>(1, std::min<size_t>(qmv::kMaxRows, (kStageTarget + row_bytes / 2) / row_bytes)));
+    const size_t slot = round128(size_t(rps) * row_bytes);
+    for (int bmax = std::min(4, batch); bmax >= 1; --bmax) {
+        const size_t limit = bmax == 1 ? size_t(qmv::kSmemLimit) / 2 - 1024 : size_t(qmv::kSmemLimit);
+        const size_t part_off = 512;                                       // barriers + tickets
+        const size_t part_bytes = size_t(qmv::kMaxSlots) * qmv::kConsumers * qmv::kMaxRows * bmax * 4;
+        const size_t codes_off = part_off + round128(part_bytes);
+        const size_t meta_off = codes_off + round128(size_t(bmax) * k);    // codes: bmax*8*(k/32) words
+        const size_t ring_off = meta_off + round128(size_t(bmax) * (k / 32) * 8);
+        if (ring_off + 3 * slot > limit) continue;
+        const int nslot = int(std::min<size_t>(qmv::kMaxSlots, (limit - ring_off) / slot));
+        plan.p.rows = rows;
+        plan.p.k = k;
+        plan.p.row_bytes = int(row_bytes);
+        plan.p.ipr = k / 64;
+        plan.p.rps = rps;
+        plan.p.nslot = nslot;
+        plan.p.slot_bytes = int(slot);
+        plan.p.part_off = int(part_off);
+        plan.p.codes_off = int(codes_off);
+        plan.p.meta_off = int(meta_off);
+        plan.p.ring_off = int(ring_off);
+        plan.bmax = bmax;
+        plan.smem = ring_off + size_t(nslot) * slot;
+        plan.threads = qmv::kThreads;
+        plan.grid = std::max(1, std::min(sms, (rows + rps - 1) / rps));
+        return true;
+    }
+    return false;
 }
 
-template <int TYPE, int B, int IPT>
+template <int TYPE, int B>
 p100_status launch_bulk_t(const QmvPlan& plan, bool pdl, cudaStream_t stream) {
-    auto kern = qmv::qmv_bulk_kernel<TYPE, B, IPT>;
+    auto kern = qmv::qmv_bulk_kernel<TYPE, B>;
     static thread_local int configured_smem[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (configured_smem[dev] < int(plan.smem)) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(plan.smem));
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, qmv::kSmemLimit);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
         if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(qmv)");
-        configured_smem[dev] = int(plan.smem);
+        configured_smem[dev] = qmv::kSmemLimit;
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(plan.grid);
-    cfg.blockDim = dim3(qmv::kThreads);
+    cfg.blockDim = dim3(plan.threads);
     cfg.dynamicSmemBytes = plan.smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
@@ -149,15 +154,84 @@ p100_status launch_bulk_t(const QmvPlan& plan, bool pdl, cudaStream_t stream) {
 
 template <int TYPE>
 p100_status launch_bulk_type(const QmvPlan& plan, int cols, bool pdl, cudaStream_t s) {
-    if (plan.ipt == 1) {
-        switch (cols) {
-            case 1: return launch_bulk_t<TYPE, 1, 1>(plan, pdl, s);
-            case 2: return launch_bulk_t<TYPE, 2, 1>(plan, pdl, s);
-            case 3: return launch_bulk_t<TYPE, 3, 1>(plan, pdl, s);
-            default: return launch_bulk_t<TYPE, 4, 1>(plan, pdl, s);
-        }
+    switch (cols) {
+        case 1: return launch_bulk_t<TYPE, 1>(plan, pdl, s);
+        case 2: return launch_bulk_t<TYPE, 2>(plan, pdl, s);
+        case 3: return launch_bulk_t<TYPE, 3>(plan, pdl, s);
+        default: return launch_bulk_t<TYPE, 4>(plan, pdl, s);
     }
-    return cols == 1 ? launch_bulk_t<TYPE, 1, 2>(plan, pdl, s) : launch_bulk_t<TYPE, 2, 2>(plan, pdl, s);
+}
+
+// ------------------------------------------------------------------ team plan
+struct TeamPlan {
+    qmvt::Params p;
+    int grid = 0;
+    size_t smem = 0;
+};
+
+// The batch-1 kernel: a lane per 256-weight column group, one row per team
+// per stage.  Needs 16-byte aligned weights and activations and k % 256 == 0.
+bool plan_team(int type, const void* w, const void* xq, int rows, int k, int batch, int sms, TeamPlan& plan) {
+    if (batch != 1 || k % 256 || reinterpret_cast<uintptr_t>(w) % 16 || reinterpret_cast<uintptr_t>(xq) % 16)
+        return false;
+    const int ngroups = k / 256;
+    int team = 1;
+    if (ngroups <= 32) {
+        while (team < ngroups) team <<= 1;
+    } else {
+        team = (ngroups + 31) / 32 * 32;
+    }
+    if (team > qmvt::kConsumers * 32) return false;
+    const size_t row_bytes = size_t(k / elems_of(type)) * bytes_of(type);
+    const int teams = qmvt::kConsumers * 32 / team;
+    const size_t slot = round128(size_t(teams) * row_bytes);
+    const size_t part_off = 128;                                          // 2 x 8 mbarriers
+    const size_t ring_off = part_off + round128(size_t(2) * teams * std::max(1, team / 32) * 4);
+    if (ring_off + 2 * slot > size_t(qmvt::kSmemLimit)) return false;
+    const int nslot = int(std::min<size_t>(qmvt::kMaxSlots, (qmvt::kSmemLimit - ring_off) / slot));
+    plan.p.rows = rows;
+    plan.p.k = k;
+    plan.p.row_bytes = int(row_bytes);
+    plan.p.ngroups = ngroups;
+    plan.p.team = team;
+    plan.p.teams = teams;
+    plan.p.nslot = nslot;
+    plan.p.slot_bytes = int(slot);
+    plan.p.part_off = int(part_off);
+    plan.p.ring_off = int(ring_off);
+    plan.smem = ring_off + size_t(nslot) * slot;
+    plan.grid = std::max(1, std::min(sms, (rows + teams - 1) / teams));
+    return true;
+}
+
+template <int TYPE>
+p100_status launch_team_t(const TeamPlan& plan, bool pdl, cudaStream_t stream) {
+    auto kern = qmvt::qmv_team_kernel<TYPE>;
+    static thread_local int configured[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!configured[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, qmvt::kSmemLimit);
+        if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(qmv_team)");
+        configured[dev] = 1;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(plan.grid);
+    cfg.blockDim = dim3(qmvt::kThreads);
+    cfg.dynamicSmemBytes = plan.smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cuda_status(cudaLaunchKernelEx(&cfg, kern, plan.p), "qmv_team_kernel launch");
+}
+
+template <int TYPE>
+p100_status launch_team_type(const TeamPlan& plan, int batch, bool pdl, cudaStream_t s) {
+    (void)batch;   // the team kernel serves one column
+    return launch_team_t<TYPE>(plan, pdl, s);
 }
 
 p100_status run_qmv(int type, const void* w, int rows, int k, const void* xq, int batch, float* y, unsigned flags,
@@ -172,8 +246,21 @@ p100_status run_qmv(int type, const void* w, int rows, int k, const void* xq, in
     if (reinterpret_cast<uintptr_t>(w) % 2) return set_error(P100_ERR_INVALID, "weights must be 2-byte aligned");
     int sms = 0;
     if (p100_status st = require_sm100(nullptr, &sms)) return st;
+    const bool pdl = (flags & P100_QMV_PDL) != 0;
+    TeamPlan tplan;
+    if (plan_team(type, w, xq, rows, k, batch, sms, tplan)) {
+        tplan.p.w = static_cast<const uint8_t*>(w);
+        tplan.p.xq = static_cast<const uint8_t*>(xq);
+        tplan.p.y = y;
+        tplan.p.col0 = 0;
+        switch (type) {
+            case P100_Q4_0: return launch_team_type<P100_Q4_0>(tplan, batch, pdl, stream);
+            case P100_Q8_0: return launch_team_type<P100_Q8_0>(tplan, batch, pdl, stream);
+            default: return launch_team_type<P100_Q4_K>(tplan, batch, pdl, stream);
+        }
+    }
     QmvPlan plan;
-    if (plan_bulk(type, w, rows, k, sms, plan)) {
+    if (plan_bulk(type, w, rows, k, batch, sms, plan)) {
         plan.p.w = static_cast<const uint8_t*>(w);
         plan.p.xq = static_cast<const uint8_t*>(xq);
         plan.p.y = y;
@@ -183,11 +270,11 @@ p100_status run_qmv(int type, const void* w, int rows, int k, const void* xq, in
             p100_status st;
             // Only the first launch may overlap the previous kernel; later
             // column chunks follow this call's own launches.
-            const bool pdl = (flags & P100_QMV_PDL) && c0 == 0;
+            const bool chained = pdl && c0 == 0;
             switch (type) {
-                case P100_Q4_0: st = launch_bulk_type<P100_Q4_0>(plan, cols, pdl, stream); break;
-                case P100_Q8_0: st = launch_bulk_type<P100_Q8_0>(plan, cols, pdl, stream); break;
-                default: st = launch_bulk_type<P100_Q4_K>(plan, cols, pdl, stream); break;
+                case P100_Q4_0: st = launch_bulk_type<P100_Q4_0>(plan, cols, chained, stream); break;
+                case P100_Q8_0: st = launch_bulk_type<P100_Q8_0>(plan, cols, chained, stream); break;
+                default: st = launch_bulk_type<P100_Q4_K>(plan, cols, chained, stream); break;
             }
             if (st) return st;
         }
@@ -260,8 +347,14 @@ p100_status plan_fa(const p100_attn_desc& d, int sms, FaPlan& plan) {
 template <int D, int GMAX>
 p100_status launch_fa_t(const FaPlan& plan, const fa::Params& prm, int heads, cudaStream_t stream) {
     auto kern = fa::fa_decode_kernel<D, GMAX>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(plan.smem));
-    if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(fa)");
+    static thread_local int configured_smem[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (configured_smem[dev] < int(plan.smem)) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(plan.smem));
+        if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(fa)");
+        configured_smem[dev] = int(plan.smem);
+    }
     kern<<<dim3(plan.parts, heads), fa::kThreads, plan.smem, stream>>>(prm);
     return launch_status("fa_decode_kernel launch");
 }

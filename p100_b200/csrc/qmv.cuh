@@ -1,19 +1,28 @@
 // qmv.cuh — quantised mat-vec y = W x for Q4_0 / Q8_0 / Q4_K weights against
 // Q8_1 activations, batch 1..16, on CUDA cores (int8 dp4a).
 //
-// Bulk path (16-byte aligned rows, k % 256 == 0):
-//   * Each CTA owns a contiguous, balanced range of rows.  Its weight bytes are
-//     one contiguous span of the matrix, streamed HBM -> shared memory in
-//     stages of whole rows by untiled bulk-async copies (cp.async.bulk, L2
-//     evict-first) into a ring of up to 4 stages with one mbarrier each.
-//   * A row is cut into "items" of 64 weights: two Q4_0 or Q8_0 blocks, or a
-//     quarter Q4_K super-block (its 16-byte header plus 32 bytes of nibbles).
-//     Thread (group g, index t) always owns items t, t+T' of every row, so its
-//     Q8_1 activations for those items are loaded once into registers; the
-//     groups split each stage's rows.
-//   * Per row, a warp sums its items' products with an XOR butterfly and
-//     lane 0 writes one partial; after the stage barrier the partials of a row
-//     are added in warp order.  The output is deterministic.
+// Bulk path (16-byte aligned rows, k % 256 == 0), warp-specialised:
+//   * Each CTA owns a contiguous, balanced range of rows; its weight bytes are
+//     one contiguous span of the matrix, cut into stages of R whole rows of
+//     about 16 KB (smaller bulk copies lose bandwidth).
+//   * One producer warp streams the stages HBM -> shared memory with untiled
+//     bulk-async copies (cp.async.bulk, L2 evict-first) into a ring of slots,
+//     each with a "full" and an "empty" mbarrier.
+//   * All eight consumer warps work on every stage, in order: the stage's
+//     R x (k/64) items (64 weights each: two Q4_0/Q8_0 blocks, or a quarter
+//     Q4_K super-block) are split into eight contiguous shares, so a stage is
+//     held only briefly and most of the ring stays in flight.  A share spans
+//     at most two rows; each warp finishes its partial row sums with an XOR
+//     butterfly and stores them.  The last warp to finish a stage (a shared-
+//     memory ticket picks it) adds the eight partials of each row in warp
+//     order, writes y and frees the slot.  The ticket decides who adds, never
+//     the order, so results are deterministic.
+//   * The activations are staged once per CTA in shared memory with the int8
+//     codes transposed (word i of every block contiguous), so a lane's 8-byte
+//     reads of its block pair are bank-conflict free.
+//   * For one column the CTA keeps to half an SM, so two launches of a chain
+//     (programmatic dependent launch) are resident together: the next one's
+//     weights stream in while this one finishes.
 //
 // The per-block arithmetic is that of qmv::evaluate's q81 path
 // (qmv_model.cpp:147-180): exact int32 block dots, then FP32 scaling with the
@@ -26,15 +35,16 @@
 namespace p100b {
 namespace qmv {
 
-constexpr int kThreads = 256;
-constexpr int kMaxStages = 4;
-constexpr int kStageCap = 32 * 1024;      // target bytes per stage
+constexpr int kConsumers = 8;
+constexpr int kThreads = (kConsumers + 1) * 32;   // 8 consumer warps + 1 producer warp
+constexpr int kMaxSlots = 16;
+constexpr int kMaxRows = 8;                       // rows per stage
 constexpr int kSmemLimit = 227 * 1024;
 
-// Activation operands of one item (two 32-value blocks) for one column.
+// Activation operands of one item (blocks A = 2*it and B = 2*it+1) for one column.
 struct ItemAct {
-    int q[16];     // int8 codes of blocks 2*it and 2*it+1, four per word
-    float f[4];    // Q4_0: dxA, sumA, dxB, sumB; Q8_0: dxA, dxB; Q4_K: dx0, dx1, sumq0, sumq1
+    int q[16];   // int8 codes: A words 0..7, then B words 0..7
+    float4 m;    // (dA, mA, dB, mB): m = fp16 sum of x (Q4_0), sum of codes (Q4_K), 0 (Q8_0)
 };
 
 struct Params {
@@ -45,37 +55,11 @@ struct Params {
     int col0;              // first activation column of this launch
     int row_bytes;
     int ipr;               // items per row = k / 64
-    int tpr;               // threads per row group (multiple of 32)
-    int groups;            // row groups per CTA
-    int rps;               // rows per stage (multiple of groups)
-    int nstage;
+    int rps;               // rows per stage (1..kMaxRows)
+    int nslot;
     int slot_bytes;        // ring slot stride (multiple of 128)
-    int part_floats;       // floats per partial buffer
+    int part_off, codes_off, meta_off, ring_off;   // shared-memory offsets
 };
-
-__device__ __forceinline__ void load_item_act(int type, const uint8_t* __restrict__ xq, int nb, int col, int it,
-                                              ItemAct& a) {
-    const uint32_t* blk = reinterpret_cast<const uint32_t*>(xq + (size_t(col) * nb + 2 * it) * 36);
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-        const uint32_t ds = __ldg(blk + 9 * h);
-        int sumq = 0;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            a.q[8 * h + i] = static_cast<int>(__ldg(blk + 9 * h + 1 + i));
-            sumq = __dp4a(a.q[8 * h + i], 0x01010101, sumq);
-        }
-        if (type == P100_Q4_0) {
-            a.f[2 * h] = half_lo(ds);
-            a.f[2 * h + 1] = half_hi(ds);
-        } else if (type == P100_Q8_0) {
-            a.f[h] = half_lo(ds);
-        } else {
-            a.f[h] = half_lo(ds);
-            a.f[2 + h] = float(sumq);
-        }
-    }
-}
 
 // Adds item `it` of one staged row to acc[c] for every column c.
 template <int TYPE, int B>
@@ -96,19 +80,19 @@ __device__ __forceinline__ void item_dot(const uint8_t* __restrict__ row, int it
         }
 #pragma unroll
         for (int c = 0; c < B; ++c) {
-            int sa = 0, sb = 0;
+            int sa0 = 0, sa1 = 0, sb0 = 0, sb1 = 0;   // four independent dp4a chains
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 // byte m: low nibble is element m, high nibble element m+16
-                sa = __dp4a(static_cast<int>(qa[i] & 0x0f0f0f0fu), a[c].q[i], sa);
-                sa = __dp4a(static_cast<int>((qa[i] >> 4) & 0x0f0f0f0fu), a[c].q[4 + i], sa);
-                sb = __dp4a(static_cast<int>(qb[i] & 0x0f0f0f0fu), a[c].q[8 + i], sb);
-                sb = __dp4a(static_cast<int>((qb[i] >> 4) & 0x0f0f0f0fu), a[c].q[12 + i], sb);
+                sa0 = __dp4a(static_cast<int>(qa[i] & 0x0f0f0f0fu), a[c].q[i], sa0);
+                sa1 = __dp4a(static_cast<int>((qa[i] >> 4) & 0x0f0f0f0fu), a[c].q[4 + i], sa1);
+                sb0 = __dp4a(static_cast<int>(qb[i] & 0x0f0f0f0fu), a[c].q[8 + i], sb0);
+                sb1 = __dp4a(static_cast<int>((qb[i] >> 4) & 0x0f0f0f0fu), a[c].q[12 + i], sb1);
             }
             // d_w * (d_x * sum(nib*q) - 8 * sum(x)): the -8 offset through the
             // block sum, as the q81 path does per half block.
-            acc[c] = fmaf(dA, fmaf(float(sa), a[c].f[0], -8.0f * a[c].f[1]), acc[c]);
-            acc[c] = fmaf(dB, fmaf(float(sb), a[c].f[2], -8.0f * a[c].f[3]), acc[c]);
+            acc[c] = fmaf(dA, fmaf(float(sa0 + sa1), a[c].m.x, -8.0f * a[c].m.y), acc[c]);
+            acc[c] = fmaf(dB, fmaf(float(sb0 + sb1), a[c].m.z, -8.0f * a[c].m.w), acc[c]);
         }
     } else if (TYPE == P100_Q8_0) {
         // 68 bytes: block A at +0 (codes at +2), block B at +34 (codes at +36).
@@ -122,14 +106,16 @@ __device__ __forceinline__ void item_dot(const uint8_t* __restrict__ row, int it
         for (int i = 0; i < 8; ++i) qa[i] = static_cast<int>(shift2(W[i], W[i + 1]));
 #pragma unroll
         for (int c = 0; c < B; ++c) {
-            int sa = 0, sb = 0;
+            int sa0 = 0, sa1 = 0, sb0 = 0, sb1 = 0;
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                sa = __dp4a(qa[i], a[c].q[i], sa);
-                sb = __dp4a(static_cast<int>(W[9 + i]), a[c].q[8 + i], sb);
+            for (int i = 0; i < 4; ++i) {
+                sa0 = __dp4a(qa[i], a[c].q[i], sa0);
+                sa1 = __dp4a(qa[4 + i], a[c].q[4 + i], sa1);
+                sb0 = __dp4a(static_cast<int>(W[9 + i]), a[c].q[8 + i], sb0);
+                sb1 = __dp4a(static_cast<int>(W[13 + i]), a[c].q[12 + i], sb1);
             }
-            acc[c] = fmaf(dA * a[c].f[0], float(sa), acc[c]);
-            acc[c] = fmaf(dB * a[c].f[1], float(sb), acc[c]);
+            acc[c] = fmaf(dA * a[c].m.x, float(sa0 + sa1), acc[c]);
+            acc[c] = fmaf(dB * a[c].m.z, float(sb0 + sb1), acc[c]);
         }
     } else {
         // Quarter super-block: header (d, dmin, 12 scale bytes) + 32 nibble
@@ -160,131 +146,168 @@ __device__ __forceinline__ void item_dot(const uint8_t* __restrict__ row, int it
         const uint32_t N[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
 #pragma unroll
         for (int c = 0; c < B; ++c) {
-            int s0 = 0, s1 = 0;
+            int s0a = 0, s0b = 0, s1a = 0, s1b = 0;
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                s0 = __dp4a(static_cast<int>(N[i] & 0x0f0f0f0fu), a[c].q[i], s0);
-                s1 = __dp4a(static_cast<int>((N[i] >> 4) & 0x0f0f0f0fu), a[c].q[8 + i], s1);
+            for (int i = 0; i < 4; ++i) {
+                s0a = __dp4a(static_cast<int>(N[i] & 0x0f0f0f0fu), a[c].q[i], s0a);
+                s0b = __dp4a(static_cast<int>(N[4 + i] & 0x0f0f0f0fu), a[c].q[4 + i], s0b);
+                s1a = __dp4a(static_cast<int>((N[i] >> 4) & 0x0f0f0f0fu), a[c].q[8 + i], s1a);
+                s1b = __dp4a(static_cast<int>((N[4 + i] >> 4) & 0x0f0f0f0fu), a[c].q[12 + i], s1b);
             }
             // d * sum_j dx_j*(dot_j*sc_j) - dmin * sum_j dx_j*(sumq_j*mn_j)
             // (qmv_model.cpp:175-178, summed over both sub-blocks)
-            const float sd = fmaf(a[c].f[0], float(s0 * sc0), a[c].f[1] * float(s1 * sc1));
-            const float sm = fmaf(a[c].f[0], a[c].f[2] * float(mn0), a[c].f[1] * (a[c].f[3] * float(mn1)));
+            const float sd = fmaf(a[c].m.x, float((s0a + s0b) * sc0), a[c].m.z * float((s1a + s1b) * sc1));
+            const float sm = fmaf(a[c].m.x, a[c].m.y * float(mn0), a[c].m.z * (a[c].m.w * float(mn1)));
             acc[c] = fmaf(d, sd, acc[c]);
             acc[c] = fmaf(-dmin, sm, acc[c]);
         }
     }
 }
 
-template <int TYPE, int B, int IPT>
-__global__ void __launch_bounds__(kThreads, 1) qmv_bulk_kernel(const Params p) {
+template <int TYPE, int B>
+__global__ void __launch_bounds__(kThreads, B == 1 ? 2 : 1) qmv_bulk_kernel(const Params p) {
     extern __shared__ __align__(128) uint8_t smem[];
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem);                    // kMaxStages barriers
-    float* partial = reinterpret_cast<float*>(smem + 128);                // 2 buffers
-    uint8_t* ring = smem + 128 + ((2 * p.part_floats * 4 + 127) & ~127);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+    uint64_t* empty = full + kMaxSlots;
+    unsigned* ticket = reinterpret_cast<unsigned*>(empty + kMaxSlots);          // [kMaxSlots]
+    float* partial = reinterpret_cast<float*>(smem + p.part_off);              // [slot][warp][row][col]
+    uint32_t* codes = reinterpret_cast<uint32_t*>(smem + p.codes_off);         // [B][8][nb] words
+    float2* meta = reinterpret_cast<float2*>(smem + p.meta_off);               // [B][nb]
+    uint8_t* ring = smem + p.ring_off;
 
-    const int tid = threadIdx.x, lane = tid & 31;
-    const int g = tid / p.tpr, t = tid % p.tpr;
-    const bool active = g < p.groups;
-    const int wpg = p.tpr >> 5;                 // warps per row group
-    const int wig = t >> 5;                     // warp index within the group
-
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int nb = p.k / 32;
     const int r0 = static_cast<int>(static_cast<long long>(p.rows) * blockIdx.x / gridDim.x);
     const int r1 = static_cast<int>(static_cast<long long>(p.rows) * (blockIdx.x + 1) / gridDim.x);
     const int nst = (r1 - r0 + p.rps - 1) / p.rps;
 
     if (tid == 0) {
-        for (int s = 0; s < p.nstage; ++s) mbar_init(&full[s], 1);
+        for (int s = 0; s < p.nslot; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+            ticket[s] = 0;
+        }
         fence_barrier_init();
     }
     __syncthreads();
-
-    uint64_t policy = 0;
-    auto issue = [&](int s) {
-        const int slot = s % p.nstage;
-        const int first = r0 + s * p.rps;
-        const int nr = min(p.rps, r1 - first);
-        const uint32_t bytes = static_cast<uint32_t>(nr) * p.row_bytes;
-        mbar_arrive_expect_tx(&full[slot], bytes);
-        bulk_load(ring + size_t(slot) * p.slot_bytes, p.w + size_t(first) * p.row_bytes, bytes, &full[slot], policy);
-    };
-    if (tid == 0) {
-        policy = l2_evict_first_policy();
-        for (int s = 0; s < min(p.nstage, nst); ++s) issue(s);
-    }
-    // Weights never depend on the previous kernel; activations may.
     pdl_allow_dependents();
-    pdl_wait_prior_grid();
 
-    const int nb = p.k / 32;
-    ItemAct act[IPT][B];
-#pragma unroll
-    for (int u = 0; u < IPT; ++u) {
-        const int it = t + u * p.tpr;
-#pragma unroll
-        for (int c = 0; c < B; ++c) {
-            if (active && it < p.ipr) {
-                load_item_act(TYPE, p.xq, nb, p.col0 + c, it, act[u][c]);
-            } else {
-#pragma unroll
-                for (int i = 0; i < 16; ++i) act[u][c].q[i] = 0;
-#pragma unroll
-                for (int i = 0; i < 4; ++i) act[u][c].f[i] = 0.f;
+    if (warp == kConsumers) {
+        // ---- producer: weights never depend on the previous kernel
+        if (lane == 0) {
+            const uint64_t policy = l2_evict_first_policy();
+            for (int s = 0; s < nst; ++s) {
+                const int slot = s % p.nslot;
+                if (s >= p.nslot && !mbar_wait(&empty[slot], ((s / p.nslot) - 1) & 1)) break;
+                const int first = r0 + s * p.rps;
+                const uint32_t bytes = static_cast<uint32_t>(min(p.rps, r1 - first)) * p.row_bytes;
+                mbar_arrive_expect_tx(&full[slot], bytes);
+                bulk_load(ring + size_t(slot) * p.slot_bytes, p.w + size_t(first) * p.row_bytes, bytes, &full[slot],
+                          policy);
             }
         }
+        return;
     }
 
-    bool ok = true;
+    // ---- consumers: stage this launch's Q8_1 activations (they may come from
+    // the previous kernel), codes transposed.
+    pdl_wait_prior_grid();
+    for (int idx = tid; idx < B * nb; idx += kConsumers * 32) {
+        const int c = idx / nb, j = idx % nb;
+        const uint32_t* blk = reinterpret_cast<const uint32_t*>(p.xq + (size_t(p.col0 + c) * nb + j) * 36);
+        const uint32_t ds = __ldg(blk);
+        int sumq = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const uint32_t wq = __ldg(blk + 1 + i);
+            codes[(c * 8 + i) * nb + j] = wq;
+            sumq = __dp4a(static_cast<int>(wq), 0x01010101, sumq);
+        }
+        const float m = TYPE == P100_Q4_0 ? half_hi(ds) : TYPE == P100_Q4_K ? float(sumq) : 0.f;
+        meta[c * nb + j] = make_float2(half_lo(ds), m);
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(kConsumers * 32) : "memory");
+
     for (int s = 0; s < nst; ++s) {
-        const int slot = s % p.nstage;
-        const bool timed_out = !mbar_wait(&full[slot], (s / p.nstage) & 1);
+        const int slot = s % p.nslot;
+        // A timed-out wait is decided for the whole warp (vote), so no lane is
+        // left in a shuffle its peers have abandoned.
+        if (!__all_sync(0xffffffffu, mbar_wait(&full[slot], (s / p.nslot) & 1))) break;
         const uint8_t* stage = ring + size_t(slot) * p.slot_bytes;
         const int first = r0 + s * p.rps;
         const int nr = min(p.rps, r1 - first);
-        float* part = partial + (s & 1) * p.part_floats;
-        if (active) {
-            for (int rl = g; rl < nr; rl += p.groups) {
-                const uint8_t* row = stage + size_t(rl) * p.row_bytes;
-                float acc[B];
+        // This warp's share of the stage's nr x ipr items: at most two rows.
+        const int n_items = nr * p.ipr;
+        const int f0 = n_items * warp / kConsumers, f1 = n_items * (warp + 1) / kConsumers;
+        const int rw = f0 / p.ipr;   // first row of the share
+        float acc[2][B];
 #pragma unroll
-                for (int c = 0; c < B; ++c) acc[c] = 0.f;
+        for (int h = 0; h < 2; ++h)
 #pragma unroll
-                for (int u = 0; u < IPT; ++u) {
-                    const int it = t + u * p.tpr;
-                    if (it < p.ipr) {
-                        float tmp[B];
+            for (int c = 0; c < B; ++c) acc[h][c] = 0.f;
+        for (int f = f0 + lane; f < f1; f += 32) {
+            const int r = f / p.ipr, it = f - r * p.ipr;
+            ItemAct a[B];
 #pragma unroll
-                        for (int c = 0; c < B; ++c) tmp[c] = 0.f;
-                        item_dot<TYPE, B>(row, it, act[u], tmp);
+            for (int c = 0; c < B; ++c) {
 #pragma unroll
-                        for (int c = 0; c < B; ++c) acc[c] += tmp[c];
-                    }
+                for (int i = 0; i < 8; ++i) {
+                    const uint2 v = *reinterpret_cast<const uint2*>(codes + (c * 8 + i) * nb + 2 * it);
+                    a[c].q[i] = static_cast<int>(v.x);
+                    a[c].q[8 + i] = static_cast<int>(v.y);
                 }
+                a[c].m = *reinterpret_cast<const float4*>(meta + c * nb + 2 * it);
+            }
+            float tmp[B];
 #pragma unroll
-                for (int c = 0; c < B; ++c) {
-                    const float v = warp_sum(acc[c]);
-                    if (lane == 0) part[(c * p.rps + rl) * wpg + wig] = v;
-                }
+            for (int c = 0; c < B; ++c) tmp[c] = 0.f;
+            item_dot<TYPE, B>(stage + size_t(r) * p.row_bytes, it, a, tmp);
+            const bool second = r != rw;
+#pragma unroll
+            for (int c = 0; c < B; ++c) {
+                acc[0][c] += second ? 0.f : tmp[c];
+                acc[1][c] += second ? tmp[c] : 0.f;
             }
         }
-        // Slot fully read and this stage's partials visible.  A timed-out wait
-        // is decided for the whole CTA here, so every thread leaves together.
-        if (__syncthreads_or(timed_out)) {
-            ok = false;
-            break;
+        float v[2][B];
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int c = 0; c < B; ++c) v[h][c] = warp_sum(acc[h][c]);
+        // partial[slot][warp][row][col]: this warp's sums, zero off its share.
+        float* mine = partial + (size_t(slot) * kConsumers + warp) * (kMaxRows * B);
+        if (lane < nr * B) {
+            const int r = lane / B, c = lane % B;
+            float out = 0.f;
+#pragma unroll
+            for (int cc = 0; cc < B; ++cc)
+                if (cc == c) out = r == rw ? v[0][cc] : r == rw + 1 ? v[1][cc] : 0.f;
+            mine[lane] = out;
         }
-        if (tid == 0 && s + p.nstage < nst) issue(s + p.nstage);
-        if (tid < nr * B) {
-            const int c = tid / nr, rl = tid % nr;
-            float v = 0.f;
-            for (int w = 0; w < wpg; ++w) v += part[(c * p.rps + rl) * wpg + w];
-            p.y[size_t(p.col0 + c) * p.rows + first + rl] = v;
+        __syncwarp();
+        unsigned last = 0;
+        if (lane == 0) {
+            __threadfence_block();
+            last = atomicAdd(&ticket[slot], 1u) == kConsumers - 1;
         }
-    }
-    if (!ok) {
-        // Drain this CTA's own copies (bounded) before its shared memory goes away.
-        if (tid == 0)
-            for (int s = 0; s < min(p.nstage, nst); ++s) (void)mbar_wait(&full[s], 0);
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (last) {
+            __syncwarp();
+            __threadfence_block();
+            if (lane < nr * B) {
+                const int r = lane / B, c = lane % B;
+                const float* base = partial + size_t(slot) * kConsumers * (kMaxRows * B) + lane;
+                float sum = 0.f;
+#pragma unroll
+                for (int w = 0; w < kConsumers; ++w) sum += base[w * (kMaxRows * B)];
+                p.y[size_t(p.col0 + c) * p.rows + first + r] = sum;
+            }
+            __syncwarp();
+            if (lane == 0) {
+                ticket[slot] = 0;
+                mbar_arrive(&empty[slot]);
+            }
+        }
     }
 }
 

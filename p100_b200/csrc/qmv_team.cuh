@@ -1,0 +1,281 @@
+// qmv_team.cuh — batch-1 quantised mat-vec with register-resident activations.
+//
+// The decode mat-vec streams every weight byte once, so its instruction cost
+// per byte of HBM is what matters:
+//   * A lane owns one fixed 256-weight column group of every row (eight Q4_0 /
+//     Q8_0 blocks or one Q4_K super-block), so its Q8_1 activations for that
+//     group live in registers for the whole launch (loaded once, 16-byte
+//     loads); no activation traffic in the inner loop.
+//   * A team of T lanes (T = k/256 rounded up to a power of two, or to whole
+//     warps past 32) covers one row; the eight consumer warps form 256/T
+//     teams, and one stage of the ring holds one row per team (32-37 KB for
+//     Q4_0/Q4_K, whole rows, contiguous).
+//   * One producer warp streams stages HBM -> shared memory with untiled
+//     bulk-async copies (L2 evict-first) into a ring of full/empty mbarrier
+//     slots; every consumer warp visits every stage in order.
+//   * A group is read with 128-bit shared loads at a 144- or 272-byte lane
+//     stride (bank-conflict free); high nibbles are multiplied in place by an
+//     unsigned x signed dp4a and the 16x factor removed by one shift.
+//   * Rows are finished by an XOR butterfly inside the team (and, for teams of
+//     several warps, a fixed-order add of the warps' partials), so the result
+//     is deterministic.
+// The arithmetic per 32-block is the q81 path of qmv::evaluate
+// (qmv_model.cpp:147-180): exact int32 block dots, FP32 scaling.
+#pragma once
+#include "common.cuh"
+
+namespace p100b {
+namespace qmvt {
+
+constexpr int kConsumers = 8;
+constexpr int kThreads = (kConsumers + 1) * 32;
+constexpr int kMaxSlots = 8;
+constexpr int kSmemLimit = 227 * 1024;
+
+// d = a (unsigned bytes) . b (signed bytes) + c
+__device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// Q8_1 activations of one 256-value group (eight blocks).
+struct GroupAct {
+    int q[64];     // int8 codes, four per word, block-major
+    float dx[8];   // fp16 block scale
+    float m[8];    // Q4_0: -8 * fp16 block sum;  Q4_K: sum of the block's codes;  Q8_0: unused
+};
+
+struct Params {
+    const uint8_t* w;
+    const uint8_t* xq;
+    float* y;
+    int rows, k;
+    int col0;
+    int row_bytes;
+    int ngroups;        // k / 256
+    int team;           // lanes per row
+    int teams;          // rows per stage
+    int nslot;
+    int slot_bytes;
+    int part_off, ring_off;
+};
+
+template <int TYPE>
+__device__ __forceinline__ void load_group_act(const uint8_t* __restrict__ xq, int nb, int col, int g, GroupAct& a) {
+    // Eight consecutive 36-byte blocks = 288 bytes = 18 aligned 16-byte loads.
+    const uint4* src = reinterpret_cast<const uint4*>(xq + (size_t(col) * nb + size_t(g) * 8) * 36);
+    uint32_t u[72];
+#pragma unroll
+    for (int i = 0; i < 18; ++i) {
+        const uint4 v = __ldg(src + i);
+        u[4 * i] = v.x;
+        u[4 * i + 1] = v.y;
+        u[4 * i + 2] = v.z;
+        u[4 * i + 3] = v.w;
+    }
+#pragma unroll
+    for (int b = 0; b < 8; ++b) {
+        int sumq = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            a.q[8 * b + i] = static_cast<int>(u[9 * b + 1 + i]);
+            sumq = __dp4a(a.q[8 * b + i], 0x01010101, sumq);
+        }
+        a.dx[b] = half_lo(u[9 * b]);
+        a.m[b] = TYPE == P100_Q4_0 ? -8.0f * half_hi(u[9 * b]) : TYPE == P100_Q4_K ? float(sumq) : 0.f;
+    }
+}
+
+// acc += (row's group at grp) . (the group's activations)
+template <int TYPE>
+__device__ __forceinline__ float group_dot(const uint8_t* __restrict__ grp, const GroupAct& a, float acc) {
+    constexpr int kWords = TYPE == P100_Q8_0 ? 68 : 36;
+    uint32_t w[kWords];
+#pragma unroll
+    for (int i = 0; i < kWords / 4; ++i) {
+        const uint4 v = *reinterpret_cast<const uint4*>(grp + 16 * i);
+        w[4 * i] = v.x;
+        w[4 * i + 1] = v.y;
+        w[4 * i + 2] = v.z;
+        w[4 * i + 3] = v.w;
+    }
+    if (TYPE == P100_Q4_0) {
+        // Pairs of 18-byte blocks at word 9p: A = (d lo(w[9p]), nibbles at +2),
+        // B = (d hi(w[9p+4]), nibbles at words 9p+5..9p+8).
+#pragma unroll
+        for (int pr = 0; pr < 4; ++pr) {
+            const int base = 9 * pr, bA = 2 * pr, bB = 2 * pr + 1;
+            int la = 0, ha = 0, lb = 0, hb = 0;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                // byte m: low nibble is element m, high nibble element m+16
+                const uint32_t qa = shift2(w[base + i], w[base + i + 1]), qb = w[base + 5 + i];
+                la = __dp4a(static_cast<int>(qa & 0x0f0f0f0fu), a.q[8 * bA + i], la);
+                ha = dp4a_us(qa & 0xf0f0f0f0u, a.q[8 * bA + 4 + i], ha);
+                lb = __dp4a(static_cast<int>(qb & 0x0f0f0f0fu), a.q[8 * bB + i], lb);
+                hb = dp4a_us(qb & 0xf0f0f0f0u, a.q[8 * bB + 4 + i], hb);
+            }
+            // d_w * (d_x * sum(nib*q) - 8 * sum(x))
+            acc = fmaf(half_lo(w[base]), fmaf(float(la + (ha >> 4)), a.dx[bA], a.m[bA]), acc);
+            acc = fmaf(half_hi(w[base + 4]), fmaf(float(lb + (hb >> 4)), a.dx[bB], a.m[bB]), acc);
+        }
+    } else if (TYPE == P100_Q8_0) {
+        // Pairs of 34-byte blocks at word 17p: A = (d lo(w[17p]), codes at +2),
+        // B = (d hi(w[17p+8]), codes at words 17p+9..17p+16).
+#pragma unroll
+        for (int pr = 0; pr < 4; ++pr) {
+            const int base = 17 * pr, bA = 2 * pr, bB = 2 * pr + 1;
+            int sa0 = 0, sa1 = 0, sb0 = 0, sb1 = 0;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                sa0 = __dp4a(static_cast<int>(shift2(w[base + i], w[base + i + 1])), a.q[8 * bA + i], sa0);
+                sa1 = __dp4a(static_cast<int>(shift2(w[base + 4 + i], w[base + 5 + i])), a.q[8 * bA + 4 + i], sa1);
+                sb0 = __dp4a(static_cast<int>(w[base + 9 + i]), a.q[8 * bB + i], sb0);
+                sb1 = __dp4a(static_cast<int>(w[base + 13 + i]), a.q[8 * bB + 4 + i], sb1);
+            }
+            acc = fmaf(half_lo(w[base]) * a.dx[bA], float(sa0 + sa1), acc);
+            acc = fmaf(half_hi(w[base + 8]) * a.dx[bB], float(sb0 + sb1), acc);
+        }
+    } else {
+        // One super-block: w[0] = d | dmin, w[1..3] = twelve 6-bit scale/min
+        // bytes, w[4 + 8q + i] = nibbles of sub-blocks 2q (low) and 2q+1 (high).
+        float sd = 0.f, sm = 0.f;
+#pragma unroll
+        for (int qq = 0; qq < 4; ++qq) {
+            const int j0 = 2 * qq, j1 = 2 * qq + 1;
+            // get_scale_min_k4 (qmv_model.cpp:72-77) for sub-blocks j0, j1
+            int sc0, mn0, sc1, mn1;
+            if (qq < 2) {
+                sc0 = (w[1] >> (8 * j0)) & 63;
+                mn0 = (w[2] >> (8 * j0)) & 63;
+                sc1 = (w[1] >> (8 * j1)) & 63;
+                mn1 = (w[2] >> (8 * j1)) & 63;
+            } else {
+                const int k0 = j0 - 4, k1 = j1 - 4;
+                sc0 = ((w[3] >> (8 * k0)) & 15) | (((w[1] >> (8 * k0 + 6)) & 3) << 4);
+                mn0 = ((w[3] >> (8 * k0 + 4)) & 15) | (((w[2] >> (8 * k0 + 6)) & 3) << 4);
+                sc1 = ((w[3] >> (8 * k1)) & 15) | (((w[1] >> (8 * k1 + 6)) & 3) << 4);
+                mn1 = ((w[3] >> (8 * k1 + 4)) & 15) | (((w[2] >> (8 * k1 + 6)) & 3) << 4);
+            }
+            int l0 = 0, l1 = 0, h0 = 0, h1 = 0;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const uint32_t n0 = w[4 + 8 * qq + i], n1 = w[8 + 8 * qq + i];
+                l0 = __dp4a(static_cast<int>(n0 & 0x0f0f0f0fu), a.q[8 * j0 + i], l0);
+                l1 = __dp4a(static_cast<int>(n1 & 0x0f0f0f0fu), a.q[8 * j0 + 4 + i], l1);
+                h0 = dp4a_us(n0 & 0xf0f0f0f0u, a.q[8 * j1 + i], h0);
+                h1 = dp4a_us(n1 & 0xf0f0f0f0u, a.q[8 * j1 + 4 + i], h1);
+            }
+            // sum_j dx_j * (dot_j * sc_j) and sum_j dx_j * (sumq_j * mn_j)
+            // (qmv_model.cpp:175-178)
+            sd = fmaf(a.dx[j0], float((l0 + l1) * sc0), sd);
+            sd = fmaf(a.dx[j1], float(((h0 + h1) >> 4) * sc1), sd);
+            sm = fmaf(a.dx[j0], a.m[j0] * float(mn0), sm);
+            sm = fmaf(a.dx[j1], a.m[j1] * float(mn1), sm);
+        }
+        acc = fmaf(half_lo(w[0]), sd, fmaf(-half_hi(w[0]), sm, acc));
+    }
+    return acc;
+}
+
+template <int TYPE>
+__global__ void __launch_bounds__(kThreads, 1) qmv_team_kernel(const Params p) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+    uint64_t* empty = full + kMaxSlots;
+    float* partial = reinterpret_cast<float*>(smem + p.part_off);   // [2][teams][warps per team]
+    uint8_t* ring = smem + p.ring_off;
+    constexpr int kGroupBytes = TYPE == P100_Q8_0 ? 272 : 144;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int r0 = static_cast<int>(static_cast<long long>(p.rows) * blockIdx.x / gridDim.x);
+    const int r1 = static_cast<int>(static_cast<long long>(p.rows) * (blockIdx.x + 1) / gridDim.x);
+    const int nst = (r1 - r0 + p.teams - 1) / p.teams;
+
+    if (tid == 0) {
+        for (int s = 0; s < p.nslot; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kConsumers);
+        }
+        fence_barrier_init();
+    }
+    __syncthreads();
+    pdl_allow_dependents();
+
+    if (warp == kConsumers) {
+        // ---- producer: weights never depend on the previous kernel
+        if (lane == 0) {
+            const uint64_t policy = l2_evict_first_policy();
+            for (int s = 0; s < nst; ++s) {
+                const int slot = s % p.nslot;
+                if (s >= p.nslot && !mbar_wait(&empty[slot], ((s / p.nslot) - 1) & 1)) break;
+                const int first = r0 + s * p.teams;
+                const uint32_t bytes = static_cast<uint32_t>(min(p.teams, r1 - first)) * p.row_bytes;
+                mbar_arrive_expect_tx(&full[slot], bytes);
+                bulk_load(ring + size_t(slot) * p.slot_bytes, p.w + size_t(first) * p.row_bytes, bytes, &full[slot],
+                          policy);
+            }
+        }
+        return;
+    }
+
+    // ---- consumers
+    const int team = tid / p.team, tl = tid % p.team;
+    const bool has_group = tl < p.ngroups;
+    const int nb = p.k / 32;
+    pdl_wait_prior_grid();   // activations may come from the previous kernel
+    GroupAct act;
+    if (has_group) {
+        load_group_act<TYPE>(p.xq, nb, p.col0, tl, act);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 64; ++i) act.q[i] = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) act.dx[i] = act.m[i] = 0.f;
+    }
+
+    for (int s = 0; s < nst; ++s) {
+        const int slot = s % p.nslot;
+        // A timed-out wait is decided for all consumer warps at once (a
+        // barrier reduction), so no team is left at a barrier alone.
+        const bool timed_out = !mbar_wait(&full[slot], (s / p.nslot) & 1);
+        int any_timeout;
+        asm volatile(
+            "{\n\t.reg .pred p, q;\n\t"
+            "setp.ne.u32 p, %1, 0;\n\t"
+            "bar.red.or.pred q, 15, %2, p;\n\t"
+            "selp.u32 %0, 1, 0, q;\n\t}"
+            : "=r"(any_timeout)
+            : "r"(static_cast<unsigned>(timed_out)), "r"(kConsumers * 32)
+            : "memory");
+        if (any_timeout) break;
+        const uint8_t* stage = ring + size_t(slot) * p.slot_bytes;
+        const int first = r0 + s * p.teams;
+        const int nr = min(p.teams, r1 - first);
+        float acc = 0.f;
+        if (team < nr && has_group)
+            acc = group_dot<TYPE>(stage + size_t(team) * p.row_bytes + size_t(tl) * kGroupBytes, act, acc);
+        if (p.team <= 32) {
+            // teams are aligned lane ranges of one warp: butterfly inside them
+            for (int off = p.team >> 1; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+            if (tl == 0 && team < nr) p.y[size_t(p.col0) * p.rows + first + team] = acc;
+        } else {
+            const int wpt = p.team >> 5, wit = tl >> 5;
+            float* part = partial + (size_t(s & 1) * p.teams + team) * wpt;
+            const float v = warp_sum(acc);
+            if (lane == 0) part[wit] = v;
+            asm volatile("bar.sync %0, %1;" ::"r"(1 + team), "r"(p.team) : "memory");
+            if (tl == 0 && team < nr) {
+                float sum = 0.f;
+                for (int i = 0; i < wpt; ++i) sum += part[i];
+                p.y[size_t(p.col0) * p.rows + first + team] = sum;
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
+    }
+}
+
+}  // namespace qmvt
+}  // namespace p100b
