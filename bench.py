@@ -450,7 +450,7 @@ def main():
                    "parallelism": f"row-split shards x{world}, no data-path collective" if world > 1 else "1 GPU",
                    "l2": f"inputs larger than L2: {copies} rotating weight copies ({copies * per_copy / 1e6:.0f} MB)",
                    "launch": "C-ABI calls captured into one CUDA graph per weight copy, replayed per step"},
-        "roofline": {"bound": "hbm", "kernel": "qmv_bulk_kernel<Q4_0,1,1> gate/up 4096x14336",
+        "roofline": {"bound": "hbm", "kernel": "qmv_team_kernel<Q4_0> gate/up 4096x14336",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_source": peak_kind,
                      "traffic": ncu_traffic("qmv_q4_0_4096x14336"), "algorithmic_bytes": target_bytes,
