@@ -140,6 +140,23 @@ p100_status p100_fa_decode(const p100_attn_desc* desc, const float* q, const voi
                            const void* v, const float* mask, float* o, float* lse,
                            void* ws, size_t ws_bytes, p100_stream_t stream);
 
+/* The same decode without a caller-supplied workspace.  It has no counterpart
+ * in the reference; it exists for callers that may not allocate device memory
+ * at all: a host whose allocator owns the whole device budget, or a loop that
+ * cannot afford the device-wide synchronisation a cudaMalloc/cudaFree implies.
+ * The split-K partials live instead in a fixed P100_FA_STATIC_SCRATCH_BYTES
+ * array inside the library, held on every GPU that loads the library until
+ * the process exits.  Calls whose split needs more (p100_fa_workspace_size of
+ * desc) are rejected with P100_ERR_INVALID; lower desc->kv_splits to fit.
+ * The first call on a device looks up that device's copy of the array, so
+ * make it before any stream capture.  All calls share one array: calls that
+ * may run at the same time on the GPU (different streams, overlapping
+ * launches) race and must be ordered by the caller.  Allocates nothing. */
+#define P100_FA_STATIC_SCRATCH_BYTES (2u << 20)
+p100_status p100_fa_decode_static(const p100_attn_desc* desc, const float* q, const void* k,
+                                  const void* v, const float* mask, float* o, float* lse,
+                                  p100_stream_t stream);
+
 /* ------------------------------------------------- tensor-parallel (NCCL) */
 /* Row-split tensor parallelism over the GPUs of one box; replaces the
  * reference's two-GPU PCIe layer (src/p2p/p2p.cpp) for the per-layer

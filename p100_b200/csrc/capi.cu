@@ -556,3 +556,55 @@ p100_status p100_fa_decode(const p100_attn_desc* desc, const float* q, const voi
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------ decode without a workspace argument
+// For callers that may not allocate device memory (see p100_fa_decode_static
+// in p100/b200.h): the split-K partials go to one fixed array per device
+// instead of a caller-owned workspace.  The array is part of this library's
+// device module, so every GPU that loads the library holds it until exit.
+namespace p100b {
+static __device__ __align__(256) unsigned char g_fa_static_scratch[P100_FA_STATIC_SCRATCH_BYTES];
+namespace {
+std::mutex g_static_mutex;
+void* g_static_scratch_ptr[64];   // the array's device address, per device ordinal
+}  // namespace
+}  // namespace p100b
+
+extern "C" p100_status p100_fa_decode_static(const p100_attn_desc* desc, const float* q, const void* k,
+                                             const void* v, const float* mask, float* o, float* lse,
+                                             p100_stream_t stream) {
+    clear_error();
+    if (!desc) return set_error(P100_ERR_INVALID, "null descriptor");
+    if (const char* why = attn_reason(*desc)) return set_error(P100_ERR_INVALID, "%s", why);
+    int dev = 0, sms = 0;
+    if (p100_status st = require_sm100(&dev, &sms)) return st;
+    FaPlan plan;
+    if (p100_status st = plan_fa(*desc, sms, plan)) return st;
+    if (plan.ws_total > P100_FA_STATIC_SCRATCH_BYTES)
+        return set_error(P100_ERR_INVALID,
+                         "split-K partials need %zu bytes, more than the %u-byte static scratch; lower kv_splits",
+                         plan.ws_total, static_cast<unsigned>(P100_FA_STATIC_SCRATCH_BYTES));
+    void* scratch = nullptr;
+    if (plan.ws_total) {
+        {
+            // Host code cannot use the array's name as a device address: look
+            // the address up once per device, with that device current.
+            std::lock_guard<std::mutex> lock(g_static_mutex);
+            if (!g_static_scratch_ptr[dev]) {
+                void* ptr = nullptr;
+                if (p100_status st = cuda_status(cudaGetSymbolAddress(&ptr, g_fa_static_scratch),
+                                                 "cudaGetSymbolAddress(static scratch)"))
+                    return st;
+                g_static_scratch_ptr[dev] = ptr;
+            }
+            scratch = g_static_scratch_ptr[dev];
+        }
+        // The array keeps the previous call's contents; the per-head tickets
+        // of the combine must start at zero.
+        if (p100_status st = cuda_status(
+                cudaMemsetAsync(static_cast<uint8_t*>(scratch) + plan.ws_o + plan.ws_ml, 0, plan.ws_tickets, stream),
+                "cudaMemsetAsync(static scratch tickets)"))
+            return st;
+    }
+    return p100_fa_decode(desc, q, k, v, mask, o, lse, scratch, plan.ws_total, stream);
+}
