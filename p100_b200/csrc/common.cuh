@@ -1,7 +1,7 @@
 // common.cuh — shared device helpers for the sm_100a kernels of p100_b200.
 //
 // Everything here is hand-written inline PTX or plain CUDA: mbarriers and
-// untiled bulk-async copies (global -> shared, no cluster multicast), bounded
+// untiled bulk-async copies (global -> this CTA's shared memory only), bounded
 // waits on %globaltimer, and the per-device flag that a timed-out wait sets.
 #pragma once
 
@@ -98,7 +98,7 @@ __device__ __forceinline__ uint64_t l2_evict_first_policy() {
 
 // Untiled bulk-async copy global -> this CTA's shared memory, completing on
 // `bar` with `bytes` transaction bytes.  dst, src 16-byte aligned; bytes a
-// multiple of 16.  No multicast: the source is always this GPU's memory.
+// multiple of 16.  One destination CTA; the source is always this GPU's memory.
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
                                           uint64_t policy) {
     asm volatile(
