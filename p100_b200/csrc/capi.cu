@@ -175,12 +175,7 @@ bool plan_team(int type, const void* w, const void* xq, int rows, int k, int bat
     if (batch != 1 || k % 256 || reinterpret_cast<uintptr_t>(w) % 16 || reinterpret_cast<uintptr_t>(xq) % 16)
         return false;
     const int ngroups = k / 256;
-    int team = 1;
-    if (ngroups <= 32) {
-        while (team < ngroups) team <<= 1;
-    } else {
-        team = (ngroups + 31) / 32 * 32;
-    }
+    const int team = qmvt::team_lanes(ngroups);
     if (team > qmvt::kConsumers * 32) return false;
     const size_t row_bytes = size_t(k / elems_of(type)) * bytes_of(type);
     const int teams = qmvt::kConsumers * 32 / team;
@@ -204,9 +199,9 @@ bool plan_team(int type, const void* w, const void* xq, int rows, int k, int bat
     return true;
 }
 
-template <int TYPE>
+template <int TYPE, int NG>
 p100_status launch_team_t(const TeamPlan& plan, bool pdl, cudaStream_t stream) {
-    auto kern = qmvt::qmv_team_kernel<TYPE>;
+    auto kern = qmvt::qmv_team_kernel<TYPE, NG>;
     static thread_local int configured[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -228,10 +223,18 @@ p100_status launch_team_t(const TeamPlan& plan, bool pdl, cudaStream_t stream) {
     return cuda_status(cudaLaunchKernelEx(&cfg, kern, plan.p), "qmv_team_kernel launch");
 }
 
+// Kernels compiled for the hidden sizes of the Llama-3 8B/70B decode shapes
+// (k = 4096, 8192, 14336, 28672); any other k % 256 == 0 takes NG = 0.
 template <int TYPE>
 p100_status launch_team_type(const TeamPlan& plan, int batch, bool pdl, cudaStream_t s) {
     (void)batch;   // the team kernel serves one column
-    return launch_team_t<TYPE>(plan, pdl, s);
+    switch (plan.p.ngroups) {
+        case 16: return launch_team_t<TYPE, 16>(plan, pdl, s);
+        case 32: return launch_team_t<TYPE, 32>(plan, pdl, s);
+        case 56: return launch_team_t<TYPE, 56>(plan, pdl, s);
+        case 112: return launch_team_t<TYPE, 112>(plan, pdl, s);
+        default: return launch_team_t<TYPE, 0>(plan, pdl, s);
+    }
 }
 
 p100_status run_qmv(int type, const void* w, int rows, int k, const void* xq, int batch, float* y, unsigned flags,

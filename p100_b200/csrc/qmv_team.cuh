@@ -12,7 +12,14 @@
 //     Q4_0/Q4_K, whole rows, contiguous).
 //   * One producer warp streams stages HBM -> shared memory with untiled
 //     bulk-async copies (L2 evict-first) into a ring of full/empty mbarrier
-//     slots; every consumer warp visits every stage in order.
+//     slots; every consumer warp visits every stage in order.  The producer
+//     keeps at most kLookahead stages in flight beyond the newest landed one:
+//     when every SM asks for its whole ring at once the memory system
+//     interleaves all of it and the first stage lands late, so consumers
+//     would start late; a short lookahead lets stage 0 land first.
+//   * The group count (k / 256) is a template parameter for the common
+//     hidden sizes, which turns the team geometry and the activation
+//     addressing into constants; 0 selects the runtime-shaped variant.
 //   * A group is read with 128-bit shared loads at a 144- or 272-byte lane
 //     stride (bank-conflict free); high nibbles are multiplied in place by an
 //     unsigned x signed dp4a and the 16x factor removed by one shift.
@@ -31,6 +38,13 @@ constexpr int kConsumers = 8;
 constexpr int kThreads = (kConsumers + 1) * 32;
 constexpr int kMaxSlots = 8;
 constexpr int kSmemLimit = 227 * 1024;
+constexpr int kLookahead = 2;   // stages in flight past the newest landed one
+
+// Lanes per row for a row of `ngroups` 256-weight groups: the next power of
+// two up to a warp, whole warps beyond (the host plan uses the same rule).
+__host__ __device__ constexpr int team_lanes(int ngroups) {
+    return ngroups <= 32 ? (ngroups <= 1 ? 1 : 2 * team_lanes((ngroups + 1) / 2)) : (ngroups + 31) / 32 * 32;
+}
 
 // d = a (unsigned bytes) . b (signed bytes) + c
 __device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
@@ -179,7 +193,8 @@ __device__ __forceinline__ float group_dot(const uint8_t* __restrict__ grp, cons
     return acc;
 }
 
-template <int TYPE>
+// NG = k / 256 when compiled for one hidden size, 0 for any (runtime shape).
+template <int TYPE, int NG>
 __global__ void __launch_bounds__(kThreads, 1) qmv_team_kernel(const Params p) {
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
@@ -187,11 +202,14 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_team_kernel(const Params p) {
     float* partial = reinterpret_cast<float*>(smem + p.part_off);   // [2][teams][warps per team]
     uint8_t* ring = smem + p.ring_off;
     constexpr int kGroupBytes = TYPE == P100_Q8_0 ? 272 : 144;
+    const int ngroups = NG > 0 ? NG : p.ngroups;
+    const int team_size = NG > 0 ? team_lanes(NG) : p.team;
+    const int teams = NG > 0 ? kConsumers * 32 / team_lanes(NG) : p.teams;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int r0 = static_cast<int>(static_cast<long long>(p.rows) * blockIdx.x / gridDim.x);
     const int r1 = static_cast<int>(static_cast<long long>(p.rows) * (blockIdx.x + 1) / gridDim.x);
-    const int nst = (r1 - r0 + p.teams - 1) / p.teams;
+    const int nst = (r1 - r0 + teams - 1) / teams;
 
     if (tid == 0) {
         for (int s = 0; s < p.nslot; ++s) {
@@ -207,11 +225,15 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_team_kernel(const Params p) {
         // ---- producer: weights never depend on the previous kernel
         if (lane == 0) {
             const uint64_t policy = l2_evict_first_policy();
+            const int look = min(kLookahead, p.nslot - 1);
             for (int s = 0; s < nst; ++s) {
                 const int slot = s % p.nslot;
+                // stage s - look has landed (its slot cannot have been refilled:
+                // that needs stage s - look + nslot > s to be issued first)
+                if (s >= look && !mbar_wait(&full[(s - look) % p.nslot], ((s - look) / p.nslot) & 1)) break;
                 if (s >= p.nslot && !mbar_wait(&empty[slot], ((s / p.nslot) - 1) & 1)) break;
-                const int first = r0 + s * p.teams;
-                const uint32_t bytes = static_cast<uint32_t>(min(p.teams, r1 - first)) * p.row_bytes;
+                const int first = r0 + s * teams;
+                const uint32_t bytes = static_cast<uint32_t>(min(teams, r1 - first)) * p.row_bytes;
                 mbar_arrive_expect_tx(&full[slot], bytes);
                 bulk_load(ring + size_t(slot) * p.slot_bytes, p.w + size_t(first) * p.row_bytes, bytes, &full[slot],
                           policy);
@@ -221,8 +243,8 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_team_kernel(const Params p) {
     }
 
     // ---- consumers
-    const int team = tid / p.team, tl = tid % p.team;
-    const bool has_group = tl < p.ngroups;
+    const int team = tid / team_size, tl = tid % team_size;
+    const bool has_group = tl < ngroups;
     const int nb = p.k / 32;
     pdl_wait_prior_grid();   // activations may come from the previous kernel
     GroupAct act;
@@ -237,43 +259,49 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_team_kernel(const Params p) {
 
     for (int s = 0; s < nst; ++s) {
         const int slot = s % p.nslot;
-        // A timed-out wait is decided for all consumer warps at once (a
-        // barrier reduction), so no team is left at a barrier alone.
         const bool timed_out = !mbar_wait(&full[slot], (s / p.nslot) & 1);
         int any_timeout;
-        asm volatile(
-            "{\n\t.reg .pred p, q;\n\t"
-            "setp.ne.u32 p, %1, 0;\n\t"
-            "bar.red.or.pred q, 15, %2, p;\n\t"
-            "selp.u32 %0, 1, 0, q;\n\t}"
-            : "=r"(any_timeout)
-            : "r"(static_cast<unsigned>(timed_out)), "r"(kConsumers * 32)
-            : "memory");
+        if (team_size <= 32) {
+            // a team lies inside one warp: the warp decides for itself
+            any_timeout = __any_sync(0xffffffffu, timed_out);
+        } else {
+            // teams span warps that meet at a named barrier below: decide for
+            // all consumer warps at once so no team is left there alone
+            asm volatile(
+                "{\n\t.reg .pred p, q;\n\t"
+                "setp.ne.u32 p, %1, 0;\n\t"
+                "bar.red.or.pred q, 15, %2, p;\n\t"
+                "selp.u32 %0, 1, 0, q;\n\t}"
+                : "=r"(any_timeout)
+                : "r"(static_cast<unsigned>(timed_out)), "r"(kConsumers * 32)
+                : "memory");
+        }
         if (any_timeout) break;
         const uint8_t* stage = ring + size_t(slot) * p.slot_bytes;
-        const int first = r0 + s * p.teams;
-        const int nr = min(p.teams, r1 - first);
+        const int first = r0 + s * teams;
+        const int nr = min(teams, r1 - first);
         float acc = 0.f;
         if (team < nr && has_group)
             acc = group_dot<TYPE>(stage + size_t(team) * p.row_bytes + size_t(tl) * kGroupBytes, act, acc);
-        if (p.team <= 32) {
+        // the stage's words are in registers: hand the slot back
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
+        if (team_size <= 32) {
             // teams are aligned lane ranges of one warp: butterfly inside them
-            for (int off = p.team >> 1; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+            for (int off = team_size >> 1; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
             if (tl == 0 && team < nr) p.y[size_t(p.col0) * p.rows + first + team] = acc;
         } else {
-            const int wpt = p.team >> 5, wit = tl >> 5;
-            float* part = partial + (size_t(s & 1) * p.teams + team) * wpt;
+            const int wpt = team_size >> 5, wit = tl >> 5;
+            float* part = partial + (size_t(s & 1) * teams + team) * wpt;
             const float v = warp_sum(acc);
             if (lane == 0) part[wit] = v;
-            asm volatile("bar.sync %0, %1;" ::"r"(1 + team), "r"(p.team) : "memory");
+            asm volatile("bar.sync %0, %1;" ::"r"(1 + team), "r"(team_size) : "memory");
             if (tl == 0 && team < nr) {
                 float sum = 0.f;
                 for (int i = 0; i < wpt; ++i) sum += part[i];
                 p.y[size_t(p.col0) * p.rows + first + team] = sum;
             }
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[slot]);
     }
 }
 

@@ -163,6 +163,21 @@ def test_qmv_edge_shapes(cuda, orc, qtype, k, rows, offset):
                      row_norms(orc, qtype, w, rows, k), x)
 
 
+@pytest.mark.parametrize("qtype", [P.Q4_0, P.Q8_0, P.Q4_K])
+@pytest.mark.parametrize("k,rows", [(256, 7), (768, 150), (4096, 301), (8192, 97), (12288, 65), (14336, 45),
+                                    (28672, 23)])
+def test_qmv_team_batch1_shapes(cuda, orc, qtype, k, rows):
+    """Batch 1 on 16-byte-aligned buffers (the team kernel): the group counts
+    compiled in (k = 4096, 8192, 14336, 28672), runtime-shaped ones (256, 768,
+    12288 whose team spans two warps), and row counts that leave a ragged
+    last stage."""
+    w = W.weights(qtype, rows, k, seed=31 * k + rows + qtype)
+    x = W.activations(1, k, seed=k + 5)
+    y = P.qmv(qtype, dev(cuda, w), rows, k, P.q8_1_quantize(dev(cuda, x)), 1).cpu().numpy()
+    assert_qmv_close(y, q81_reference(orc, qtype, w, rows, k, x).astype(np.float64),
+                     row_norms(orc, qtype, w, rows, k), x)
+
+
 def test_qmv_k32_generic(cuda, orc):
     for qtype in (P.Q4_0, P.Q8_0):
         w = orc.random_rows(qtype, 32, 9, 4)
