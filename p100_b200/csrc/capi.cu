@@ -180,8 +180,9 @@ bool plan_team(int type, const void* w, const void* xq, int rows, int k, int bat
     const size_t row_bytes = size_t(k / elems_of(type)) * bytes_of(type);
     const int teams = qmvt::kConsumers * 32 / team;
     const size_t slot = round128(size_t(teams) * row_bytes);
-    const size_t part_off = 128;                                          // 2 x 8 mbarriers
-    const size_t ring_off = part_off + round128(size_t(2) * teams * std::max(1, team / 32) * 4);
+    const size_t part_off = 256;                                 // 2 x 8 ring mbarriers + the activation one
+    const size_t act_off = part_off + round128(size_t(2) * teams * std::max(1, team / 32) * 4);
+    const size_t ring_off = act_off + round128(size_t(k / 32) * 36);   // the Q8_1 row
     if (ring_off + 2 * slot > size_t(qmvt::kSmemLimit)) return false;
     const int nslot = int(std::min<size_t>(qmvt::kMaxSlots, (qmvt::kSmemLimit - ring_off) / slot));
     plan.p.rows = rows;
@@ -193,6 +194,7 @@ bool plan_team(int type, const void* w, const void* xq, int rows, int k, int bat
     plan.p.nslot = nslot;
     plan.p.slot_bytes = int(slot);
     plan.p.part_off = int(part_off);
+    plan.p.act_off = int(act_off);
     plan.p.ring_off = int(ring_off);
     plan.smem = ring_off + size_t(nslot) * slot;
     plan.grid = std::max(1, std::min(sms, (rows + teams - 1) / teams));
