@@ -47,6 +47,8 @@ typedef enum p100_qtype { P100_Q4_0 = 0, P100_Q8_0 = 1, P100_Q4_K = 2 } p100_qty
 
 /* Same type as cudaStream_t; 0 is the legacy default stream. */
 typedef struct CUstream_st* p100_stream_t;
+/* A tensor-parallel rank (see the tensor-parallel section). */
+typedef struct p100_tp p100_tp;
 
 /* ------------------------------------------------------------------ library */
 int p100_abi_version(void);
@@ -55,9 +57,10 @@ const char* p100_last_error(void);
 const char* p100_status_name(p100_status status);
 /* P100_OK if `device` is an sm_100 GPU this build has code for. */
 p100_status p100_device_check(int device);
-/* Reads, and with clear != 0 resets, the current device's bounded-wait flag:
- * P100_ERR_TIMEOUT if any kernel gave up waiting since the last clear.
- * Synchronises the current device. */
+/* Reads, and with clear != 0 resets, the current device's error flag:
+ * P100_ERR_TIMEOUT if a kernel gave up a bounded wait since the last clear,
+ * P100_ERR_INVALID if a kernel read a device-resident token or position out
+ * of range.  Synchronises the current device. */
 p100_status p100_device_error(int clear);
 
 /* --------------------------------------------------------- quantised mat-vec */
@@ -157,11 +160,106 @@ p100_status p100_fa_decode_static(const p100_attn_desc* desc, const float* q, co
                                   const void* v, const float* mask, float* o, float* lse,
                                   p100_stream_t stream);
 
+/* ---------------------------------------------------- decode-step glue */
+/* The reference stops at one mat-vec and one attention call; it has no decode
+ * step, so these have no reference counterpart.  They follow Llama-3 as
+ * llama.cpp runs it, with every floating-point operation in a fixed order
+ * that the CPU restatement in oracle/ repeats, so each is bit-exact against
+ * it.  All take device buffers and run on `stream`. */
+
+/* x: batch rows of k fp32 (the residual stream).  If delta is not NULL,
+ * x += delta first (written back to x).  Then
+ * y = (x * (1 / sqrt(sum(x^2) / k + eps))) * w, quantised to Q8_1 into
+ * x_q8_1 (p100_q8_1_bytes(k, batch)); y is also stored to y_out if not NULL.
+ * k % 32 == 0. */
+p100_status p100_rmsnorm_q8_1(float* x, const float* delta, const float* w, float eps, int k, int batch,
+                              void* x_q8_1, float* y_out, p100_stream_t stream);
+
+/* Host: the RoPE table rope_cs[pos][i] = {cos, sin} of
+ * pos * theta^(-2i/head_dim) (computed in double) for pos < max_pos. */
+void p100_rope_table(float* rope_cs, int max_pos, int head_dim, float theta);
+
+/* qkv: [n_head q | n_head_kv k | n_head_kv v] x head_dim fp32 (the fused QKV
+ * mat-vec output).  At the device-resident position *pos_dev: rotates each
+ * adjacent pair (2i, 2i+1) of the q and k heads by rope_cs[pos][i] (q in
+ * place), and stores the rotated k and the v heads as fp16 (nearest) into
+ * row pos of k_cache / v_cache, laid out [head][max_pos][head_dim] with
+ * kv_head_stride elements between heads.  A position outside [0, max_pos)
+ * writes nothing and sets the device flag (p100_device_error reports
+ * P100_ERR_INVALID). */
+p100_status p100_rope_kv_append(float* qkv, int n_head, int n_head_kv, int head_dim, const float* rope_cs,
+                                int max_pos, const int* pos_dev, void* k_cache, void* v_cache,
+                                long long kv_head_stride, p100_stream_t stream);
+
+/* gate_up: batch rows of [gate (n) | up (n)] fp32.  h = silu(gate) * up with
+ * silu(g) = g / (1 + exp(-g)), quantised to Q8_1 into x_q8_1.  n % 32 == 0. */
+p100_status p100_swiglu_q8_1(const float* gate_up, int n, int batch, void* x_q8_1, p100_stream_t stream);
+
+/* idx[b] (and val[b] if not NULL) = argmax of row b of x (n fp32): the lowest
+ * index among equal maxima; NaN never wins. */
+p100_status p100_argmax(const float* x, int n, int batch, int* idx, float* val, p100_stream_t stream);
+
+/* --------------------------------------------------- batch-1 decoder */
+/* A Llama-3-shaped model with synthetic weights, decoded one token per
+ * p100_decoder_step.  No reference counterpart (see above).  Every linear
+ * weight and the embedding use wtype; norms are fp32; the KV cache is fp16.
+ * With a tensor-parallel handle the decoder holds that rank's slices: q/k/v
+ * and gate/up split by output rows, o and down along K with an NCCL
+ * all-reduce after each, the LM head by vocabulary rows with an all-gather of
+ * each rank's best candidate.  Position and token live on the device: a step
+ * embeds *token, appends row *pos, attends over [0, *pos], writes the argmax
+ * token and advances *pos, so steps chain without the host. */
+typedef struct p100_llama_config {
+    int n_layer, hidden, n_head, n_head_kv, head_dim, ffn, vocab, max_ctx;
+    float rope_theta, norm_eps;
+    int wtype;
+} p100_llama_config;
+typedef struct p100_decoder p100_decoder;
+/* Tensor ids (per layer where it applies). */
+enum {
+    P100_T_EMBED = 0,     /* [vocab][hidden] wtype                          */
+    P100_T_ATTN_NORM,     /* [hidden] fp32                                  */
+    P100_T_WQKV,          /* rows [q heads | k heads | v heads] x hidden    */
+    P100_T_WO,            /* [hidden] x (this rank's q heads * head_dim)    */
+    P100_T_FFN_NORM,      /* [hidden] fp32                                  */
+    P100_T_WGATE_UP,      /* rows [gate slice | up slice] x hidden          */
+    P100_T_WDOWN,         /* [hidden] x (this rank's FFN slice)             */
+    P100_T_OUT_NORM,      /* [hidden] fp32                                  */
+    P100_T_LM_HEAD        /* this rank's vocabulary rows x hidden           */
+};
+/* Buffer ids. */
+enum { P100_B_HIDDEN = 0, P100_B_LOGITS, P100_B_KCACHE, P100_B_VCACHE, P100_B_ROPE };
+/* Allocates everything (weights, fp16 KV cache for max_ctx, scratch) on the
+ * current device, or tp's device; tp may be NULL. */
+p100_status p100_decoder_create(const p100_llama_config* cfg, p100_tp* tp, p100_decoder** out);
+/* Synthetic weights from seed: blocks as the BASELINE configs describe
+ * (Q4_0 d = |N(0,1)|*0.02, codes uniform), norms uniform in [0.9, 1.1].
+ * Every value is a function of (seed, tensor, global coordinates), so the
+ * slices of a tensor-parallel rank equal the unsplit model's. */
+p100_status p100_decoder_init_random(p100_decoder* d, unsigned long long seed);
+/* KV rows [0, n_pos) of every layer: N(0,1) * scale as fp16. */
+p100_status p100_decoder_fill_kv(p100_decoder* d, int n_pos, unsigned long long seed, float scale);
+p100_status p100_decoder_set_state(p100_decoder* d, int pos, int token);
+/* Synchronises the device, then reads the position and the last token. */
+p100_status p100_decoder_state(p100_decoder* d, int* pos, int* token);
+/* n_steps tokens on stream.  The first call captures one step as a CUDA
+ * graph (on a stream of its own, so make it outside any capture); every step
+ * replays it.  With tp, every rank must call it the same number of times. */
+p100_status p100_decoder_step(p100_decoder* d, int n_steps, p100_stream_t stream);
+/* Device address and size of a tensor or buffer (for tests and tools). */
+p100_status p100_decoder_tensor(p100_decoder* d, int layer, int which, void** ptr, size_t* bytes, int* rows,
+                                int* cols);
+p100_status p100_decoder_buffer(p100_decoder* d, int which, void** ptr, size_t* bytes);
+/* First vocabulary id of this rank's LM-head rows. */
+int p100_decoder_vocab_offset(const p100_decoder* d);
+/* Weight bytes one step streams on this rank (all layers' matrices + LM head). */
+size_t p100_decoder_weight_bytes_per_token(const p100_decoder* d);
+p100_status p100_decoder_destroy(p100_decoder* d);
+
 /* ------------------------------------------------- tensor-parallel (NCCL) */
 /* Row-split tensor parallelism over the GPUs of one box; replaces the
  * reference's two-GPU PCIe layer (src/p2p/p2p.cpp) for the per-layer
  * partial-sum exchange.  One handle per rank. */
-typedef struct p100_tp p100_tp;
 #define P100_TP_ID_BYTES 128
 /* A fresh communicator id (ncclGetUniqueId) for rank 0 to share. */
 p100_status p100_tp_unique_id(void* id /* P100_TP_ID_BYTES */);

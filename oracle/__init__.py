@@ -135,6 +135,12 @@ class Oracle(_Base):
         self._eff_scale = f("attn_effective_scale", fp, vp)
         self._fill_normal = f("fill_normal", None, C.c_uint32, fp, fp, ip, C.c_size_t, vp)
         self._fill_uniform = f("fill_uniform", None, C.c_uint32, fp, fp, ip, C.c_size_t, vp)
+        self._rmsnorm = f("rmsnorm_q8_1", ip, vp, vp, vp, fp, ip, vp, vp)
+        self._rope = f("rope_kv_append", ip, vp, ip, ip, ip, vp, ip, ip, vp, vp, C.c_longlong)
+        self.dec_exp = f("dec_exp", fp, fp)
+        self._swiglu = f("swiglu_q8_1", ip, vp, ip, vp)
+        self._argmax = f("argmax", ip, vp, ip, vp)
+        self._decode_step = f("decode_step", ip, vp, vp, vp, vp, vp, ip, ip, vp, vp)
 
     # ------------------------------------------------------------ seeded inputs
     def fill_normal(self, seed, n, mean=0.0, stddev=1.0, round_fp16=False):
@@ -239,6 +245,81 @@ class Oracle(_Base):
         args = [np.ascontiguousarray(a, dtype=np.float32) if a is not None else None for a in (q, k, v, mask)]
         self._check(self._attn_tiled(C.byref(p), C.byref(cfg), *[_ptr(a) for a in args], _ptr(o), _ptr(lse)))
         return o, lse
+
+
+    # ------------------------------------------------------- decode-step glue
+    def rmsnorm_q8_1(self, x, w, eps, delta=None):
+        """Returns (x after x += delta, Q8_1 bytes, y) for one row (decode_oracle.cpp)."""
+        x = np.array(x, dtype=np.float32, copy=True)
+        k = x.size
+        out = np.zeros(k // 32 * 36, dtype=np.uint8)
+        y = np.zeros(k, dtype=np.float32)
+        d = None if delta is None else np.ascontiguousarray(delta, dtype=np.float32)
+        self._check(self._rmsnorm(_ptr(x), _ptr(d), _ptr(np.ascontiguousarray(w, dtype=np.float32)), eps, k,
+                                  _ptr(out), _ptr(y)))
+        return x, out, y
+
+    def rope_kv_append(self, qkv, nq, nkv, hd, rope_cs, max_pos, pos, k_cache, v_cache, head_stride):
+        """qkv rotated (copy); k_cache/v_cache (uint16 fp16 bits) updated in place."""
+        qkv = np.array(qkv, dtype=np.float32, copy=True)
+        self._check(self._rope(_ptr(qkv), nq, nkv, hd, _ptr(np.ascontiguousarray(rope_cs, dtype=np.float32)),
+                               max_pos, pos, _ptr(k_cache), _ptr(v_cache), head_stride))
+        return qkv
+
+    def swiglu_q8_1(self, gate_up, n):
+        out = np.zeros(n // 32 * 36, dtype=np.uint8)
+        self._check(self._swiglu(_ptr(np.ascontiguousarray(gate_up, dtype=np.float32)), n, _ptr(out)))
+        return out
+
+    def argmax(self, x):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        val = np.zeros(1, dtype=np.float32)
+        return self._argmax(_ptr(x), x.size, _ptr(val)), float(val[0])
+
+    def decode_step(self, cfg, weights, k_cache, v_cache, rope_cs, pos, token):
+        """One token of the restated decoder.  cfg: LlamaConfig; weights: dict of
+        host numpy arrays named as the decoder's tensors ('embed', 'attn_norm'
+        [per layer], 'wqkv', 'wo', 'ffn_norm', 'wgu', 'wdown', 'out_norm',
+        'lm_head').  Caches (uint16 fp16 bits) are updated in place.  Returns
+        (next token, logits, final residual)."""
+        L = cfg.n_layer
+        keep = []
+
+        def arr(a):
+            a = np.ascontiguousarray(a)
+            keep.append(a)
+            return a.ctypes.data_as(C.c_void_p)
+
+        def table(name):
+            t = (C.c_void_p * L)(*[arr(a) for a in weights[name]])
+            keep.append(t)
+            return t
+
+        w = LlamaWeights(arr(weights["embed"]), C.cast(table("attn_norm"), C.c_void_p),
+                         C.cast(table("wqkv"), C.c_void_p), C.cast(table("wo"), C.c_void_p),
+                         C.cast(table("ffn_norm"), C.c_void_p), C.cast(table("wgu"), C.c_void_p),
+                         C.cast(table("wdown"), C.c_void_p), arr(weights["out_norm"]), arr(weights["lm_head"]))
+        logits = np.zeros(cfg.vocab, dtype=np.float32)
+        hidden = np.zeros(cfg.hidden, dtype=np.float32)
+        tok = self._decode_step(C.byref(cfg), C.byref(w), _ptr(k_cache), _ptr(v_cache),
+                                _ptr(np.ascontiguousarray(rope_cs, dtype=np.float32)), pos, token, _ptr(logits),
+                                _ptr(hidden))
+        if tok < 0:
+            raise ValueError("decode_step rejected its arguments")
+        return tok, logits, hidden
+
+
+class LlamaConfig(C.Structure):
+    """p100o_llama, the same fields as p100_llama_config."""
+    _fields_ = [("n_layer", C.c_int), ("hidden", C.c_int), ("n_head", C.c_int), ("n_head_kv", C.c_int),
+                ("head_dim", C.c_int), ("ffn", C.c_int), ("vocab", C.c_int), ("max_ctx", C.c_int),
+                ("rope_theta", C.c_float), ("norm_eps", C.c_float), ("wtype", C.c_int)]
+
+
+class LlamaWeights(C.Structure):
+    """p100o_llama_weights: host pointers (per-layer ones as pointer tables)."""
+    _fields_ = [(n, C.c_void_p) for n in ("embed", "attn_norm", "wqkv", "wo", "ffn_norm", "wgu", "wdown",
+                                          "out_norm", "lm_head")]
 
 
 class Ref(_Base):

@@ -128,6 +128,43 @@ double p100o_attention_reference_threaded(const p100o_attn* p, const float* q,
                                           const float* k, const float* v,
                                           float* o, float* lse, int nthreads);
 
+/* ---- decode-step glue and one decode step (decode_oracle.cpp).  The
+ * reference has no decode step: these restate the Llama-3 decode math in the
+ * operation order of the GPU glue kernels (bit-exact targets) and chain the
+ * pinned pieces above for a whole step (a tolerance target). */
+int   p100o_rmsnorm_q8_1(float* x, const float* delta, const float* w, float eps, int k,
+                         void* out_q81, float* y_out);
+int   p100o_rope_kv_append(float* qkv, int nq, int nkv, int hd, const float* rope_cs, int max_pos,
+                           int pos, uint16_t* k_cache, uint16_t* v_cache, long long head_stride);
+float p100o_dec_exp(float x);
+int   p100o_swiglu_q8_1(const float* gate_up, int n, void* out_q81);
+/* Index of the largest value, lowest among equal ones; NaN never wins. */
+int   p100o_argmax(const float* x, int n, float* val);
+
+typedef struct p100o_llama {
+    int n_layer, hidden, n_head, n_head_kv, head_dim, ffn, vocab, max_ctx;
+    float rope_theta, norm_eps;
+    int wtype;
+} p100o_llama;
+/* Host copies of the unsplit model, laid out as the GPU decoder's tensors. */
+typedef struct p100o_llama_weights {
+    const void* embed;
+    const float* const* attn_norm;
+    const void* const* wqkv;
+    const void* const* wo;
+    const float* const* ffn_norm;
+    const void* const* wgu;
+    const void* const* wdown;
+    const float* out_norm;
+    const void* lm_head;
+} p100o_llama_weights;
+/* One token at pos: appends row pos to the fp16 caches (as uint16 bits,
+ * [layer][n_head_kv][max_ctx][head_dim]), writes vocab logits and the final
+ * residual stream (hidden_out, optional), returns the argmax token (or -1). */
+int p100o_decode_step(const p100o_llama* cfg, const p100o_llama_weights* w, uint16_t* k_cache,
+                      uint16_t* v_cache, const float* rope_cs, int pos, int token, float* logits,
+                      float* hidden_out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -109,6 +109,22 @@ def _bind(lib):
         "p100_peer_link_path": (ip, [vp]),
         "p100_peer_link_copy": (ip, [vp, vp, vp, sz, st]),
         "p100_peer_link_destroy": (ip, [vp]),
+        "p100_rmsnorm_q8_1": (ip, [vp, vp, vp, C.c_float, ip, ip, vp, vp, st]),
+        "p100_rope_table": (None, [vp, ip, ip, C.c_float]),
+        "p100_rope_kv_append": (ip, [vp, ip, ip, ip, vp, ip, vp, vp, vp, C.c_longlong, st]),
+        "p100_swiglu_q8_1": (ip, [vp, ip, ip, vp, st]),
+        "p100_argmax": (ip, [vp, ip, ip, vp, vp, st]),
+        "p100_decoder_create": (ip, [vp, vp, C.POINTER(vp)]),
+        "p100_decoder_init_random": (ip, [vp, C.c_ulonglong]),
+        "p100_decoder_fill_kv": (ip, [vp, ip, C.c_ulonglong, C.c_float]),
+        "p100_decoder_set_state": (ip, [vp, ip, ip]),
+        "p100_decoder_state": (ip, [vp, C.POINTER(ip), C.POINTER(ip)]),
+        "p100_decoder_step": (ip, [vp, ip, st]),
+        "p100_decoder_tensor": (ip, [vp, ip, ip, C.POINTER(vp), C.POINTER(sz), C.POINTER(ip), C.POINTER(ip)]),
+        "p100_decoder_buffer": (ip, [vp, ip, C.POINTER(vp), C.POINTER(sz)]),
+        "p100_decoder_vocab_offset": (ip, [vp]),
+        "p100_decoder_weight_bytes_per_token": (sz, [vp]),
+        "p100_decoder_destroy": (ip, [vp]),
     }
     for name, (res, args) in sigs.items():
         fn = getattr(lib, name)
@@ -280,6 +296,154 @@ class TP:
         if self.handle:
             h, self.handle = self.handle, None
             check(lib().p100_tp_destroy(h))
+
+
+# ------------------------------------------------------------ decode-step glue
+def rmsnorm_q8_1(x, w, eps, delta=None, y_out=None, xq=None, stream=None):
+    """x += delta (in place, when given); Q8_1 of RMSNorm(x) * w (p100_rmsnorm_q8_1)."""
+    torch = _torch()
+    k = x.shape[-1]
+    batch = x.numel() // k
+    if xq is None:
+        xq = torch.empty(batch * (k // 32) * Q8_1_BLOCK_BYTES, dtype=torch.uint8, device=x.device)
+    check(lib().p100_rmsnorm_q8_1(_ptr(x), _ptr(delta), _ptr(w), eps, k, batch, _ptr(xq), _ptr(y_out),
+                                  _stream(stream)))
+    return xq
+
+
+def rope_table(max_pos, head_dim, theta):
+    """Host numpy [max_pos, head_dim/2, 2] (cos, sin) table (p100_rope_table)."""
+    import numpy as np
+    out = np.zeros((max_pos, head_dim // 2, 2), dtype=np.float32)
+    lib().p100_rope_table(out.ctypes.data_as(C.c_void_p), max_pos, head_dim, theta)
+    return out
+
+
+def rope_kv_append(qkv, n_head, n_head_kv, head_dim, rope_cs, max_pos, pos_dev, k_cache, v_cache,
+                   kv_head_stride, stream=None):
+    check(lib().p100_rope_kv_append(_ptr(qkv), n_head, n_head_kv, head_dim, _ptr(rope_cs), max_pos, _ptr(pos_dev),
+                                    _ptr(k_cache), _ptr(v_cache), kv_head_stride, _stream(stream)))
+
+
+def swiglu_q8_1(gate_up, n, xq=None, stream=None):
+    torch = _torch()
+    batch = gate_up.numel() // (2 * n)
+    if xq is None:
+        xq = torch.empty(batch * (n // 32) * Q8_1_BLOCK_BYTES, dtype=torch.uint8, device=gate_up.device)
+    check(lib().p100_swiglu_q8_1(_ptr(gate_up), n, batch, _ptr(xq), _stream(stream)))
+    return xq
+
+
+def argmax(x, stream=None):
+    """(idx int32 [batch], val fp32 [batch]) of the rows of x (p100_argmax)."""
+    torch = _torch()
+    n = x.shape[-1]
+    batch = x.numel() // n
+    idx = torch.empty(batch, dtype=torch.int32, device=x.device)
+    val = torch.empty(batch, dtype=torch.float32, device=x.device)
+    check(lib().p100_argmax(_ptr(x), n, batch, _ptr(idx), _ptr(val), _stream(stream)))
+    return idx, val
+
+
+class LlamaConfig(C.Structure):
+    """p100_llama_config."""
+    _fields_ = [("n_layer", C.c_int), ("hidden", C.c_int), ("n_head", C.c_int), ("n_head_kv", C.c_int),
+                ("head_dim", C.c_int), ("ffn", C.c_int), ("vocab", C.c_int), ("max_ctx", C.c_int),
+                ("rope_theta", C.c_float), ("norm_eps", C.c_float), ("wtype", C.c_int)]
+
+    def __init__(self, n_layer, hidden, n_head, n_head_kv, head_dim, ffn, vocab, max_ctx, rope_theta=500000.0,
+                 norm_eps=1e-5, wtype=0):
+        super().__init__(n_layer, hidden, n_head, n_head_kv, head_dim, ffn, vocab, max_ctx, rope_theta, norm_eps,
+                         wtype)
+
+
+T_EMBED, T_ATTN_NORM, T_WQKV, T_WO, T_FFN_NORM, T_WGATE_UP, T_WDOWN, T_OUT_NORM, T_LM_HEAD = range(9)
+B_HIDDEN, B_LOGITS, B_KCACHE, B_VCACHE, B_ROPE = range(5)
+
+
+class Decoder:
+    """A batch-1 Llama-shaped decoder (p100_decoder_*), one GPU or one TP rank."""
+
+    def __init__(self, cfg: LlamaConfig, tp: "TP | None" = None):
+        h = C.c_void_p()
+        self.cfg = cfg
+        check(lib().p100_decoder_create(C.byref(cfg), tp.handle if tp is not None else None, C.byref(h)))
+        self.handle = h
+
+    def init_random(self, seed):
+        check(lib().p100_decoder_init_random(self.handle, seed))
+
+    def fill_kv(self, n_pos, seed, scale=0.5):
+        check(lib().p100_decoder_fill_kv(self.handle, n_pos, seed, scale))
+
+    def set_state(self, pos, token):
+        check(lib().p100_decoder_set_state(self.handle, pos, token))
+
+    def state(self):
+        pos, tok = C.c_int(), C.c_int()
+        check(lib().p100_decoder_state(self.handle, C.byref(pos), C.byref(tok)))
+        return pos.value, tok.value
+
+    def step(self, n=1, stream=None):
+        check(lib().p100_decoder_step(self.handle, n, _stream(stream)))
+
+    def tensor(self, which, layer=0):
+        """(device address, bytes, rows, cols) of a weight tensor."""
+        ptr, n, rows, cols = C.c_void_p(), C.c_size_t(), C.c_int(), C.c_int()
+        check(lib().p100_decoder_tensor(self.handle, layer, which, C.byref(ptr), C.byref(n), C.byref(rows),
+                                        C.byref(cols)))
+        return ptr.value, n.value, rows.value, cols.value
+
+    def buffer(self, which):
+        ptr, n = C.c_void_p(), C.c_size_t()
+        check(lib().p100_decoder_buffer(self.handle, which, C.byref(ptr), C.byref(n)))
+        return ptr.value, n.value
+
+    @property
+    def vocab_offset(self):
+        return lib().p100_decoder_vocab_offset(self.handle)
+
+    @property
+    def weight_bytes_per_token(self):
+        return lib().p100_decoder_weight_bytes_per_token(self.handle)
+
+    def read(self, ptr, nbytes):
+        """Host bytes (numpy uint8) of nbytes at a device address (synchronises)."""
+        return device_to_host(ptr, nbytes)
+
+    def write(self, ptr, data):
+        """Copy host bytes (numpy array) to a device address (synchronises)."""
+        host_to_device(ptr, data)
+
+    def close(self):
+        if self.handle:
+            h, self.handle = self.handle, None
+            check(lib().p100_decoder_destroy(h))
+
+
+def _runtime():
+    from cuda.bindings import runtime as rt   # cuda-python: raw-address copies for tests and tools
+    return rt
+
+
+def device_to_host(ptr, nbytes):
+    """numpy uint8 copy of nbytes at a device address (cudaMemcpy, synchronous)."""
+    import numpy as np
+    rt = _runtime()
+    out = np.empty(nbytes, dtype=np.uint8)
+    (err,) = rt.cudaMemcpy(out.ctypes.data, ptr, nbytes, rt.cudaMemcpyKind.cudaMemcpyDeviceToHost)
+    if int(err) != 0:
+        raise P100Error(ERR_CUDA, f"cudaMemcpy device to host failed ({err})")
+    return out
+
+
+def host_to_device(ptr, data):
+    import numpy as np
+    rt = _runtime()
+    data = np.ascontiguousarray(data)
+    (err,) = rt.cudaMemcpy(ptr, data.ctypes.data, data.nbytes, rt.cudaMemcpyKind.cudaMemcpyHostToDevice)
+    if int(err) != 0:
+        raise P100Error(ERR_CUDA, f"cudaMemcpy host to device failed ({err})")
 
 
 # ---------------------------------------------------------------- peer copies

@@ -4,14 +4,18 @@
 //
 // Single CUDA translation unit: every kernel header is included here so the
 // library has one device module and one g_device_error word per device.
+#include <cmath>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <utility>
+#include <vector>
 
 #include "common.cuh"
 #include "fa_decode.cuh"
+#include "fa_mma.cuh"
 #include "qmv.cuh"
 #include "qmv_team.cuh"
 #include "quant.cuh"
@@ -336,7 +340,9 @@ p100_status plan_fa(const p100_attn_desc& d, int sms, FaPlan& plan) {
     const int max_parts = std::max(1, d.seq_kv / fa::kTile);
     int parts = d.kv_splits;
     if (parts <= 0) parts = std::max(1, sms / heads);
-    plan.parts = std::min(parts, max_parts);
+    // at most 512 parts: the last-CTA merge keeps every part's (m, l) and
+    // weight in shared memory (2 * parts * G floats, inside the idle ring)
+    plan.parts = std::min(std::min(parts, max_parts), 512);
     plan.nstage = d.d_qk == 256 ? 2 : 4;
     const size_t head = ((64 + (plan.gmax * fa::kTile + fa::kTile * 8 + 24 + plan.gmax * plan.D + 4) * 4) + 127) & ~size_t(127);
     plan.smem = head + size_t(plan.nstage) * 2 * fa::kTile * plan.D * 2;
@@ -350,7 +356,7 @@ p100_status plan_fa(const p100_attn_desc& d, int sms, FaPlan& plan) {
 }
 
 template <int D, int GMAX>
-p100_status launch_fa_t(const FaPlan& plan, const fa::Params& prm, int heads, cudaStream_t stream) {
+p100_status launch_fa_t(const FaPlan& plan, const fa::Params& prm, int heads, cudaStream_t stream, bool pdl) {
     auto kern = fa::fa_decode_kernel<D, GMAX>;
     static thread_local int configured_smem[64] = {};
     int dev = 0;
@@ -360,17 +366,77 @@ p100_status launch_fa_t(const FaPlan& plan, const fa::Params& prm, int heads, cu
         if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(fa)");
         configured_smem[dev] = int(plan.smem);
     }
-    kern<<<dim3(plan.parts, heads), fa::kThreads, plan.smem, stream>>>(prm);
-    return launch_status("fa_decode_kernel launch");
+    if (!pdl) {
+        kern<<<dim3(plan.parts, heads), fa::kThreads, plan.smem, stream>>>(prm);
+        return launch_status("fa_decode_kernel launch");
+    }
+    // PDL only with a device-resident length: the kernel then waits for the
+    // previous kernel before it reads any K/V (see fa::Params::len_dev).
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(plan.parts, heads);
+    cfg.blockDim = dim3(fa::kThreads);
+    cfg.dynamicSmemBytes = plan.smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cuda_status(cudaLaunchKernelEx(&cfg, kern, prm), "fa_decode_kernel launch");
+}
+
+template <int D, int G>
+p100_status launch_fa_mma_t(const FaPlan& plan, const fa::Params& prm, int heads, cudaStream_t stream, bool pdl) {
+    auto kern = fam::fa_mma_kernel<D, G>;
+    constexpr size_t smem = fam::smem_bytes<D, G>();
+    static thread_local int configured[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!configured[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+        if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(fa_mma)");
+        configured[dev] = 1;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(plan.parts, heads);
+    cfg.blockDim = dim3(fam::kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cuda_status(cudaLaunchKernelEx(&cfg, kern, prm), "fa_mma_kernel launch");
 }
 
 template <int D>
-p100_status launch_fa_d(const FaPlan& plan, const fa::Params& prm, int heads, cudaStream_t s) {
+p100_status launch_fa_mma_d(const FaPlan& plan, const fa::Params& prm, int heads, cudaStream_t s, bool pdl) {
+    switch (plan.G) {
+        case 1: return launch_fa_mma_t<D, 1>(plan, prm, heads, s, pdl);
+        case 2: return launch_fa_mma_t<D, 2>(plan, prm, heads, s, pdl);
+        case 4: return launch_fa_mma_t<D, 4>(plan, prm, heads, s, pdl);
+        default: return launch_fa_mma_t<D, 8>(plan, prm, heads, s, pdl);
+    }
+}
+
+// The tensor-core kernel serves head_dim 64/128 with 1, 2, 4 or 8 query heads
+// per kv head and 16-byte aligned K/V; the SIMT kernel serves the rest.
+bool fa_use_mma(const FaPlan& plan, const fa::Params& prm) {
+    const bool g_ok = plan.G == 1 || plan.G == 2 || plan.G == 4 || plan.G == 8;
+    const bool aligned = reinterpret_cast<uintptr_t>(prm.k) % 16 == 0 && reinterpret_cast<uintptr_t>(prm.v) % 16 == 0;
+    return (plan.D == 64 || plan.D == 128) && g_ok && aligned;
+}
+
+template <int D>
+p100_status launch_fa_d(const FaPlan& plan, const fa::Params& prm, int heads, cudaStream_t s, bool pdl = false) {
+    if constexpr (D != 256)
+        if (fa_use_mma(plan, prm)) return launch_fa_mma_d<D>(plan, prm, heads, s, pdl);
     switch (plan.gmax) {
-        case 1: return launch_fa_t<D, 1>(plan, prm, heads, s);
-        case 2: return launch_fa_t<D, 2>(plan, prm, heads, s);
-        case 4: return launch_fa_t<D, 4>(plan, prm, heads, s);
-        default: return launch_fa_t<D, 8>(plan, prm, heads, s);
+        case 1: return launch_fa_t<D, 1>(plan, prm, heads, s, pdl);
+        case 2: return launch_fa_t<D, 2>(plan, prm, heads, s, pdl);
+        case 4: return launch_fa_t<D, 4>(plan, prm, heads, s, pdl);
+        default: return launch_fa_t<D, 8>(plan, prm, heads, s, pdl);
     }
 }
 
@@ -425,6 +491,8 @@ p100_status p100_device_error(int clear) {
         if (p100_status st = cuda_status(cudaMemcpyToSymbol(g_device_error, &zero, sizeof zero), "clear device flag"))
             return st;
     }
+    if (value == kDevErrInput)
+        return set_error(P100_ERR_INVALID, "a kernel read a device-resident token or position out of range");
     return value ? set_error(P100_ERR_TIMEOUT, "a kernel gave up a bounded wait") : P100_OK;
 }
 
@@ -613,3 +681,6 @@ extern "C" p100_status p100_fa_decode_static(const p100_attn_desc* desc, const f
     }
     return p100_fa_decode(desc, q, k, v, mask, o, lse, scratch, plan.ws_total, stream);
 }
+
+// The batch-1 decoder and the decode-step glue entry points.
+#include "decoder.cuh"

@@ -27,6 +27,7 @@ p100_status require_sm100(int* device_out, int* sm_count_out);
 // so this definition exists once per device module.
 __device__ int g_device_error = 0;
 constexpr int kDevErrTimeout = 1;
+constexpr int kDevErrInput = 2;    // a device-resident index (token, position) out of range
 // One second: far above any legitimate wait in these kernels (microseconds).
 constexpr unsigned long long kWaitLimitNs = 1000000000ull;
 

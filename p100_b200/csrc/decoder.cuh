@@ -1,0 +1,605 @@
+// decoder.cuh — a batch-1 Llama-3-shaped decode step on one GPU or one rank
+// of a tensor-parallel group, replayed as one CUDA graph per token.
+//
+// Included at the end of capi.cu (one translation unit): it drives the
+// library's own mat-vec (run_qmv), attention (plan_fa/launch_fa_d) and glue
+// kernels (decode.cuh).  The step per layer:
+//   x += delta; xq = Q8_1(RMSNorm(x) * attn_norm)            rmsnorm_q8_1
+//   qkv = Wqkv . xq                    (fused q|k|v rows)     team mat-vec
+//   RoPE(q, k) at pos; k, v -> fp16 cache row pos             rope_kv_append
+//   attn = FA(q, K[0..pos], V[0..pos])  (length from device)  fa_decode
+//   delta = Wo . Q8_1(attn)            (TP: all-reduce)       quantize + mat-vec
+//   x += delta; xq = Q8_1(RMSNorm(x) * ffn_norm)
+//   gu = Wgate_up . xq                 (fused gate|up rows)
+//   delta = Wdown . Q8_1(silu(g) * u)  (TP: all-reduce)       swiglu_q8_1 + mat-vec
+// then x += delta, RMSNorm, the LM head and argmax; argmax writes the next
+// token and advances the position, both device-resident, so a step needs no
+// host round trip and the captured graph is the same every token.
+//
+// Tensor parallelism (Megatron split, the row-split of BASELINE config 5):
+// q/k/v and gate/up by output rows (heads, FFN slice), o and down along K
+// (their inputs are local), the LM head by vocabulary rows; RMSNorm, the
+// embedding and the residual stream are replicated.  Each rank initialises
+// its slices from global coordinates, so TP=N holds the same model as TP=1.
+#pragma once
+#include "decode.cuh"
+
+namespace p100b {
+namespace {
+
+struct DecTensor {
+    uint8_t* ptr = nullptr;
+    size_t bytes = 0;
+    int rows = 0, cols = 0;   // cols in elements (weights) or 1 (vectors)
+};
+
+struct Decoder {
+    p100_llama_config cfg{};
+    p100_tp* tp = nullptr;
+    int rank = 0, nranks = 1, device = 0, sms = 0;
+    int nq = 0, nkv = 0, ffn = 0, vocab0 = 0, vocab_n = 0;   // this rank's slice
+    size_t row_bytes_h = 0;                                  // one hidden-K weight row
+    uint8_t* arena = nullptr;
+    size_t arena_bytes = 0;
+    std::vector<DecTensor> attn_norm, wqkv, wo, ffn_norm, wgu, wdown;
+    DecTensor embed, out_norm, lm_head;
+    __half *kcache = nullptr, *vcache = nullptr;   // [layer][nkv][max_ctx][hd]
+    float *x = nullptr, *delta = nullptr, *qkv = nullptr, *attn = nullptr, *gu = nullptr, *logits = nullptr;
+    float *rope = nullptr, *pair = nullptr, *cand = nullptr;
+    uint8_t* xq = nullptr;
+    int *pos = nullptr, *token = nullptr;
+    uint8_t* fa_ws = nullptr;
+    FaPlan fa_plan;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t graph_exec = nullptr;
+};
+
+size_t dec_weight_bytes(int type, int rows, int cols) {
+    return size_t(rows) * (cols / elems_of(type)) * bytes_of(type);
+}
+
+template <typename... Exp, typename... Act>
+p100_status launch_glue(void (*kern)(Exp...), dim3 grid, dim3 block, cudaStream_t s, const char* what,
+                        Act&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cuda_status(cudaLaunchKernelEx(&cfg, kern, std::forward<Act>(args)...), what);
+}
+
+const char* config_reason(const p100_llama_config& c, int nranks) {
+    if (c.n_layer <= 0 || c.hidden <= 0 || c.n_head <= 0 || c.n_head_kv <= 0 || c.head_dim <= 0 || c.ffn <= 0 ||
+        c.vocab <= 0 || c.max_ctx <= 0)
+        return "all model dimensions must be positive";
+    if (c.wtype != P100_Q4_0 && c.wtype != P100_Q8_0 && c.wtype != P100_Q4_K) return "unknown weight type";
+    if (c.n_head % c.n_head_kv) return "n_head must be divisible by n_head_kv";
+    if (c.head_dim != 64 && c.head_dim != 128 && c.head_dim != 256) return "head_dim must be 64, 128 or 256";
+    if (c.n_head / c.n_head_kv > 8) return "at most 8 query heads per kv head";
+    if (c.n_head % nranks || c.n_head_kv % nranks) return "heads must split evenly over the ranks";
+    const int blk = elems_of(c.wtype);
+    if (c.hidden % blk || c.hidden % 32) return "hidden must be whole weight blocks";
+    if (c.hidden > dec::kNormMaxK) return "hidden above the RMSNorm kernel's limit (16384)";
+    if ((c.n_head / nranks) * c.head_dim % blk) return "a rank's attention slice must be whole weight blocks";
+    if (c.ffn % nranks || (c.ffn / nranks) % blk || (c.ffn / nranks) % 32)
+        return "a rank's FFN slice must be whole weight blocks";
+    if (c.vocab < nranks) return "vocab smaller than the number of ranks";
+    if (!(c.norm_eps >= 0.0f) || !(c.rope_theta > 0.0f)) return "norm_eps must be >= 0 and rope_theta > 0";
+    return nullptr;
+}
+
+p100_status dec_alloc(Decoder& d) {
+    const p100_llama_config& c = d.cfg;
+    const int t = c.wtype, hd = c.head_dim, L = c.n_layer;
+    d.nq = c.n_head / d.nranks;
+    d.nkv = c.n_head_kv / d.nranks;
+    d.ffn = c.ffn / d.nranks;
+    d.vocab0 = static_cast<int>(static_cast<long long>(c.vocab) * d.rank / d.nranks);
+    d.vocab_n = static_cast<int>(static_cast<long long>(c.vocab) * (d.rank + 1) / d.nranks) - d.vocab0;
+    d.row_bytes_h = dec_weight_bytes(t, 1, c.hidden);
+    size_t off = 0;
+    auto take = [&](size_t bytes) { const size_t at = off; off += align256(bytes); return at; };
+    struct Req { DecTensor* t; size_t at; };
+    std::vector<Req> reqs;
+    auto tensor = [&](DecTensor& dt, int rows, int cols, size_t bytes) {
+        dt.rows = rows;
+        dt.cols = cols;
+        dt.bytes = bytes;
+        reqs.push_back({&dt, take(bytes)});
+    };
+    d.attn_norm.resize(L); d.wqkv.resize(L); d.wo.resize(L); d.ffn_norm.resize(L); d.wgu.resize(L); d.wdown.resize(L);
+    for (int l = 0; l < L; ++l) {
+        const int qkv_rows = (d.nq + 2 * d.nkv) * hd;
+        tensor(d.attn_norm[l], c.hidden, 1, size_t(c.hidden) * 4);
+        tensor(d.wqkv[l], qkv_rows, c.hidden, dec_weight_bytes(t, qkv_rows, c.hidden));
+        tensor(d.wo[l], c.hidden, d.nq * hd, dec_weight_bytes(t, c.hidden, d.nq * hd));
+        tensor(d.ffn_norm[l], c.hidden, 1, size_t(c.hidden) * 4);
+        tensor(d.wgu[l], 2 * d.ffn, c.hidden, dec_weight_bytes(t, 2 * d.ffn, c.hidden));
+        tensor(d.wdown[l], c.hidden, d.ffn, dec_weight_bytes(t, c.hidden, d.ffn));
+    }
+    tensor(d.embed, c.vocab, c.hidden, dec_weight_bytes(t, c.vocab, c.hidden));
+    tensor(d.out_norm, c.hidden, 1, size_t(c.hidden) * 4);
+    tensor(d.lm_head, d.vocab_n, c.hidden, dec_weight_bytes(t, d.vocab_n, c.hidden));
+    const size_t kv_elems = size_t(L) * d.nkv * c.max_ctx * hd;
+    const size_t at_k = take(kv_elems * 2), at_v = take(kv_elems * 2);
+    const int xq_k = std::max(c.hidden, std::max(d.nq * hd, d.ffn));
+    const size_t at_x = take(size_t(c.hidden) * 4), at_delta = take(size_t(c.hidden) * 4);
+    const size_t at_qkv = take(size_t(d.nq + 2 * d.nkv) * hd * 4), at_attn = take(size_t(d.nq) * hd * 4);
+    const size_t at_gu = take(size_t(2) * d.ffn * 4), at_logits = take(size_t(d.vocab_n) * 4);
+    const size_t at_rope = take(size_t(c.max_ctx) * (hd / 2) * 8);
+    const size_t at_pair = take(8), at_cand = take(size_t(d.nranks) * 8);
+    const size_t at_xq = take(size_t(xq_k / 32) * 36), at_pos = take(4), at_token = take(4);
+    // attention over [0, max_ctx): split plan and its workspace
+    p100_attn_desc ad = {};
+    ad.batch = 1;
+    ad.n_head_q = d.nq;
+    ad.n_head_kv = d.nkv;
+    ad.seq_q = 1;
+    ad.seq_kv = c.max_ctx;
+    ad.d_qk = ad.d_v = hd;
+    ad.kv_head_stride = static_cast<long long>(c.max_ctx) * hd;
+    if (p100_status st = plan_fa(ad, d.sms, d.fa_plan)) return st;
+    const size_t at_ws = take(std::max<size_t>(d.fa_plan.ws_total, 256));
+    d.arena_bytes = off;
+    if (p100_status st = cuda_status(cudaMalloc(&d.arena, d.arena_bytes), "cudaMalloc(decoder)")) return st;
+    for (const Req& r : reqs) r.t->ptr = d.arena + r.at;
+    d.kcache = reinterpret_cast<__half*>(d.arena + at_k);
+    d.vcache = reinterpret_cast<__half*>(d.arena + at_v);
+    d.x = reinterpret_cast<float*>(d.arena + at_x);
+    d.delta = reinterpret_cast<float*>(d.arena + at_delta);
+    d.qkv = reinterpret_cast<float*>(d.arena + at_qkv);
+    d.attn = reinterpret_cast<float*>(d.arena + at_attn);
+    d.gu = reinterpret_cast<float*>(d.arena + at_gu);
+    d.logits = reinterpret_cast<float*>(d.arena + at_logits);
+    d.rope = reinterpret_cast<float*>(d.arena + at_rope);
+    d.pair = reinterpret_cast<float*>(d.arena + at_pair);
+    d.cand = reinterpret_cast<float*>(d.arena + at_cand);
+    d.xq = d.arena + at_xq;
+    d.pos = reinterpret_cast<int*>(d.arena + at_pos);
+    d.token = reinterpret_cast<int*>(d.arena + at_token);
+    d.fa_ws = d.arena + at_ws;
+    if (p100_status st = cuda_status(cudaMemset(d.arena, 0, d.arena_bytes), "cudaMemset(decoder)")) return st;
+    std::vector<float> table(size_t(c.max_ctx) * (hd / 2) * 2);
+    p100_rope_table(table.data(), c.max_ctx, hd, c.rope_theta);
+    return cuda_status(cudaMemcpy(d.rope, table.data(), table.size() * 4, cudaMemcpyHostToDevice), "copy rope table");
+}
+
+// Tensor ids mixed into the initialisation key (with the layer).
+uint64_t dec_key(uint64_t seed, int layer, int id) {
+    uint64_t z = seed ^ (uint64_t(layer + 1) << 32) ^ uint64_t(id + 1) * 0x9e3779b97f4a7c15ull;
+    z = (z ^ (z >> 31)) * 0xd6e8feb86659fd93ull;
+    return z ^ (z >> 32);
+}
+
+template <int T>
+p100_status dec_init_w(uint8_t* w, size_t row_bytes, int rows, int blocks, uint64_t key, long long row0,
+                       long long block0) {
+    const long long n = static_cast<long long>(rows) * blocks;
+    if (n == 0) return P100_OK;
+    dec::init_weights_kernel<T><<<unsigned((n + 255) / 256), 256>>>(w, row_bytes, rows, blocks, key, row0, block0);
+    return launch_status("init_weights_kernel launch");
+}
+
+p100_status dec_init_matrix(int t, uint8_t* w, size_t row_bytes, int rows, int cols, uint64_t key, long long row0,
+                            long long col0) {
+    const int blocks = cols / elems_of(t);
+    const long long block0 = col0 / elems_of(t);
+    switch (t) {
+        case P100_Q4_0: return dec_init_w<P100_Q4_0>(w, row_bytes, rows, blocks, key, row0, block0);
+        case P100_Q8_0: return dec_init_w<P100_Q8_0>(w, row_bytes, rows, blocks, key, row0, block0);
+        default: return dec_init_w<P100_Q4_K>(w, row_bytes, rows, blocks, key, row0, block0);
+    }
+}
+
+p100_status dec_init_vector(float* v, long long n, uint64_t key) {
+    dec::init_uniform_kernel<<<unsigned((n + 255) / 256), 256>>>(v, n, key, 0, 0.9f, 1.1f);
+    return launch_status("init_uniform_kernel launch");
+}
+
+// Every weight of this rank's slices.  Global coordinates: q rows of head h
+// are h*hd.., k/v rows likewise per kv head; o and down columns are the K
+// positions of this rank's heads / FFN slice; LM head rows are vocabulary ids.
+p100_status dec_init_random(Decoder& d, uint64_t seed) {
+    const p100_llama_config& c = d.cfg;
+    const int t = c.wtype, hd = c.head_dim;
+    const size_t rb_h = d.row_bytes_h;
+    enum { K_NORM1, K_Q, K_K, K_V, K_O, K_NORM2, K_GATE, K_UP, K_DOWN, K_EMB, K_NORM3, K_LM };
+    for (int l = 0; l < c.n_layer; ++l) {
+        p100_status st = P100_OK;
+        uint8_t* w = d.wqkv[l].ptr;
+        const long long q0 = static_cast<long long>(d.rank) * d.nq * hd, kv0 = static_cast<long long>(d.rank) * d.nkv * hd;
+        if (!st) st = dec_init_vector(reinterpret_cast<float*>(d.attn_norm[l].ptr), c.hidden, dec_key(seed, l, K_NORM1));
+        if (!st) st = dec_init_matrix(t, w, rb_h, d.nq * hd, c.hidden, dec_key(seed, l, K_Q), q0, 0);
+        if (!st) st = dec_init_matrix(t, w + size_t(d.nq * hd) * rb_h, rb_h, d.nkv * hd, c.hidden, dec_key(seed, l, K_K), kv0, 0);
+        if (!st) st = dec_init_matrix(t, w + size_t((d.nq + d.nkv) * hd) * rb_h, rb_h, d.nkv * hd, c.hidden,
+                                      dec_key(seed, l, K_V), kv0, 0);
+        if (!st) st = dec_init_matrix(t, d.wo[l].ptr, dec_weight_bytes(t, 1, d.nq * hd), c.hidden, d.nq * hd,
+                                      dec_key(seed, l, K_O), 0, q0);
+        if (!st) st = dec_init_vector(reinterpret_cast<float*>(d.ffn_norm[l].ptr), c.hidden, dec_key(seed, l, K_NORM2));
+        const long long f0 = static_cast<long long>(d.rank) * d.ffn;
+        if (!st) st = dec_init_matrix(t, d.wgu[l].ptr, rb_h, d.ffn, c.hidden, dec_key(seed, l, K_GATE), f0, 0);
+        if (!st) st = dec_init_matrix(t, d.wgu[l].ptr + size_t(d.ffn) * rb_h, rb_h, d.ffn, c.hidden, dec_key(seed, l, K_UP),
+                                      f0, 0);
+        if (!st) st = dec_init_matrix(t, d.wdown[l].ptr, dec_weight_bytes(t, 1, d.ffn), c.hidden, d.ffn,
+                                      dec_key(seed, l, K_DOWN), 0, f0);
+        if (st) return st;
+    }
+    p100_status st = dec_init_matrix(t, d.embed.ptr, rb_h, c.vocab, c.hidden, dec_key(seed, -1, K_EMB), 0, 0);
+    if (!st) st = dec_init_vector(reinterpret_cast<float*>(d.out_norm.ptr), c.hidden, dec_key(seed, -1, K_NORM3));
+    if (!st) st = dec_init_matrix(t, d.lm_head.ptr, rb_h, d.vocab_n, c.hidden, dec_key(seed, -1, K_LM), d.vocab0, 0);
+    if (!st) st = cuda_status(cudaDeviceSynchronize(), "decoder initialisation");
+    return st;
+}
+
+p100_status dec_fill_kv(Decoder& d, int npos, uint64_t seed, float scale) {
+    const p100_llama_config& c = d.cfg;
+    const int hd = c.head_dim;
+    const long long hs = static_cast<long long>(c.max_ctx) * hd;
+    const long long n = static_cast<long long>(d.nkv) * npos * hd;
+    for (int l = 0; l < c.n_layer && n > 0; ++l) {
+        const size_t layer_off = size_t(l) * d.nkv * hs;
+        const unsigned grid = unsigned((n + 255) / 256);
+        dec::init_kv_kernel<<<grid, 256>>>(d.kcache + layer_off, d.nkv, npos, hd, hs, dec_key(seed, l, 100),
+                                           d.rank * d.nkv, scale);
+        dec::init_kv_kernel<<<grid, 256>>>(d.vcache + layer_off, d.nkv, npos, hd, hs, dec_key(seed, l, 101),
+                                           d.rank * d.nkv, scale);
+        if (p100_status st = launch_status("init_kv_kernel launch")) return st;
+    }
+    return cuda_status(cudaDeviceSynchronize(), "KV fill");
+}
+
+template <int T>
+p100_status dec_embed_t(Decoder& d, cudaStream_t s) {
+    const int slabs = d.cfg.hidden / 32;
+    return launch_glue(dec::embed_kernel<T>, dim3((slabs + 255) / 256), dim3(256), s, "embed_kernel launch",
+                       static_cast<const uint8_t*>(d.embed.ptr), d.row_bytes_h, d.cfg.vocab, d.cfg.hidden,
+                       static_cast<const int*>(d.token), d.x);
+}
+
+p100_status dec_rmsnorm(Decoder& d, const float* delta, const DecTensor& w, cudaStream_t s) {
+    return launch_glue(dec::rmsnorm_q8_1_kernel, dim3(1), dim3(dec::kNormThreads), s, "rmsnorm_q8_1_kernel launch",
+                       d.x, delta, reinterpret_cast<const float*>(w.ptr), d.cfg.norm_eps, d.cfg.hidden, d.xq,
+                       static_cast<float*>(nullptr));
+}
+
+// One token, recorded into stream s (a capture stream).
+p100_status dec_record_step(Decoder& d, cudaStream_t s) {
+    const p100_llama_config& c = d.cfg;
+    const int t = c.wtype, hd = c.head_dim;
+    const long long hs = static_cast<long long>(c.max_ctx) * hd;
+    p100_status st = P100_OK;
+    switch (t) {
+        case P100_Q4_0: st = dec_embed_t<P100_Q4_0>(d, s); break;
+        case P100_Q8_0: st = dec_embed_t<P100_Q8_0>(d, s); break;
+        default: st = dec_embed_t<P100_Q4_K>(d, s); break;
+    }
+    for (int l = 0; l < c.n_layer && !st; ++l) {
+        const size_t layer_off = size_t(l) * d.nkv * hs;
+        st = dec_rmsnorm(d, l == 0 ? nullptr : d.delta, d.attn_norm[l], s);
+        if (!st) st = run_qmv(t, d.wqkv[l].ptr, d.wqkv[l].rows, c.hidden, d.xq, 1, d.qkv, P100_QMV_PDL, s);
+        if (!st)
+            st = launch_glue(dec::rope_kv_append_kernel, dim3(d.nq + 2 * d.nkv), dim3(hd / 2), s,
+                             "rope_kv_append_kernel launch", d.qkv, d.nq, d.nkv, hd,
+                             reinterpret_cast<const float2*>(d.rope), c.max_ctx, static_cast<const int*>(d.pos),
+                             d.kcache + layer_off, d.vcache + layer_off, hs);
+        if (!st) {
+            fa::Params prm = {};
+            const FaPlan& plan = d.fa_plan;
+            prm.q = d.qkv;
+            prm.k = d.kcache + layer_off;
+            prm.v = d.vcache + layer_off;
+            prm.o = d.attn;
+            prm.ws_o = plan.parts > 1 ? reinterpret_cast<float*>(d.fa_ws) : nullptr;
+            prm.ws_ml = plan.parts > 1 ? reinterpret_cast<float*>(d.fa_ws + plan.ws_o) : nullptr;
+            prm.tickets = plan.parts > 1 ? reinterpret_cast<unsigned*>(d.fa_ws + plan.ws_o + plan.ws_ml) : nullptr;
+            prm.nkv = d.nkv;
+            prm.G = plan.G;
+            prm.seq = c.max_ctx;
+            prm.parts = plan.parts;
+            prm.nstage = plan.nstage;
+            prm.head_stride = plan.head_stride;
+            prm.batch_stride = plan.batch_stride;
+            prm.scale = 1.0f / std::sqrt(float(hd));
+            prm.softcap = 0.0f;
+            prm.len_dev = d.pos;
+            prm.len_add = 1;   // the row appended at pos is part of the context
+            switch (hd) {
+                case 64: st = launch_fa_d<64>(plan, prm, d.nkv, s, true); break;
+                case 128: st = launch_fa_d<128>(plan, prm, d.nkv, s, true); break;
+                default: st = launch_fa_d<256>(plan, prm, d.nkv, s, true); break;
+            }
+        }
+        if (!st) {
+            const int k_o = d.nq * hd;
+            st = launch_glue(q8_1_quantize_kernel, dim3((k_o / 32 + 7) / 8, 1), dim3(256), s,
+                             "q8_1_quantize_kernel launch", static_cast<const float*>(d.attn), d.xq, k_o, k_o / 32);
+        }
+        if (!st) st = run_qmv(t, d.wo[l].ptr, c.hidden, d.nq * hd, d.xq, 1, d.delta, P100_QMV_PDL, s);
+        if (!st && d.tp) st = p100_tp_allreduce_sum(d.tp, d.delta, size_t(c.hidden), s);
+        if (!st) st = dec_rmsnorm(d, d.delta, d.ffn_norm[l], s);
+        if (!st) st = run_qmv(t, d.wgu[l].ptr, 2 * d.ffn, c.hidden, d.xq, 1, d.gu, P100_QMV_PDL, s);
+        if (!st)
+            st = launch_glue(dec::swiglu_q8_1_kernel, dim3((d.ffn / 32 + 7) / 8, 1), dim3(256), s,
+                             "swiglu_q8_1_kernel launch", static_cast<const float*>(d.gu), d.ffn, d.xq);
+        if (!st) st = run_qmv(t, d.wdown[l].ptr, c.hidden, d.ffn, d.xq, 1, d.delta, P100_QMV_PDL, s);
+        if (!st && d.tp) st = p100_tp_allreduce_sum(d.tp, d.delta, size_t(c.hidden), s);
+    }
+    if (!st) st = dec_rmsnorm(d, d.delta, d.out_norm, s);
+    if (!st) st = run_qmv(t, d.lm_head.ptr, d.vocab_n, c.hidden, d.xq, 1, d.logits, P100_QMV_PDL, s);
+    if (st) return st;
+    if (!d.tp) {
+        return launch_glue(dec::argmax_kernel, dim3(1), dim3(dec::kArgmaxThreads), s, "argmax_kernel launch",
+                           static_cast<const float*>(d.logits), d.vocab_n, 0, static_cast<int*>(nullptr),
+                           static_cast<float*>(nullptr), d.token, d.pos);
+    }
+    st = launch_glue(dec::argmax_pair_kernel, dim3(1), dim3(dec::kArgmaxThreads), s, "argmax_pair_kernel launch",
+                     static_cast<const float*>(d.logits), d.vocab_n, d.vocab0, d.pair);
+    if (!st) st = p100_tp_allgather(d.tp, d.pair, d.cand, 2, s);
+    if (!st)
+        st = launch_glue(dec::pick_candidates_kernel, dim3(1), dim3(32), s, "pick_candidates_kernel launch",
+                         static_cast<const float*>(d.cand), d.nranks, d.token, d.pos);
+    return st;
+}
+
+void dec_release_graph(Decoder& d) {
+    if (d.graph_exec) cudaGraphExecDestroy(d.graph_exec);
+    if (d.graph) cudaGraphDestroy(d.graph);
+    d.graph_exec = nullptr;
+    d.graph = nullptr;
+}
+
+p100_status dec_capture(Decoder& d) {
+    cudaStream_t cs = nullptr;
+    if (p100_status st = cuda_status(cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking), "capture stream"))
+        return st;
+    p100_status st = cuda_status(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal), "begin capture");
+    if (!st) {
+        const p100_status rec = dec_record_step(d, cs);
+        const std::string why = t_error;
+        cudaGraph_t g = nullptr;
+        const cudaError_t e = cudaStreamEndCapture(cs, &g);
+        if (rec) {
+            if (g) cudaGraphDestroy(g);
+            st = set_error(rec, "%s", why.c_str());
+        } else if (e != cudaSuccess) {
+            st = cuda_status(e, "end capture");
+        } else {
+            d.graph = g;
+            st = cuda_status(cudaGraphInstantiate(&d.graph_exec, g, 0), "instantiate decode graph");
+            if (st) dec_release_graph(d);
+        }
+    }
+    cudaStreamDestroy(cs);
+    return st;
+}
+
+struct DeviceGuard {
+    int prev = 0;
+    explicit DeviceGuard(int dev) { cudaGetDevice(&prev); cudaSetDevice(dev); }
+    ~DeviceGuard() { cudaSetDevice(prev); }
+};
+
+}  // namespace
+}  // namespace p100b
+
+struct p100_decoder {
+    p100b::Decoder d;
+};
+
+extern "C" {
+
+void p100_rope_table(float* out, int max_pos, int head_dim, float theta) {
+    const int half = head_dim / 2;
+    for (int p = 0; p < max_pos; ++p)
+        for (int i = 0; i < half; ++i) {
+            const double a = double(p) * std::pow(double(theta), -2.0 * i / double(head_dim));
+            out[(size_t(p) * half + i) * 2] = float(std::cos(a));
+            out[(size_t(p) * half + i) * 2 + 1] = float(std::sin(a));
+        }
+}
+
+p100_status p100_rmsnorm_q8_1(float* x, const float* delta, const float* w, float eps, int k, int batch,
+                              void* x_q8_1, float* y_out, p100_stream_t stream) {
+    clear_error();
+    if (k <= 0 || k % 32 || batch <= 0) return set_error(P100_ERR_INVALID, "k must be a positive multiple of 32");
+    if (k > dec::kNormMaxK) return set_error(P100_ERR_UNSUPPORTED, "k above %d", dec::kNormMaxK);
+    if (!x || !w || !x_q8_1) return set_error(P100_ERR_INVALID, "null buffer");
+    if (p100_status st = require_sm100(nullptr, nullptr)) return st;
+    dec::rmsnorm_q8_1_kernel<<<batch, dec::kNormThreads, 0, stream>>>(x, delta, w, eps, k,
+                                                                        static_cast<uint8_t*>(x_q8_1), y_out);
+    return launch_status("rmsnorm_q8_1_kernel launch");
+}
+
+p100_status p100_rope_kv_append(float* qkv, int n_head, int n_head_kv, int head_dim, const float* rope_cs,
+                                int max_pos, const int* pos_dev, void* k_cache, void* v_cache,
+                                long long kv_head_stride, p100_stream_t stream) {
+    clear_error();
+    if (n_head <= 0 || n_head_kv <= 0 || head_dim <= 0 || head_dim % 2 || head_dim > 2048 || max_pos <= 0)
+        return set_error(P100_ERR_INVALID, "bad RoPE shape");
+    if (kv_head_stride < static_cast<long long>(max_pos) * head_dim)
+        return set_error(P100_ERR_INVALID, "kv_head_stride must cover max_pos rows");
+    if (!qkv || !rope_cs || !pos_dev || !k_cache || !v_cache) return set_error(P100_ERR_INVALID, "null buffer");
+    if (p100_status st = require_sm100(nullptr, nullptr)) return st;
+    dec::rope_kv_append_kernel<<<n_head + 2 * n_head_kv, head_dim / 2, 0, stream>>>(
+        qkv, n_head, n_head_kv, head_dim, reinterpret_cast<const float2*>(rope_cs), max_pos, pos_dev,
+        static_cast<__half*>(k_cache), static_cast<__half*>(v_cache), kv_head_stride);
+    return launch_status("rope_kv_append_kernel launch");
+}
+
+p100_status p100_swiglu_q8_1(const float* gate_up, int n, int batch, void* x_q8_1, p100_stream_t stream) {
+    clear_error();
+    if (n <= 0 || n % 32 || batch <= 0) return set_error(P100_ERR_INVALID, "n must be a positive multiple of 32");
+    if (!gate_up || !x_q8_1) return set_error(P100_ERR_INVALID, "null buffer");
+    if (p100_status st = require_sm100(nullptr, nullptr)) return st;
+    dec::swiglu_q8_1_kernel<<<dim3((n / 32 + 7) / 8, batch), 256, 0, stream>>>(gate_up, n,
+                                                                               static_cast<uint8_t*>(x_q8_1));
+    return launch_status("swiglu_q8_1_kernel launch");
+}
+
+p100_status p100_argmax(const float* x, int n, int batch, int* idx, float* val, p100_stream_t stream) {
+    clear_error();
+    if (n <= 0 || batch <= 0) return set_error(P100_ERR_INVALID, "n and batch must be positive");
+    if (!x || !idx) return set_error(P100_ERR_INVALID, "null buffer");
+    if (p100_status st = require_sm100(nullptr, nullptr)) return st;
+    dec::argmax_kernel<<<batch, dec::kArgmaxThreads, 0, stream>>>(x, n, 0, idx, val, nullptr, nullptr);
+    return launch_status("argmax_kernel launch");
+}
+
+p100_status p100_decoder_create(const p100_llama_config* cfg, p100_tp* tp, p100_decoder** out) {
+    clear_error();
+    if (!cfg || !out) return set_error(P100_ERR_INVALID, "null argument");
+    *out = nullptr;
+    const int nranks = tp ? p100_tp_size(tp) : 1;
+    if (const char* why = config_reason(*cfg, nranks)) return set_error(P100_ERR_INVALID, "%s", why);
+    int dev = 0;
+    if (tp) {
+        dev = p100_tp_device(tp);
+    } else if (p100_status st = cuda_status(cudaGetDevice(&dev), "cudaGetDevice")) {
+        return st;
+    }
+    DeviceGuard guard(dev);
+    int sms = 0;
+    if (p100_status st = require_sm100(nullptr, &sms)) return st;
+    auto* h = new p100_decoder();
+    h->d.cfg = *cfg;
+    h->d.tp = tp;
+    h->d.rank = tp ? p100_tp_rank(tp) : 0;
+    h->d.nranks = nranks;
+    h->d.device = dev;
+    h->d.sms = sms;
+    if (p100_status st = dec_alloc(h->d)) {
+        const std::string why = t_error;
+        if (h->d.arena) cudaFree(h->d.arena);
+        delete h;
+        return set_error(st, "%s", why.c_str());
+    }
+    *out = h;
+    return P100_OK;
+}
+
+p100_status p100_decoder_init_random(p100_decoder* h, unsigned long long seed) {
+    clear_error();
+    if (!h) return set_error(P100_ERR_INVALID, "null decoder");
+    DeviceGuard guard(h->d.device);
+    return dec_init_random(h->d, seed);
+}
+
+p100_status p100_decoder_fill_kv(p100_decoder* h, int n_pos, unsigned long long seed, float scale) {
+    clear_error();
+    if (!h) return set_error(P100_ERR_INVALID, "null decoder");
+    if (n_pos < 0 || n_pos > h->d.cfg.max_ctx) return set_error(P100_ERR_INVALID, "n_pos outside [0, max_ctx]");
+    DeviceGuard guard(h->d.device);
+    return dec_fill_kv(h->d, n_pos, seed, scale);
+}
+
+p100_status p100_decoder_set_state(p100_decoder* h, int pos, int token) {
+    clear_error();
+    if (!h) return set_error(P100_ERR_INVALID, "null decoder");
+    if (pos < 0 || pos >= h->d.cfg.max_ctx) return set_error(P100_ERR_INVALID, "pos outside [0, max_ctx)");
+    if (token < 0 || token >= h->d.cfg.vocab) return set_error(P100_ERR_INVALID, "token outside [0, vocab)");
+    DeviceGuard guard(h->d.device);
+    const int v[2] = {pos, token};
+    p100_status st = cuda_status(cudaMemcpy(h->d.pos, &v[0], 4, cudaMemcpyHostToDevice), "set position");
+    if (!st) st = cuda_status(cudaMemcpy(h->d.token, &v[1], 4, cudaMemcpyHostToDevice), "set token");
+    return st;
+}
+
+p100_status p100_decoder_state(p100_decoder* h, int* pos, int* token) {
+    clear_error();
+    if (!h) return set_error(P100_ERR_INVALID, "null decoder");
+    DeviceGuard guard(h->d.device);
+    int v[2] = {0, 0};
+    p100_status st = cuda_status(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+    if (!st) st = cuda_status(cudaMemcpy(&v[0], h->d.pos, 4, cudaMemcpyDeviceToHost), "read position");
+    if (!st) st = cuda_status(cudaMemcpy(&v[1], h->d.token, 4, cudaMemcpyDeviceToHost), "read token");
+    if (pos) *pos = v[0];
+    if (token) *token = v[1];
+    return st;
+}
+
+p100_status p100_decoder_step(p100_decoder* h, int n_steps, p100_stream_t stream) {
+    clear_error();
+    if (!h) return set_error(P100_ERR_INVALID, "null decoder");
+    if (n_steps < 0) return set_error(P100_ERR_INVALID, "n_steps must be >= 0");
+    DeviceGuard guard(h->d.device);
+    if (!h->d.graph_exec)
+        if (p100_status st = dec_capture(h->d)) return st;
+    for (int i = 0; i < n_steps; ++i)
+        if (p100_status st = cuda_status(cudaGraphLaunch(h->d.graph_exec, stream), "launch decode graph")) return st;
+    return P100_OK;
+}
+
+p100_status p100_decoder_tensor(p100_decoder* h, int layer, int which, void** ptr, size_t* bytes, int* rows,
+                                int* cols) {
+    clear_error();
+    if (!h) return set_error(P100_ERR_INVALID, "null decoder");
+    p100b::Decoder& d = h->d;
+    const p100b::DecTensor* t = nullptr;
+    const bool per_layer = which == P100_T_ATTN_NORM || which == P100_T_WQKV || which == P100_T_WO ||
+                           which == P100_T_FFN_NORM || which == P100_T_WGATE_UP || which == P100_T_WDOWN;
+    if (per_layer && (layer < 0 || layer >= d.cfg.n_layer)) return set_error(P100_ERR_INVALID, "layer out of range");
+    switch (which) {
+        case P100_T_EMBED: t = &d.embed; break;
+        case P100_T_ATTN_NORM: t = &d.attn_norm[layer]; break;
+        case P100_T_WQKV: t = &d.wqkv[layer]; break;
+        case P100_T_WO: t = &d.wo[layer]; break;
+        case P100_T_FFN_NORM: t = &d.ffn_norm[layer]; break;
+        case P100_T_WGATE_UP: t = &d.wgu[layer]; break;
+        case P100_T_WDOWN: t = &d.wdown[layer]; break;
+        case P100_T_OUT_NORM: t = &d.out_norm; break;
+        case P100_T_LM_HEAD: t = &d.lm_head; break;
+        default: return set_error(P100_ERR_INVALID, "unknown tensor id %d", which);
+    }
+    if (ptr) *ptr = t->ptr;
+    if (bytes) *bytes = t->bytes;
+    if (rows) *rows = t->rows;
+    if (cols) *cols = t->cols;
+    return P100_OK;
+}
+
+p100_status p100_decoder_buffer(p100_decoder* h, int which, void** ptr, size_t* bytes) {
+    clear_error();
+    if (!h) return set_error(P100_ERR_INVALID, "null decoder");
+    p100b::Decoder& d = h->d;
+    const size_t kv = size_t(d.cfg.n_layer) * d.nkv * d.cfg.max_ctx * d.cfg.head_dim * 2;
+    void* p = nullptr;
+    size_t n = 0;
+    switch (which) {
+        case P100_B_HIDDEN: p = d.x; n = size_t(d.cfg.hidden) * 4; break;
+        case P100_B_LOGITS: p = d.logits; n = size_t(d.vocab_n) * 4; break;
+        case P100_B_KCACHE: p = d.kcache; n = kv; break;
+        case P100_B_VCACHE: p = d.vcache; n = kv; break;
+        case P100_B_ROPE: p = d.rope; n = size_t(d.cfg.max_ctx) * d.cfg.head_dim * 4; break;
+        default: return set_error(P100_ERR_INVALID, "unknown buffer id %d", which);
+    }
+    if (ptr) *ptr = p;
+    if (bytes) *bytes = n;
+    return P100_OK;
+}
+
+int p100_decoder_vocab_offset(const p100_decoder* h) { return h ? h->d.vocab0 : 0; }
+size_t p100_decoder_weight_bytes_per_token(const p100_decoder* h) {
+    if (!h) return 0;
+    const p100b::Decoder& d = h->d;
+    size_t n = d.lm_head.bytes;
+    for (int l = 0; l < d.cfg.n_layer; ++l) n += d.wqkv[l].bytes + d.wo[l].bytes + d.wgu[l].bytes + d.wdown[l].bytes;
+    return n;
+}
+
+p100_status p100_decoder_destroy(p100_decoder* h) {
+    clear_error();
+    if (!h) return P100_OK;
+    DeviceGuard guard(h->d.device);
+    p100b::dec_release_graph(h->d);
+    p100_status st = P100_OK;
+    if (h->d.arena) st = cuda_status(cudaFree(h->d.arena), "cudaFree(decoder)");
+    delete h;
+    return st;
+}
+
+}  // extern "C"

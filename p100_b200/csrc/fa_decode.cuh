@@ -39,6 +39,12 @@ struct Params {
     int nkv, G, seq, parts, nstage;
     long long head_stride, batch_stride;   // elements
     float scale, softcap;
+    // Decode chain: keys are [0, *len_dev + len_add) clamped to [0, seq], read
+    // after the wait for the previous kernel (which may have appended the
+    // newest row); the K/V stream then starts after that wait too.  Null:
+    // seq keys, streamed before the wait.
+    const int* len_dev;
+    int len_add;
 };
 
 __device__ __forceinline__ void half8_to_float(const uint4 v, float (&f)[8]) {
@@ -49,6 +55,61 @@ __device__ __forceinline__ void half8_to_float(const uint4 v, float (&f)[8]) {
         f[2 * i] = t.x;
         f[2 * i + 1] = t.y;
     }
+}
+
+// Last CTA of kv head bk: merges the parts' partials {m, l, unnormalised O}
+// into o (and lse) with the rebased combine of attention_tiled_model.cpp:
+// 183-222: M = max m_p, den = sum_p exp(m_p - M) l_p, o = sum_p exp(m_p - M)
+// O_p / den over parts in order (parts with l = 0 skipped).  All (m, l) are
+// loaded at once and the weights kept in shared memory (scratch: at least
+// 2 * parts * G + 2 * G floats), so the only loop over parts with global
+// loads is the last, unrolled so its loads are in flight together.
+template <int THREADS>
+__device__ __forceinline__ void merge_parts(const Params& p, int bk, int G, int D, size_t row0, float* scratch) {
+    const int tid = threadIdx.x;
+    const int np = p.parts;
+    const float* all_o = p.ws_o + size_t(bk) * np * G * D;
+    const float* all_ml = p.ws_ml + size_t(bk) * np * G * 2;
+    float* s_pm = scratch;            // [parts][G] m, then the weights
+    float* s_pl = s_pm + np * G;      // [parts][G] l
+    float* s_gm = s_pl + np * G;      // [G]
+    float* s_den = s_gm + G;          // [G]
+    for (int i = tid; i < np * G; i += THREADS) {
+        s_pm[i] = __ldcg(all_ml + 2 * i);
+        s_pl[i] = __ldcg(all_ml + 2 * i + 1);
+    }
+    __syncthreads();
+    if (tid < G) {
+        float gmax = -INFINITY;
+        for (int q = 0; q < np; ++q) gmax = fmaxf(gmax, s_pm[q * G + tid]);
+        float den = 0.f;
+        for (int q = 0; q < np; ++q) {
+            const float l = s_pl[q * G + tid];
+            den += l == 0.f ? 0.f : expf(s_pm[q * G + tid] - gmax) * l;
+        }
+        s_gm[tid] = gmax;
+        s_den[tid] = den;
+        if (p.lse) p.lse[row0 + tid] = den == 0.f ? -INFINITY : gmax + logf(den);
+    }
+    __syncthreads();
+    for (int i = tid; i < np * G; i += THREADS) {   // weights replace m
+        const int h = i % G;
+        s_pm[i] = s_pl[i] == 0.f ? 0.f : expf(s_pm[i] - s_gm[h]);
+    }
+    __syncthreads();
+    for (int i = tid; i < G * D; i += THREADS) {
+        const int h = i / D;
+        float num = 0.f;
+#pragma unroll 8
+        for (int q = 0; q < np; ++q) {
+            const float w = s_pm[q * G + h];
+            const float v = __ldcg(all_o + size_t(q) * G * D + i);
+            if (s_pl[q * G + h] != 0.f) num = fmaf(w, v, num);
+        }
+        const float den = s_den[h];
+        p.o[(row0 + h) * D + (i % D)] = den == 0.f ? 0.f : num / den;
+    }
+    if (tid == 0) p.tickets[bk] = 0;   // ready for the next call
 }
 
 template <int D, int GMAX>
@@ -81,8 +142,13 @@ __global__ void __launch_bounds__(kThreads, 1) fa_decode_kernel(const Params p) 
     const int bk = blockIdx.y, part = blockIdx.x;
     const int b = bk / p.nkv, kvh = bk % p.nkv;
     const int G = p.G;
-    const int key0 = static_cast<int>(static_cast<long long>(p.seq) * part / p.parts);
-    const int key1 = static_cast<int>(static_cast<long long>(p.seq) * (part + 1) / p.parts);
+    int seq = p.seq;
+    if (p.len_dev) {
+        pdl_wait_prior_grid();
+        seq = min(max(*p.len_dev + p.len_add, 0), p.seq);
+    }
+    const int key0 = static_cast<int>(static_cast<long long>(seq) * part / p.parts);
+    const int key1 = static_cast<int>(static_cast<long long>(seq) * (part + 1) / p.parts);
     const int ntiles = (key1 - key0 + kTile - 1) / kTile;
     const __half* kbase = p.k + b * p.batch_stride + kvh * p.head_stride;
     const __half* vbase = p.v + b * p.batch_stride + kvh * p.head_stride;
@@ -302,34 +368,8 @@ __global__ void __launch_bounds__(kThreads, 1) fa_decode_kernel(const Params p) 
     if (!s_flag[0]) return;
     __threadfence();
 
-    // Last CTA of this kv head: merge the parts.
-    const float* all_o = p.ws_o + size_t(bk) * p.parts * G * D;
-    const float* all_ml = p.ws_ml + size_t(bk) * p.parts * G * 2;
-    if (tid < G) {
-        float gmax = neg_inf;
-        for (int q = 0; q < p.parts; ++q) gmax = fmaxf(gmax, __ldcg(all_ml + (q * G + tid) * 2));
-        float den = 0.f;
-        for (int q = 0; q < p.parts; ++q) {
-            const float m = __ldcg(all_ml + (q * G + tid) * 2), l = __ldcg(all_ml + (q * G + tid) * 2 + 1);
-            den += l == 0.f ? 0.f : expf(m - gmax) * l;
-        }
-        s_m[tid] = gmax;
-        s_l[tid] = den;
-        if (p.lse) p.lse[row0 + tid] = den == 0.f ? neg_inf : gmax + logf(den);
-    }
-    __syncthreads();
-    for (int i = tid; i < G * D; i += kThreads) {
-        const int h = i / D;
-        const float gmax = s_m[h], den = s_l[h];
-        float num = 0.f;
-        for (int q = 0; q < p.parts; ++q) {
-            const float m = __ldcg(all_ml + (q * G + h) * 2), l = __ldcg(all_ml + (q * G + h) * 2 + 1);
-            if (l == 0.f) continue;
-            num = fmaf(expf(m - gmax), __ldcg(all_o + size_t(q) * G * D + i), num);
-        }
-        p.o[(row0 + h) * D + (i % D)] = den == 0.f ? 0.f : num / den;
-    }
-    if (tid == 0) p.tickets[bk] = 0;   // ready for the next call
+    // Last CTA of this kv head: merge the parts (the ring is idle).
+    merge_parts<kThreads>(p, bk, G, D, row0, reinterpret_cast<float*>(ring));
 }
 
 }  // namespace fa

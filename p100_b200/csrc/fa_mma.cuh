@@ -1,0 +1,356 @@
+// fa_mma.cuh — FlashAttention-vec decode with the dot products on the tensor
+// cores (mma.sync m16n8k16, f16 inputs, f32 accumulation) at FP32-level
+// accuracy.
+//
+// Decode attention is HBM-bound: the math is G query heads x D per key, and a
+// SIMT kernel spends most of its instructions on shuffles, conversions and
+// barriers around it.  Here each warp owns 16 keys of every 64-key tile and
+// runs its own online softmax over them (no barrier inside a tile):
+//   S = Q K^T   A = the query rows, B = K via ldmatrix from the stage;
+//   O += P V    A = P straight from S's accumulator fragments (two 8-key
+//               n-tiles make one 16-key k-step), B = V via ldmatrix.trans.
+// Accuracy: the operands must be f16, so Q and P are split in two,
+// x = hi + lo with hi = f16(x), lo = f16(x - hi): rows 0..G-1 of A carry hi,
+// rows G..2G-1 carry lo, and the f32 accumulators add the halves back
+// (K and V are f16 already, so S and O keep ~22 significant bits).  Q is
+// scaled per head by a power of two so its largest entry sits near 2^13
+// (no f16 overflow, lo well above the subnormals); S is scaled back exactly.
+//
+// K/V tiles are copied with 16-byte cp.async into rows padded to D + 8
+// halves, so the eight 16-byte rows an ldmatrix reads fall on distinct banks;
+// rows past the part's last key are zero-filled (a masked key's V then adds
+// exactly 0).  Split-K parts and the last-CTA combine are those of
+// fa_decode.cuh (fa::Params, partials {m, l, unnormalised O}).
+#pragma once
+#include "fa_decode.cuh"
+
+namespace p100b {
+namespace fam {
+
+constexpr int kWarps = 4;
+constexpr int kThreads = kWarps * 32;
+constexpr int kTile = 64;   // keys per tile: 16 per warp
+
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
+    return uint32_t(__half_as_ushort(__float2half_rn(lo))) | (uint32_t(__half_as_ushort(__float2half_rn(hi))) << 16);
+}
+// f16 residual of x: f16(x - f16(x))
+__device__ __forceinline__ float half_rest(float x) { return x - __half2float(__float2half_rn(x)); }
+
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], uint32_t addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+// 16 bytes global -> shared; src_bytes 0 writes zeros (src is not read).
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, int src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+template <int D>
+__host__ __device__ constexpr int stages() { return D >= 256 ? 2 : 4; }
+template <int D, int G>
+__host__ __device__ constexpr size_t smem_bytes() {
+    return size_t(stages<D>()) * 2 * kTile * (D + 8) * 2 + size_t(G) * D * 4 + 256;
+}
+
+// Grid (parts, batch * n_kv); G = query heads per kv head (1, 2, 4 or 8);
+// D = 64 or 128.
+template <int D, int G>
+__global__ void __launch_bounds__(kThreads, 1) fa_mma_kernel(const fa::Params p) {
+    static_assert(G == 1 || G == 2 || G == 4 || G == 8, "G");
+    constexpr int RS = D + 8;        // padded row stride (halves)
+    constexpr int NS = stages<D>();
+    constexpr int KSQ = D / 16;      // k-steps of Q K^T
+    constexpr int NTV = D / 8;       // n-tiles of P V
+    constexpr int CHUNKS = kTile * D / 8;   // 16-byte chunks per K (or V) tile
+    extern __shared__ __align__(128) uint8_t smem[];
+    __half* ring = reinterpret_cast<__half*>(smem);                     // [NS][K|V][kTile][RS]
+    float* s_q = reinterpret_cast<float*>(smem + size_t(NS) * 2 * kTile * RS * 2);   // [G][D]
+    float* s_qs = s_q + G * D;                                          // [8] per-head power-of-two scale
+    unsigned* s_flag = reinterpret_cast<unsigned*>(s_qs + 8);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int g = lane >> 2, t = lane & 3;
+    const int bk = blockIdx.y, part = blockIdx.x;
+    const int b = bk / p.nkv, kvh = bk % p.nkv;
+    int seq = p.seq;
+    if (p.len_dev) {
+        pdl_wait_prior_grid();
+        seq = min(max(*p.len_dev + p.len_add, 0), p.seq);
+    }
+    const int key0 = static_cast<int>(static_cast<long long>(seq) * part / p.parts);
+    const int key1 = static_cast<int>(static_cast<long long>(seq) * (part + 1) / p.parts);
+    const int ntiles = (key1 - key0 + kTile - 1) / kTile;
+    const __half* kbase = p.k + b * p.batch_stride + kvh * p.head_stride;
+    const __half* vbase = p.v + b * p.batch_stride + kvh * p.head_stride;
+    const uint32_t ring_addr = smem_addr(ring);
+
+    auto issue = [&](int tile) {
+        if (tile < ntiles) {
+            const int j0 = key0 + tile * kTile;
+            const int n = min(kTile, key1 - j0);
+            const uint32_t kdst = ring_addr + uint32_t((tile % NS) * 2 * kTile * RS * 2);
+            const uint32_t vdst = kdst + uint32_t(kTile * RS * 2);
+#pragma unroll
+            for (int i = 0; i < CHUNKS / kThreads; ++i) {
+                const int c = tid + i * kThreads;
+                const int r = c / (D / 8), col = c % (D / 8);
+                const bool valid = r < n;
+                const size_t src = size_t(j0 + (valid ? r : 0)) * D + col * 8;
+                const uint32_t off = uint32_t((r * RS + col * 8) * 2);
+                cp_async16(kdst + off, kbase + src, valid ? 16 : 0);
+                cp_async16(vdst + off, vbase + src, valid ? 16 : 0);
+            }
+        }
+        cp_async_commit();   // one group per tile slot, empty past the end
+    };
+
+    if (!p.len_dev)
+        for (int s = 0; s < NS - 1; ++s) issue(s);   // K/V never come from the previous kernel here
+    pdl_allow_dependents();
+    pdl_wait_prior_grid();
+    if (p.len_dev)
+        for (int s = 0; s < NS - 1; ++s) issue(s);
+
+    // ---- queries: q * scale per head, scaled by a power of two 2^e so the
+    // largest |entry| lies in [2^13, 2^14)
+    const float* qg = p.q + (size_t(b) * p.nkv * G + size_t(kvh) * G) * D;
+    for (int i = tid; i < G * D; i += kThreads) s_q[i] = qg[i] * p.scale;
+    __syncthreads();
+    for (int h = warp; h < G; h += kWarps) {
+        float m = 0.f;
+        for (int d = lane; d < D; d += 32) m = fmaxf(m, fabsf(s_q[h * D + d]));
+        m = warp_max(m);
+        if (lane == 0) {
+            int e = 0;   // clamped so 2^e and 2^-e stay normal floats
+            if (m > 0.f && m < INFINITY) e = max(-120, min(120, 13 - ilogbf(m)));
+            s_qs[h] = ldexpf(1.0f, e);
+        }
+    }
+    __syncthreads();
+    // A fragments: row r < G -> hi of head r, G <= r < 2G -> lo of head r - G
+    uint32_t qa[KSQ][4];
+    {
+        auto qv = [&](int r, int d) -> float {
+            if (r < G) return __half2float(__float2half_rn(s_q[r * D + d] * s_qs[r]));
+            if (r < 2 * G) return half_rest(s_q[(r - G) * D + d] * s_qs[r - G]);
+            return 0.f;
+        };
+#pragma unroll
+        for (int ks = 0; ks < KSQ; ++ks) {
+            const int d0 = ks * 16 + 2 * t;
+            qa[ks][0] = pack_half2(qv(g, d0), qv(g, d0 + 1));
+            qa[ks][1] = pack_half2(qv(g + 8, d0), qv(g + 8, d0 + 1));
+            qa[ks][2] = pack_half2(qv(g, d0 + 8), qv(g, d0 + 9));
+            qa[ks][3] = pack_half2(qv(g + 8, d0 + 8), qv(g + 8, d0 + 9));
+        }
+    }
+    // this lane's head (rows g and, for G = 8, g + 8 belong to head g mod G)
+    const int hh = g % G;
+    const bool row_live = g < 2 * G;
+    const float unscale = 1.0f / s_qs[hh];   // exact: a power of two
+
+    float o[NTV][4];
+#pragma unroll
+    for (int n = 0; n < NTV; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+    float m_run = -INFINITY, l_run = 0.f;
+
+    for (int tile = 0; tile < ntiles; ++tile) {
+        cp_async_wait<NS - 2>();
+        __syncthreads();   // tile's copies visible to all; the slot refilled next is no longer read
+        issue(tile + NS - 1);
+        const uint32_t kst = ring_addr + uint32_t((tile % NS) * 2 * kTile * RS * 2);
+        const uint32_t vst = kst + uint32_t(kTile * RS * 2);
+        const int j0 = key0 + tile * kTile;
+        const int n = min(kTile, key1 - j0);
+
+        // ---- S = Q K^T over this warp's 16 keys (two n-tiles of 8)
+        float s[2][4];
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+            s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+            const int krow = warp * 16 + nt * 8 + (lane & 7);
+#pragma unroll
+            for (int ks = 0; ks < KSQ; ks += 2) {
+                uint32_t r[4];
+                ldsm_x4(r, kst + uint32_t((krow * RS + ks * 16 + (lane >> 3) * 8) * 2));
+                mma16816(s[nt], qa[ks], r[0], r[1]);
+                mma16816(s[nt], qa[ks + 1], r[2], r[3]);
+            }
+        }
+        // hi + lo rows -> the head's scores for keys (nt, 2t + e)
+        float x[2][2];
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                float v;
+                if (G == 8) {
+                    v = s[nt][e] + s[nt][2 + e];
+                } else {
+                    v = s[nt][e] + __shfl_xor_sync(0xffffffffu, s[nt][e], 4 * G);
+                }
+                v *= unscale;
+                if (p.softcap > 0.f) v = p.softcap * tanhf(v / p.softcap);
+                const int kt = warp * 16 + nt * 8 + 2 * t + e;
+                if (kt < n && p.mask) v += p.mask[j0 + kt];
+                x[nt][e] = (kt < n && row_live) ? v : -INFINITY;
+            }
+        // ---- online softmax of this warp's keys, per head row
+        float tmax = fmaxf(fmaxf(x[0][0], x[0][1]), fmaxf(x[1][0], x[1][1]));
+        tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 1));
+        tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 2));
+        const float m_new = fmaxf(m_run, tmax);
+        // m_new is shared by the four lanes of a row, but rows differ (unused
+        // rows never see a key): the shuffles below run in every lane and only
+        // rows with a visible key update m, l and O.
+        const bool seen = m_new != -INFINITY;
+        float alpha = 1.f, pr[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+        if (seen) {
+            alpha = m_run == -INFINITY ? 0.f : expf(m_run - m_new);
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                for (int e = 0; e < 2; ++e) pr[nt][e] = expf(x[nt][e] - m_new);
+        }
+        float ps = (pr[0][0] + pr[0][1]) + (pr[1][0] + pr[1][1]);
+        ps += __shfl_xor_sync(0xffffffffu, ps, 1);
+        ps += __shfl_xor_sync(0xffffffffu, ps, 2);
+        if (seen) {
+            l_run = l_run * alpha + ps;
+            m_run = m_new;
+        }
+        // ---- P as the A operand: rows < G hi, G..2G-1 lo (G = 8: row g+8 lo)
+        uint32_t pa[4];
+        if (G == 8) {
+            pa[0] = pack_half2(pr[0][0], pr[0][1]);
+            pa[1] = pack_half2(half_rest(pr[0][0]), half_rest(pr[0][1]));
+            pa[2] = pack_half2(pr[1][0], pr[1][1]);
+            pa[3] = pack_half2(half_rest(pr[1][0]), half_rest(pr[1][1]));
+        } else {
+            const bool lo = g >= G;
+            pa[0] = !row_live ? 0u : lo ? pack_half2(half_rest(pr[0][0]), half_rest(pr[0][1]))
+                                        : pack_half2(pr[0][0], pr[0][1]);
+            pa[2] = !row_live ? 0u : lo ? pack_half2(half_rest(pr[1][0]), half_rest(pr[1][1]))
+                                        : pack_half2(pr[1][0], pr[1][1]);
+            pa[1] = pa[3] = 0u;
+        }
+        // ---- O = O * alpha + P V
+#pragma unroll
+        for (int nv = 0; nv < NTV; ++nv) {
+            o[nv][0] *= alpha;
+            o[nv][1] *= alpha;
+            o[nv][2] *= alpha;
+            o[nv][3] *= alpha;
+        }
+#pragma unroll
+        for (int n2 = 0; n2 < NTV / 2; ++n2) {
+            uint32_t r[4];
+            const int m = lane >> 3;
+            const int vrow = warp * 16 + (lane & 7) + 8 * (m & 1);
+            ldsm_x4_trans(r, vst + uint32_t((vrow * RS + n2 * 16 + 8 * (m >> 1)) * 2));
+            mma16816(o[2 * n2], pa, r[0], r[1]);
+            mma16816(o[2 * n2 + 1], pa, r[2], r[3]);
+        }
+    }
+    cp_async_wait<0>();
+    __syncthreads();   // every copy landed and every warp is done with the ring
+
+    // ---- hi + lo rows of O; then merge the four warps through shared memory
+    float* s_wm = reinterpret_cast<float*>(smem);          // [kWarps][8]
+    float* s_wl = s_wm + kWarps * 8;                        // [kWarps][8]
+    float* s_wo = s_wl + kWarps * 8;                        // [kWarps][G][D]
+#pragma unroll
+    for (int nv = 0; nv < NTV; ++nv)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            float v;
+            if (G == 8) {
+                v = o[nv][e] + o[nv][2 + e];
+            } else {
+                v = o[nv][e] + __shfl_xor_sync(0xffffffffu, o[nv][e], 4 * G);
+            }
+            if (g < G) s_wo[(warp * G + g) * D + nv * 8 + 2 * t + e] = v;
+        }
+    if (g < G && t == 0) {
+        s_wm[warp * 8 + g] = m_run;
+        s_wl[warp * 8 + g] = l_run;
+    }
+    __syncthreads();
+    float* s_m = s_wo + kWarps * G * D;   // [G]
+    float* s_l = s_m + 8;                 // [G]
+    if (tid < G) {
+        float m = -INFINITY;
+        for (int w = 0; w < kWarps; ++w) m = fmaxf(m, s_wm[w * 8 + tid]);
+        float l = 0.f;
+        for (int w = 0; w < kWarps; ++w) {
+            const float lw = s_wl[w * 8 + tid];
+            if (lw != 0.f) l = fmaf(expf(s_wm[w * 8 + tid] - m), lw, l);
+        }
+        s_m[tid] = m;
+        s_l[tid] = l;
+    }
+    __syncthreads();
+    float* red = s_l + 8;   // [G][D] the CTA's unnormalised O
+    for (int i = tid; i < G * D; i += kThreads) {
+        const int h = i / D;
+        const float m = s_m[h];
+        float acc = 0.f;
+        for (int w = 0; w < kWarps; ++w)
+            if (s_wl[w * 8 + h] != 0.f) acc = fmaf(expf(s_wm[w * 8 + h] - m), s_wo[(w * G + h) * D + (i % D)], acc);
+        red[i] = acc;
+    }
+    __syncthreads();
+
+    const size_t row0 = size_t(b) * p.nkv * G + size_t(kvh) * G;   // first query head row
+    if (p.parts == 1) {
+        for (int i = tid; i < G * D; i += kThreads) {
+            const int h = i / D, d = i % D;
+            const float l = s_l[h];
+            p.o[(row0 + h) * D + d] = l == 0.f ? 0.f : red[i] / l;
+            if (d == 0 && p.lse) p.lse[row0 + h] = l == 0.f ? -INFINITY : s_m[h] + logf(l);
+        }
+        return;
+    }
+    float* my_o = p.ws_o + (size_t(bk) * p.parts + part) * G * D;
+    float* my_ml = p.ws_ml + (size_t(bk) * p.parts + part) * G * 2;
+    for (int i = tid; i < G * D; i += kThreads) my_o[i] = red[i];
+    if (tid < G) {
+        my_ml[2 * tid] = s_m[tid];
+        my_ml[2 * tid + 1] = s_l[tid];
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        const unsigned ticket = atomicAdd(&p.tickets[bk], 1u);
+        s_flag[0] = ticket == static_cast<unsigned>(p.parts - 1);
+    }
+    __syncthreads();
+    if (!s_flag[0]) return;
+    __threadfence();
+
+    // Last CTA of this kv head: merge the parts (scratch past the CTA's own
+    // partial sums in shared memory).
+    fa::merge_parts<kThreads>(p, bk, G, D, row0, red + G * D);
+}
+
+}  // namespace fam
+}  // namespace p100b

@@ -7,30 +7,37 @@
 
 namespace p100b {
 
-// One warp per 32-value block; 8 blocks per 256-thread CTA; blockIdx.y = row.
-// Mirrors prepare() (qmv_model.cpp:53-71) and llama.cpp quantize.cu:88-110:
+// Q8_1 block of the 32 values a warp holds, one per lane (lane i = element
+// i), written to the 36 bytes at blk.  Mirrors prepare() (qmv_model.cpp:53-71)
+// and llama.cpp quantize.cu:88-110:
 //   amax = max|x|, d = amax/127 (IEEE division), q = round-half-away(x/d),
 //   sum  = XOR-butterfly (16,8,4,2,1) FP32 sum of the original x,
 //   block = {fp16(d), fp16(sum), int8 q[32]}.
 // No fast-math anywhere in this library: x/d and amax/127 stay IEEE.
-__global__ void __launch_bounds__(256) q8_1_quantize_kernel(const float* __restrict__ x,
-                                                            uint8_t* __restrict__ out, int k, int blocks) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int b = blockIdx.x * 8 + warp;
-    if (b >= blocks) return;
-    const size_t row = blockIdx.y;
-    const float v = x[row * size_t(k) + size_t(b) * 32 + lane];
+__device__ __forceinline__ void warp_q8_1_block(float v, int lane, uint8_t* blk) {
     const float amax = warp_max(fabsf(v));
     const float d = amax / 127.0f;
     const int q = amax == 0.0f ? 0 : static_cast<int>(roundf(v / d));
     const float sum = warp_sum(v);
-    uint8_t* blk = out + (row * blocks + b) * 36;
     if (lane == 0) {
         const uint32_t ds = uint32_t(__half_as_ushort(__float2half_rn(d))) |
                             (uint32_t(__half_as_ushort(__float2half_rn(sum))) << 16);
         *reinterpret_cast<uint32_t*>(blk) = ds;
     }
     blk[4 + lane] = static_cast<uint8_t>(static_cast<int8_t>(q));
+}
+
+// One warp per 32-value block; 8 blocks per 256-thread CTA; blockIdx.y = row.
+__global__ void __launch_bounds__(256) q8_1_quantize_kernel(const float* __restrict__ x,
+                                                            uint8_t* __restrict__ out, int k, int blocks) {
+    pdl_allow_dependents();
+    pdl_wait_prior_grid();   // x may come from the previous kernel
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int b = blockIdx.x * 8 + warp;
+    if (b >= blocks) return;
+    const size_t row = blockIdx.y;
+    const float v = x[row * size_t(k) + size_t(b) * 32 + lane];
+    warp_q8_1_block(v, lane, out + (row * blocks + b) * 36);
 }
 
 // Six-bit scale and min of Q4_K sub-block j from the 12 packed bytes
@@ -54,15 +61,13 @@ __device__ __forceinline__ float load_half_bytes(const uint8_t* p) {
 // exact value rounded once to FP32, as float(double(...)) is in the model: the
 // products are exact in FP32 and the double difference is exact for any fp16
 // d/dmin, so a single fused rounding gives the same bits.
+// The 32 values of slab j (a Q4_0/Q8_0 block, or one Q4_K sub-block) of a
+// weight row: Q4_0 d*(nib-8), Q8_0 d*q, Q4_K fma(d*sc, q, -(dmin*mn)).  Each
+// is the exact value rounded once to FP32, as float(double(...)) is in the
+// model: the products are exact in FP32 and the double difference is exact
+// for any fp16 d/dmin, so a single fused rounding gives the same bits.
 template <int TYPE>
-__global__ void __launch_bounds__(256) dequantize_kernel(const uint8_t* __restrict__ w, float* __restrict__ out,
-                                                         int rows, int k, size_t row_bytes) {
-    const int slabs = k / 32;
-    const long long id = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (id >= static_cast<long long>(rows) * slabs) return;
-    const int r = static_cast<int>(id / slabs), j = static_cast<int>(id % slabs);
-    const uint8_t* row = w + r * row_bytes;
-    float vals[32];
+__device__ __forceinline__ void dequant_slab(const uint8_t* __restrict__ row, int j, float (&vals)[32]) {
     if (TYPE == P100_Q4_0) {
         const uint8_t* blk = row + size_t(j) * 18;
         const float d = load_half_bytes(blk);
@@ -89,6 +94,18 @@ __global__ void __launch_bounds__(256) dequantize_kernel(const uint8_t* __restri
 #pragma unroll
         for (int i = 0; i < 32; ++i) vals[i] = fmaf(ds, float((qs[i] >> shift) & 15), -ms);
     }
+}
+
+// One thread per 32-value slab.
+template <int TYPE>
+__global__ void __launch_bounds__(256) dequantize_kernel(const uint8_t* __restrict__ w, float* __restrict__ out,
+                                                         int rows, int k, size_t row_bytes) {
+    const int slabs = k / 32;
+    const long long id = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (id >= static_cast<long long>(rows) * slabs) return;
+    const int r = static_cast<int>(id / slabs), j = static_cast<int>(id % slabs);
+    float vals[32];
+    dequant_slab<TYPE>(w + r * row_bytes, j, vals);
     float4* dst = reinterpret_cast<float4*>(out + size_t(r) * k + size_t(j) * 32);
 #pragma unroll
     for (int i = 0; i < 8; ++i) dst[i] = make_float4(vals[4 * i], vals[4 * i + 1], vals[4 * i + 2], vals[4 * i + 3]);

@@ -1,0 +1,186 @@
+"""Decode-step glue kernels and the batch-1 decoder on B200, through the C-ABI,
+against the CPU restatement (oracle/decode_oracle.cpp).
+
+Glue kernels are bit-exact: RMSNorm+Q8_1, RoPE+KV append, SwiGLU+Q8_1 and
+argmax repeat the restatement's floating-point operations in the same order.
+The whole decoder is compared step by step with the restated step on a tiny
+model (weights and KV cache read back from the device, teacher-forced from
+the device cache every step): the restatement's mat-vecs accumulate
+sequentially and its attention is FP64, so the residual stream and logits
+agree within the bounds below and the tokens agree where the top two logits
+are further apart than the logit error."""
+import numpy as np
+import pytest
+
+import oracle
+import p100_b200 as P
+
+pytestmark = pytest.mark.gpu
+
+# Bounds per step, relative to the largest magnitude of the restated value.
+# Both sides agree to ~1e-7 until a value lands within ~1e-7 of a Q8_1
+# rounding boundary: the two summation orders then round one code apart,
+# which moves the residual stream by ~1e-5 and the logits by up to ~3e-3 of
+# their range on this model (measured).  A wiring error (wrong layer, head,
+# position or cache row) moves them by 1e-1 or more.
+DECODE_HIDDEN_TOL = 1e-4
+DECODE_LOGIT_TOL = 1e-2
+
+
+def dev(torch, a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+@pytest.mark.parametrize("k,batch,with_delta", [(4096, 1, True), (8192, 2, True), (256, 3, False), (14336, 1, False),
+                                              (4128, 1, True)])
+def test_rmsnorm_q8_1_bit_exact(cuda, orc, k, batch, with_delta):
+    rng = np.random.default_rng(k + batch)
+    x = rng.standard_normal((batch, k)).astype(np.float32)
+    delta = (0.3 * rng.standard_normal((batch, k))).astype(np.float32) if with_delta else None
+    w = rng.uniform(0.9, 1.1, k).astype(np.float32)
+    xd = dev(cuda, x)
+    y = cuda.empty(batch, k, device="cuda")
+    q = P.rmsnorm_q8_1(xd, dev(cuda, w), 1e-5, delta=dev(cuda, delta) if with_delta else None, y_out=y)
+    got_q = q.cpu().numpy().reshape(batch, -1)
+    for b in range(batch):
+        xs, oq, oy = orc.rmsnorm_q8_1(x[b], w, 1e-5, delta=None if delta is None else delta[b])
+        assert np.array_equal(xd[b].cpu().numpy(), xs)
+        assert np.array_equal(y[b].cpu().numpy().view(np.uint32), oy.view(np.uint32))
+        assert np.array_equal(got_q[b], oq)
+
+
+@pytest.mark.parametrize("pos", [0, 1, 4095])
+def test_rope_kv_append_bit_exact(cuda, orc, pos):
+    nq, nkv, hd, max_pos = 32, 8, 128, 4096
+    stride = max_pos * hd
+    rng = np.random.default_rng(pos)
+    qkv = rng.standard_normal((nq + 2 * nkv) * hd).astype(np.float32)
+    cs = P.rope_table(max_pos, hd, 500000.0)
+    kc = cuda.zeros(nkv * stride, dtype=cuda.float16, device="cuda")
+    vc = cuda.zeros(nkv * stride, dtype=cuda.float16, device="cuda")
+    qd = dev(cuda, qkv)
+    P.rope_kv_append(qd, nq, nkv, hd, dev(cuda, cs), max_pos, cuda.tensor([pos], dtype=cuda.int32, device="cuda"),
+                     kc, vc, stride)
+    hk = np.zeros(nkv * stride, dtype=np.uint16)
+    hv = np.zeros(nkv * stride, dtype=np.uint16)
+    want = orc.rope_kv_append(qkv, nq, nkv, hd, cs, max_pos, pos, hk, hv, stride)
+    assert np.array_equal(qd.cpu().numpy()[:nq * hd].view(np.uint32), want[:nq * hd].view(np.uint32))
+    assert np.array_equal(kc.cpu().numpy().view(np.uint16), hk)
+    assert np.array_equal(vc.cpu().numpy().view(np.uint16), hv)
+
+
+def test_rope_position_out_of_range_sets_flag(cuda):
+    nq, nkv, hd, max_pos = 4, 2, 64, 16
+    qkv = cuda.ones((nq + 2 * nkv) * hd, device="cuda")
+    kc = cuda.zeros(nkv * max_pos * hd, dtype=cuda.float16, device="cuda")
+    vc = cuda.zeros_like(kc)
+    cs = dev(cuda, P.rope_table(max_pos, hd, 10000.0))
+    assert P.device_error(clear=True) == P.OK
+    P.rope_kv_append(qkv, nq, nkv, hd, cs, max_pos, cuda.tensor([max_pos], dtype=cuda.int32, device="cuda"), kc, vc,
+                     max_pos * hd)
+    assert P.device_error(clear=True) == P.ERR_INVALID
+    assert cuda.count_nonzero(kc).item() == 0 and cuda.count_nonzero(vc).item() == 0
+    assert P.device_error(clear=True) == P.OK
+
+
+@pytest.mark.parametrize("n,batch", [(14336, 1), (1792, 2), (32, 1)])
+def test_swiglu_q8_1_bit_exact(cuda, orc, n, batch):
+    rng = np.random.default_rng(n)
+    gu = (3 * rng.standard_normal((batch, 2 * n))).astype(np.float32)
+    gu[0, :6] = [0.0, -90.0, 95.0, -20.0, 1e-30, -1e-30]
+    got = P.swiglu_q8_1(dev(cuda, gu), n).cpu().numpy().reshape(batch, -1)
+    for b in range(batch):
+        assert np.array_equal(got[b], orc.swiglu_q8_1(gu[b], n))
+
+
+def test_argmax_matches(cuda, orc):
+    rng = np.random.default_rng(9)
+    x = rng.standard_normal((3, 128256)).astype(np.float32)
+    x[1, 1000] = x[1, 77] = 50.0            # tie: the lower index wins
+    x[2, :] = np.nan
+    x[2, 99999] = -3.0                      # NaN never wins
+    idx, val = P.argmax(dev(cuda, x))
+    idx, val = idx.cpu().numpy(), val.cpu().numpy()
+    for b in range(3):
+        oi, ov = orc.argmax(x[b])
+        assert idx[b] == oi and val[b] == np.float32(ov)
+    assert idx[1] == 77
+
+
+TINY = dict(n_layer=2, hidden=256, n_head=4, n_head_kv=2, head_dim=64, ffn=512, vocab=300, max_ctx=512)
+
+
+def read_model(dec, cfg):
+    """Host copies of the decoder's weights in the restatement's layout."""
+    def t(which, layer=0, dtype=np.uint8):
+        ptr, nbytes, _, _ = dec.tensor(which, layer)
+        return dec.read(ptr, nbytes).view(dtype)
+    w = {"embed": t(P.T_EMBED), "out_norm": t(P.T_OUT_NORM, dtype=np.float32), "lm_head": t(P.T_LM_HEAD)}
+    names = {"attn_norm": (P.T_ATTN_NORM, np.float32), "ffn_norm": (P.T_FFN_NORM, np.float32),
+             "wqkv": (P.T_WQKV, np.uint8), "wo": (P.T_WO, np.uint8), "wgu": (P.T_WGATE_UP, np.uint8),
+             "wdown": (P.T_WDOWN, np.uint8)}
+    for name, (which, dt) in names.items():
+        w[name] = [t(which, l, dt) for l in range(cfg.n_layer)]
+    return w
+
+
+@pytest.mark.parametrize("wtype", [P.Q4_0, P.Q8_0, P.Q4_K])
+def test_decoder_matches_restated_steps(cuda, orc, wtype):
+    cfg = P.LlamaConfig(**TINY, wtype=wtype)
+    ocfg = oracle.LlamaConfig(*[getattr(cfg, f) for f, _ in oracle.LlamaConfig._fields_])
+    dec = P.Decoder(cfg)
+    try:
+        dec.init_random(1234 + wtype)
+        npos = 200
+        dec.fill_kv(npos, 77, 0.5)
+        dec.set_state(npos, 5)
+        w = read_model(dec, cfg)
+        kc = dec.read(*dec.buffer(P.B_KCACHE)).view(np.uint16).copy()
+        vc = dec.read(*dec.buffer(P.B_VCACHE)).view(np.uint16).copy()
+        cs = dec.read(*dec.buffer(P.B_ROPE)).view(np.float32)
+        assert np.array_equal(cs, P.rope_table(cfg.max_ctx, cfg.head_dim, cfg.rope_theta).ravel())
+        tok = 5
+        for step in range(4):
+            pos = npos + step
+            # each step starts from the device's own cache (teacher forcing):
+            # the comparison measures this step's arithmetic only
+            kc = dec.read(*dec.buffer(P.B_KCACHE)).view(np.uint16).copy()
+            vc = dec.read(*dec.buffer(P.B_VCACHE)).view(np.uint16).copy()
+            otok, ologits, ohidden = orc.decode_step(ocfg, w, kc, vc, cs, pos, tok)
+            dec.step(1)
+            gpos, gtok = dec.state()
+            assert gpos == pos + 1
+            glogits = dec.read(*dec.buffer(P.B_LOGITS)).view(np.float32)
+            ghidden = dec.read(*dec.buffer(P.B_HIDDEN)).view(np.float32)
+            err = np.max(np.abs(glogits - ologits))
+            herr = np.max(np.abs(ghidden - ohidden)) / np.max(np.abs(ohidden))
+            print(f"wtype {wtype} step {step}: logit err {err / np.max(np.abs(ologits)):.2e}, hidden err {herr:.2e}")
+            assert herr <= DECODE_HIDDEN_TOL, (step, herr)
+            assert err <= DECODE_LOGIT_TOL * np.max(np.abs(ologits)), (step, err)
+            top2 = np.sort(ologits)[-2:]
+            if top2[1] - top2[0] > 2 * err:
+                assert gtok == otok
+            assert gtok == int(np.argmax(glogits))
+            tok = gtok
+            # the appended rows: fp16 of nearly equal values
+            gk = dec.read(*dec.buffer(P.B_KCACHE)).view(np.float16).astype(np.float32)
+            ok = kc.view(np.float16).astype(np.float32)
+            assert np.max(np.abs(gk - ok)) <= 1e-2 * max(1.0, np.max(np.abs(ok)))
+        assert P.device_error() == P.OK
+    finally:
+        dec.close()
+
+
+def test_decoder_rejects_bad_configs(cuda):
+    with pytest.raises(P.InvalidArgument):
+        P.Decoder(P.LlamaConfig(**{**TINY, "n_head": 3}))
+    with pytest.raises(P.InvalidArgument):
+        P.Decoder(P.LlamaConfig(**{**TINY, "head_dim": 96}))
+    dec = P.Decoder(P.LlamaConfig(**TINY))
+    try:
+        with pytest.raises(P.InvalidArgument):
+            dec.set_state(TINY["max_ctx"], 0)
+        with pytest.raises(P.InvalidArgument):
+            dec.set_state(0, TINY["vocab"])
+    finally:
+        dec.close()
