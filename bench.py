@@ -25,6 +25,10 @@ row shards of an N-times wider layer stack — the same per-GPU shapes — with
 no collective on the data path (row-split mat-vecs exchange nothing).
 --impl reference times the reference's own CPU path (prepare + evaluate per
 row, oracle/_ref) on the host cores over a bounded sample of the same rows.
+decode  = configs 4/5: batch-1 decode tokens/s of the Llama-3 8B and 70B
+          shapes (random-init Q4_0, KV prefilled to 4096 / 8192), split over
+          the ranks (TP = N), with each GPU's bytes per token against the HBM
+          roofline.
 """
 from __future__ import annotations
 
@@ -261,6 +265,71 @@ def fa_section(torch, P, stream):
     return out
 
 
+DECODE_MODELS = {   # BASELINE configs 4 and 5: Llama-3 8B / 70B shapes, random-init Q4_0
+    "llama3-8b": dict(n_layer=32, hidden=4096, n_head=32, n_head_kv=8, head_dim=128, ffn=14336, vocab=128256,
+                      ctx=4096),
+    "llama3-70b": dict(n_layer=80, hidden=8192, n_head=64, n_head_kv=8, head_dim=128, ffn=28672, vocab=128256,
+                       ctx=8192),
+}
+DECODE_STEPS, DECODE_WARMUP = 48, 4
+
+
+def decode_section(torch, P, stream, rank, world, dist, max_over_ranks):
+    """Configs 4/5: batch-1 decode tokens/s of the 8B and 70B shapes, the model
+    row-split over the `world` ranks (TP=world, NCCL all-reduce after o and
+    down).  KV prefilled to the config's context (N(0,1)*0.5 fp16); each step
+    appends one row and attends over the whole cache, one CUDA graph per token
+    replayed back to back; CUDA events, max over ranks.  e2e additionally
+    reads every token on the host (4 bytes per step)."""
+    out = {}
+    peak, _ = peak_gbs()
+    tp = None
+    if world > 1:
+        box = [P.tp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(box, src=0)
+        tp = P.TP(box[0], world, rank, torch.cuda.current_device())
+    try:
+        for name, m in DECODE_MODELS.items():
+            ctx = m["ctx"]
+            cfg = P.LlamaConfig(m["n_layer"], m["hidden"], m["n_head"], m["n_head_kv"], m["head_dim"], m["ffn"],
+                                m["vocab"], ctx + DECODE_WARMUP + 2 * DECODE_STEPS + 8)
+            dec = P.Decoder(cfg, tp)
+            try:
+                dec.init_random(20261201)
+                dec.fill_kv(ctx, 7, 0.5)
+                dec.set_state(ctx, 1)
+                dec.step(DECODE_WARMUP, stream)
+                torch.cuda.synchronize()
+                if dist is not None:
+                    dist.barrier()
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                dec.step(DECODE_STEPS, stream)
+                b.record(stream)
+                b.synchronize()
+                ms = max_over_ranks(a.elapsed_time(b)) / DECODE_STEPS
+                t0 = time.perf_counter()
+                for _ in range(DECODE_STEPS):
+                    dec.step(1, stream)
+                    dec.state()               # synchronises and reads the token on the host
+                e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1e3) / DECODE_STEPS
+                pos, tok = dec.state()
+                kv_rank = m["n_layer"] * 2 * (m["n_head_kv"] // world) * m["head_dim"] * 2 * (ctx + DECODE_WARMUP
+                                                                                            + DECODE_STEPS)
+                rank_bytes = dec.weight_bytes_per_token + kv_rank
+                out[name] = {"tok_s": round(1e3 / ms, 2), "ms_per_token": round(ms, 4), "context": ctx,
+                             "tp": world, "bytes_per_token_per_gpu": rank_bytes,
+                             "hbm_frac_per_gpu": round(rank_bytes / (ms / 1e3) / 1e9 / peak, 4),
+                             "e2e_tok_s": round(1e3 / e2e_ms, 2), "last_token": tok, "position": pos}
+            finally:
+                dec.close()   # releases the graph (and its NCCL calls) before the communicator
+            P.check(P.device_error())
+    finally:
+        if tp is not None:
+            tp.close()
+    return out
+
+
 def kernel_only(args):
     """Eager launches of one kernel over rotating inputs larger than L2 — the
     small cases for ncu captures: the target mat-vec (5 weight copies, 165 MB)
@@ -301,6 +370,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-decode", action="store_true", help="skip the 8B/70B decode section")
     ap.add_argument("--kernel-only", choices=["qmv", "fa"], help="one kernel's launches only (ncu cases)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
@@ -438,6 +508,7 @@ def main():
     del e2e_graphs
     fa = fa_section(torch, P, stream) if rank == 0 else None
     P.check(P.device_error())
+    decode = decode_section(torch, P, stream, rank, world, dist, max_over_ranks) if not args.no_decode else None
 
     peak, peak_kind = peak_gbs()
     target_bytes = W.qmv_algorithmic_bytes(W.Q4_0, TARGET[2], TARGET[1], 1)
@@ -463,6 +534,7 @@ def main():
         "gpu_launches": launches_per_step * args.steps,
         "shapes": shape_gbs,
         "fa_decode": fa,
+        "decode": decode,
         "clocks": clocks.summary(),
         "checksum": round(checksum, 3),
     }

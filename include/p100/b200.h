@@ -232,8 +232,10 @@ enum { P100_B_HIDDEN = 0, P100_B_LOGITS, P100_B_KCACHE, P100_B_VCACHE, P100_B_RO
 /* Allocates everything (weights, fp16 KV cache for max_ctx, scratch) on the
  * current device, or tp's device; tp may be NULL. */
 p100_status p100_decoder_create(const p100_llama_config* cfg, p100_tp* tp, p100_decoder** out);
-/* Synthetic weights from seed: blocks as the BASELINE configs describe
- * (Q4_0 d = |N(0,1)|*0.02, codes uniform), norms uniform in [0.9, 1.1].
+/* Synthetic weights from seed: block scales d = |N(0,1)| * 0.02 *
+ * sqrt(256 / K) (K the unsplit matrix's input width, so activations keep
+ * their scale at any width and depth), codes uniform; norms uniform in
+ * [0.9, 1.1].
  * Every value is a function of (seed, tensor, global coordinates), so the
  * slices of a tensor-parallel rank equal the unsplit model's. */
 p100_status p100_decoder_init_random(p100_decoder* d, unsigned long long seed);

@@ -355,22 +355,22 @@ __device__ __forceinline__ void store_half(uint8_t* p, float v) {
 }
 
 // Weight blocks of a rows x blocks matrix slice whose (row, block) (0, 0)
-// sits at global (row0, block0).  Q4_0: d = |N(0,1)| * 0.02, codes U{0..15};
-// Q8_0: d likewise, codes U{-127..127}; Q4_K: d and dmin |N|*0.02, scale
-// bytes and nibbles uniform.  One thread per block.
+// sits at global (row0, block0).  Q4_0: d = |N(0,1)| * dscale, codes
+// U{0..15}; Q8_0: d likewise, codes U{-127..127}; Q4_K: d and dmin
+// |N| * dscale, scale bytes and nibbles uniform.  One thread per block.
 template <int TYPE>
 __global__ void init_weights_kernel(uint8_t* __restrict__ w, size_t row_bytes, int rows, int blocks, uint64_t key,
-                                    long long row0, long long block0) {
+                                    long long row0, long long block0, float dscale) {
     const long long id = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (id >= static_cast<long long>(rows) * blocks) return;
     const int r = static_cast<int>(id / blocks), b = static_cast<int>(id % blocks);
     const uint64_t h = mix64(key ^ mix64((uint64_t(row0 + r) << 24) ^ uint64_t(block0 + b)));
     constexpr int kBytes = TYPE == P100_Q4_0 ? 18 : TYPE == P100_Q8_0 ? 34 : 144;
     uint8_t* blk = w + size_t(r) * row_bytes + size_t(b) * kBytes;
-    store_half(blk, fabsf(normal_from(h)) * 0.02f);
+    store_half(blk, fabsf(normal_from(h)) * dscale);
     uint64_t z = mix64(h ^ 0x5bd1e995ull);
     if (TYPE == P100_Q4_K) {
-        store_half(blk + 2, fabsf(normal_from(z)) * 0.02f);
+        store_half(blk + 2, fabsf(normal_from(z)) * dscale);
         for (int i = 4; i < kBytes; ++i) {
             if ((i & 7) == 4) z = mix64(z);
             blk[i] = uint8_t(z >> (8 * (i & 7)));

@@ -178,21 +178,27 @@ uint64_t dec_key(uint64_t seed, int layer, int id) {
 
 template <int T>
 p100_status dec_init_w(uint8_t* w, size_t row_bytes, int rows, int blocks, uint64_t key, long long row0,
-                       long long block0) {
+                       long long block0, float dscale) {
     const long long n = static_cast<long long>(rows) * blocks;
     if (n == 0) return P100_OK;
-    dec::init_weights_kernel<T><<<unsigned((n + 255) / 256), 256>>>(w, row_bytes, rows, blocks, key, row0, block0);
+    dec::init_weights_kernel<T><<<unsigned((n + 255) / 256), 256>>>(w, row_bytes, rows, blocks, key, row0, block0,
+                                                                      dscale);
     return launch_status("init_weights_kernel launch");
 }
 
+// Block scales |N(0,1)| * 0.02 * sqrt(256 / K), K the unsplit matrix's input
+// width: the 0.02 of the mat-vec configs at K = 256, shrinking with fan-in so
+// every projection's output keeps about the RMS of its input and the
+// residual stream stays inside the fp16 fields of Q8_1 at any depth.
 p100_status dec_init_matrix(int t, uint8_t* w, size_t row_bytes, int rows, int cols, uint64_t key, long long row0,
-                            long long col0) {
+                            long long col0, int k_global) {
     const int blocks = cols / elems_of(t);
     const long long block0 = col0 / elems_of(t);
+    const float dscale = 0.02f * std::sqrt(256.0f / float(k_global));
     switch (t) {
-        case P100_Q4_0: return dec_init_w<P100_Q4_0>(w, row_bytes, rows, blocks, key, row0, block0);
-        case P100_Q8_0: return dec_init_w<P100_Q8_0>(w, row_bytes, rows, blocks, key, row0, block0);
-        default: return dec_init_w<P100_Q4_K>(w, row_bytes, rows, blocks, key, row0, block0);
+        case P100_Q4_0: return dec_init_w<P100_Q4_0>(w, row_bytes, rows, blocks, key, row0, block0, dscale);
+        case P100_Q8_0: return dec_init_w<P100_Q8_0>(w, row_bytes, rows, blocks, key, row0, block0, dscale);
+        default: return dec_init_w<P100_Q4_K>(w, row_bytes, rows, blocks, key, row0, block0, dscale);
     }
 }
 
@@ -214,24 +220,26 @@ p100_status dec_init_random(Decoder& d, uint64_t seed) {
         uint8_t* w = d.wqkv[l].ptr;
         const long long q0 = static_cast<long long>(d.rank) * d.nq * hd, kv0 = static_cast<long long>(d.rank) * d.nkv * hd;
         if (!st) st = dec_init_vector(reinterpret_cast<float*>(d.attn_norm[l].ptr), c.hidden, dec_key(seed, l, K_NORM1));
-        if (!st) st = dec_init_matrix(t, w, rb_h, d.nq * hd, c.hidden, dec_key(seed, l, K_Q), q0, 0);
-        if (!st) st = dec_init_matrix(t, w + size_t(d.nq * hd) * rb_h, rb_h, d.nkv * hd, c.hidden, dec_key(seed, l, K_K), kv0, 0);
+        if (!st) st = dec_init_matrix(t, w, rb_h, d.nq * hd, c.hidden, dec_key(seed, l, K_Q), q0, 0, c.hidden);
+        if (!st) st = dec_init_matrix(t, w + size_t(d.nq * hd) * rb_h, rb_h, d.nkv * hd, c.hidden, dec_key(seed, l, K_K),
+                                      kv0, 0, c.hidden);
         if (!st) st = dec_init_matrix(t, w + size_t((d.nq + d.nkv) * hd) * rb_h, rb_h, d.nkv * hd, c.hidden,
-                                      dec_key(seed, l, K_V), kv0, 0);
+                                      dec_key(seed, l, K_V), kv0, 0, c.hidden);
         if (!st) st = dec_init_matrix(t, d.wo[l].ptr, dec_weight_bytes(t, 1, d.nq * hd), c.hidden, d.nq * hd,
-                                      dec_key(seed, l, K_O), 0, q0);
+                                      dec_key(seed, l, K_O), 0, q0, c.n_head * hd);
         if (!st) st = dec_init_vector(reinterpret_cast<float*>(d.ffn_norm[l].ptr), c.hidden, dec_key(seed, l, K_NORM2));
         const long long f0 = static_cast<long long>(d.rank) * d.ffn;
-        if (!st) st = dec_init_matrix(t, d.wgu[l].ptr, rb_h, d.ffn, c.hidden, dec_key(seed, l, K_GATE), f0, 0);
+        if (!st) st = dec_init_matrix(t, d.wgu[l].ptr, rb_h, d.ffn, c.hidden, dec_key(seed, l, K_GATE), f0, 0, c.hidden);
         if (!st) st = dec_init_matrix(t, d.wgu[l].ptr + size_t(d.ffn) * rb_h, rb_h, d.ffn, c.hidden, dec_key(seed, l, K_UP),
-                                      f0, 0);
+                                      f0, 0, c.hidden);
         if (!st) st = dec_init_matrix(t, d.wdown[l].ptr, dec_weight_bytes(t, 1, d.ffn), c.hidden, d.ffn,
-                                      dec_key(seed, l, K_DOWN), 0, f0);
+                                      dec_key(seed, l, K_DOWN), 0, f0, c.ffn);
         if (st) return st;
     }
-    p100_status st = dec_init_matrix(t, d.embed.ptr, rb_h, c.vocab, c.hidden, dec_key(seed, -1, K_EMB), 0, 0);
+    p100_status st = dec_init_matrix(t, d.embed.ptr, rb_h, c.vocab, c.hidden, dec_key(seed, -1, K_EMB), 0, 0, c.hidden);
     if (!st) st = dec_init_vector(reinterpret_cast<float*>(d.out_norm.ptr), c.hidden, dec_key(seed, -1, K_NORM3));
-    if (!st) st = dec_init_matrix(t, d.lm_head.ptr, rb_h, d.vocab_n, c.hidden, dec_key(seed, -1, K_LM), d.vocab0, 0);
+    if (!st) st = dec_init_matrix(t, d.lm_head.ptr, rb_h, d.vocab_n, c.hidden, dec_key(seed, -1, K_LM), d.vocab0, 0,
+                                  c.hidden);
     if (!st) st = cuda_status(cudaDeviceSynchronize(), "decoder initialisation");
     return st;
 }

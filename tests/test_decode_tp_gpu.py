@@ -1,0 +1,105 @@
+"""Tensor-parallel decoder (row split over 2 GPUs, NCCL all-reduce after o and
+down, all-gathered argmax) against the same model at TP=1.
+
+Each rank initialises its own slices from global coordinates, so TP=2 holds
+the TP=1 model exactly; the steps differ only in the summation order of the
+row-split partial sums, so logits agree within the decoder bounds of
+test_decode_gpu.py and the tokens agree where the top two logits are further
+apart than the logit error.  Two ranks, one process per GPU; skipped with
+fewer than two GPUs."""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+import p100_b200 as P
+from test_decode_gpu import DECODE_LOGIT_TOL, TINY
+
+pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
+
+SEED, NPOS, STEPS, TOKEN = 99, 100, 3, 7
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _run(dec):
+    import torch
+    dec.init_random(SEED)
+    dec.fill_kv(NPOS, 5, 0.5)
+    dec.set_state(NPOS, TOKEN)
+    out = []
+    for _ in range(STEPS):
+        dec.step(1, torch.cuda.current_stream())
+        pos, tok = dec.state()
+        logits = dec.read(*dec.buffer(P.B_LOGITS)).view(np.float32).copy()
+        out.append((pos, tok, logits))
+    return out
+
+
+def _rank(rank, world, port, q):
+    import datetime
+    import torch
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    tp = dec = None
+    try:
+        box = [P.tp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(box, src=0)
+        tp = P.TP(box[0], world, rank, rank)
+        dec = P.Decoder(P.LlamaConfig(**TINY), tp)
+        out = _run(dec)
+        q.put((rank, dec.vocab_offset, [(p, t, l.tolist()) for p, t, l in out]))
+    except Exception as e:  # noqa: BLE001
+        q.put((rank, "error", repr(e)))
+    finally:
+        if dec is not None:
+            dec.close()   # releases the graph that holds the NCCL calls first
+        if tp is not None:
+            tp.close()
+        dist.destroy_process_group()
+
+
+def test_tp2_matches_tp1(cuda):
+    if cuda.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted([q.get(timeout=300) for _ in range(2)], key=lambda r: r[0])
+    for p in procs:
+        p.join(timeout=120)
+        assert not p.is_alive()
+    for r in res:
+        assert r[1] != "error", r
+    with cuda.cuda.device(0):
+        dec = P.Decoder(P.LlamaConfig(**TINY))
+        try:
+            ref = _run(dec)
+        finally:
+            dec.close()
+    for step in range(STEPS):
+        pos1, tok1, logits1 = ref[step]
+        full = np.zeros(TINY["vocab"], dtype=np.float32)
+        for rank, off, out in res:
+            pos, tok, logits = out[step]
+            assert pos == pos1
+            full[off:off + len(logits)] = logits
+        assert res[0][2][step][1] == res[1][2][step][1]   # every rank picks the same token
+        err = np.max(np.abs(full - logits1))
+        assert err <= DECODE_LOGIT_TOL * np.max(np.abs(logits1)), (step, err)
+        top2 = np.sort(logits1)[-2:]
+        if top2[1] - top2[0] > 2 * err:
+            assert res[0][2][step][1] == tok1
+        if res[0][2][step][1] != tok1:
+            break   # the runs continue from different tokens: later steps are not comparable
