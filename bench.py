@@ -336,6 +336,22 @@ def kernel_only(args):
     or FA decode at 32K context (2 K/V copies, 268 MB)."""
     import torch
     import p100_b200 as P
+    if args.kernel_only == "decode":
+        # the 8B decoder (config 4): warmup + steps tokens, 324 launches each
+        m = DECODE_MODELS["llama3-8b"]
+        cfg = P.LlamaConfig(m["n_layer"], m["hidden"], m["n_head"], m["n_head_kv"], m["head_dim"], m["ffn"], m["vocab"],
+                            m["ctx"] + args.warmup + args.steps + 8)
+        dec = P.Decoder(cfg)
+        dec.init_random(20261201)
+        dec.fill_kv(m["ctx"], 7, 0.5)
+        dec.set_state(m["ctx"], 1)
+        dec.step(args.warmup + args.steps, torch.cuda.current_stream())
+        pos, tok = dec.state()
+        dec.close()
+        P.check(P.device_error())
+        print(json.dumps({"kernel_only": "decode llama3-8b ctx 4096", "steps": args.warmup + args.steps,
+                          "position": pos, "token": tok}))
+        return 0
     if args.kernel_only == "fa":
         seq = 32768
         q, k, v = W.attention_inputs(1, 32, 8, seq, 128, seed=seq)
@@ -371,7 +387,7 @@ def main():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the 8B/70B decode section")
-    ap.add_argument("--kernel-only", choices=["qmv", "fa"], help="one kernel's launches only (ncu cases)")
+    ap.add_argument("--kernel-only", choices=["qmv", "fa", "decode"], help="one kernel's launches only (ncu cases)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
