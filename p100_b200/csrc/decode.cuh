@@ -29,6 +29,60 @@ namespace dec {
 constexpr int kNormThreads = 1024;    // 32 warps; float4 chunk c belongs to thread c % 1024
 constexpr int kArgmaxThreads = 1024;
 
+// ------------------------------------------------- one-shot peer all-reduce
+// Tensor-parallel sum of an n-float partial vector over `world` GPUs of one
+// box through NVLink peer memory (CUDA IPC mappings).  Every rank owns an
+// arena of slots [2][world][n] fp32 and flags [2][world][nblk] u32; slot and
+// flag pointers of every rank (own and peers') are in PeerAr.
+//   push (ar_push_kernel, after the producing mat-vec): block b stores its
+//     n/nblk chunk of the partial into slot [e&1][rank] of every rank, makes
+//     the stores visible system-wide, then sets flag [e&1][rank][b] = e on
+//     every rank (release store);
+//   reduce (rmsnorm_q8_1_kernel with ar.world > 0): waits, bounded, until all
+//     world*nblk flags of epoch e in its own arena read e (acquire loads),
+//     sums the world slots in rank order (the same order on every rank, so
+//     every rank holds the same bits), then stores e as the completed epoch.
+// e = completed epoch + 1, read from a device counter, so a replayed graph
+// uses a new epoch every call.  Slots are double-buffered by e & 1: a rank
+// writes epoch e+2 into a peer only after seeing every rank's e+1 flags, and
+// a rank raises e+1 only after its reduce of e finished reading.
+constexpr int kArMaxRanks = 8;
+constexpr int kArBlocks = 8;
+struct PeerAr {
+    float* slots[kArMaxRanks];
+    unsigned* flags[kArMaxRanks];
+    int world, rank, n;
+    int* epoch;   // this rank's completed-epoch counter
+};
+
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Grid kArBlocks x 256; n % (4 * kArBlocks) == 0.
+__global__ void __launch_bounds__(256) ar_push_kernel(const float* __restrict__ y, const PeerAr ar) {
+    pdl_allow_dependents();
+    pdl_wait_prior_grid();
+    const unsigned e = unsigned(*ar.epoch) + 1u;
+    const int par = int(e & 1u);
+    const int n4 = ar.n / 4, per = n4 / kArBlocks;
+    const float4* src = reinterpret_cast<const float4*>(y) + blockIdx.x * per;
+    for (int i = threadIdx.x; i < per; i += blockDim.x) {
+        const float4 v = src[i];
+        for (int r = 0; r < ar.world; ++r)
+            reinterpret_cast<float4*>(ar.slots[r] + (size_t(par) * ar.world + ar.rank) * ar.n)[blockIdx.x * per + i] = v;
+    }
+    __threadfence_system();   // this thread's stores, system scope, before the block's flags
+    __syncthreads();
+    if (threadIdx.x < ar.world)
+        st_release_sys(ar.flags[threadIdx.x] + (size_t(par) * ar.world + ar.rank) * kArBlocks + blockIdx.x, e);
+}
+
 // ------------------------------------------------------------------ RMSNorm
 // Q8_1 block of 32 values held four per lane by 8 consecutive lanes (lane j
 // of the octet holds elements 4j..4j+3 in v[0..3]).  Same bytes as
@@ -74,7 +128,8 @@ constexpr int kNormChunks = 4;    // float4 chunks per thread at most
 constexpr int kNormMaxK = kNormChunks * kNormThreads * 4;
 __global__ void __launch_bounds__(kNormThreads) rmsnorm_q8_1_kernel(float* __restrict__ x, const float* __restrict__ delta,
                                                                   const float* __restrict__ w, float eps, int k,
-                                                                  uint8_t* __restrict__ xq, float* __restrict__ y_out) {
+                                                                  uint8_t* __restrict__ xq, float* __restrict__ y_out,
+                                                                  const PeerAr ar) {
     pdl_allow_dependents();
     pdl_wait_prior_grid();
     __shared__ float s_part[kNormThreads / 32];
@@ -100,6 +155,39 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_q8_1_kernel(float* __res
                 xr[c] = v[i];
             }
         }
+    } else if (ar.world > 0) {
+        // delta = the peer all-reduce of this epoch (batch 1, n = k)
+        const unsigned e = unsigned(*ar.epoch) + 1u;
+        const int par = int(e & 1u);
+        bool ok = true;
+        if (tid < ar.world * kArBlocks) {
+            const unsigned* f = ar.flags[ar.rank] + size_t(par) * ar.world * kArBlocks + tid;
+            const unsigned long long start = globaltimer_ns();
+            while (ld_acquire_sys(f) != e) {
+                if (globaltimer_ns() - start > kWaitLimitNs) {
+                    ok = false;
+                    break;
+                }
+            }
+        }
+        if (!__syncthreads_and(ok) && tid == 0) atomicExch(&g_device_error, kDevErrTimeout);
+        const float* base = ar.slots[ar.rank] + size_t(par) * ar.world * ar.n;
+#pragma unroll
+        for (int i = 0; i < kNormChunks; ++i) {
+            const int c = tid + i * kNormThreads;
+            if (c < nc) {
+                float4 d4 = reinterpret_cast<const float4*>(base)[c];
+                for (int r = 1; r < ar.world; ++r) {
+                    const float4 o = reinterpret_cast<const float4*>(base + size_t(r) * ar.n)[c];
+                    d4 = make_float4(__fadd_rn(d4.x, o.x), __fadd_rn(d4.y, o.y), __fadd_rn(d4.z, o.z),
+                                     __fadd_rn(d4.w, o.w));
+                }
+                v[i] = make_float4(__fadd_rn(v[i].x, d4.x), __fadd_rn(v[i].y, d4.y), __fadd_rn(v[i].z, d4.z),
+                                   __fadd_rn(v[i].w, d4.w));
+                xr[c] = v[i];
+            }
+        }
+        if (tid == 0) *ar.epoch = int(e);   // read by the next push, which starts after this kernel ends
     }
     float s = 0.f;
 #pragma unroll

@@ -52,6 +52,12 @@ struct Decoder {
     FaPlan fa_plan;
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t graph_exec = nullptr;
+    // one-shot all-reduce over NVLink peer memory (tensor parallelism)
+    bool peer_ar = false;
+    uint8_t* ar_arena = nullptr;             // this rank's slots + flags
+    void* ar_peer[dec::kArMaxRanks] = {};    // IPC mappings of the other ranks' arenas
+    int* ar_epoch = nullptr;                 // completed-epoch counter (in the arena above)
+    dec::PeerAr ar{};
 };
 
 size_t dec_weight_bytes(int type, int rows, int cols) {
@@ -269,10 +275,26 @@ p100_status dec_embed_t(Decoder& d, cudaStream_t s) {
                        static_cast<const int*>(d.token), d.x);
 }
 
-p100_status dec_rmsnorm(Decoder& d, const float* delta, const DecTensor& w, cudaStream_t s) {
+// x += delta (or, with peer_reduce, += the peer all-reduce of this epoch),
+// then RMSNorm * w and Q8_1 into d.xq.
+p100_status dec_rmsnorm(Decoder& d, const float* delta, const DecTensor& w, cudaStream_t s, bool peer_reduce = false) {
+    dec::PeerAr ar{};
+    if (peer_reduce) {
+        ar = d.ar;
+        delta = nullptr;
+    }
     return launch_glue(dec::rmsnorm_q8_1_kernel, dim3(1), dim3(dec::kNormThreads), s, "rmsnorm_q8_1_kernel launch",
                        d.x, delta, reinterpret_cast<const float*>(w.ptr), d.cfg.norm_eps, d.cfg.hidden, d.xq,
-                       static_cast<float*>(nullptr));
+                       static_cast<float*>(nullptr), ar);
+}
+
+// The partial sums in d.delta to every rank: NCCL all-reduce, or the push of
+// the one-shot peer all-reduce (whose reduce runs in the next RMSNorm).
+p100_status dec_allreduce(Decoder& d, cudaStream_t s) {
+    if (!d.tp) return P100_OK;
+    if (!d.peer_ar) return p100_tp_allreduce_sum(d.tp, d.delta, size_t(d.cfg.hidden), s);
+    return launch_glue(dec::ar_push_kernel, dim3(dec::kArBlocks), dim3(256), s, "ar_push_kernel launch",
+                       static_cast<const float*>(d.delta), d.ar);
 }
 
 // One token, recorded into stream s (a capture stream).
@@ -288,7 +310,7 @@ p100_status dec_record_step(Decoder& d, cudaStream_t s) {
     }
     for (int l = 0; l < c.n_layer && !st; ++l) {
         const size_t layer_off = size_t(l) * d.nkv * hs;
-        st = dec_rmsnorm(d, l == 0 ? nullptr : d.delta, d.attn_norm[l], s);
+        st = dec_rmsnorm(d, l == 0 ? nullptr : d.delta, d.attn_norm[l], s, l > 0 && d.peer_ar);
         if (!st) st = run_qmv(t, d.wqkv[l].ptr, d.wqkv[l].rows, c.hidden, d.xq, 1, d.qkv, P100_QMV_PDL, s);
         if (!st)
             st = launch_glue(dec::rope_kv_append_kernel, dim3(d.nq + 2 * d.nkv), dim3(hd / 2), s,
@@ -328,16 +350,16 @@ p100_status dec_record_step(Decoder& d, cudaStream_t s) {
                              "q8_1_quantize_kernel launch", static_cast<const float*>(d.attn), d.xq, k_o, k_o / 32);
         }
         if (!st) st = run_qmv(t, d.wo[l].ptr, c.hidden, d.nq * hd, d.xq, 1, d.delta, P100_QMV_PDL, s);
-        if (!st && d.tp) st = p100_tp_allreduce_sum(d.tp, d.delta, size_t(c.hidden), s);
-        if (!st) st = dec_rmsnorm(d, d.delta, d.ffn_norm[l], s);
+        if (!st) st = dec_allreduce(d, s);
+        if (!st) st = dec_rmsnorm(d, d.delta, d.ffn_norm[l], s, d.peer_ar);
         if (!st) st = run_qmv(t, d.wgu[l].ptr, 2 * d.ffn, c.hidden, d.xq, 1, d.gu, P100_QMV_PDL, s);
         if (!st)
             st = launch_glue(dec::swiglu_q8_1_kernel, dim3((d.ffn / 32 + 7) / 8, 1), dim3(256), s,
                              "swiglu_q8_1_kernel launch", static_cast<const float*>(d.gu), d.ffn, d.xq);
         if (!st) st = run_qmv(t, d.wdown[l].ptr, c.hidden, d.ffn, d.xq, 1, d.delta, P100_QMV_PDL, s);
-        if (!st && d.tp) st = p100_tp_allreduce_sum(d.tp, d.delta, size_t(c.hidden), s);
+        if (!st) st = dec_allreduce(d, s);
     }
-    if (!st) st = dec_rmsnorm(d, d.delta, d.out_norm, s);
+    if (!st) st = dec_rmsnorm(d, d.delta, d.out_norm, s, d.peer_ar);
     if (!st) st = run_qmv(t, d.lm_head.ptr, d.vocab_n, c.hidden, d.xq, 1, d.logits, P100_QMV_PDL, s);
     if (st) return st;
     if (!d.tp) {
@@ -386,6 +408,117 @@ p100_status dec_capture(Decoder& d) {
     return st;
 }
 
+// One-shot all-reduce setup: every rank allocates its arena, the IPC handles
+// go round an NCCL all-gather (as raw bytes in floats), and every rank maps
+// the others'.  Used only if every pair of ranks' GPUs has peer access (an
+// NCCL all-reduce of the verdict keeps all ranks on the same path) and
+// P100_TP_ALLREDUCE is not "nccl".  Collective: every rank calls it.
+p100_status dec_setup_peer_ar(Decoder& d) {
+    const int world = d.nranks;
+    if (!d.tp || world < 2 || world > dec::kArMaxRanks) return P100_OK;
+    const char* mode = std::getenv("P100_TP_ALLREDUCE");
+    const bool want = !(mode && std::strcmp(mode, "nccl") == 0);
+    const int n = d.cfg.hidden;
+    if (n % (4 * dec::kArBlocks)) return P100_OK;
+    cudaStream_t s = nullptr;
+    if (p100_status st = cuda_status(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "stream")) return st;
+    // scratch: a gather's input (up to 16 floats) and output (16 per rank), then the verdict
+    const int verdict_at = 16 + 16 * world;
+    float* scratch = nullptr;
+    p100_status st = cuda_status(cudaMalloc(&scratch, sizeof(float) * (verdict_at + 2)), "cudaMalloc(ar scratch)");
+    auto gather = [&](const float* mine, int count, float* out_host) -> p100_status {
+        p100_status r = cuda_status(cudaMemcpyAsync(scratch, mine, sizeof(float) * count, cudaMemcpyHostToDevice, s),
+                                    "ar gather in");
+        if (!r) r = p100_tp_allgather(d.tp, scratch, scratch + count, size_t(count), s);
+        if (!r) r = cuda_status(cudaMemcpyAsync(out_host, scratch + count, sizeof(float) * count * world,
+                                                cudaMemcpyDeviceToHost, s), "ar gather out");
+        if (!r) r = cuda_status(cudaStreamSynchronize(s), "ar gather sync");
+        return r;
+    };
+    // 1. device ids -> peer access verdict, agreed by all ranks
+    std::vector<float> devs(world);
+    if (!st) {
+        const float me = float(d.device);
+        st = gather(&me, 1, devs.data());
+    }
+    float ok = want ? 1.f : 0.f;
+    for (int r = 0; r < world && !st && ok > 0.f; ++r) {
+        if (r == d.rank) continue;
+        int can = 0;
+        cudaDeviceCanAccessPeer(&can, d.device, int(devs[r]));
+        if (!can) ok = 0.f;
+    }
+    if (!st) st = cuda_status(cudaMemcpyAsync(scratch + verdict_at, &ok, sizeof(float), cudaMemcpyHostToDevice, s), "v");
+    if (!st) st = p100_tp_allreduce_sum(d.tp, scratch + verdict_at, 1, s);
+    float votes = 0.f;
+    if (!st) st = cuda_status(cudaMemcpyAsync(&votes, scratch + verdict_at, sizeof(float), cudaMemcpyDeviceToHost, s), "v");
+    if (!st) st = cuda_status(cudaStreamSynchronize(s), "verdict sync");
+    if (!st && votes == float(world)) {
+        // 2. arenas: slots [2][world][n] fp32, flags [2][world][kArBlocks] u32, epoch
+        const size_t slot_bytes = size_t(2) * world * n * 4;
+        const size_t flag_bytes = size_t(2) * world * dec::kArBlocks * 4;
+        st = cuda_status(cudaMalloc(&d.ar_arena, slot_bytes + flag_bytes + 256), "cudaMalloc(ar arena)");
+        if (!st) st = cuda_status(cudaMemset(d.ar_arena, 0, slot_bytes + flag_bytes + 256), "cudaMemset(ar arena)");
+        if (!st) st = cuda_status(cudaDeviceSynchronize(), "ar arena sync");
+        cudaIpcMemHandle_t h;
+        if (!st) st = cuda_status(cudaIpcGetMemHandle(&h, d.ar_arena), "cudaIpcGetMemHandle");
+        std::vector<float> mine(16), all(size_t(world) * 16);
+        static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+        std::memcpy(mine.data(), &h, 64);
+        if (!st) st = gather(mine.data(), 16, all.data());
+        for (int r = 0; r < world && !st; ++r) {
+            uint8_t* base = nullptr;
+            if (r == d.rank) {
+                base = d.ar_arena;
+            } else {
+                cudaIpcMemHandle_t hr;
+                std::memcpy(&hr, all.data() + size_t(r) * 16, 64);
+                void* p = nullptr;
+                st = cuda_status(cudaIpcOpenMemHandle(&p, hr, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+                d.ar_peer[r] = p;
+                base = static_cast<uint8_t*>(p);
+            }
+            if (!st) {
+                d.ar.slots[r] = reinterpret_cast<float*>(base);
+                d.ar.flags[r] = reinterpret_cast<unsigned*>(base + slot_bytes);
+            }
+        }
+        if (!st) {
+            d.ar_epoch = reinterpret_cast<int*>(d.ar_arena + slot_bytes + flag_bytes);
+            d.ar.world = world;
+            d.ar.rank = d.rank;
+            d.ar.n = n;
+            d.ar.epoch = d.ar_epoch;
+            // every rank's arena is zeroed and mapped before any rank pushes
+            st = p100_tp_allreduce_sum(d.tp, scratch, 1, s);
+            if (!st) st = cuda_status(cudaStreamSynchronize(s), "ar setup barrier");
+            d.peer_ar = !st;
+        }
+    }
+    if (scratch) cudaFree(scratch);
+    cudaStreamDestroy(s);
+    return st;
+}
+
+// Collective: no rank unmaps or frees its arena before every rank's work is
+// done (a peer's in-flight stores must never reach freed memory).
+void dec_teardown_peer_ar(Decoder& d) {
+    if (!d.ar_arena) return;
+    if (d.tp) {
+        cudaStream_t s = nullptr;
+        cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
+        cudaDeviceSynchronize();
+        p100_tp_allreduce_sum(d.tp, reinterpret_cast<float*>(d.ar_arena), 1, s);
+        cudaStreamSynchronize(s);
+        cudaStreamDestroy(s);
+    }
+    for (int r = 0; r < dec::kArMaxRanks; ++r)
+        if (d.ar_peer[r]) cudaIpcCloseMemHandle(d.ar_peer[r]);
+    cudaFree(d.ar_arena);
+    d.ar_arena = nullptr;
+    d.peer_ar = false;
+}
+
 struct DeviceGuard {
     int prev = 0;
     explicit DeviceGuard(int dev) { cudaGetDevice(&prev); cudaSetDevice(dev); }
@@ -419,7 +552,8 @@ p100_status p100_rmsnorm_q8_1(float* x, const float* delta, const float* w, floa
     if (!x || !w || !x_q8_1) return set_error(P100_ERR_INVALID, "null buffer");
     if (p100_status st = require_sm100(nullptr, nullptr)) return st;
     dec::rmsnorm_q8_1_kernel<<<batch, dec::kNormThreads, 0, stream>>>(x, delta, w, eps, k,
-                                                                        static_cast<uint8_t*>(x_q8_1), y_out);
+                                                                        static_cast<uint8_t*>(x_q8_1), y_out,
+                                                                        dec::PeerAr{});
     return launch_status("rmsnorm_q8_1_kernel launch");
 }
 
@@ -480,8 +614,11 @@ p100_status p100_decoder_create(const p100_llama_config* cfg, p100_tp* tp, p100_
     h->d.nranks = nranks;
     h->d.device = dev;
     h->d.sms = sms;
-    if (p100_status st = dec_alloc(h->d)) {
+    p100_status st = dec_alloc(h->d);
+    if (!st) st = dec_setup_peer_ar(h->d);
+    if (st) {
         const std::string why = t_error;
+        dec_teardown_peer_ar(h->d);
         if (h->d.arena) cudaFree(h->d.arena);
         delete h;
         return set_error(st, "%s", why.c_str());
@@ -604,6 +741,7 @@ p100_status p100_decoder_destroy(p100_decoder* h) {
     if (!h) return P100_OK;
     DeviceGuard guard(h->d.device);
     p100b::dec_release_graph(h->d);
+    p100b::dec_teardown_peer_ar(h->d);
     p100_status st = P100_OK;
     if (h->d.arena) st = cuda_status(cudaFree(h->d.arena), "cudaFree(decoder)");
     delete h;

@@ -1,7 +1,9 @@
 """Tensor-parallel decoder (row split over 2 GPUs, NCCL all-reduce after o and
 down, all-gathered argmax) against the same model at TP=1.
 
-Each rank initialises its own slices from global coordinates, so TP=2 holds
+Both all-reduce paths are checked: the one-shot all-reduce over NVLink peer
+memory and NCCL.  Each rank initialises its own slices from global
+coordinates, so TP=2 holds
 the TP=1 model exactly; the steps differ only in the summation order of the
 row-split partial sums, so logits agree within the decoder bounds of
 test_decode_gpu.py and the tokens agree where the top two logits are further
@@ -41,11 +43,12 @@ def _run(dec):
     return out
 
 
-def _rank(rank, world, port, q):
+def _rank(rank, world, port, q, allreduce):
     import datetime
     import torch
     import torch.distributed as dist
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0",
+                      P100_TP_ALLREDUCE=allreduce)
     torch.cuda.set_device(rank)
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
     tp = dec = None
@@ -66,14 +69,17 @@ def _rank(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def test_tp2_matches_tp1(cuda):
+@pytest.mark.parametrize("allreduce", ["peer", "nccl"])
+def test_tp2_matches_tp1(cuda, allreduce):
+    """allreduce: 'peer' = the one-shot all-reduce over NVLink peer memory
+    (push kernel + reduce inside the next RMSNorm), 'nccl' = ncclAllReduce."""
     if cuda.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, q, allreduce)) for r in range(2)]
     for p in procs:
         p.start()
     res = sorted([q.get(timeout=300) for _ in range(2)], key=lambda r: r[0])
