@@ -478,6 +478,27 @@ def main():
         if (name, k, rows) == TARGET:
             target_us, target_us_isolated = per["chained"], per["isolated"]
 
+    # Config 2's batch sweep on the target shape: batch 1-16 columns per
+    # launch (the batch >= 2 kernel), chained back-to-back launches.
+    batch_sweep = {}
+    _, tk, trows = TARGET
+    ti = [i for i, sh in enumerate(SHAPES) if sh == TARGET][0]
+    for b in (1, 2, 4, 8, 16):
+        xb = torch.from_numpy(W.activations(b, tk, seed=4000 + b)).cuda()
+        xqb = P.q8_1_quantize(xb)
+        yb = torch.empty(b, trows, dtype=torch.float32, device="cuda")
+        n_in_graph = 4 * copies
+        g = capture(torch, lambda xqb=xqb, yb=yb, b=b: [
+            P.qmv(W.Q4_0, wdev[ti][r % copies], trows, tk, xqb, b, y=yb, flags=P.QMV_PDL) for r in range(n_in_graph)])
+        time_graphs(torch, [g], 3, stream)
+        reps = 10
+        us = time_graphs(torch, [g], reps, stream) / (reps * n_in_graph) * 1e3
+        nbytes = W.qmv_algorithmic_bytes(W.Q4_0, trows, tk, b)
+        batch_sweep[str(b)] = {"us": round(us, 3), "GB/s": round(nbytes / (us / 1e6) / 1e9, 1),
+                               "frac": round(nbytes / (us / 1e6) / 1e9 / peak_gbs()[0], 4),
+                               "int8_tops": round(2.0 * trows * tk * b / (us / 1e6) / 1e12, 2)}
+        del g
+
     # End to end through the C-ABI with host buffers: each step copies its
     # activations in from pinned memory, runs, copies y out and synchronises
     # before the host reads the result.  "graph": the calls captured once and
@@ -549,6 +570,7 @@ def main():
                 "form": "graph replay + stream sync + host read per step", "eager_value": round(e2e_eager, 2)},
         "gpu_launches": launches_per_step * args.steps,
         "shapes": shape_gbs,
+        "batch_sweep": {"shape": f"{TARGET[0]} {TARGET[1]}x{TARGET[2]} Q4_0", "per_batch": batch_sweep},
         "fa_decode": fa,
         "decode": decode,
         "clocks": clocks.summary(),

@@ -6,9 +6,11 @@
 // kernels (decode.cuh).  The step per layer:
 //   x += delta; xq = Q8_1(RMSNorm(x) * attn_norm)            rmsnorm_q8_1
 //   qkv = Wqkv . xq                    (fused q|k|v rows)     team mat-vec
-//   RoPE(q, k) at pos; k, v -> fp16 cache row pos             rope_kv_append
-//   attn = FA(q, K[0..pos], V[0..pos])  (length from device)  fa_decode
-//   delta = Wo . Q8_1(attn)            (TP: all-reduce)       quantize + mat-vec
+//   RoPE(q, k) at pos; k, v -> fp16 cache row pos;
+//   attn = FA(q, K[0..pos], V[0..pos]) (length from device);
+//   Q8_1(attn)                            one fa_mma_kernel (fused), or
+//                                         rope_kv_append + FA + quantize
+//   delta = Wo . Q8_1(attn)            (TP: all-reduce)       mat-vec
 //   x += delta; xq = Q8_1(RMSNorm(x) * ffn_norm)
 //   gu = Wgate_up . xq                 (fused gate|up rows)
 //   delta = Wdown . Q8_1(silu(g) * u)  (TP: all-reduce)       swiglu_q8_1 + mat-vec
@@ -312,11 +314,6 @@ p100_status dec_record_step(Decoder& d, cudaStream_t s) {
         const size_t layer_off = size_t(l) * d.nkv * hs;
         st = dec_rmsnorm(d, l == 0 ? nullptr : d.delta, d.attn_norm[l], s, l > 0 && d.peer_ar);
         if (!st) st = run_qmv(t, d.wqkv[l].ptr, d.wqkv[l].rows, c.hidden, d.xq, 1, d.qkv, P100_QMV_PDL, s);
-        if (!st)
-            st = launch_glue(dec::rope_kv_append_kernel, dim3(d.nq + 2 * d.nkv), dim3(hd / 2), s,
-                             "rope_kv_append_kernel launch", d.qkv, d.nq, d.nkv, hd,
-                             reinterpret_cast<const float2*>(d.rope), c.max_ctx, static_cast<const int*>(d.pos),
-                             d.kcache + layer_off, d.vcache + layer_off, hs);
         if (!st) {
             fa::Params prm = {};
             const FaPlan& plan = d.fa_plan;
@@ -338,16 +335,31 @@ p100_status dec_record_step(Decoder& d, cudaStream_t s) {
             prm.softcap = 0.0f;
             prm.len_dev = d.pos;
             prm.len_add = 1;   // the row appended at pos is part of the context
-            switch (hd) {
-                case 64: st = launch_fa_d<64>(plan, prm, d.nkv, s, true); break;
-                case 128: st = launch_fa_d<128>(plan, prm, d.nkv, s, true); break;
-                default: st = launch_fa_d<256>(plan, prm, d.nkv, s, true); break;
+            const bool fused = fa_use_mma(plan, prm);
+            if (fused) {
+                // RoPE, the KV append and the Q8_1 of the output run inside
+                // the attention kernel (fa::Params, fused decode step)
+                prm.rope_cs = reinterpret_cast<const float2*>(d.rope);
+                prm.nq_total = d.nq;
+                prm.o_q81 = d.xq;
+            } else {
+                st = launch_glue(dec::rope_kv_append_kernel, dim3(d.nq + 2 * d.nkv), dim3(hd / 2), s,
+                                 "rope_kv_append_kernel launch", d.qkv, d.nq, d.nkv, hd,
+                                 reinterpret_cast<const float2*>(d.rope), c.max_ctx, static_cast<const int*>(d.pos),
+                                 d.kcache + layer_off, d.vcache + layer_off, hs);
             }
-        }
-        if (!st) {
-            const int k_o = d.nq * hd;
-            st = launch_glue(q8_1_quantize_kernel, dim3((k_o / 32 + 7) / 8, 1), dim3(256), s,
-                             "q8_1_quantize_kernel launch", static_cast<const float*>(d.attn), d.xq, k_o, k_o / 32);
+            if (!st) {
+                switch (hd) {
+                    case 64: st = launch_fa_d<64>(plan, prm, d.nkv, s, true); break;
+                    case 128: st = launch_fa_d<128>(plan, prm, d.nkv, s, true); break;
+                    default: st = launch_fa_d<256>(plan, prm, d.nkv, s, true); break;
+                }
+            }
+            if (!st && !fused) {
+                const int k_o = d.nq * hd;
+                st = launch_glue(q8_1_quantize_kernel, dim3((k_o / 32 + 7) / 8, 1), dim3(256), s,
+                                 "q8_1_quantize_kernel launch", static_cast<const float*>(d.attn), d.xq, k_o, k_o / 32);
+            }
         }
         if (!st) st = run_qmv(t, d.wo[l].ptr, c.hidden, d.nq * hd, d.xq, 1, d.delta, P100_QMV_PDL, s);
         if (!st) st = dec_allreduce(d, s);

@@ -19,6 +19,7 @@
 // log(den) (attention_tiled_model.cpp:183-222, fattn-common.cuh:963-977).
 #pragma once
 #include "common.cuh"
+#include "quant.cuh"
 
 namespace p100b {
 namespace fa {
@@ -45,6 +46,16 @@ struct Params {
     // seq keys, streamed before the wait.
     const int* len_dev;
     int len_add;
+    // Fused decode step (fa_mma_kernel only; null otherwise): q points at the
+    // raw fused QKV row [nq_total q heads | nkv k heads | nkv v heads] of
+    // position pos = *len_dev; every CTA rotates its query heads by
+    // rope_cs[pos] ((cos, sin) per adjacent pair, as rope_kv_append_kernel
+    // does), the CTA of the last part rotates the kv head's k row and stores
+    // it and the v row as fp16 into cache row pos before it reads K/V, and the
+    // context is keys [0, pos].  o_q81, if set, receives o as Q8_1 blocks.
+    const float2* rope_cs;
+    int nq_total;
+    uint8_t* o_q81;
 };
 
 __device__ __forceinline__ void half8_to_float(const uint4 v, float (&f)[8]) {
@@ -62,7 +73,7 @@ __device__ __forceinline__ void half8_to_float(const uint4 v, float (&f)[8]) {
 // 183-222: M = max m_p, den = sum_p exp(m_p - M) l_p, o = sum_p exp(m_p - M)
 // O_p / den over parts in order (parts with l = 0 skipped).  All (m, l) are
 // loaded at once and the weights kept in shared memory (scratch: at least
-// 2 * parts * G + 2 * G floats), so the only loop over parts with global
+// 2 * parts * G + 2 * G + G * D floats), so the only loop over parts with global
 // loads is the last, unrolled so its loads are in flight together.
 template <int THREADS>
 __device__ __forceinline__ void merge_parts(const Params& p, int bk, int G, int D, size_t row0, float* scratch) {
@@ -97,6 +108,7 @@ __device__ __forceinline__ void merge_parts(const Params& p, int bk, int G, int 
         s_pm[i] = s_pl[i] == 0.f ? 0.f : expf(s_pm[i] - s_gm[h]);
     }
     __syncthreads();
+    float* s_out = s_den + G;         // [G][D] the merged o, for the Q8_1 epilogue
     for (int i = tid; i < G * D; i += THREADS) {
         const int h = i / D;
         float num = 0.f;
@@ -107,9 +119,16 @@ __device__ __forceinline__ void merge_parts(const Params& p, int bk, int G, int 
             if (s_pl[q * G + h] != 0.f) num = fmaf(w, v, num);
         }
         const float den = s_den[h];
-        p.o[(row0 + h) * D + (i % D)] = den == 0.f ? 0.f : num / den;
+        const float o = den == 0.f ? 0.f : num / den;
+        p.o[(row0 + h) * D + (i % D)] = o;
+        s_out[i] = o;
     }
     if (tid == 0) p.tickets[bk] = 0;   // ready for the next call
+    if (p.o_q81) {
+        __syncthreads();
+        for (int j = tid >> 5; j < G * D / 32; j += THREADS / 32)
+            warp_q8_1_block(s_out[j * 32 + (tid & 31)], tid & 31, p.o_q81 + (row0 * D / 32 + j) * 36);
+    }
 }
 
 template <int D, int GMAX>

@@ -91,8 +91,16 @@ __global__ void __launch_bounds__(kThreads, 1) fa_mma_kernel(const fa::Params p)
     const int g = lane >> 2, t = lane & 3;
     const int bk = blockIdx.y, part = blockIdx.x;
     const int b = bk / p.nkv, kvh = bk % p.nkv;
-    int seq = p.seq;
-    if (p.len_dev) {
+    int seq = p.seq, pos = -1;
+    if (p.rope_cs) {   // fused decode step: keys [0, pos], pos device-resident
+        pdl_wait_prior_grid();
+        pos = *p.len_dev;
+        if (pos < 0 || pos >= p.seq) {
+            if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0) atomicExch(&g_device_error, kDevErrInput);
+            pos = -1;
+        }
+        seq = pos + 1;
+    } else if (p.len_dev) {
         pdl_wait_prior_grid();
         seq = min(max(*p.len_dev + p.len_add, 0), p.seq);
     }
@@ -127,13 +135,42 @@ __global__ void __launch_bounds__(kThreads, 1) fa_mma_kernel(const fa::Params p)
         for (int s = 0; s < NS - 1; ++s) issue(s);   // K/V never come from the previous kernel here
     pdl_allow_dependents();
     pdl_wait_prior_grid();
+    if (p.rope_cs && pos >= 0 && part == p.parts - 1) {
+        // the new row: rotated k and v of this kv head into cache row pos
+        // (only this part's key range reaches pos), visible before any copy
+        const float* kr = p.q + (size_t(p.nq_total) + kvh) * D;
+        const float* vr = p.q + (size_t(p.nq_total) + p.nkv + kvh) * D;
+        for (int i = tid; i < D / 2; i += kThreads) {
+            const float2 t = p.rope_cs[size_t(pos) * (D / 2) + i];
+            const float x0 = kr[2 * i], x1 = kr[2 * i + 1];
+            const float y0 = __fsub_rn(__fmul_rn(x0, t.x), __fmul_rn(x1, t.y));
+            const float y1 = __fadd_rn(__fmul_rn(x0, t.y), __fmul_rn(x1, t.x));
+            *reinterpret_cast<__half2*>(const_cast<__half*>(kbase) + size_t(pos) * D + 2 * i) =
+                __halves2half2(__float2half_rn(y0), __float2half_rn(y1));
+            *reinterpret_cast<__half2*>(const_cast<__half*>(vbase) + size_t(pos) * D + 2 * i) =
+                __halves2half2(__float2half_rn(vr[2 * i]), __float2half_rn(vr[2 * i + 1]));
+        }
+        __threadfence();
+        __syncthreads();
+    }
     if (p.len_dev)
         for (int s = 0; s < NS - 1; ++s) issue(s);
 
     // ---- queries: q * scale per head, scaled by a power of two 2^e so the
     // largest |entry| lies in [2^13, 2^14)
     const float* qg = p.q + (size_t(b) * p.nkv * G + size_t(kvh) * G) * D;
-    for (int i = tid; i < G * D; i += kThreads) s_q[i] = qg[i] * p.scale;
+    if (p.rope_cs) {   // rotate the raw q pairs (rope_kv_append_kernel's arithmetic)
+        const int pr = pos >= 0 ? pos : 0;
+        for (int i = tid; i < G * D / 2; i += kThreads) {
+            const int h = i / (D / 2), pi = i % (D / 2);
+            const float2 t = p.rope_cs[size_t(pr) * (D / 2) + pi];
+            const float x0 = qg[h * D + 2 * pi], x1 = qg[h * D + 2 * pi + 1];
+            s_q[h * D + 2 * pi] = __fsub_rn(__fmul_rn(x0, t.x), __fmul_rn(x1, t.y)) * p.scale;
+            s_q[h * D + 2 * pi + 1] = __fadd_rn(__fmul_rn(x0, t.y), __fmul_rn(x1, t.x)) * p.scale;
+        }
+    } else {
+        for (int i = tid; i < G * D; i += kThreads) s_q[i] = qg[i] * p.scale;
+    }
     __syncthreads();
     for (int h = warp; h < G; h += kWarps) {
         float m = 0.f;
@@ -325,8 +362,15 @@ __global__ void __launch_bounds__(kThreads, 1) fa_mma_kernel(const fa::Params p)
         for (int i = tid; i < G * D; i += kThreads) {
             const int h = i / D, d = i % D;
             const float l = s_l[h];
-            p.o[(row0 + h) * D + d] = l == 0.f ? 0.f : red[i] / l;
+            const float o = l == 0.f ? 0.f : red[i] / l;
+            p.o[(row0 + h) * D + d] = o;
+            red[i] = o;
             if (d == 0 && p.lse) p.lse[row0 + h] = l == 0.f ? -INFINITY : s_m[h] + logf(l);
+        }
+        if (p.o_q81) {
+            __syncthreads();
+            for (int j = warp; j < G * D / 32; j += kWarps)
+                warp_q8_1_block(red[j * 32 + lane], lane, p.o_q81 + (row0 * D / 32 + j) * 36);
         }
         return;
     }

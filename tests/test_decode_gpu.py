@@ -124,9 +124,16 @@ def read_model(dec, cfg):
     return w
 
 
-@pytest.mark.parametrize("wtype", [P.Q4_0, P.Q8_0, P.Q4_K])
-def test_decoder_matches_restated_steps(cuda, orc, wtype):
-    cfg = P.LlamaConfig(**TINY, wtype=wtype)
+# head_dim 256 takes the SIMT attention kernel, so its decoder runs RoPE/append
+# and the output quantisation as separate kernels; the others fuse them into
+# the tensor-core attention kernel.
+TINY_D256 = dict(TINY, n_head=2, n_head_kv=1, head_dim=256)
+
+
+@pytest.mark.parametrize("wtype,shape", [(P.Q4_0, TINY), (P.Q8_0, TINY), (P.Q4_K, TINY), (P.Q4_0, TINY_D256)],
+                         ids=["q4_0", "q8_0", "q4_k", "q4_0-d256-unfused"])
+def test_decoder_matches_restated_steps(cuda, orc, wtype, shape):
+    cfg = P.LlamaConfig(**shape, wtype=wtype)
     ocfg = oracle.LlamaConfig(*[getattr(cfg, f) for f, _ in oracle.LlamaConfig._fields_])
     dec = P.Decoder(cfg)
     try:
