@@ -332,8 +332,8 @@ def decode_section(torch, P, stream, rank, world, dist, max_over_ranks):
 
 def kernel_only(args):
     """Eager launches of one kernel over rotating inputs larger than L2 — the
-    small cases for ncu captures: the target mat-vec (5 weight copies, 165 MB)
-    or FA decode at 32K context (2 K/V copies, 268 MB)."""
+    small cases for ncu captures: the target mat-vec at batch 1 or 16 (5 weight
+    copies, 165 MB) or FA decode at 32K context (2 K/V copies, 268 MB)."""
     import torch
     import p100_b200 as P
     if args.kernel_only == "decode":
@@ -367,15 +367,16 @@ def kernel_only(args):
         print(json.dumps({"kernel_only": f"fa_decode 32/8 heads d128 ctx {seq}", "launches": args.warmup + args.steps}))
         return 0
     _, k, rows = TARGET
+    batch = 16 if args.kernel_only == "qmvb" else 1
     base = torch.from_numpy(W.weights(W.Q4_0, rows, k, seed=1)).cuda()
     ws = [base] + [base.clone() for _ in range(4)]
-    xq = P.q8_1_quantize(torch.from_numpy(W.activations(1, k, seed=2)).cuda())
-    y = torch.empty(1, rows, device="cuda")
+    xq = P.q8_1_quantize(torch.from_numpy(W.activations(batch, k, seed=2)).cuda())
+    y = torch.empty(batch, rows, device="cuda")
     for i in range(args.warmup + args.steps):
-        P.qmv(W.Q4_0, ws[i % len(ws)], rows, k, xq, 1, y=y)
+        P.qmv(W.Q4_0, ws[i % len(ws)], rows, k, xq, batch, y=y)
     torch.cuda.synchronize()
     P.check(P.device_error())
-    print(json.dumps({"kernel_only": f"qmv Q4_0 {k}x{rows}", "launches": args.warmup + args.steps}))
+    print(json.dumps({"kernel_only": f"qmv Q4_0 {k}x{rows} batch {batch}", "launches": args.warmup + args.steps}))
     return 0
 
 
@@ -387,7 +388,8 @@ def main():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the 8B/70B decode section")
-    ap.add_argument("--kernel-only", choices=["qmv", "fa", "decode"], help="one kernel's launches only (ncu cases)")
+    ap.add_argument("--kernel-only", choices=["qmv", "qmvb", "fa", "decode"],
+                    help="one kernel's launches only (ncu cases); qmvb = the target shape at batch 16")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))

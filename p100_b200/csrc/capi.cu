@@ -18,6 +18,7 @@
 #include "fa_decode.cuh"
 #include "fa_mma.cuh"
 #include "qmv.cuh"
+#include "qmv_mma.cuh"
 #include "qmv_team.cuh"
 #include "quant.cuh"
 
@@ -244,6 +245,180 @@ p100_status launch_team_type(const TeamPlan& plan, int batch, bool pdl, cudaStre
     }
 }
 
+// ------------------------------------------------------------------ batched plan
+using MmaKernel = void (*)(qmvm::Params);
+
+MmaKernel mma_kernel(int type, int bpw) {
+#define P100_MMA_CASES(T)                                \
+    switch (bpw) {                                       \
+        case 2: return qmvm::qmv_mma_kernel<T, 2>;       \
+        case 4: return qmvm::qmv_mma_kernel<T, 4>;       \
+        case 8: return qmvm::qmv_mma_kernel<T, 8>;       \
+        case 16: return qmvm::qmv_mma_kernel<T, 16>;     \
+        case 32: return qmvm::qmv_mma_kernel<T, 32>;     \
+        default: return nullptr;                         \
+    }
+    switch (type) {
+        case P100_Q4_0: P100_MMA_CASES(P100_Q4_0)
+        case P100_Q8_0: P100_MMA_CASES(P100_Q8_0)
+        default:
+            switch (bpw) {
+                case 8: return qmvm::qmv_mma_kernel<P100_Q4_K, 8>;
+                case 16: return qmvm::qmv_mma_kernel<P100_Q4_K, 16>;
+                case 32: return qmvm::qmv_mma_kernel<P100_Q4_K, 32>;
+                default: return nullptr;
+            }
+    }
+#undef P100_MMA_CASES
+}
+
+// The largest dynamic shared memory on every batched kernel, once per device;
+// for a K split also the number of S-CTA clusters that fit the GPU at once.
+bool mma_prepare(MmaKernel kern, int slices, int threads, int* max_clusters) {
+    struct Entry { int dev; MmaKernel kern; int slices, threads, clusters; };
+    static std::mutex mu;
+    static std::vector<Entry> cache;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return false;
+    std::lock_guard<std::mutex> lock(mu);
+    bool attr_done = false;
+    for (const Entry& e : cache) {
+        if (e.dev != dev || e.kern != kern) continue;
+        attr_done = true;
+        if (e.slices == slices && e.threads == threads) {
+            *max_clusters = e.clusters;
+            return true;
+        }
+    }
+    if (!attr_done &&
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, qmvm::kSmemLimit) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return false;
+    }
+    int clusters = 0;
+    if (slices > 1) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(slices);
+        cfg.blockDim = dim3(threads);
+        cfg.dynamicSmemBytes = qmvm::kSmemLimit;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = slices;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess) {
+            (void)cudaGetLastError();
+            clusters = 0;
+        }
+    }
+    cache.push_back({dev, kern, slices, threads, clusters});
+    *max_clusters = clusters;
+    return true;
+}
+
+struct MmaPlan {
+    qmvm::Params p;
+    MmaKernel kern = nullptr;
+    int grid = 0, threads = 0;
+    size_t smem = 0;
+};
+
+// Batch 2..16 on the tensor cores (every type): 16-byte aligned weights and
+// activations, k % 256 == 0.  Picks the fewest K slices (CTAs per cluster),
+// then the most consumer warps, whose per-warp share of blocks is compiled
+// in and whose layout fits: two ring slots ahead of the activations.
+bool plan_mma(int type, const void* w, const void* xq, int rows, int k, int batch, int sms, MmaPlan& plan) {
+    if (batch < 2 || batch > 16 || !known_type(type)) return false;
+    if (reinterpret_cast<uintptr_t>(w) % 16 || reinterpret_cast<uintptr_t>(xq) % 16 || k % 256) return false;
+    const int nb = k / 32;
+    const size_t row_bytes = size_t(k / elems_of(type)) * bytes_of(type);
+    const int rows_per_stage = 8 * qmvm::stage_tiles(type);
+    for (int slices : {1, 2, 4, 8}) {
+        for (int nw = qmvm::kMaxConsumers; nw >= 4; --nw) {
+            if (nb % (slices * nw)) continue;
+            const int bpw = nb / (slices * nw);
+            const int nbs = nw * bpw;
+            const size_t slice = size_t(qmvm::slice_bytes_of(type, nbs));
+            if (slice % 16 || (size_t(nbs) * 36) % 16) continue;
+            const MmaKernel kern = mma_kernel(type, bpw);
+            if (!kern) continue;
+            const int threads = (nw + 1) * 32;
+            if (threads > qmvm::max_threads(bpw)) continue;
+            int max_clusters = 0;
+            if (!mma_prepare(kern, slices, threads, &max_clusters)) continue;
+            int nrb = (rows + rows_per_stage - 1) / rows_per_stage;
+            nrb = std::min(nrb, slices == 1 ? sms : max_clusters);
+            if (nrb < 1) continue;
+            const size_t row_stride = slice + 16;   // padded: rows in distinct banks
+            const size_t slot = round128(size_t(rows_per_stage) * row_stride);
+            const size_t act_stride = size_t(nbs) * 36 + 16;
+            const size_t act_bytes = size_t(batch) * act_stride;
+            const size_t dm_off = 256;                                   // 2 x 8 ring mbarriers + 2
+            const size_t part_off = dm_off + size_t(nbs) * 16 * 16;
+            const size_t res_off = part_off + size_t(2) * nw * rows_per_stage * qmvm::kPartStride * 4;
+            const size_t res_bytes = slices > 1 ? size_t((rows + nrb - 1) / nrb) * 16 * 4 : 0;
+            const size_t scr_off = res_off + round128(res_bytes);
+            const size_t scr_bytes = type == P100_Q4_K ? size_t(nw) * qmvm::stage_tiles(type) * 32 * 16 : 0;
+            const size_t ring_off = round128(scr_off + scr_bytes);
+            if (ring_off + 3 * slot > size_t(qmvm::kSmemLimit)) continue;
+            const int nslot = int(std::min<size_t>(qmvm::kMaxSlots, (qmvm::kSmemLimit - ring_off) / slot));
+            const int act_slot = nslot - int((act_bytes + slot - 1) / slot);
+            if (act_slot < 2) continue;   // the first two stages go ahead of the activations
+            qmvm::Params& p = plan.p;
+            p.rows = rows;
+            p.k = k;
+            p.batch = batch;
+            p.consumers = nw;
+            p.slices = slices;
+            p.row_bytes = int(row_bytes);
+            p.slice_bytes = int(slice);
+            p.row_stride = int(row_stride);
+            p.act_stride = int(act_stride);
+            p.nslot = nslot;
+            p.slot_bytes = int(slot);
+            p.act_slot = act_slot;
+            p.dm_off = int(dm_off);
+            p.part_off = int(part_off);
+            p.res_off = int(res_off);
+            p.scr_off = int(scr_off);
+            p.ring_off = int(ring_off);
+            plan.kern = kern;
+            plan.grid = nrb * slices;
+            plan.threads = threads;
+            plan.smem = ring_off + size_t(nslot) * slot;
+            return true;
+        }
+    }
+    return false;
+}
+
+p100_status launch_mma(const MmaPlan& plan, bool pdl, cudaStream_t stream) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(plan.grid);
+    cfg.blockDim = dim3(plan.threads);
+    cfg.dynamicSmemBytes = plan.smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    int n = 0;
+    if (pdl) {
+        attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[n].val.programmaticStreamSerializationAllowed = 1;
+        ++n;
+    }
+    if (plan.p.slices > 1) {
+        attr[n].id = cudaLaunchAttributeClusterDimension;
+        attr[n].val.clusterDim.x = plan.p.slices;
+        attr[n].val.clusterDim.y = 1;
+        attr[n].val.clusterDim.z = 1;
+        ++n;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = n;
+    return cuda_status(cudaLaunchKernelEx(&cfg, plan.kern, plan.p), "qmv_mma_kernel launch");
+}
+
 p100_status run_qmv(int type, const void* w, int rows, int k, const void* xq, int batch, float* y, unsigned flags,
                     cudaStream_t stream) {
     if (!known_type(type)) return set_error(P100_ERR_INVALID, "unknown weight type %d", type);
@@ -268,6 +443,13 @@ p100_status run_qmv(int type, const void* w, int rows, int k, const void* xq, in
             case P100_Q8_0: return launch_team_type<P100_Q8_0>(tplan, batch, pdl, stream);
             default: return launch_team_type<P100_Q4_K>(tplan, batch, pdl, stream);
         }
+    }
+    MmaPlan mplan;
+    if (plan_mma(type, w, xq, rows, k, batch, sms, mplan)) {
+        mplan.p.w = static_cast<const uint8_t*>(w);
+        mplan.p.xq = static_cast<const uint8_t*>(xq);
+        mplan.p.y = y;
+        return launch_mma(mplan, pdl, stream);
     }
     QmvPlan plan;
     if (plan_bulk(type, w, rows, k, batch, sms, plan)) {

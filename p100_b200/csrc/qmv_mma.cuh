@@ -1,0 +1,469 @@
+// qmv_mma.cuh — batch 2..16 quantised mat-vec on the tensor cores:
+// mma.sync m16n8k32 (int8 x int8 -> int32), the batch columns as the M rows of
+// A, 8 weight rows as the N columns of B, one 32-element block (a Q4_0/Q8_0
+// block, a Q4_K sub-block) as K = 32.
+//
+// Why this form: a K = 32 step is exactly one scale block, so the int32
+// result of a step is that block's integer dot for 16 columns x 8 rows, and
+// the FP32 scaling of qmv::evaluate's q81 path (qmv_model.cpp:147-180) is
+// applied per step in registers.  The B fragment a thread holds (elements
+// 4t..4t+3 and 4t+16..4t+19 of one row) is the low and the high nibbles of
+// one 32-bit word of a Q4_0 block (the low nibbles of two words of a Q4_K
+// chunk), so B is unpacked in registers and weights touch shared memory once,
+// as the bulk copies wrote them.  (tcgen05 takes B from shared memory or TMEM
+// only, so 4-bit weights would have to be unpacked into shared memory first;
+// with the per-block scale epilogue that round trip costs more than the
+// weight stream at 16 columns.)
+//
+// Epilogue arithmetic per block and output: the int32 accumulators start at
+// the bits of 1.5 * 2^23, so the mma leaves the float 1.5 * 2^23 + dot
+// (exact for |dot| < 2^22); one packed f32x2 add recovers float(dot) for two
+// outputs, and packed f32x2 FMAs apply the activation and weight scales.
+//
+// Layout: one producer warp streams stages of whole rows (16 Q4_0/Q4_K or 8
+// Q8_0 rows, stage_tiles below) with one bulk copy per row into an mbarrier
+// ring; rows land row_stride = bytes + 16 apart so that the 8 rows an mma
+// reads sit in distinct banks.  The batch's Q8_1 rows are copied once (after
+// the PDL wait) into the last ring slots: the consumers move them into
+// registers and a per-block scale table, then release those slots to the
+// ring.  Each consumer warp owns a contiguous share of the K blocks: its
+// activation fragments stay in registers for the whole launch; per stage it
+// accumulates the stage's rows x 16 columns, writes them to shared memory,
+// and after a barrier the partials are added in warp order: deterministic.
+//
+// Long rows (k = 14336, 28672 at batch 16) do not fit one CTA's shared
+// memory: the K range is then split over the CTAs of a thread-block cluster
+// (one slice each, the same rows), and after the last stage each CTA sums
+// its share of the rows over the slices through distributed shared memory,
+// in slice order.
+#pragma once
+#include "common.cuh"
+
+namespace p100b {
+namespace qmvm {
+
+constexpr int kMaxConsumers = 8;
+constexpr int kMaxThreads = (kMaxConsumers + 1) * 32;
+constexpr int kMaxSlots = 8;
+constexpr int kSmemLimit = 227 * 1024;
+constexpr int kLookahead = 2;          // stages in flight past the newest landed one
+constexpr int kMaxBlocksPerWarp = 32;  // register-resident activation fragments
+// Row pitch (floats) of the per-warp partials: rows 2t of the mma results
+// fall in distinct banks for t = 0..3.
+constexpr int kPartStride = 20;
+constexpr uint32_t kBiasBits = 0x4B400000u;   // 1.5 * 2^23 as a float
+constexpr float kBias = 12582912.0f;
+
+// n-tiles of 8 weight rows per stage: about 36 KB of weights per stage at
+// k = 4096 for every type (16 Q4_0/Q4_K rows, 8 Q8_0 rows).
+__host__ __device__ constexpr int stage_tiles(int type) { return type == P100_Q8_0 ? 1 : 2; }
+
+// Bytes of `blocks` 32-element K blocks of one row.
+__host__ __device__ constexpr int slice_bytes_of(int type, int blocks) {
+    return type == P100_Q4_0 ? blocks * 18 : type == P100_Q8_0 ? blocks * 34 : blocks / 8 * 144;
+}
+
+struct Params {
+    const uint8_t* w;
+    const uint8_t* xq;
+    float* y;
+    int rows, k, batch;
+    int consumers;     // consumer warps; warp `consumers` is the producer
+    int slices;        // K slices = CTAs per cluster (1: no split)
+    int row_bytes;     // one row in global memory
+    int slice_bytes;   // one row's K slice
+    int row_stride;    // stage row pitch: slice_bytes + 16
+    int act_stride;    // one column's Q8_1 slice + 16
+    int nslot, slot_bytes, act_slot;   // the activations overlay slots [act_slot, nslot)
+    int dm_off, part_off, res_off, scr_off, ring_off;
+};
+
+// ------------------------------------------------------------ packed f32x2
+__device__ __forceinline__ uint64_t pk(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ uint64_t pk_bits(int lo, int hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
+    return r;
+}
+__device__ __forceinline__ float2 unpk(uint64_t v) {
+    float2 r;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+    return r;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+
+// D = A(16x32 s8) * B(32x8, u8 nibbles or s8 codes) + C, int32
+template <bool B_U8>
+__device__ __forceinline__ void mma_i8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    if (B_U8) {
+        asm volatile(
+            "mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+    } else {
+        asm volatile(
+            "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+    }
+}
+
+// acc(col, rows r, r+1) += w(r, r+1) * fma(dot, d8, m): the Q4_0 / Q8_0 step
+// (qmv_model.cpp:151-161; m = -8 * fp16 sum for Q4_0, 0 for Q8_0).  `biased`
+// holds 1.5 * 2^23 + dot for the two rows; dm = {d8, d8, m, m}.
+__device__ __forceinline__ void scale_step(uint64_t& acc, int biased0, int biased1, const float4& dm, uint64_t w,
+                                           uint64_t nbias) {
+    uint64_t v = add2(pk_bits(biased0, biased1), nbias);
+    v = fma2(v, pk(dm.x, dm.y), pk(dm.z, dm.w));
+    acc = fma2(v, w, acc);
+}
+
+// The Q4_K step (qmv_model.cpp:163-179): acc += (d*sc) * d8 * dot
+// - (dmin*mn) * (d8 * sum of codes); dm = {d8, d8, s, s}, sc = {d*sc(r),
+// d*sc(r+1), -dmin*mn(r), -dmin*mn(r+1)}.
+__device__ __forceinline__ void scale_step_k(uint64_t& acc, int biased0, int biased1, const float4& dm,
+                                             const float4& sc, uint64_t nbias) {
+    uint64_t v = add2(pk_bits(biased0, biased1), nbias);
+    v = mul2(v, pk(dm.x, dm.y));
+    acc = fma2(v, pk(sc.x, sc.y), acc);
+    acc = fma2(pk(dm.z, dm.w), pk(sc.z, sc.w), acc);
+}
+
+// Six-bit scale and min of Q4_K sub-block j (the get_scale_min_k4 rule of
+// qmv_model.cpp:72-77) from the super-block header words h (d/dmin, then the
+// 12 packed scale bytes), times d and dmin.
+__device__ __forceinline__ void q4k_sub_scale(const uint4& h, int j, float& dsc, float& dmn) {
+    int sc, mn;
+    if (j < 4) {
+        sc = (h.y >> (8 * j)) & 63;
+        mn = (h.z >> (8 * j)) & 63;
+    } else {
+        const int s = 8 * (j - 4);
+        sc = ((h.w >> s) & 15) | (((h.y >> (s + 6)) & 3) << 4);
+        mn = ((h.w >> (s + 4)) & 15) | (((h.z >> (s + 6)) & 3) << 4);
+    }
+    dsc = half_lo(h.x) * float(sc);
+    dmn = half_hi(h.x) * float(mn);
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+
+__device__ __forceinline__ float ld_cluster_f32(const float* local, int rank) {
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_addr(local)), "r"(rank));
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+    return v;
+}
+
+// Threads a block of the BPW kernel may have: with 9 warps one SM sub-partition
+// holds three of them, which caps a thread at 168 registers; BPW = 32 (128
+// registers of activation fragments) runs with at most 7 consumer warps.
+__host__ __device__ constexpr int max_threads(int bpw) { return bpw >= 32 ? 256 : kMaxThreads; }
+
+// BPW = 32-element K blocks per consumer warp: even; a multiple of 8 (whole
+// super-blocks) for Q4_K.
+template <int TYPE, int BPW>
+__global__ void __launch_bounds__(max_threads(BPW), 1) qmv_mma_kernel(const Params p) {
+    static_assert(BPW % 2 == 0 && BPW <= kMaxBlocksPerWarp, "blocks per warp");
+    static_assert(TYPE != P100_Q4_K || BPW % 8 == 0, "whole Q4_K super-blocks per warp");
+    constexpr int kBlk = TYPE == P100_Q4_0 ? 18 : 34;
+    constexpr int kPairWords = kBlk / 2;     // 32-bit words per pair of Q4_0/Q8_0 blocks (9 or 17)
+    constexpr int kNT = stage_tiles(TYPE);
+    constexpr int kRows = 8 * kNT;
+    constexpr bool kNibbles = TYPE != P100_Q8_0;
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+    uint64_t* empty = full + kMaxSlots;
+    uint64_t* act_bar = empty + kMaxSlots;
+    uint64_t* act_free = act_bar + 1;
+    float4* dm = reinterpret_cast<float4*>(smem + p.dm_off);     // [slice blocks][16 cols]
+    float* part = reinterpret_cast<float*>(smem + p.part_off);   // [2][consumers][kRows][kPartStride]
+    float* res = reinterpret_cast<float*>(smem + p.res_off);     // [rows of this CTA][16]: K split only
+    uint8_t* ring = smem + p.ring_off;
+    uint8_t* act = ring + size_t(p.act_slot) * p.slot_bytes;     // [batch][act_stride]
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int g = lane >> 2, t = lane & 3;
+    const int nw = p.consumers, nct = nw * 32;
+    const int nbs = nw * BPW;                                    // 32-blocks in this CTA's K slice
+    const int slice = static_cast<int>(blockIdx.x) % p.slices;  // the cluster rank
+    const int nrb = static_cast<int>(gridDim.x) / p.slices, rb = static_cast<int>(blockIdx.x) / p.slices;
+    const int r0 = static_cast<int>(static_cast<long long>(p.rows) * rb / nrb);
+    const int r1 = static_cast<int>(static_cast<long long>(p.rows) * (rb + 1) / nrb);
+    const int nst = (r1 - r0 + kRows - 1) / kRows;
+
+    if (tid == 0) {
+        for (int s = 0; s < p.nslot; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], nw);
+        }
+        mbar_init(act_bar, 1);
+        mbar_init(act_free, nw);
+        fence_barrier_init();
+    }
+    __syncthreads();
+    pdl_allow_dependents();
+
+    if (warp == nw) {
+        // ---- producer: the batch-1 team kernel's ring and lookahead, one
+        // bulk copy per row (its lane), the activations after the PDL wait.
+        const uint64_t policy = l2_evict_first_policy();
+        const int look = min(kLookahead, p.nslot - 1);
+        const uint8_t* wslice = p.w + size_t(slice) * p.slice_bytes;
+        auto issue = [&](int s) {
+            const int slot = s % p.nslot;
+            const int first = r0 + s * kRows;
+            const int n = min(kRows, r1 - first);
+            if (lane == 0) mbar_arrive_expect_tx(&full[slot], static_cast<uint32_t>(n * p.slice_bytes));
+            __syncwarp();
+            if (lane < n)
+                bulk_load(ring + size_t(slot) * p.slot_bytes + size_t(lane) * p.row_stride,
+                          wslice + size_t(first + lane) * p.row_bytes, p.slice_bytes, &full[slot], policy);
+        };
+        const int pre = min(look, nst);
+        for (int s = 0; s < pre; ++s) issue(s);
+        pdl_wait_prior_grid();   // the activations may come from the previous kernel
+        if (lane == 0) {
+            asm volatile("fence.proxy.async.global;" ::: "memory");
+            mbar_arrive_expect_tx(act_bar, static_cast<uint32_t>(p.batch * nbs * 36));
+        }
+        __syncwarp();
+        if (lane < p.batch)
+            bulk_load(act + size_t(lane) * p.act_stride, p.xq + (size_t(lane) * (p.k / 32) + size_t(slice) * nbs) * 36,
+                      static_cast<uint32_t>(nbs * 36), act_bar, policy);
+        int issued = pre;
+        for (int s = pre; s < nst; ++s) {
+            bool ok = mbar_wait(&full[(s - look) % p.nslot], ((s - look) / p.nslot) & 1);
+            if (ok && s >= p.nslot) ok = mbar_wait(&empty[s % p.nslot], ((s / p.nslot) - 1) & 1);
+            if (ok && s == p.act_slot) ok = mbar_wait(act_free, 0);   // first use of the activation slots
+            if (__any_sync(0xffffffffu, !ok)) break;
+            issue(s);
+            issued = s + 1;
+        }
+        if (lane == 0) {   // no copy in flight when the block exits
+            mbar_wait(act_bar, 0);
+            for (int s = max(0, issued - p.nslot); s < issued; ++s) mbar_wait(&full[s % p.nslot], (s / p.nslot) & 1);
+        }
+        __syncwarp();
+        if (p.slices == 1) return;
+    } else {
+        // ---- consumers.  A timeout is decided for all consumer warps at
+        // once: they meet at barrier 1 every stage.
+        auto any_of_consumers = [&](bool v) {
+            int r;
+            asm volatile(
+                "{\n\t.reg .pred p, q;\n\t"
+                "setp.ne.u32 p, %1, 0;\n\t"
+                "bar.red.or.pred q, 15, %2, p;\n\t"
+                "selp.u32 %0, 1, 0, q;\n\t}"
+                : "=r"(r)
+                : "r"(static_cast<unsigned>(v)), "r"(nct)
+                : "memory");
+            return r != 0;
+        };
+        const bool failed = any_of_consumers(!mbar_wait(act_bar, 0));
+        const uint64_t nbias = pk(-kBias, -kBias);
+        const int kb0 = warp * BPW;   // this warp's first block in the slice
+        uint32_t a[BPW][4];
+        if (!failed) {
+            // {d8, d8, m, m} per block and column (columns >= batch zero)
+            for (int i = tid; i < nbs * 16; i += nct) {
+                const int b = i >> 4, c = i & 15;
+                float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (c < p.batch) {
+                    const uint32_t* blk = reinterpret_cast<const uint32_t*>(act + size_t(c) * p.act_stride + b * 36);
+                    const float d8 = half_lo(blk[0]);
+                    float m = 0.f;
+                    if (TYPE == P100_Q4_0) m = -8.0f * half_hi(blk[0]);
+                    if (TYPE == P100_Q4_K) {
+                        int sq = 0;
+#pragma unroll
+                        for (int q = 1; q <= 8; ++q) sq = __dp4a(static_cast<int>(blk[q]), 0x01010101, sq);
+                        m = d8 * float(sq);
+                    }
+                    v = make_float4(d8, d8, m, m);
+                }
+                dm[i] = v;
+            }
+#pragma unroll
+            for (int j = 0; j < BPW; ++j) {
+                const uint32_t* c_lo =
+                    reinterpret_cast<const uint32_t*>(act + size_t(g) * p.act_stride + (kb0 + j) * 36 + 4);
+                const uint32_t* c_hi =
+                    reinterpret_cast<const uint32_t*>(act + size_t(g + 8) * p.act_stride + (kb0 + j) * 36 + 4);
+                a[j][0] = g < p.batch ? c_lo[t] : 0u;
+                a[j][2] = g < p.batch ? c_lo[t + 4] : 0u;
+                a[j][1] = g + 8 < p.batch ? c_hi[t] : 0u;
+                a[j][3] = g + 8 < p.batch ? c_hi[t + 4] : 0u;
+            }
+        }
+        asm volatile("bar.sync 1, %0;" ::"r"(nct) : "memory");   // dm complete, activations read
+        if (lane == 0) mbar_arrive(act_free);
+
+        float4* scr = reinterpret_cast<float4*>(smem + p.scr_off) + warp * (kNT * 32);   // Q4_K: [kNT][8 sub][4 t]
+        for (int s = 0; s < (failed ? 0 : nst); ++s) {
+            const int slot = s % p.nslot;
+            if (any_of_consumers(!mbar_wait(&full[slot], (s / p.nslot) & 1))) break;
+            const uint8_t* stage = ring + size_t(slot) * p.slot_bytes;
+            uint64_t acc[kNT][2];
+#pragma unroll
+            for (int nt = 0; nt < kNT; ++nt) acc[nt][0] = acc[nt][1] = 0ull;
+            if constexpr (TYPE != P100_Q4_K) {
+#pragma unroll
+                for (int jp = 0; jp < BPW / 2; ++jp) {
+                    const int b = kb0 + 2 * jp;   // even: the pair starts 4-byte aligned
+                    const float4 dmA0 = dm[b * 16 + g], dmA1 = dm[b * 16 + g + 8];
+                    const float4 dmB0 = dm[(b + 1) * 16 + g], dmB1 = dm[(b + 1) * 16 + g + 8];
+#pragma unroll
+                    for (int nt = 0; nt < kNT; ++nt) {
+                        // B fragments: weight row nt*8 + g of the stage
+                        const uint32_t* pw = reinterpret_cast<const uint32_t*>(
+                            stage + size_t(nt * 8 + g) * p.row_stride + size_t(b) * kBlk);
+                        uint32_t bA0, bA1, bB0, bB1;
+                        if (TYPE == P100_Q4_0) {
+                            const uint32_t nA = shift2(pw[t], pw[t + 1]), nB = pw[5 + t];
+                            bA0 = nA & 0x0f0f0f0fu;
+                            bA1 = (nA >> 4) & 0x0f0f0f0fu;
+                            bB0 = nB & 0x0f0f0f0fu;
+                            bB1 = (nB >> 4) & 0x0f0f0f0fu;
+                        } else {
+                            bA0 = shift2(pw[t], pw[t + 1]);
+                            bA1 = shift2(pw[t + 4], pw[t + 5]);
+                            bB0 = pw[9 + t];
+                            bB1 = pw[13 + t];
+                        }
+                        int dA[4] = {int(kBiasBits), int(kBiasBits), int(kBiasBits), int(kBiasBits)};
+                        int dB[4] = {int(kBiasBits), int(kBiasBits), int(kBiasBits), int(kBiasBits)};
+                        mma_i8<kNibbles>(dA, a[2 * jp], bA0, bA1);
+                        mma_i8<kNibbles>(dB, a[2 * jp + 1], bB0, bB1);
+                        // scales of weight rows nt*8 + 2t and + 1 (block b: low
+                        // half of the pair's word 0; block b+1: high half of
+                        // word kPairWords/2)
+                        const uint32_t* q0 = reinterpret_cast<const uint32_t*>(
+                            stage + size_t(nt * 8 + 2 * t) * p.row_stride + size_t(b) * kBlk);
+                        const uint32_t* q1 = reinterpret_cast<const uint32_t*>(
+                            stage + size_t(nt * 8 + 2 * t + 1) * p.row_stride + size_t(b) * kBlk);
+                        const uint64_t wA = pk(half_lo(q0[0]), half_lo(q1[0]));
+                        const uint64_t wB = pk(half_hi(q0[kPairWords / 2]), half_hi(q1[kPairWords / 2]));
+                        // d: (col g, rows 2t, 2t+1), (col g+8, rows 2t, 2t+1)
+                        scale_step(acc[nt][0], dA[0], dA[1], dmA0, wA, nbias);
+                        scale_step(acc[nt][1], dA[2], dA[3], dmA1, wA, nbias);
+                        scale_step(acc[nt][0], dB[0], dB[1], dmB0, wB, nbias);
+                        scale_step(acc[nt][1], dB[2], dB[3], dmB1, wB, nbias);
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int sj = 0; sj < BPW / 8; ++sj) {
+                    const int sb = warp * (BPW / 8) + sj;   // super-block within the slice
+                    // lane (g, t) decodes sub-block g of rows nt*8 + 2t, +1
+#pragma unroll
+                    for (int nt = 0; nt < kNT; ++nt) {
+                        const uint4 h0 =
+                            *reinterpret_cast<const uint4*>(stage + size_t(nt * 8 + 2 * t) * p.row_stride + sb * 144);
+                        const uint4 h1 = *reinterpret_cast<const uint4*>(stage + size_t(nt * 8 + 2 * t + 1) * p.row_stride +
+                                                                         sb * 144);
+                        float s0, s1, m0, m1;
+                        q4k_sub_scale(h0, g, s0, m0);
+                        q4k_sub_scale(h1, g, s1, m1);
+                        scr[(nt * 8 + g) * 4 + t] = make_float4(s0, s1, -m0, -m1);
+                    }
+                    __syncwarp();
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        const int b = kb0 + sj * 8 + 2 * c;   // sub-blocks 2c (low nibbles) and 2c+1 (high)
+                        const float4 dmA0 = dm[b * 16 + g], dmA1 = dm[b * 16 + g + 8];
+                        const float4 dmB0 = dm[(b + 1) * 16 + g], dmB1 = dm[(b + 1) * 16 + g + 8];
+#pragma unroll
+                        for (int nt = 0; nt < kNT; ++nt) {
+                            const uint32_t* pw =
+                                reinterpret_cast<const uint32_t*>(stage + size_t(nt * 8 + g) * p.row_stride + sb * 144);
+                            const uint32_t lo = pw[4 + 8 * c + t], hi = pw[8 + 8 * c + t];
+                            int dA[4] = {int(kBiasBits), int(kBiasBits), int(kBiasBits), int(kBiasBits)};
+                            int dB[4] = {int(kBiasBits), int(kBiasBits), int(kBiasBits), int(kBiasBits)};
+                            mma_i8<true>(dA, a[sj * 8 + 2 * c], lo & 0x0f0f0f0fu, hi & 0x0f0f0f0fu);
+                            mma_i8<true>(dB, a[sj * 8 + 2 * c + 1], (lo >> 4) & 0x0f0f0f0fu, (hi >> 4) & 0x0f0f0f0fu);
+                            const float4 sA = scr[(nt * 8 + 2 * c) * 4 + t], sB = scr[(nt * 8 + 2 * c + 1) * 4 + t];
+                            scale_step_k(acc[nt][0], dA[0], dA[1], dmA0, sA, nbias);
+                            scale_step_k(acc[nt][1], dA[2], dA[3], dmA1, sA, nbias);
+                            scale_step_k(acc[nt][0], dB[0], dB[1], dmB0, sB, nbias);
+                            scale_step_k(acc[nt][1], dB[2], dB[3], dmB1, sB, nbias);
+                        }
+                    }
+                    __syncwarp();   // scr is rewritten for the next super-block
+                }
+            }
+            // the stage's words are in registers: hand the slot back
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+            // partials [row][col] of this warp, then the fixed-order sum
+            float* pp = part + (size_t(s & 1) * nw + warp) * kRows * kPartStride;
+#pragma unroll
+            for (int nt = 0; nt < kNT; ++nt) {
+                const float2 c0 = unpk(acc[nt][0]), c1 = unpk(acc[nt][1]);
+                pp[(nt * 8 + 2 * t) * kPartStride + g] = c0.x;
+                pp[(nt * 8 + 2 * t + 1) * kPartStride + g] = c0.y;
+                pp[(nt * 8 + 2 * t) * kPartStride + g + 8] = c1.x;
+                pp[(nt * 8 + 2 * t + 1) * kPartStride + g + 8] = c1.y;
+            }
+            asm volatile("bar.sync 1, %0;" ::"r"(nct) : "memory");
+            for (int o = tid; o < kRows * 16; o += nct) {
+                const int row = o >> 4, col = o & 15;
+                const int r = r0 + s * kRows + row;
+                if (col < p.batch && r < r1) {
+                    const float* pb = part + size_t(s & 1) * nw * kRows * kPartStride + row * kPartStride + col;
+                    float sum = pb[0];
+                    for (int w = 1; w < nw; ++w) sum += pb[w * kRows * kPartStride];
+                    if (p.slices == 1)
+                        p.y[size_t(col) * p.rows + r] = sum;
+                    else
+                        res[(r - r0) * 16 + col] = sum;
+                }
+            }
+        }
+    }
+    if (p.slices > 1) {
+        // K split: every thread of the cluster meets here after its last
+        // stage; CTA `slice` then sums rows [n*slice/S, n*(slice+1)/S) of the
+        // row block over the slices in slice order, and no CTA leaves while
+        // another may still read its shared memory.
+        cluster_sync_all();
+        const int n = r1 - r0;
+        const int q0 = n * slice / p.slices, q1 = n * (slice + 1) / p.slices;
+        for (int o = tid; o < (q1 - q0) * 16; o += static_cast<int>(blockDim.x)) {
+            const int row = q0 + (o >> 4), col = o & 15;
+            if (col < p.batch) {
+                float sum = ld_cluster_f32(res + row * 16 + col, 0);
+                for (int q = 1; q < p.slices; ++q) sum += ld_cluster_f32(res + row * 16 + col, q);
+                p.y[size_t(col) * p.rows + r0 + row] = sum;
+            }
+        }
+        cluster_sync_all();
+    }
+}
+
+}  // namespace qmvm
+}  // namespace p100b
