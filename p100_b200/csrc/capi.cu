@@ -248,28 +248,37 @@ p100_status launch_team_type(const TeamPlan& plan, int batch, bool pdl, cudaStre
 // ------------------------------------------------------------------ batched plan
 using MmaKernel = void (*)(qmvm::Params);
 
-MmaKernel mma_kernel(int type, int bpw) {
-#define P100_MMA_CASES(T)                                \
-    switch (bpw) {                                       \
-        case 2: return qmvm::qmv_mma_kernel<T, 2>;       \
-        case 4: return qmvm::qmv_mma_kernel<T, 4>;       \
-        case 8: return qmvm::qmv_mma_kernel<T, 8>;       \
-        case 16: return qmvm::qmv_mma_kernel<T, 16>;     \
-        case 32: return qmvm::qmv_mma_kernel<T, 32>;     \
-        default: return nullptr;                         \
+MmaKernel mma_kernel(int type, int bpw, int ncg) {
+#define P100_MMA_BPW(T, N)                                  \
+    switch (bpw) {                                          \
+        case 2: return qmvm::qmv_mma_kernel<T, 2, N>;       \
+        case 4: return qmvm::qmv_mma_kernel<T, 4, N>;       \
+        case 8: return qmvm::qmv_mma_kernel<T, 8, N>;       \
+        case 16: return qmvm::qmv_mma_kernel<T, 16, N>;     \
+        case 32: return qmvm::qmv_mma_kernel<T, 32, N>;     \
+        default: return nullptr;                            \
+    }
+#define P100_MMA_BPW_K(N)                                   \
+    switch (bpw) {                                          \
+        case 8: return qmvm::qmv_mma_kernel<P100_Q4_K, 8, N>;   \
+        case 16: return qmvm::qmv_mma_kernel<P100_Q4_K, 16, N>; \
+        case 32: return qmvm::qmv_mma_kernel<P100_Q4_K, 32, N>; \
+        default: return nullptr;                            \
+    }
+    if (ncg == 1) {
+        switch (type) {
+            case P100_Q4_0: P100_MMA_BPW(P100_Q4_0, 1)
+            case P100_Q8_0: P100_MMA_BPW(P100_Q8_0, 1)
+            default: P100_MMA_BPW_K(1)
+        }
     }
     switch (type) {
-        case P100_Q4_0: P100_MMA_CASES(P100_Q4_0)
-        case P100_Q8_0: P100_MMA_CASES(P100_Q8_0)
-        default:
-            switch (bpw) {
-                case 8: return qmvm::qmv_mma_kernel<P100_Q4_K, 8>;
-                case 16: return qmvm::qmv_mma_kernel<P100_Q4_K, 16>;
-                case 32: return qmvm::qmv_mma_kernel<P100_Q4_K, 32>;
-                default: return nullptr;
-            }
+        case P100_Q4_0: P100_MMA_BPW(P100_Q4_0, 2)
+        case P100_Q8_0: P100_MMA_BPW(P100_Q8_0, 2)
+        default: P100_MMA_BPW_K(2)
     }
-#undef P100_MMA_CASES
+#undef P100_MMA_BPW
+#undef P100_MMA_BPW_K
 }
 
 // The largest dynamic shared memory on every batched kernel, once per device;
@@ -326,15 +335,17 @@ struct MmaPlan {
 };
 
 // Batch 2..16 on the tensor cores (every type): 16-byte aligned weights and
-// activations, k % 256 == 0.  Picks the fewest K slices (CTAs per cluster),
-// then the most consumer warps, whose per-warp share of blocks is compiled
-// in and whose layout fits: two ring slots ahead of the activations.
+// activations, k % 256 == 0.  One column group of 8 up to batch 8, two
+// above.  Picks the fewest K slices (CTAs per cluster), then the most
+// consumer warps, whose per-warp share of blocks is compiled in and whose
+// layout fits: two ring slots ahead of the activations.
 bool plan_mma(int type, const void* w, const void* xq, int rows, int k, int batch, int sms, MmaPlan& plan) {
     if (batch < 2 || batch > 16 || !known_type(type)) return false;
     if (reinterpret_cast<uintptr_t>(w) % 16 || reinterpret_cast<uintptr_t>(xq) % 16 || k % 256) return false;
     const int nb = k / 32;
     const size_t row_bytes = size_t(k / elems_of(type)) * bytes_of(type);
-    const int rows_per_stage = 8 * qmvm::stage_tiles(type);
+    const int rows_per_stage = qmvm::stage_rows(type);
+    const int ncg = batch > 8 ? 2 : 1;   // column groups of 8
     for (int slices : {1, 2, 4, 8}) {
         for (int nw = qmvm::kMaxConsumers; nw >= 4; --nw) {
             if (nb % (slices * nw)) continue;
@@ -342,10 +353,10 @@ bool plan_mma(int type, const void* w, const void* xq, int rows, int k, int batc
             const int nbs = nw * bpw;
             const size_t slice = size_t(qmvm::slice_bytes_of(type, nbs));
             if (slice % 16 || (size_t(nbs) * 36) % 16) continue;
-            const MmaKernel kern = mma_kernel(type, bpw);
+            const MmaKernel kern = mma_kernel(type, bpw, ncg);
             if (!kern) continue;
             const int threads = (nw + 1) * 32;
-            if (threads > qmvm::max_threads(bpw)) continue;
+            if (threads > qmvm::max_threads(bpw, ncg)) continue;
             int max_clusters = 0;
             if (!mma_prepare(kern, slices, threads, &max_clusters)) continue;
             int nrb = (rows + rows_per_stage - 1) / rows_per_stage;
@@ -356,11 +367,11 @@ bool plan_mma(int type, const void* w, const void* xq, int rows, int k, int batc
             const size_t act_stride = size_t(nbs) * 36 + 16;
             const size_t act_bytes = size_t(batch) * act_stride;
             const size_t dm_off = 256;                                   // 2 x 8 ring mbarriers + 2
-            const size_t part_off = dm_off + size_t(nbs) * 16 * 16;
+            const size_t part_off = dm_off + size_t(nbs) * 8 * 16;
             const size_t res_off = part_off + size_t(2) * nw * rows_per_stage * qmvm::kPartStride * 4;
             const size_t res_bytes = slices > 1 ? size_t((rows + nrb - 1) / nrb) * 16 * 4 : 0;
             const size_t scr_off = res_off + round128(res_bytes);
-            const size_t scr_bytes = type == P100_Q4_K ? size_t(nw) * qmvm::stage_tiles(type) * 32 * 16 : 0;
+            const size_t scr_bytes = type == P100_Q4_K ? size_t(nw) * 16 * 8 * 16 : 0;
             const size_t ring_off = round128(scr_off + scr_bytes);
             if (ring_off + 3 * slot > size_t(qmvm::kSmemLimit)) continue;
             const int nslot = int(std::min<size_t>(qmvm::kMaxSlots, (qmvm::kSmemLimit - ring_off) / slot));
