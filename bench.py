@@ -330,6 +330,42 @@ def decode_section(torch, P, stream, rank, world, dist, max_over_ranks):
     return out
 
 
+def c2_grid(torch, P, stream):
+    """Config 2: every layer shape x Q4_0/Q8_0/Q4_K x batch 1, 2, 4, 8, 16,
+    one C-ABI call per launch, graph-replayed back to back with PDL over
+    rotating weight copies that together exceed 3x L2.  Batch 1 runs the team
+    kernel, batch 2-16 the tensor-core kernel (one launch for all columns).
+    GB/s counts the algorithmic bytes (weights + activations + outputs)."""
+    peak = peak_gbs()[0]
+    out = {}
+    for qtype, tname in ((W.Q4_0, "Q4_0"), (W.Q8_0, "Q8_0"), (W.Q4_K, "Q4_K")):
+        per_type = {}
+        for si, (name, k, rows) in enumerate(SHAPES):
+            base = torch.from_numpy(W.weights(qtype, rows, k, seed=5000 + 31 * si + qtype)).cuda()
+            copies = max(4, int(np.ceil(3 * L2_BYTES / base.numel())) + 1)
+            ws = [base] + [base.clone() for _ in range(copies - 1)]
+            n_in_graph = max(16, copies)
+            per_shape = {}
+            for b in (1, 2, 4, 8, 16):
+                xqb = P.q8_1_quantize(torch.from_numpy(W.activations(b, k, seed=4000 + b + k)).cuda())
+                yb = torch.empty(b, rows, dtype=torch.float32, device="cuda")
+                g = capture(torch, lambda xqb=xqb, yb=yb, b=b: [
+                    P.qmv(qtype, ws[r % copies], rows, k, xqb, b, y=yb, flags=P.QMV_PDL) for r in range(n_in_graph)])
+                time_graphs(torch, [g], 2, stream)
+                reps = 5
+                us = time_graphs(torch, [g], reps, stream) / (reps * n_in_graph) * 1e3
+                nbytes = W.qmv_algorithmic_bytes(qtype, rows, k, b)
+                per_shape[str(b)] = {"us": round(us, 3), "GB/s": round(nbytes / (us / 1e6) / 1e9, 1),
+                                     "frac": round(nbytes / (us / 1e6) / 1e9 / peak, 4)}
+                del g
+            per_type[f"{name} {k}x{rows}"] = per_shape
+            del ws, base
+        out[tname] = per_type
+    torch.cuda.synchronize()
+    P.check(P.device_error())
+    return out
+
+
 def kernel_only(args):
     """Eager launches of one kernel over rotating inputs larger than L2 — the
     small cases for ncu captures: the target mat-vec at batch 1 or 16 (5 weight
@@ -480,26 +516,7 @@ def main():
         if (name, k, rows) == TARGET:
             target_us, target_us_isolated = per["chained"], per["isolated"]
 
-    # Config 2's batch sweep on the target shape: batch 1-16 columns per
-    # launch (the batch >= 2 kernel), chained back-to-back launches.
-    batch_sweep = {}
-    _, tk, trows = TARGET
-    ti = [i for i, sh in enumerate(SHAPES) if sh == TARGET][0]
-    for b in (1, 2, 4, 8, 16):
-        xb = torch.from_numpy(W.activations(b, tk, seed=4000 + b)).cuda()
-        xqb = P.q8_1_quantize(xb)
-        yb = torch.empty(b, trows, dtype=torch.float32, device="cuda")
-        n_in_graph = 4 * copies
-        g = capture(torch, lambda xqb=xqb, yb=yb, b=b: [
-            P.qmv(W.Q4_0, wdev[ti][r % copies], trows, tk, xqb, b, y=yb, flags=P.QMV_PDL) for r in range(n_in_graph)])
-        time_graphs(torch, [g], 3, stream)
-        reps = 10
-        us = time_graphs(torch, [g], reps, stream) / (reps * n_in_graph) * 1e3
-        nbytes = W.qmv_algorithmic_bytes(W.Q4_0, trows, tk, b)
-        batch_sweep[str(b)] = {"us": round(us, 3), "GB/s": round(nbytes / (us / 1e6) / 1e9, 1),
-                               "frac": round(nbytes / (us / 1e6) / 1e9 / peak_gbs()[0], 4),
-                               "int8_tops": round(2.0 * trows * tk * b / (us / 1e6) / 1e12, 2)}
-        del g
+    batch_sweep = c2_grid(torch, P, stream) if rank == 0 else None
 
     # End to end through the C-ABI with host buffers: each step copies its
     # activations in from pinned memory, runs, copies y out and synchronises
@@ -572,7 +589,7 @@ def main():
                 "form": "graph replay + stream sync + host read per step", "eager_value": round(e2e_eager, 2)},
         "gpu_launches": launches_per_step * args.steps,
         "shapes": shape_gbs,
-        "batch_sweep": {"shape": f"{TARGET[0]} {TARGET[1]}x{TARGET[2]} Q4_0", "per_batch": batch_sweep},
+        "batch_sweep": batch_sweep,
         "fa_decode": fa,
         "decode": decode,
         "clocks": clocks.summary(),
