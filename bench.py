@@ -82,7 +82,10 @@ def ncu_traffic(name):
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    """nvidia-smi clocks and throttle reasons sampled during the timed region
+    (every 20 ms; the sampler's first line is awaited before timing starts).
+    A timed region shorter than the interval may hold no sample: the summary
+    then uses the samples just around it and says so."""
 
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -92,16 +95,21 @@ class ClockSampler:
         self.device = device
         self.proc = None
         self.lines = []
+        self.first = self.last = 0
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True)
+                 "-lms", "20"], stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True)
             self.reader = threading.Thread(target=self._read, daemon=True)
             self.reader.start()
+            deadline = time.time() + 5.0
+            while not self.lines and time.time() < deadline and self.proc.poll() is None:
+                time.sleep(0.01)
         except OSError:
             self.proc = None
+        self.first = len(self.lines)
         return self
 
     def _read(self):
@@ -109,7 +117,9 @@ class ClockSampler:
             self.lines.append(line.strip())
 
     def __exit__(self, *exc):
+        self.last = len(self.lines)
         if self.proc:
+            time.sleep(0.05)   # one more sample just after the region
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -118,9 +128,13 @@ class ClockSampler:
             self.reader.join(timeout=2)
 
     def summary(self):
+        window, where = self.lines[self.first:self.last], "during the timed region"
+        if not window:
+            window = self.lines[max(0, self.first - 2):self.first + 2]
+            where = "just before and after the timed region (shorter than the 20 ms interval)"
         sm, mx, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
+        for line in window:
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 7:
                 continue
@@ -135,7 +149,7 @@ class ClockSampler:
         if not sm:
             return {"error": (self.lines[:2] or ["nvidia-smi gave no samples"])[0][:200]}
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "window": where}
 
 
 # ------------------------------------------------------------------ reference arm

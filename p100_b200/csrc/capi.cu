@@ -83,6 +83,9 @@ int bytes_of(int t) { return t == P100_Q4_0 ? 18 : t == P100_Q8_0 ? 34 : 144; }
 
 p100_status launch_status(const char* what) { return cuda_status(cudaGetLastError(), what); }
 
+// SM count of a device that require_sm100 has seen.
+int sms_of(int dev) { return dev >= 0 && dev < 64 ? g_dev_sms[dev] : 0; }
+
 // ------------------------------------------------------------------ qmv plan
 struct QmvPlan {
     qmv::Params p;
@@ -511,6 +514,9 @@ struct FaPlan {
     int D = 0, G = 0, gmax = 0, parts = 1, nstage = 0;
     long long head_stride = 0, batch_stride = 0;
     size_t smem = 0, ws_o = 0, ws_ml = 0, ws_tickets = 0, ws_total = 0;
+    bool auto_parts = false;   // kv_splits == 0: the split may change (fa_mma cluster merge)
+    int parts_wide = 1;        // fa_mma with the workspace merge: two CTAs per SM
+    int seq = 0;
 };
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
@@ -533,16 +539,22 @@ p100_status plan_fa(const p100_attn_desc& d, int sms, FaPlan& plan) {
     const int heads = d.batch * d.n_head_kv;
     const int max_parts = std::max(1, d.seq_kv / fa::kTile);
     int parts = d.kv_splits;
+    plan.auto_parts = parts <= 0;
     if (parts <= 0) parts = std::max(1, sms / heads);
     // at most 512 parts: the last-CTA merge keeps every part's (m, l) and
     // weight in shared memory (2 * parts * G floats, inside the idle ring)
     plan.parts = std::min(std::min(parts, max_parts), 512);
+    // fa_mma_kernel fits two CTAs per SM: with automatic splitting and the
+    // workspace merge it runs twice the parts (the workspace covers both).
+    plan.parts_wide = plan.auto_parts ? std::min(std::min(2 * std::max(1, sms / heads), max_parts), 512) : plan.parts;
+    plan.seq = d.seq_kv;
+    const int ws_parts = std::max(plan.parts, plan.parts_wide);
     plan.nstage = d.d_qk == 256 ? 2 : 4;
     const size_t head = ((64 + (plan.gmax * fa::kTile + fa::kTile * 8 + 24 + plan.gmax * plan.D + 4) * 4) + 127) & ~size_t(127);
     plan.smem = head + size_t(plan.nstage) * 2 * fa::kTile * plan.D * 2;
-    if (plan.parts > 1) {
-        plan.ws_o = align256(size_t(heads) * plan.parts * G * plan.D * 4);
-        plan.ws_ml = align256(size_t(heads) * plan.parts * G * 2 * 4);
+    if (ws_parts > 1) {
+        plan.ws_o = align256(size_t(heads) * ws_parts * G * plan.D * 4);
+        plan.ws_ml = align256(size_t(heads) * ws_parts * G * 2 * 4);
         plan.ws_tickets = align256(size_t(heads) * 4);
     }
     plan.ws_total = plan.ws_o + plan.ws_ml + plan.ws_tickets;
@@ -584,24 +596,79 @@ p100_status launch_fa_mma_t(const FaPlan& plan, const fa::Params& prm, int heads
     auto kern = fam::fa_mma_kernel<D, G>;
     constexpr size_t smem = fam::smem_bytes<D, G>();
     static thread_local int configured[64] = {};
+    static thread_local int cluster_fits[64][5] = {};   // per log2(parts): clusters that fit, 0 unknown, -1 none
     int dev = 0;
     cudaGetDevice(&dev);
     if (!configured[dev]) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
         if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(fa_mma)");
         configured[dev] = 1;
     }
+    // Cluster merge: with automatic splitting and up to 16384 keys, the
+    // parts of a kv head become one cluster of np = a power of two <= 16
+    // CTAs (and <= G*D/32, so each CTA merges whole Q8_1 blocks), if that
+    // keeps at least half the parts.  Longer contexts amortise the workspace
+    // merge and run twice the parts instead (two CTAs per SM).
+    fa::Params run = prm;
+    int np = 0;
+    if (plan.auto_parts && plan.parts >= 2 && plan.seq <= 16384) {
+        np = 1;
+        while (np * 2 <= std::min(16, plan.parts) && np * 2 <= G * D / 32) np *= 2;
+        if (np < 2 || 2 * np < plan.parts) np = 0;
+    }
+    int lg = 0;
+    while (np && (1 << lg) < np) ++lg;
+    if (np && cluster_fits[dev][lg] == 0) {
+        cudaLaunchConfig_t q = {};
+        q.gridDim = dim3(np, 1);
+        q.blockDim = dim3(fam::kThreads);
+        q.dynamicSmemBytes = smem;
+        cudaLaunchAttribute ca[1];
+        ca[0].id = cudaLaunchAttributeClusterDimension;
+        ca[0].val.clusterDim.x = np;
+        ca[0].val.clusterDim.y = 1;
+        ca[0].val.clusterDim.z = 1;
+        q.attrs = ca;
+        q.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, kern, &q) != cudaSuccess) {
+            (void)cudaGetLastError();
+            n = 0;
+        }
+        cluster_fits[dev][lg] = n >= 1 ? n : -1;
+    }
+    // every cluster of the launch resident at once, or the GPU full
+    if (np && (cluster_fits[dev][lg] < 0 || (cluster_fits[dev][lg] < heads && cluster_fits[dev][lg] * np * 2 < sms_of(dev))))
+        np = 0;
+    if (np) {
+        run.parts = np;
+        run.cluster_merge = 1;
+    } else if (run.parts > 1) {
+        run.parts = plan.parts_wide;
+    }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(plan.parts, heads);
+    cfg.gridDim = dim3(run.parts, heads);
     cfg.blockDim = dim3(fam::kThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchAttribute attr[2];
+    int na = 0;
+    if (pdl) {
+        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na].val.programmaticStreamSerializationAllowed = 1;
+        ++na;
+    }
+    if (np) {
+        attr[na].id = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = np;
+        attr[na].val.clusterDim.y = 1;
+        attr[na].val.clusterDim.z = 1;
+        ++na;
+    }
     cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 1 : 0;
-    return cuda_status(cudaLaunchKernelEx(&cfg, kern, prm), "fa_mma_kernel launch");
+    cfg.numAttrs = na;
+    return cuda_status(cudaLaunchKernelEx(&cfg, kern, run), "fa_mma_kernel launch");
 }
 
 template <int D>

@@ -56,6 +56,10 @@ struct Params {
     const float2* rope_cs;
     int nq_total;
     uint8_t* o_q81;
+    // fa_mma_kernel only: the parts of a kv head form one thread-block
+    // cluster (gridDim.x == parts <= 16) and merge through distributed shared
+    // memory instead of ws_o / ws_ml / tickets.
+    int cluster_merge;
 };
 
 __device__ __forceinline__ void half8_to_float(const uint4 v, float (&f)[8]) {

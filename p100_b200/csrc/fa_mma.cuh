@@ -19,8 +19,13 @@
 // K/V tiles are copied with 16-byte cp.async into rows padded to D + 8
 // halves, so the eight 16-byte rows an ldmatrix reads fall on distinct banks;
 // rows past the part's last key are zero-filled (a masked key's V then adds
-// exactly 0).  Split-K parts and the last-CTA combine are those of
-// fa_decode.cuh (fa::Params, partials {m, l, unnormalised O}).
+// exactly 0).  The query is loaded into registers before the first K/V copy
+// is issued (loads issued after 96 KB of copies waited ~2.6 us behind them).
+// Split-K parts are those of fa_decode.cuh (fa::Params, partials {m, l,
+// unnormalised O}); they are combined either by the last CTA through the
+// global workspace, or, when the parts of a kv head form one thread-block
+// cluster, through distributed shared memory: every CTA then merges its own
+// slice of the outputs (no workspace, fence, ticket or L2 round trips).
 #pragma once
 #include "fa_decode.cuh"
 
@@ -64,8 +69,25 @@ __device__ __forceinline__ void cp_async_wait() {
     asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
+// Every thread of the cluster arrives; release/acquire orders the shared
+// memory written before it with the remote reads after it.
+__device__ __forceinline__ void cluster_barrier() {
+    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+// A float of CTA `rank`'s shared memory at the address of `local` in ours.
+__device__ __forceinline__ float ld_cluster(const float* local, int rank) {
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_addr(local)), "r"(rank));
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+    return v;
+}
+
+// Three 64-key stages (107 KB of shared memory at D = 128): two CTAs fit an SM,
+// so a cluster of 16 parts per kv head fits a GPC (7 such clusters fit the
+// GPU at four stages, 14 at three).
 template <int D>
-__host__ __device__ constexpr int stages() { return D >= 256 ? 2 : 4; }
+__host__ __device__ constexpr int stages() { return D >= 256 ? 2 : 3; }
 template <int D, int G>
 __host__ __device__ constexpr size_t smem_bytes() {
     return size_t(stages<D>()) * 2 * kTile * (D + 8) * 2 + size_t(G) * D * 4 + 256;
@@ -110,6 +132,17 @@ __global__ void __launch_bounds__(kThreads, 1) fa_mma_kernel(const fa::Params p)
     const __half* kbase = p.k + b * p.batch_stride + kvh * p.head_stride;
     const __half* vbase = p.v + b * p.batch_stride + kvh * p.head_stride;
     const uint32_t ring_addr = smem_addr(ring);
+
+    // The raw query pairs of this group, loaded before any K/V copy is issued
+    // (after the wait when they come from the previous kernel).
+    constexpr int QPT = (G * D / 2 + kThreads - 1) / kThreads;   // pairs per thread
+    const float* qg = p.q + (size_t(b) * p.nkv * G + size_t(kvh) * G) * D;
+    float2 qr[QPT];
+#pragma unroll
+    for (int j = 0; j < QPT; ++j) {
+        const int i = tid + j * kThreads;
+        qr[j] = i < G * D / 2 ? *reinterpret_cast<const float2*>(qg + 2 * i) : make_float2(0.f, 0.f);
+    }
 
     auto issue = [&](int tile) {
         if (tile < ntiles) {
@@ -158,18 +191,20 @@ __global__ void __launch_bounds__(kThreads, 1) fa_mma_kernel(const fa::Params p)
 
     // ---- queries: q * scale per head, scaled by a power of two 2^e so the
     // largest |entry| lies in [2^13, 2^14)
-    const float* qg = p.q + (size_t(b) * p.nkv * G + size_t(kvh) * G) * D;
-    if (p.rope_cs) {   // rotate the raw q pairs (rope_kv_append_kernel's arithmetic)
-        const int pr = pos >= 0 ? pos : 0;
-        for (int i = tid; i < G * D / 2; i += kThreads) {
-            const int h = i / (D / 2), pi = i % (D / 2);
-            const float2 t = p.rope_cs[size_t(pr) * (D / 2) + pi];
-            const float x0 = qg[h * D + 2 * pi], x1 = qg[h * D + 2 * pi + 1];
-            s_q[h * D + 2 * pi] = __fsub_rn(__fmul_rn(x0, t.x), __fmul_rn(x1, t.y)) * p.scale;
-            s_q[h * D + 2 * pi + 1] = __fadd_rn(__fmul_rn(x0, t.y), __fmul_rn(x1, t.x)) * p.scale;
+#pragma unroll
+    for (int j = 0; j < QPT; ++j) {
+        const int i = tid + j * kThreads;
+        if (i >= G * D / 2) break;
+        const float x0 = qr[j].x, x1 = qr[j].y;
+        if (p.rope_cs) {   // rotate the raw q pair (rope_kv_append_kernel's arithmetic)
+            const int pr = pos >= 0 ? pos : 0;
+            const float2 t = p.rope_cs[size_t(pr) * (D / 2) + i % (D / 2)];
+            s_q[2 * i] = __fsub_rn(__fmul_rn(x0, t.x), __fmul_rn(x1, t.y)) * p.scale;
+            s_q[2 * i + 1] = __fadd_rn(__fmul_rn(x0, t.y), __fmul_rn(x1, t.x)) * p.scale;
+        } else {
+            s_q[2 * i] = x0 * p.scale;
+            s_q[2 * i + 1] = x1 * p.scale;
         }
-    } else {
-        for (int i = tid; i < G * D; i += kThreads) s_q[i] = qg[i] * p.scale;
     }
     __syncthreads();
     for (int h = warp; h < G; h += kWarps) {
@@ -358,6 +393,65 @@ __global__ void __launch_bounds__(kThreads, 1) fa_mma_kernel(const fa::Params p)
     __syncthreads();
 
     const size_t row0 = size_t(b) * p.nkv * G + size_t(kvh) * G;   // first query head row
+    if (p.cluster_merge) {
+        // The parts of this kv head are the CTAs of one cluster (rank =
+        // part).  Once every part's {m, l, unnormalised O} is final, CTA q
+        // merges outputs [q*per, (q+1)*per) of the G x D block with
+        // merge_parts' arithmetic, parts in order, reading the others' shared
+        // memory; a second cluster barrier keeps every CTA resident until no
+        // one reads it any more.
+        cluster_barrier();
+        const int np = p.parts, per = G * D / np;
+        float* s_pm = red + G * D;        // [np][G] m, then the weights
+        float* s_pl = s_pm + np * G;      // [np][G] l
+        float* s_gm = s_pl + np * G;      // [G]
+        float* s_den = s_gm + G;          // [G]
+        float* s_out = s_den + G;         // [per] this CTA's merged outputs
+        for (int i = tid; i < np * G; i += kThreads) {
+            const int q = i / G, h = i % G;
+            s_pm[i] = ld_cluster(s_m + h, q);
+            s_pl[i] = ld_cluster(s_l + h, q);
+        }
+        __syncthreads();
+        if (tid < G) {
+            float gmax = -INFINITY;
+            for (int q = 0; q < np; ++q) gmax = fmaxf(gmax, s_pm[q * G + tid]);
+            float den = 0.f;
+            for (int q = 0; q < np; ++q) {
+                const float l = s_pl[q * G + tid];
+                den += l == 0.f ? 0.f : expf(s_pm[q * G + tid] - gmax) * l;
+            }
+            s_gm[tid] = gmax;
+            s_den[tid] = den;
+            if (part == 0 && p.lse) p.lse[row0 + tid] = den == 0.f ? -INFINITY : gmax + logf(den);
+        }
+        __syncthreads();
+        for (int i = tid; i < np * G; i += kThreads) {   // weights replace m
+            const int h = i % G;
+            s_pm[i] = s_pl[i] == 0.f ? 0.f : expf(s_pm[i] - s_gm[h]);
+        }
+        __syncthreads();
+        for (int i = tid; i < per; i += kThreads) {
+            const int idx = part * per + i, h = idx / D;
+            float num = 0.f;
+#pragma unroll 8
+            for (int q = 0; q < np; ++q) {
+                const float v = ld_cluster(red + idx, q);
+                if (s_pl[q * G + h] != 0.f) num = fmaf(s_pm[q * G + h], v, num);
+            }
+            const float den = s_den[h];
+            const float o = den == 0.f ? 0.f : num / den;
+            p.o[(row0 + h) * D + (idx % D)] = o;
+            s_out[i] = o;
+        }
+        if (p.o_q81) {   // per is a multiple of 32: whole Q8_1 blocks
+            __syncthreads();
+            for (int j = warp; j < per / 32; j += kWarps)
+                warp_q8_1_block(s_out[j * 32 + lane], lane, p.o_q81 + (row0 * D / 32 + part * per / 32 + j) * 36);
+        }
+        cluster_barrier();
+        return;
+    }
     if (p.parts == 1) {
         for (int i = tid; i < G * D; i += kThreads) {
             const int h = i / D, d = i % D;
