@@ -74,13 +74,11 @@ __device__ __forceinline__ void cp_async_wait() {
 __device__ __forceinline__ void cluster_barrier() {
     asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
 }
-// A float of CTA `rank`'s shared memory at the address of `local` in ours.
-__device__ __forceinline__ float ld_cluster(const float* local, int rank) {
+// Stores v into CTA `rank`'s shared memory at the address of `local` in ours.
+__device__ __forceinline__ void st_cluster(float* local, int rank, float v) {
     uint32_t remote;
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_addr(local)), "r"(rank));
-    float v;
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
-    return v;
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(remote), "f"(v) : "memory");
 }
 
 // Three 64-key stages (107 KB of shared memory at D = 128): two CTAs fit an SM,
@@ -88,9 +86,15 @@ __device__ __forceinline__ float ld_cluster(const float* local, int rank) {
 // GPU at four stages, 14 at three).
 template <int D>
 __host__ __device__ constexpr int stages() { return D >= 256 ? 2 : 3; }
+// Cluster-merge receive area: [16 parts][G][D] slices of O (G*D floats in
+// all) and [16][G] m and l; its own region, so a peer that finishes early can
+// store into it while this CTA still streams K/V.
+constexpr int kMaxClusterParts = 16;
+template <int D, int G>
+__host__ __device__ constexpr size_t rx_floats() { return size_t(G) * D + 2 * kMaxClusterParts * G; }
 template <int D, int G>
 __host__ __device__ constexpr size_t smem_bytes() {
-    return size_t(stages<D>()) * 2 * kTile * (D + 8) * 2 + size_t(G) * D * 4 + 256;
+    return size_t(stages<D>()) * 2 * kTile * (D + 8) * 2 + size_t(G) * D * 4 + 256 + rx_floats<D, G>() * 4;
 }
 
 // Grid (parts, batch * n_kv); G = query heads per kv head (1, 2, 4 or 8);
@@ -108,6 +112,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_mma_kernel(const fa::Params p)
     float* s_q = reinterpret_cast<float*>(smem + size_t(NS) * 2 * kTile * RS * 2);   // [G][D]
     float* s_qs = s_q + G * D;                                          // [8] per-head power-of-two scale
     unsigned* s_flag = reinterpret_cast<unsigned*>(s_qs + 8);
+    float* rx = reinterpret_cast<float*>(smem + smem_bytes<D, G>() - rx_floats<D, G>() * 4);   // cluster merge
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, t = lane & 3;
@@ -369,25 +374,27 @@ __global__ void __launch_bounds__(kThreads, 1) fa_mma_kernel(const fa::Params p)
     __syncthreads();
     float* s_m = s_wo + kWarps * G * D;   // [G]
     float* s_l = s_m + 8;                 // [G]
+    float* s_ww = s_l + 8;                // [kWarps][8] rebase weights exp(m_w - m)
     if (tid < G) {
         float m = -INFINITY;
         for (int w = 0; w < kWarps; ++w) m = fmaxf(m, s_wm[w * 8 + tid]);
         float l = 0.f;
         for (int w = 0; w < kWarps; ++w) {
             const float lw = s_wl[w * 8 + tid];
-            if (lw != 0.f) l = fmaf(expf(s_wm[w * 8 + tid] - m), lw, l);
+            const float wt = lw != 0.f ? expf(s_wm[w * 8 + tid] - m) : 0.f;
+            s_ww[w * 8 + tid] = wt;
+            if (lw != 0.f) l = fmaf(wt, lw, l);
         }
         s_m[tid] = m;
         s_l[tid] = l;
     }
     __syncthreads();
-    float* red = s_l + 8;   // [G][D] the CTA's unnormalised O
+    float* red = s_ww + kWarps * 8;   // [G][D] the CTA's unnormalised O
     for (int i = tid; i < G * D; i += kThreads) {
         const int h = i / D;
-        const float m = s_m[h];
         float acc = 0.f;
         for (int w = 0; w < kWarps; ++w)
-            if (s_wl[w * 8 + h] != 0.f) acc = fmaf(expf(s_wm[w * 8 + h] - m), s_wo[(w * G + h) * D + (i % D)], acc);
+            if (s_wl[w * 8 + h] != 0.f) acc = fmaf(s_ww[w * 8 + h], s_wo[(w * G + h) * D + (i % D)], acc);
         red[i] = acc;
     }
     __syncthreads();
@@ -395,50 +402,51 @@ __global__ void __launch_bounds__(kThreads, 1) fa_mma_kernel(const fa::Params p)
     const size_t row0 = size_t(b) * p.nkv * G + size_t(kvh) * G;   // first query head row
     if (p.cluster_merge) {
         // The parts of this kv head are the CTAs of one cluster (rank =
-        // part).  Once every part's {m, l, unnormalised O} is final, CTA q
-        // merges outputs [q*per, (q+1)*per) of the G x D block with
-        // merge_parts' arithmetic, parts in order, reading the others' shared
-        // memory; a second cluster barrier keeps every CTA resident until no
-        // one reads it any more.
-        cluster_barrier();
+        // part); CTA q owns outputs [q*per, (q+1)*per) of the G x D block.
+        // Every CTA stores its m, l (to all) and each owner's slice of its
+        // unnormalised O into the owners' receive areas, one cluster barrier
+        // makes them visible, and each CTA merges its slice from its own
+        // shared memory with merge_parts' arithmetic, parts in order.  After
+        // the barrier no CTA touches another's memory, so no second barrier.
         const int np = p.parts, per = G * D / np;
-        float* s_pm = red + G * D;        // [np][G] m, then the weights
-        float* s_pl = s_pm + np * G;      // [np][G] l
-        float* s_gm = s_pl + np * G;      // [G]
-        float* s_den = s_gm + G;          // [G]
-        float* s_out = s_den + G;         // [per] this CTA's merged outputs
+        float* rx_o = rx;                 // [np][per]
+        float* rx_m = rx + G * D;         // [np][G]
+        float* rx_l = rx_m + np * G;      // [np][G]
+        for (int i = tid; i < G * D; i += kThreads) st_cluster(rx_o + part * per + i % per, i / per, red[i]);
         for (int i = tid; i < np * G; i += kThreads) {
             const int q = i / G, h = i % G;
-            s_pm[i] = ld_cluster(s_m + h, q);
-            s_pl[i] = ld_cluster(s_l + h, q);
+            st_cluster(rx_m + part * G + h, q, s_m[h]);
+            st_cluster(rx_l + part * G + h, q, s_l[h]);
         }
-        __syncthreads();
+        cluster_barrier();
+        float* s_w = red + G * D;         // [np][G] weights (local scratch)
+        float* s_gm = s_w + np * G;       // [G]
+        float* s_den = s_gm + G;          // [G]
+        float* s_out = s_den + G;         // [per] this CTA's merged outputs
         if (tid < G) {
             float gmax = -INFINITY;
-            for (int q = 0; q < np; ++q) gmax = fmaxf(gmax, s_pm[q * G + tid]);
+            for (int q = 0; q < np; ++q) gmax = fmaxf(gmax, rx_m[q * G + tid]);
             float den = 0.f;
             for (int q = 0; q < np; ++q) {
-                const float l = s_pl[q * G + tid];
-                den += l == 0.f ? 0.f : expf(s_pm[q * G + tid] - gmax) * l;
+                const float l = rx_l[q * G + tid];
+                den += l == 0.f ? 0.f : expf(rx_m[q * G + tid] - gmax) * l;
             }
             s_gm[tid] = gmax;
             s_den[tid] = den;
             if (part == 0 && p.lse) p.lse[row0 + tid] = den == 0.f ? -INFINITY : gmax + logf(den);
         }
         __syncthreads();
-        for (int i = tid; i < np * G; i += kThreads) {   // weights replace m
+        for (int i = tid; i < np * G; i += kThreads) {
             const int h = i % G;
-            s_pm[i] = s_pl[i] == 0.f ? 0.f : expf(s_pm[i] - s_gm[h]);
+            s_w[i] = rx_l[i] == 0.f ? 0.f : expf(rx_m[i] - s_gm[h]);
         }
         __syncthreads();
         for (int i = tid; i < per; i += kThreads) {
             const int idx = part * per + i, h = idx / D;
             float num = 0.f;
 #pragma unroll 8
-            for (int q = 0; q < np; ++q) {
-                const float v = ld_cluster(red + idx, q);
-                if (s_pl[q * G + h] != 0.f) num = fmaf(s_pm[q * G + h], v, num);
-            }
+            for (int q = 0; q < np; ++q)
+                if (rx_l[q * G + h] != 0.f) num = fmaf(s_w[q * G + h], rx_o[q * per + i], num);
             const float den = s_den[h];
             const float o = den == 0.f ? 0.f : num / den;
             p.o[(row0 + h) * D + (idx % D)] = o;
@@ -449,7 +457,6 @@ __global__ void __launch_bounds__(kThreads, 1) fa_mma_kernel(const fa::Params p)
             for (int j = warp; j < per / 32; j += kWarps)
                 warp_q8_1_block(s_out[j * 32 + lane], lane, p.o_q81 + (row0 * D / 32 + part * per / 32 + j) * 36);
         }
-        cluster_barrier();
         return;
     }
     if (p.parts == 1) {
