@@ -175,6 +175,18 @@ p100_status p100_fa_decode_static(const p100_attn_desc* desc, const float* q, co
 p100_status p100_rmsnorm_q8_1(float* x, const float* delta, const float* w, float eps, int k, int batch,
                               void* x_q8_1, float* y_out, p100_stream_t stream);
 
+/* The decode step's RMSNorm fused into the batch-1 mat-vec that consumes it:
+ * y[rows] = W * Q8_1(RMSNorm(x_in + delta) * norm_w), with x_in + delta also
+ * stored to x_out (if not NULL; x_out must not alias x_in).  The Q8_1 row and
+ * y equal p100_rmsnorm_q8_1 (x = x_in, delta) followed by p100_qmv bit for
+ * bit; the row is built inside the mat-vec kernel while its weights stream
+ * in, saving a launch.  k = 4096 or 8192, 16-byte aligned w, x_in, delta,
+ * x_out and norm_w; other shapes return P100_ERR_UNSUPPORTED (use the two
+ * calls).  flags as p100_qmv_ex.  No reference counterpart. */
+p100_status p100_qmv_rmsnorm(int type, const void* w, int rows, int k, const float* x_in, const float* delta,
+                             float* x_out, const float* norm_w, float eps, float* y, unsigned flags,
+                             p100_stream_t stream);
+
 /* Host: the RoPE table rope_cs[pos][i] = {cos, sin} of
  * pos * theta^(-2i/head_dim) (computed in double) for pos < max_pos. */
 void p100_rope_table(float* rope_cs, int max_pos, int head_dim, float theta);
@@ -213,7 +225,16 @@ typedef struct p100_llama_config {
     int n_layer, hidden, n_head, n_head_kv, head_dim, ffn, vocab, max_ctx;
     float rope_theta, norm_eps;
     int wtype;
+    int flags;   /* P100_DEC_* (0: defaults) */
 } p100_llama_config;
+/* Run each RMSNorm inside the mat-vec that consumes it (p100_qmv_rmsnorm;
+ * hidden 4096 or 8192, no peer-memory all-reduce): the same bits with one
+ * launch less per norm.  Off by default: on B200 at batch 1 it measured
+ * slower (8B 579 against 604 tokens/s), because every block of the mat-vec
+ * then repeats the norm after waiting for the previous kernel, where the
+ * separate one-block norm kernel fits beside the previous mat-vec and starts
+ * the moment it ends. */
+#define P100_DEC_FUSED_NORM 1
 typedef struct p100_decoder p100_decoder;
 /* Tensor ids (per layer where it applies). */
 enum {

@@ -110,6 +110,7 @@ def _bind(lib):
         "p100_peer_link_copy": (ip, [vp, vp, vp, sz, st]),
         "p100_peer_link_destroy": (ip, [vp]),
         "p100_rmsnorm_q8_1": (ip, [vp, vp, vp, C.c_float, ip, ip, vp, vp, st]),
+        "p100_qmv_rmsnorm": (ip, [ip, vp, ip, ip, vp, vp, vp, vp, C.c_float, vp, C.c_uint, st]),
         "p100_rope_table": (None, [vp, ip, ip, C.c_float]),
         "p100_rope_kv_append": (ip, [vp, ip, ip, ip, vp, ip, vp, vp, vp, C.c_longlong, st]),
         "p100_swiglu_q8_1": (ip, [vp, ip, ip, vp, st]),
@@ -311,6 +312,17 @@ def rmsnorm_q8_1(x, w, eps, delta=None, y_out=None, xq=None, stream=None):
     return xq
 
 
+def qmv_rmsnorm(qtype, w, rows, k, x_in, norm_w, eps, delta=None, x_out=None, y=None, flags=0, stream=None):
+    """y = W * Q8_1(RMSNorm(x_in + delta) * norm_w), x_in + delta into x_out
+    (p100_qmv_rmsnorm: the RMSNorm fused into the batch-1 mat-vec)."""
+    torch = _torch()
+    if y is None:
+        y = torch.empty(1, rows, dtype=torch.float32, device=x_in.device)
+    check(lib().p100_qmv_rmsnorm(qtype, _ptr(w), rows, k, _ptr(x_in), _ptr(delta), _ptr(x_out), _ptr(norm_w), eps,
+                                 _ptr(y), flags, _stream(stream)))
+    return y
+
+
 def rope_table(max_pos, head_dim, theta):
     """Host numpy [max_pos, head_dim/2, 2] (cos, sin) table (p100_rope_table)."""
     import numpy as np
@@ -349,12 +361,15 @@ class LlamaConfig(C.Structure):
     """p100_llama_config."""
     _fields_ = [("n_layer", C.c_int), ("hidden", C.c_int), ("n_head", C.c_int), ("n_head_kv", C.c_int),
                 ("head_dim", C.c_int), ("ffn", C.c_int), ("vocab", C.c_int), ("max_ctx", C.c_int),
-                ("rope_theta", C.c_float), ("norm_eps", C.c_float), ("wtype", C.c_int)]
+                ("rope_theta", C.c_float), ("norm_eps", C.c_float), ("wtype", C.c_int), ("flags", C.c_int)]
 
     def __init__(self, n_layer, hidden, n_head, n_head_kv, head_dim, ffn, vocab, max_ctx, rope_theta=500000.0,
-                 norm_eps=1e-5, wtype=0):
+                 norm_eps=1e-5, wtype=0, flags=0):
         super().__init__(n_layer, hidden, n_head, n_head_kv, head_dim, ffn, vocab, max_ctx, rope_theta, norm_eps,
-                         wtype)
+                         wtype, flags)
+
+
+DEC_FUSED_NORM = 1   # P100_DEC_FUSED_NORM
 
 
 T_EMBED, T_ATTN_NORM, T_WQKV, T_WO, T_FFN_NORM, T_WGATE_UP, T_WDOWN, T_OUT_NORM, T_LM_HEAD = range(9)

@@ -88,7 +88,7 @@ int sms_of(int dev) { return dev >= 0 && dev < 64 ? g_dev_sms[dev] : 0; }
 
 // ------------------------------------------------------------------ qmv plan
 struct QmvPlan {
-    qmv::Params p;
+    qmv::Params p{};
     int bmax = 0, grid = 0, threads = 0;
     size_t smem = 0;
 };
@@ -173,7 +173,7 @@ p100_status launch_bulk_type(const QmvPlan& plan, int cols, bool pdl, cudaStream
 
 // ------------------------------------------------------------------ team plan
 struct TeamPlan {
-    qmvt::Params p;
+    qmvt::Params p{};
     int grid = 0;
     size_t smem = 0;
 };
@@ -189,7 +189,7 @@ bool plan_team(int type, const void* w, const void* xq, int rows, int k, int bat
     const size_t row_bytes = size_t(k / elems_of(type)) * bytes_of(type);
     const int teams = qmvt::kConsumers * 32 / team;
     const size_t slot = round128(size_t(teams) * row_bytes);
-    const size_t part_off = 256;                                 // 2 x 8 ring mbarriers + the activation one
+    const size_t part_off = 384;   // 2 x 8 ring mbarriers + the activation one; the fused norm's partials at 256
     const size_t act_off = part_off + round128(size_t(2) * teams * std::max(1, team / 32) * 4);
     const size_t ring_off = act_off + round128(size_t(k / 32) * 36);   // the Q8_1 row
     if (ring_off + 2 * slot > size_t(qmvt::kSmemLimit)) return false;
@@ -331,7 +331,7 @@ bool mma_prepare(MmaKernel kern, int slices, int threads, int* max_clusters) {
 }
 
 struct MmaPlan {
-    qmvm::Params p;
+    qmvm::Params p{};
     MmaKernel kern = nullptr;
     int grid = 0, threads = 0;
     size_t smem = 0;
@@ -496,6 +496,43 @@ p100_status run_qmv(int type, const void* w, int rows, int k, const void* xq, in
         default: qmv::qmv_generic_kernel<P100_Q4_K><<<grid, 256, 0, stream>>>(wb, xb, y, rows, k, batch, row_bytes); break;
     }
     return launch_status("qmv_generic_kernel launch");
+}
+
+// Batch-1 mat-vec whose Q8_1 row is rmsnorm(x_in + delta) * norm_w (the
+// decode step's RMSNorm fused into the team kernel; block 0 writes x_in +
+// delta to x_out).  Applies to the team kernel with k = 4096 or 8192 and
+// 16-byte aligned vectors; qmv_norm_applies says whether it does.
+bool qmv_norm_applies(int type, const void* w, int rows, int k, const float* x_in, const float* x_out) {
+    int sms = 0;
+    if (require_sm100(nullptr, &sms) || !known_type(type) || (k != 4096 && k != 8192) || rows <= 0) return false;
+    if (reinterpret_cast<uintptr_t>(x_in) % 16 || reinterpret_cast<uintptr_t>(x_out) % 16 || x_in == x_out) return false;
+    TeamPlan plan;
+    return plan_team(type, w, x_in, rows, k, 1, sms, plan);
+}
+
+p100_status run_qmv_norm(int type, const void* w, int rows, int k, const float* x_in, const float* delta, float* x_out,
+                         const float* norm_w, float eps, float* y, unsigned flags, cudaStream_t stream) {
+    int sms = 0;
+    if (p100_status st = require_sm100(nullptr, &sms)) return st;
+    TeamPlan plan;
+    if (!qmv_norm_applies(type, w, rows, k, x_in, x_out) || !plan_team(type, w, x_in, rows, k, 1, sms, plan) ||
+        reinterpret_cast<uintptr_t>(delta) % 16 || reinterpret_cast<uintptr_t>(norm_w) % 16)
+        return set_error(P100_ERR_INVALID, "fused RMSNorm mat-vec needs the team kernel with k 4096 or 8192");
+    plan.p.w = static_cast<const uint8_t*>(w);
+    plan.p.xq = nullptr;
+    plan.p.y = y;
+    plan.p.col0 = 0;
+    plan.p.x_in = x_in;
+    plan.p.delta = delta;
+    plan.p.x_out = x_out;
+    plan.p.norm_w = norm_w;
+    plan.p.eps = eps;
+    const bool pdl = (flags & P100_QMV_PDL) != 0;
+    switch (type) {
+        case P100_Q4_0: return launch_team_type<P100_Q4_0>(plan, 1, pdl, stream);
+        case P100_Q8_0: return launch_team_type<P100_Q8_0>(plan, 1, pdl, stream);
+        default: return launch_team_type<P100_Q4_K>(plan, 1, pdl, stream);
+    }
 }
 
 // ------------------------------------------------------------------ attention

@@ -47,6 +47,11 @@ struct Decoder {
     DecTensor embed, out_norm, lm_head;
     __half *kcache = nullptr, *vcache = nullptr;   // [layer][nkv][max_ctx][hd]
     float *x = nullptr, *delta = nullptr, *qkv = nullptr, *attn = nullptr, *gu = nullptr, *logits = nullptr;
+    // P100_DEC_FUSED_NORM: the RMSNorms run inside the next mat-vec (team
+    // kernel); the residual alternates between x2 and x, ending in x (2 per
+    // layer + 1 swaps).
+    bool fuse_norm = false;
+    float* x2 = nullptr;
     float *rope = nullptr, *pair = nullptr, *cand = nullptr;
     uint8_t* xq = nullptr;
     int *pos = nullptr, *token = nullptr;
@@ -86,6 +91,7 @@ const char* config_reason(const p100_llama_config& c, int nranks) {
         c.vocab <= 0 || c.max_ctx <= 0)
         return "all model dimensions must be positive";
     if (c.wtype != P100_Q4_0 && c.wtype != P100_Q8_0 && c.wtype != P100_Q4_K) return "unknown weight type";
+    if (c.flags & ~P100_DEC_FUSED_NORM) return "unknown decoder flags";
     if (c.n_head % c.n_head_kv) return "n_head must be divisible by n_head_kv";
     if (c.head_dim != 64 && c.head_dim != 128 && c.head_dim != 256) return "head_dim must be 64, 128 or 256";
     if (c.n_head / c.n_head_kv > 8) return "at most 8 query heads per kv head";
@@ -137,6 +143,7 @@ p100_status dec_alloc(Decoder& d) {
     const size_t at_k = take(kv_elems * 2), at_v = take(kv_elems * 2);
     const int xq_k = std::max(c.hidden, std::max(d.nq * hd, d.ffn));
     const size_t at_x = take(size_t(c.hidden) * 4), at_delta = take(size_t(c.hidden) * 4);
+    const size_t at_x2 = take(size_t(c.hidden) * 4);
     const size_t at_qkv = take(size_t(d.nq + 2 * d.nkv) * hd * 4), at_attn = take(size_t(d.nq) * hd * 4);
     const size_t at_gu = take(size_t(2) * d.ffn * 4), at_logits = take(size_t(d.vocab_n) * 4);
     const size_t at_rope = take(size_t(c.max_ctx) * (hd / 2) * 8);
@@ -160,6 +167,7 @@ p100_status dec_alloc(Decoder& d) {
     d.vcache = reinterpret_cast<__half*>(d.arena + at_v);
     d.x = reinterpret_cast<float*>(d.arena + at_x);
     d.delta = reinterpret_cast<float*>(d.arena + at_delta);
+    d.x2 = reinterpret_cast<float*>(d.arena + at_x2);
     d.qkv = reinterpret_cast<float*>(d.arena + at_qkv);
     d.attn = reinterpret_cast<float*>(d.arena + at_attn);
     d.gu = reinterpret_cast<float*>(d.arena + at_gu);
@@ -274,7 +282,7 @@ p100_status dec_embed_t(Decoder& d, cudaStream_t s) {
     const int slabs = d.cfg.hidden / 32;
     return launch_glue(dec::embed_kernel<T>, dim3((slabs + 255) / 256), dim3(256), s, "embed_kernel launch",
                        static_cast<const uint8_t*>(d.embed.ptr), d.row_bytes_h, d.cfg.vocab, d.cfg.hidden,
-                       static_cast<const int*>(d.token), d.x);
+                       static_cast<const int*>(d.token), d.fuse_norm ? d.x2 : d.x);
 }
 
 // x += delta (or, with peer_reduce, += the peer all-reduce of this epoch),
@@ -310,10 +318,24 @@ p100_status dec_record_step(Decoder& d, cudaStream_t s) {
         case P100_Q8_0: st = dec_embed_t<P100_Q8_0>(d, s); break;
         default: st = dec_embed_t<P100_Q4_K>(d, s); break;
     }
+    // With the fused norms, cur is the residual stream and each norm writes
+    // the updated stream to the other buffer.
+    float* cur = d.fuse_norm ? d.x2 : d.x;
+    auto norm_qmv = [&](const float* delta, const DecTensor& nw, const DecTensor& w, int rows, float* y) {
+        if (!d.fuse_norm) {
+            p100_status e = dec_rmsnorm(d, delta, nw, s, delta != nullptr && d.peer_ar);
+            if (!e) e = run_qmv(t, w.ptr, rows, c.hidden, d.xq, 1, y, P100_QMV_PDL, s);
+            return e;
+        }
+        float* next = cur == d.x ? d.x2 : d.x;
+        const p100_status e = run_qmv_norm(t, w.ptr, rows, c.hidden, cur, delta, next,
+                                           reinterpret_cast<const float*>(nw.ptr), c.norm_eps, y, P100_QMV_PDL, s);
+        cur = next;
+        return e;
+    };
     for (int l = 0; l < c.n_layer && !st; ++l) {
         const size_t layer_off = size_t(l) * d.nkv * hs;
-        st = dec_rmsnorm(d, l == 0 ? nullptr : d.delta, d.attn_norm[l], s, l > 0 && d.peer_ar);
-        if (!st) st = run_qmv(t, d.wqkv[l].ptr, d.wqkv[l].rows, c.hidden, d.xq, 1, d.qkv, P100_QMV_PDL, s);
+        st = norm_qmv(l == 0 ? nullptr : d.delta, d.attn_norm[l], d.wqkv[l], d.wqkv[l].rows, d.qkv);
         if (!st) {
             fa::Params prm = {};
             const FaPlan& plan = d.fa_plan;
@@ -363,16 +385,14 @@ p100_status dec_record_step(Decoder& d, cudaStream_t s) {
         }
         if (!st) st = run_qmv(t, d.wo[l].ptr, c.hidden, d.nq * hd, d.xq, 1, d.delta, P100_QMV_PDL, s);
         if (!st) st = dec_allreduce(d, s);
-        if (!st) st = dec_rmsnorm(d, d.delta, d.ffn_norm[l], s, d.peer_ar);
-        if (!st) st = run_qmv(t, d.wgu[l].ptr, 2 * d.ffn, c.hidden, d.xq, 1, d.gu, P100_QMV_PDL, s);
+        if (!st) st = norm_qmv(d.delta, d.ffn_norm[l], d.wgu[l], 2 * d.ffn, d.gu);
         if (!st)
             st = launch_glue(dec::swiglu_q8_1_kernel, dim3((d.ffn / 32 + 7) / 8, 1), dim3(256), s,
                              "swiglu_q8_1_kernel launch", static_cast<const float*>(d.gu), d.ffn, d.xq);
         if (!st) st = run_qmv(t, d.wdown[l].ptr, c.hidden, d.ffn, d.xq, 1, d.delta, P100_QMV_PDL, s);
         if (!st) st = dec_allreduce(d, s);
     }
-    if (!st) st = dec_rmsnorm(d, d.delta, d.out_norm, s, d.peer_ar);
-    if (!st) st = run_qmv(t, d.lm_head.ptr, d.vocab_n, c.hidden, d.xq, 1, d.logits, P100_QMV_PDL, s);
+    if (!st) st = norm_qmv(d.delta, d.out_norm, d.lm_head, d.vocab_n, d.logits);
     if (st) return st;
     if (!d.tp) {
         return launch_glue(dec::argmax_kernel, dim3(1), dim3(dec::kArgmaxThreads), s, "argmax_kernel launch",
@@ -569,6 +589,24 @@ p100_status p100_rmsnorm_q8_1(float* x, const float* delta, const float* w, floa
     return launch_status("rmsnorm_q8_1_kernel launch");
 }
 
+p100_status p100_qmv_rmsnorm(int type, const void* w, int rows, int k, const float* x_in, const float* delta,
+                             float* x_out, const float* norm_w, float eps, float* y, unsigned flags,
+                             p100_stream_t stream) {
+    clear_error();
+    if (!known_type(type)) return set_error(P100_ERR_INVALID, "unknown weight type %d", type);
+    if (rows < 0 || k <= 0 || k % elems_of(type)) return set_error(P100_ERR_INVALID, "whole weight blocks required");
+    if (!w || !x_in || !norm_w || !y) return set_error(P100_ERR_INVALID, "null buffer");
+    if (flags & ~P100_QMV_PDL) return set_error(P100_ERR_INVALID, "unknown flags 0x%x", flags);
+    if (p100_status st = require_sm100(nullptr, nullptr)) return st;
+    if (rows == 0) return P100_OK;
+    if (x_out == x_in) return set_error(P100_ERR_INVALID, "x_out must not alias x_in");
+    const float* probe_out = x_out ? x_out : x_in + 4;   // alignment probe only when x_out is absent
+    if (!qmv_norm_applies(type, w, rows, k, x_in, probe_out) || reinterpret_cast<uintptr_t>(delta) % 16 ||
+        reinterpret_cast<uintptr_t>(norm_w) % 16)
+        return set_error(P100_ERR_UNSUPPORTED, "fused RMSNorm mat-vec: k 4096 or 8192 and 16-byte aligned buffers");
+    return run_qmv_norm(type, w, rows, k, x_in, delta, x_out, norm_w, eps, y, flags, stream);
+}
+
 p100_status p100_rope_kv_append(float* qkv, int n_head, int n_head_kv, int head_dim, const float* rope_cs,
                                 int max_pos, const int* pos_dev, void* k_cache, void* v_cache,
                                 long long kv_head_stride, p100_stream_t stream) {
@@ -628,6 +666,17 @@ p100_status p100_decoder_create(const p100_llama_config* cfg, p100_tp* tp, p100_
     h->d.sms = sms;
     p100_status st = dec_alloc(h->d);
     if (!st) st = dec_setup_peer_ar(h->d);
+    if (!st) {
+        // P100_DEC_FUSED_NORM: RMSNorm inside the following mat-vec where
+        // the team kernel has it (hidden 4096 or 8192); the one-shot peer
+        // all-reduce keeps its reduce inside the separate RMSNorm kernel.
+        Decoder& d = h->d;
+        const int t = d.cfg.wtype, k = d.cfg.hidden;
+        d.fuse_norm = (d.cfg.flags & P100_DEC_FUSED_NORM) && !d.peer_ar && qmv_norm_applies(t, d.wqkv[0].ptr, d.wqkv[0].rows, k, d.x2, d.x) &&
+                      qmv_norm_applies(t, d.wgu[0].ptr, 2 * d.ffn, k, d.x, d.x2) &&
+                      qmv_norm_applies(t, d.lm_head.ptr, d.vocab_n, k, d.x2, d.x);
+        clear_error();
+    }
     if (st) {
         const std::string why = t_error;
         dec_teardown_peer_ar(h->d);

@@ -34,8 +34,18 @@
 //     is deterministic.
 // The arithmetic per 32-block is the q81 path of qmv::evaluate
 // (qmv_model.cpp:147-180): exact int32 block dots, FP32 scaling.
+//
+// Fused RMSNorm (the decode step, k = 4096 or 8192): instead of reading a
+// Q8_1 row, the consumers build it from the residual stream: v = x_in +
+// delta, y = (v * 1/sqrt(sum v^2 / k + eps)) * w, quantised into shared
+// memory; block 0 also writes v to x_out.  Every consumer warp stands in for
+// four (eight) warps of rmsnorm_q8_1_kernel's 1024-thread layout, with its
+// chunk order, warp butterfly, in-order sum of warp partials and octet
+// quantiser, so the Q8_1 bytes equal that kernel's; the weight stream starts
+// before the norm as usual.
 #pragma once
 #include "common.cuh"
+#include "decode.cuh"
 
 namespace p100b {
 namespace qmvt {
@@ -45,6 +55,9 @@ constexpr int kThreads = (kConsumers + 1) * 32;
 constexpr int kMaxSlots = 8;
 constexpr int kSmemLimit = 227 * 1024;
 constexpr int kLookahead = 2;   // stages in flight past the newest landed one
+// 32 warp partials of the fused norm, between the mbarriers (2 x 8 ring
+// mbarriers + the activation one end at byte 136) and part_off (384).
+constexpr int kNormScratchOff = 256;
 
 // Lanes per row for a row of `ngroups` 256-weight groups: the next power of
 // two up to a warp, whole warps beyond (the host plan uses the same rule).
@@ -79,7 +92,71 @@ struct Params {
     int nslot;
     int slot_bytes;
     int part_off, act_off, ring_off;   // act_off: the Q8_1 row in shared memory
+    // Fused RMSNorm (norm_w not null; the Q8_1 row then comes from these):
+    // x_in, delta (may be null), x_out (may be null; x_in != x_out), eps.
+    const float* x_in;
+    const float* delta;
+    float* x_out;
+    const float* norm_w;
+    float eps;
 };
+
+// The fused RMSNorm prologue: the Q8_1 row of rmsnorm(x_in + delta) * w into
+// xs, by the 8 consumer warps (256 threads), bit-identical to
+// rmsnorm_q8_1_kernel.  NG = k / 256 (16 or 32).
+template <int NG>
+__device__ __forceinline__ void fused_norm_row(const Params& p, uint8_t* xs, float* s_part) {
+    constexpr int k = NG * 256;
+    constexpr int kNC = k / 4;                    // float4 chunks
+    constexpr int kPer = kNC / dec::kNormThreads; // chunks per thread of the 1024-thread layout
+    constexpr int kVW = dec::kNormThreads / 32 / kConsumers;   // its warps per consumer warp
+    static_assert(kNC % dec::kNormThreads == 0 && kPer <= dec::kNormChunks, "k");
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float4* xr = reinterpret_cast<const float4*>(p.x_in);
+    const float4* dr = reinterpret_cast<const float4*>(p.delta);
+    float4* xo = blockIdx.x == 0 ? reinterpret_cast<float4*>(p.x_out) : nullptr;
+    float4 v[kVW][kPer];
+#pragma unroll
+    for (int j = 0; j < kVW; ++j) {
+        const int vt = (warp + kConsumers * j) * 32 + lane;   // thread of the 1024-thread layout
+        float s = 0.f;
+#pragma unroll
+        for (int i = 0; i < kPer; ++i) {
+            const int c = vt + i * dec::kNormThreads;
+            float4 x = xr[c];
+            if (dr) {
+                const float4 d4 = dr[c];
+                x = make_float4(__fadd_rn(x.x, d4.x), __fadd_rn(x.y, d4.y), __fadd_rn(x.z, d4.z), __fadd_rn(x.w, d4.w));
+            }
+            if (xo) xo[c] = x;
+            v[j][i] = x;
+            s = fmaf(x.x, x.x, s);
+            s = fmaf(x.y, x.y, s);
+            s = fmaf(x.z, x.z, s);
+            s = fmaf(x.w, x.w, s);
+        }
+        s = warp_sum(s);
+        if (lane == 0) s_part[warp + kConsumers * j] = s;
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(kConsumers * 32) : "memory");
+    float t = s_part[0];
+    for (int i = 1; i < dec::kNormThreads / 32; ++i) t = __fadd_rn(t, s_part[i]);
+    const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, float(k)), p.eps)));
+    const float4* w4 = reinterpret_cast<const float4*>(p.norm_w);
+#pragma unroll
+    for (int j = 0; j < kVW; ++j) {
+        const int vt = (warp + kConsumers * j) * 32 + lane;
+#pragma unroll
+        for (int i = 0; i < kPer; ++i) {
+            const int c = vt + i * dec::kNormThreads;
+            const float4 wv = w4[c];
+            const float y[4] = {__fmul_rn(__fmul_rn(v[j][i].x, r), wv.x), __fmul_rn(__fmul_rn(v[j][i].y, r), wv.y),
+                                __fmul_rn(__fmul_rn(v[j][i].z, r), wv.z), __fmul_rn(__fmul_rn(v[j][i].w, r), wv.w)};
+            dec::octet_q8_1_block(y, c & 7, xs + size_t(c >> 3) * 36);
+        }
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(kConsumers * 32) : "memory");   // the whole row is written
+}
 
 // Group g of a Q8_1 row held in shared memory.
 template <int TYPE>
@@ -245,12 +322,15 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_team_kernel(const Params p) {
                 bulk_load(ring + size_t(s) * p.slot_bytes, p.w + size_t(first) * p.row_bytes, bytes, &full[s],
                           policy);
             }
-            // the activations may come from the previous kernel
+            // the activations may come from the previous kernel (with the
+            // fused norm the consumers build them and the barrier is unused)
             pdl_wait_prior_grid();
-            asm volatile("fence.proxy.async.global;" ::: "memory");
-            const uint32_t abytes = static_cast<uint32_t>(p.k / 32 * 36);
-            mbar_arrive_expect_tx(act_bar, abytes);
-            bulk_load(smem + p.act_off, p.xq + size_t(p.col0) * abytes, abytes, act_bar, policy);
+            if (!p.norm_w) {
+                asm volatile("fence.proxy.async.global;" ::: "memory");
+                const uint32_t abytes = static_cast<uint32_t>(p.k / 32 * 36);
+                mbar_arrive_expect_tx(act_bar, abytes);
+                bulk_load(smem + p.act_off, p.xq + size_t(p.col0) * abytes, abytes, act_bar, policy);
+            }
             int issued = pre;
             for (int s = pre; s < nst; ++s) {
                 const int slot = s % p.nslot;
@@ -267,7 +347,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_team_kernel(const Params p) {
             }
             // no copy may still be writing shared memory when the block exits
             // (normally everything has landed: the consumers needed it)
-            mbar_wait(act_bar, 0);
+            if (!p.norm_w) mbar_wait(act_bar, 0);
             for (int s = max(0, issued - p.nslot); s < issued; ++s) mbar_wait(&full[s % p.nslot], (s / p.nslot) & 1);
         }
         return;
@@ -278,7 +358,14 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_team_kernel(const Params p) {
     const int team = tid / team_size, tl = tid % team_size;
     const bool has_group = tl < ngroups;
     GroupAct act;
-    {
+    if constexpr (NG == 16 || NG == 32) {
+        if (p.norm_w) {
+            // x_in and delta come from earlier kernels: every consumer waits
+            pdl_wait_prior_grid();
+            fused_norm_row<NG>(p, smem + p.act_off, reinterpret_cast<float*>(smem + kNormScratchOff));
+        }
+    }
+    if (!p.norm_w) {
         const bool ok = mbar_wait(act_bar, 0);
         int any_timeout;
         if (team_size <= 32) {

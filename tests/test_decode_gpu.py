@@ -49,6 +49,42 @@ def test_rmsnorm_q8_1_bit_exact(cuda, orc, k, batch, with_delta):
         assert np.array_equal(got_q[b], oq)
 
 
+@pytest.mark.parametrize("qtype", [P.Q4_0, P.Q8_0, P.Q4_K])
+@pytest.mark.parametrize("k,rows,with_delta", [(4096, 6144, True), (8192, 1000, True), (4096, 300, False)])
+def test_qmv_rmsnorm_equals_two_calls(cuda, qtype, k, rows, with_delta):
+    """The RMSNorm fused into the mat-vec (p100_qmv_rmsnorm) gives the bytes of
+    p100_rmsnorm_q8_1 followed by p100_qmv: same y bits, same residual."""
+    from p100_b200 import workloads as W
+    rng = np.random.default_rng(k + rows)
+    x = rng.standard_normal(k).astype(np.float32)
+    delta = (0.3 * rng.standard_normal(k)).astype(np.float32)
+    nw = rng.uniform(0.9, 1.1, k).astype(np.float32)
+    w = dev(cuda, W.weights(qtype, rows, k, seed=k + rows + qtype))
+    xin, dl, nwd = dev(cuda, x), dev(cuda, delta), dev(cuda, nw)
+    xout = cuda.full((k,), float("nan"), device="cuda")
+    y = P.qmv_rmsnorm(qtype, w, rows, k, xin, nwd, 1e-5, delta=dl if with_delta else None, x_out=xout)
+    ref_x = dev(cuda, x)
+    xq = P.rmsnorm_q8_1(ref_x.view(1, k), nwd, 1e-5, delta=dl.view(1, k) if with_delta else None)
+    yref = P.qmv(qtype, w, rows, k, xq, 1)
+    cuda.cuda.synchronize()
+    assert np.array_equal(xin.cpu().numpy(), x)                      # x_in untouched
+    assert np.array_equal(xout.cpu().numpy(), ref_x.cpu().numpy())   # x_in + delta
+    assert np.array_equal(y.cpu().numpy().view(np.uint32), yref.cpu().numpy().view(np.uint32))
+    assert P.device_error() == P.OK
+
+
+def test_qmv_rmsnorm_rejects_other_shapes(cuda):
+    k, rows = 256, 8
+    w = cuda.zeros(rows * k // 32 * 18, dtype=cuda.uint8, device="cuda")
+    x = cuda.zeros(k, device="cuda")
+    with pytest.raises(P.P100Error):
+        P.qmv_rmsnorm(P.Q4_0, w, rows, k, x, x, 1e-5)
+    x4 = cuda.zeros(4096, device="cuda")
+    w4 = cuda.zeros(rows * 4096 // 32 * 18, dtype=cuda.uint8, device="cuda")
+    with pytest.raises(P.InvalidArgument):
+        P.qmv_rmsnorm(P.Q4_0, w4, rows, 4096, x4, x4, 1e-5, x_out=x4)
+
+
 @pytest.mark.parametrize("pos", [0, 1, 4095])
 def test_rope_kv_append_bit_exact(cuda, orc, pos):
     nq, nkv, hd, max_pos = 32, 8, 128, 4096
@@ -176,6 +212,42 @@ def test_decoder_matches_restated_steps(cuda, orc, wtype, shape):
         assert P.device_error() == P.OK
     finally:
         dec.close()
+
+
+# Hidden 4096 (the 8B head geometry) with P100_DEC_FUSED_NORM: the RMSNorms
+# run inside the following mat-vecs.  The restatement comparison above stays
+# on the tiny model: with 4096-wide normalised activations of O(1) feeding a
+# residual stream of O(0.1), one Q8_1 code that the two summation orders
+# round apart moves the residual by ~5e-3 of its maximum, and at this width
+# that happens every few steps (measured on both the fused and the
+# separate-kernel decoder).  The
+# fusion itself is checked exactly: the same model with every RMSNorm as its
+# own kernel (the default) gives the same bits, step after step.
+H4096 = dict(TINY, hidden=4096, n_head=32, n_head_kv=8, head_dim=128)
+
+
+@pytest.mark.parametrize("wtype", [P.Q4_0, P.Q8_0, P.Q4_K])
+def test_fused_norm_decoder_equals_separate_norm(cuda, wtype):
+    out = []
+    for flags in (P.DEC_FUSED_NORM, 0):
+        dec = P.Decoder(P.LlamaConfig(**H4096, wtype=wtype, flags=flags))
+        try:
+            dec.init_random(4321 + wtype)
+            dec.fill_kv(300, 11, 0.5)
+            dec.set_state(300, 9)
+            steps = []
+            for _ in range(4):
+                dec.step(1)
+                pos, tok = dec.state()
+                steps.append((pos, tok, dec.read(*dec.buffer(P.B_HIDDEN)).copy(),
+                              dec.read(*dec.buffer(P.B_LOGITS)).copy()))
+            out.append(steps)
+            assert P.device_error() == P.OK
+        finally:
+            dec.close()
+    for (pa, ta, ha, la), (pb, tb, hb, lb) in zip(*out):
+        assert (pa, ta) == (pb, tb)
+        assert np.array_equal(ha, hb) and np.array_equal(la, lb)
 
 
 def test_decoder_rejects_bad_configs(cuda):
