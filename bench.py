@@ -383,7 +383,7 @@ def c2_grid(torch, P, stream):
 def kernel_only(args):
     """Eager launches of one kernel over rotating inputs larger than L2 — the
     small cases for ncu captures: the target mat-vec at batch 1 or 16 (5 weight
-    copies, 165 MB) or FA decode at 32K context (2 K/V copies, 268 MB)."""
+    copies, 165 MB) or FA decode at 32K context (2 K/V copies, 268 MB) or 4K."""
     import torch
     import p100_b200 as P
     if args.kernel_only == "decode":
@@ -402,8 +402,8 @@ def kernel_only(args):
         print(json.dumps({"kernel_only": "decode llama3-8b ctx 4096", "steps": args.warmup + args.steps,
                           "position": pos, "token": tok}))
         return 0
-    if args.kernel_only == "fa":
-        seq = 32768
+    if args.kernel_only in ("fa", "fa4096"):
+        seq = 32768 if args.kernel_only == "fa" else 4096
         q, k, v = W.attention_inputs(1, 32, 8, seq, 128, seed=seq)
         qd = torch.from_numpy(q).cuda()
         kd = [torch.from_numpy(k).cuda() for _ in range(2)]
@@ -438,8 +438,9 @@ def main():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the 8B/70B decode section")
-    ap.add_argument("--kernel-only", choices=["qmv", "qmvb", "fa", "decode"],
-                    help="one kernel's launches only (ncu cases); qmvb = the target shape at batch 16")
+    ap.add_argument("--kernel-only", choices=["qmv", "qmvb", "fa", "fa4096", "decode"],
+                    help="one kernel's launches only (ncu cases); qmvb = the target shape at batch 16, "
+                         "fa = 32768 keys, fa4096 = 4096 keys")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
