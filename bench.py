@@ -250,6 +250,32 @@ def time_graphs(torch, graphs, n, stream):
 FA_CONTEXTS = (512, 4096, 16384, 32768)
 
 
+def h16_section(torch, P, stream):
+    """The h16 activation path (qmv::h16_model; HFMA2 chain 16) on the
+    Llama-3-8B layer shapes at batch 1, Q4_0: graph-replayed back-to-back
+    calls over rotating weight copies beyond 3x L2.  GB/s counts the weights,
+    the fp16 activations with their {scale, sum} record, and the outputs."""
+    peak = peak_gbs()[0]
+    out = {}
+    for si, (name, k, rows) in enumerate(SHAPES):
+        base = torch.from_numpy(W.weights(W.Q4_0, rows, k, seed=6000 + si)).cuda()
+        copies = max(4, int(np.ceil(3 * L2_BYTES / base.numel())) + 1)
+        ws = [base] + [base.clone() for _ in range(copies - 1)]
+        h, ss = P.h16_prepare(torch.from_numpy(W.activations(1, k, seed=6100 + si)).cuda())
+        y = torch.empty(1, rows, dtype=torch.float32, device="cuda")
+        n_in_graph = max(16, copies)
+        g = capture(torch, lambda: [P.qmv_h16(W.Q4_0, ws[r % copies], rows, k, h, ss, 1, 16, y=y)
+                                    for r in range(n_in_graph)])
+        time_graphs(torch, [g], 2, stream)
+        reps = 5
+        us = time_graphs(torch, [g], reps, stream) / (reps * n_in_graph) * 1e3
+        nbytes = base.numel() + k * 2 + (k // 32) * 8 + rows * 4
+        out[f"{name} {k}x{rows}"] = {"us": round(us, 3), "GB/s": round(nbytes / (us / 1e6) / 1e9, 1),
+                                     "frac": round(nbytes / (us / 1e6) / 1e9 / peak, 4)}
+        del g, ws, base
+    return out
+
+
 def fa_section(torch, P, stream):
     """Config 3: FA-vec decode, 32 query / 8 KV heads, d 128, per context
     length; K/V rotate over copies totalling more than 3x L2; a CUDA graph of
@@ -578,6 +604,7 @@ def main():
     e2e_eager = per_step * world * args.steps / (e2e_eager_ms / 1e3) / 1e9
     del e2e_graphs
     fa = fa_section(torch, P, stream) if rank == 0 else None
+    h16 = h16_section(torch, P, stream) if rank == 0 else None
     P.check(P.device_error())
     decode = decode_section(torch, P, stream, rank, world, dist, max_over_ranks) if not args.no_decode else None
 
@@ -606,6 +633,7 @@ def main():
         "shapes": shape_gbs,
         "batch_sweep": batch_sweep,
         "fa_decode": fa,
+        "h16_qmv": h16,
         "decode": decode,
         "clocks": clocks.summary(),
         "checksum": round(checksum, 3),

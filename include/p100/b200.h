@@ -105,6 +105,23 @@ p100_status p100_qmv(int type, const void* w, int rows, int k, const void* x_q8_
 p100_status p100_qmv_ex(int type, const void* w, int rows, int k, const void* x_q8_1,
                         int batch, float* y, unsigned flags, p100_stream_t stream);
 
+/* ---------------------------------------------------- h16 activation path */
+/* The FP16-activation mat-vec, qmv::h16_model (qmv_model.cpp:53-71,92-133;
+ * the reference's GPU prototype h16_prepass / mmv_h2_<type>,
+ * bench/micro/h2_mmv.cu:99-176, with the same two-buffer layout).
+ * p100_h16_prepare: x [batch][k] fp32 -> h [batch][k] fp16 (per 32-block
+ * fp16(x / max|x|) in the 0,2,1,3 order of each group of four) and
+ * ss [batch][k/32][2] fp32 {max|x|, butterfly sum of the rounded h}; the
+ * same bits as qmv::prepare.  k % 32 == 0, ss 8-byte aligned. */
+p100_status p100_h16_prepare(const float* x, void* h, float* ss, int k, int batch, p100_stream_t stream);
+/* y[c*rows + r] = h16_model(row r, column c) with HFMA2 chains of `chain`
+ * (8: the model's h8, 16: h16): each 32-block's value equals the model's bit
+ * for bit; a row adds its blocks in order within each 128-column range and
+ * the ranges by a fixed butterfly (k = 128: the model's row exactly).
+ * k % 128 == 0 (Q4_K: % 256), k <= 32768, w and h 16-byte aligned. */
+p100_status p100_qmv_h16(int type, const void* w, int rows, int k, const void* h, const float* ss, int batch,
+                         int chain, float* y, p100_stream_t stream);
+
 /* ---------------------------------------------------- FlashAttention decode */
 /* AttnParams (include/p100/attention.h:27-41) plus the split and the strides of
  * a KV cache whose capacity exceeds seq_kv.  Layouts (attention.h:8-14):

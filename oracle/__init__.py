@@ -127,6 +127,7 @@ class Oracle(_Base):
         self._dequantize = f("dequantize", ip, ip, vp, ip, ip, vp)
         self._evaluate = f("evaluate", ip, ip, vp, vp, ip, vp, vp)
         self._qmv = f("qmv_q81", ip, ip, vp, ip, ip, vp, ip, vp)
+        self._qmv_h16 = f("qmv_h16", ip, ip, vp, ip, ip, vp, ip, ip, vp)
         self._qmv_mt = f("qmv_q81_threaded", C.c_double, ip, vp, ip, ip, vp, ip, vp, ip)
         self._validate = f("attn_validate", ip, vp, C.c_char_p, ip)
         self._attn_ref = f("attention_reference", ip, vp, vp, vp, vp, vp, vp, vp)
@@ -201,6 +202,12 @@ class Oracle(_Base):
     def qmv_q81(self, type_, w, rows, k, acts, batch):
         y = np.zeros(batch * rows, dtype=np.float32)
         self._check(self._qmv(type_, _ptr(np.ascontiguousarray(w)), rows, k, _ptr(acts), batch, _ptr(y)))
+        return y.reshape(batch, rows)
+
+    def qmv_h16(self, type_, w, rows, k, acts, batch, chain):
+        """qmv::h16_model for every row and column (chain 8 = h8, 16 = h16)."""
+        y = np.zeros(batch * rows, dtype=np.float32)
+        self._check(self._qmv_h16(type_, _ptr(np.ascontiguousarray(w)), rows, k, _ptr(acts), batch, chain, _ptr(y)))
         return y.reshape(batch, rows)
 
     def qmv_q81_threaded(self, type_, w, rows, k, acts, batch, nthreads):

@@ -452,6 +452,20 @@ int p100o_evaluate(int type, const void* w_row, const float* x, int k, const p10
     return 0;
 }
 
+// qmv::h16_model (qmv_model.cpp:120-133) for every row and column,
+// y[c*rows + r]; acts holds batch rows of k/32 blocks.
+int p100o_qmv_h16(int type, const void* w, int rows, int k, const p100o_act* acts, int batch, int chain, float* y) {
+    if (!check_qmv_shape(type, k)) return -1;
+    if (rows < 0 || batch <= 0) return fail("rows must be non-negative and batch positive");
+    if (chain != 8 && chain != 16) return fail("invalid h16 shape/chain");   // qmv_model.cpp:122
+    const size_t rb = size_t(k / elems_of(type)) * bytes_of(type);
+    const uint8_t* wb = static_cast<const uint8_t*>(w);
+    for (int c = 0; c < batch; ++c)
+        for (int r = 0; r < rows; ++r)
+            y[size_t(c) * rows + r] = h16_model(type, wb + r * rb, k, acts + size_t(c) * (k / 32), chain);
+    return 0;
+}
+
 int p100o_qmv_q81(int type, const void* w, int rows, int k, const p100o_act* acts, int batch, float* y) {
     if (!check_qmv_shape(type, k)) return -1;
     if (rows < 0 || batch <= 0) return fail("rows must be non-negative and batch positive");

@@ -84,6 +84,9 @@ typedef struct p100o_eval {
 int p100o_evaluate(int type, const void* w_row, const float* x, int k,
                    const p100o_act* acts, p100o_eval* out);
 
+/* The h16 path only (qmv::h16_model, qmv_model.cpp:120-133, HFMA2 chain of
+ * 8 or 16) for rows x batch outputs, y[c*rows + r]. */
+int p100o_qmv_h16(int type, const void* w, int rows, int k, const p100o_act* acts, int batch, int chain, float* y);
 /* The q81 path only (qmv_model.cpp:147-180) for rows x batch outputs,
  * y[c*rows + r]; acts holds batch rows of k/32 blocks. */
 int p100o_qmv_q81(int type, const void* w, int rows, int k,

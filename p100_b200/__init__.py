@@ -89,6 +89,8 @@ def _bind(lib):
         "p100_dequantize": (ip, [ip, vp, ip, ip, vp, st]),
         "p100_qmv": (ip, [ip, vp, ip, ip, vp, ip, vp, st]),
         "p100_qmv_ex": (ip, [ip, vp, ip, ip, vp, ip, vp, C.c_uint, st]),
+        "p100_h16_prepare": (ip, [vp, vp, vp, ip, ip, st]),
+        "p100_qmv_h16": (ip, [ip, vp, ip, ip, vp, vp, ip, ip, vp, st]),
         "p100_attn_validate": (ip, [vp, C.c_char_p, sz]),
         "p100_fa_workspace_size": (sz, [vp]),
         "p100_fa_workspace_init": (ip, [vp, sz, st]),
@@ -208,6 +210,29 @@ def q8_1_quantize(x, out=None, stream=None):
         out = torch.empty(batch * (k // 32) * Q8_1_BLOCK_BYTES, dtype=torch.uint8, device=x.device)
     check(lib().p100_q8_1_quantize(_ptr(x), _ptr(out), k, batch, _stream(stream)))
     return out
+
+
+def h16_prepare(x, stream=None):
+    """h16 activations of x (fp32 [batch, k] on the GPU): (h fp16 [batch, k] in
+    the stored 0,2,1,3 order, ss fp32 [batch, k/32, 2] {scale, sum})
+    (p100_h16_prepare, qmv::prepare's h16 fields)."""
+    torch = _torch()
+    x = x.contiguous()
+    k = x.shape[-1]
+    batch = x.numel() // k
+    h = torch.empty(batch, k, dtype=torch.float16, device=x.device)
+    ss = torch.empty(batch, k // 32, 2, dtype=torch.float32, device=x.device)
+    check(lib().p100_h16_prepare(_ptr(x), _ptr(h), _ptr(ss), k, batch, _stream(stream)))
+    return h, ss
+
+
+def qmv_h16(qtype, w, rows, k, h, ss, batch=1, chain=16, y=None, stream=None):
+    """y[batch, rows] = qmv::h16_model with HFMA2 chains of `chain` (p100_qmv_h16)."""
+    torch = _torch()
+    if y is None:
+        y = torch.empty(batch, rows, dtype=torch.float32, device=h.device)
+    check(lib().p100_qmv_h16(qtype, _ptr(w), rows, k, _ptr(h), _ptr(ss), batch, chain, _ptr(y), _stream(stream)))
+    return y
 
 
 def dequantize(qtype, w, rows, k, out=None, stream=None):

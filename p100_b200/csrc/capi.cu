@@ -17,6 +17,7 @@
 #include "common.cuh"
 #include "fa_decode.cuh"
 #include "fa_mma.cuh"
+#include "h16.cuh"
 #include "qmv.cuh"
 #include "qmv_mma.cuh"
 #include "qmv_team.cuh"
@@ -927,6 +928,79 @@ p100_status p100_fa_decode(const p100_attn_desc* desc, const float* q, const voi
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------ h16 path
+namespace p100b {
+namespace {
+template <int TYPE, int CHAIN>
+p100_status launch_h16_t(const h16::Params& p, int grid, cudaStream_t stream) {
+    h16::qmv_h16_kernel<TYPE, CHAIN><<<grid, h16::kThreads, h16::kWarps * sizeof(float), stream>>>(p);
+    return launch_status("qmv_h16_kernel launch");
+}
+template <int TYPE>
+p100_status launch_h16_type(const h16::Params& p, int chain, int grid, cudaStream_t s) {
+    return chain == 8 ? launch_h16_t<TYPE, 8>(p, grid, s) : launch_h16_t<TYPE, 16>(p, grid, s);
+}
+}  // namespace
+}  // namespace p100b
+
+extern "C" p100_status p100_h16_prepare(const float* x, void* h, float* ss, int k, int batch, p100_stream_t stream) {
+    clear_error();
+    if (k <= 0 || k % 32) return set_error(P100_ERR_INVALID, "whole activation blocks required");
+    if (batch <= 0) return set_error(P100_ERR_INVALID, "batch must be positive");
+    if (!x || !h || !ss) return set_error(P100_ERR_INVALID, "null buffer");
+    if (reinterpret_cast<uintptr_t>(ss) % 8) return set_error(P100_ERR_INVALID, "ss must be 8-byte aligned");
+    if (p100_status st = require_sm100(nullptr, nullptr)) return st;
+    const long long nblk = static_cast<long long>(batch) * (k / 32);
+    if (nblk > (1ll << 30)) return set_error(P100_ERR_INVALID, "activation too large");
+    const int per = 256 / 32;
+    h16::h16_prepare_kernel<<<static_cast<int>((nblk + per - 1) / per), 256, 0, stream>>>(
+        x, static_cast<__half*>(h), reinterpret_cast<float2*>(ss), k, static_cast<int>(nblk));
+    return launch_status("h16_prepare_kernel launch");
+}
+
+extern "C" p100_status p100_qmv_h16(int type, const void* w, int rows, int k, const void* h, const float* ss, int batch,
+                                    int chain, float* y, p100_stream_t stream) {
+    clear_error();
+    if (!known_type(type)) return set_error(P100_ERR_INVALID, "unknown weight type %d", type);
+    if (k <= 0 || k % elems_of(type)) return set_error(P100_ERR_INVALID, "whole weight blocks required");
+    if (chain != 8 && chain != 16) return set_error(P100_ERR_INVALID, "invalid h16 shape/chain");
+    if (rows < 0 || batch <= 0) return set_error(P100_ERR_INVALID, "rows must be non-negative and batch positive");
+    if (!w || !h || !ss || !y) return set_error(P100_ERR_INVALID, "null buffer");
+    if (k % h16::kLaneElems || k / h16::kLaneElems > h16::kThreads)
+        return set_error(P100_ERR_UNSUPPORTED, "h16 mat-vec needs k a multiple of 128, at most %d",
+                         h16::kLaneElems * h16::kThreads);
+    if (reinterpret_cast<uintptr_t>(w) % 16 || reinterpret_cast<uintptr_t>(h) % 16 ||
+        reinterpret_cast<uintptr_t>(ss) % 8)
+        return set_error(P100_ERR_INVALID, "w and h must be 16-byte aligned, ss 8-byte aligned");
+    int sms = 0;
+    if (p100_status st = require_sm100(nullptr, &sms)) return st;
+    if (rows == 0) return P100_OK;
+    h16::Params p{};
+    p.w = static_cast<const uint8_t*>(w);
+    p.rows = rows;
+    p.k = k;
+    p.row_bytes = static_cast<int>(size_t(k / elems_of(type)) * bytes_of(type));
+    p.team = k / h16::kLaneElems;
+    int pad = 1;
+    while (pad < p.team) pad *= 2;
+    p.team_pad = pad;
+    const int teams = h16::kThreads / pad;
+    const int grid = std::max(1, std::min(sms, (rows + teams - 1) / teams));
+    for (int c = 0; c < batch; ++c) {
+        p.h = static_cast<const __half*>(h) + size_t(c) * k;
+        p.ss = reinterpret_cast<const float2*>(ss) + size_t(c) * (k / 32);
+        p.y = y + size_t(c) * rows;
+        p100_status st;
+        switch (type) {
+            case P100_Q4_0: st = launch_h16_type<P100_Q4_0>(p, chain, grid, stream); break;
+            case P100_Q8_0: st = launch_h16_type<P100_Q8_0>(p, chain, grid, stream); break;
+            default: st = launch_h16_type<P100_Q4_K>(p, chain, grid, stream); break;
+        }
+        if (st) return st;
+    }
+    return P100_OK;
+}
 
 // ------------------------------------------------------------------ decode without a workspace argument
 // For callers that may not allocate device memory (see p100_fa_decode_static

@@ -193,7 +193,6 @@ __global__ void __launch_bounds__(max_threads(BPW, NCG), 1) qmv_mma_kernel(const
     static_assert(TYPE != P100_Q4_K || BPW % 8 == 0, "whole Q4_K super-blocks per warp");
     static_assert(NCG == 1 || NCG == 2, "column groups");
     constexpr int kBlk = TYPE == P100_Q4_0 ? 18 : 34;
-    constexpr int kPairWords = kBlk / 2;     // 32-bit words per pair of Q4_0/Q8_0 blocks (9 or 17)
     constexpr int kRows = stage_rows(TYPE);
     constexpr bool kHi = kRows == 16;        // rows g+8 of the m16 tile hold weights
     constexpr bool kNibbles = TYPE != P100_Q8_0;
@@ -351,8 +350,8 @@ __global__ void __launch_bounds__(max_threads(BPW, NCG), 1) qmv_mma_kernel(const
                     const uint32_t* p1 = reinterpret_cast<const uint32_t*>(row_hi + size_t(b) * kBlk);
                     // Weight scales of rows g (and g+8): block b in the low
                     // half of the pair's word 0, block b+1 in the high half of
-                    // word kPairWords/2.  Lane t = 0 of the row's quad loaded
-                    // word 0 and lane t = 3 loaded word kPairWords/2 for the
+                    // word 4 (Q4_0) or 8 (Q8_0).  Lane t = 0 of the row's quad
+                    // loaded word 0 and lane t = 3 the other for the
                     // fragments; shuffles hand them to the quad, so shared
                     // memory serves only fragment words.
                     const int quad0 = lane & ~3, quad3 = lane | 3;

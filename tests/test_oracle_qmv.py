@@ -138,3 +138,20 @@ def test_evaluate_matches_reference(orc, ref, t):
             b = ref.evaluate(t, w[r * rb:(r + 1) * rb], x, acts)
             for field in a:
                 assert np.asarray(a[field]).tobytes() == np.asarray(b[field]).tobytes(), field
+
+
+@pytest.mark.parametrize("qtype", [0, 1, 2])
+def test_h16_rows_equal_evaluate(orc, qtype):
+    """p100o_qmv_h16 (the rows x columns h16 path the GPU tests compare with)
+    is evaluate().h16 / .h8 row by row, bit for bit."""
+    k, rows = 512, 6
+    w = orc.random_rows(qtype, k, rows, 13 + qtype)
+    x = np.random.default_rng(qtype).standard_normal((2, k)).astype(np.float32)
+    acts = np.concatenate([orc.prepare(xc) for xc in x])
+    rb = w.size // rows
+    for chain, key in ((16, "h16"), (8, "h8")):
+        y = orc.qmv_h16(qtype, w, rows, k, acts, 2, chain)
+        for c in range(2):
+            for r in range(rows):
+                e = orc.evaluate(qtype, w[r * rb:(r + 1) * rb], x[c], orc.prepare(x[c]))
+                assert np.float32(e[key]).view(np.uint32) == y[c, r].view(np.uint32)
