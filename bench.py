@@ -305,6 +305,63 @@ def fa_section(torch, P, stream):
     return out
 
 
+def kv_quant_section(torch, P, stream):
+    """Quantised K/V cache (llama.cpp -ctk/-ctv q8_0, q4_0; bench/phase0.sh:127):
+    (1) FA-vec decode over q8_0 / q4_0 K/V, config 3's heads (32 q / 8 kv,
+    d 128) per context length, timed as fa_section times fp16; GB/s counts the
+    quantised K/V bytes.  (2) p100_kv_to_f16 on the reference's conversion
+    shapes (bench/micro/dequant_nc.cu:209-214; its token-major view), GB/s =
+    block bytes read + fp16 bytes written, sources rotating beyond 3x L2."""
+    peak = peak_gbs()[0]
+    fa, conv = {}, {}
+    for kv_type, name in ((P.KV_Q8_0, "q8_0"), (P.KV_Q4_0, "q4_0")):
+        fa[name] = {}
+        for seq in FA_CONTEXTS:
+            q, _, _ = W.attention_inputs(1, 32, 8, seq, 128, seed=seq)
+            kb = W.kv_cache_blocks(kv_type, 1, 8, seq, 128, seed=seq + 1)
+            vb = W.kv_cache_blocks(kv_type, 1, 8, seq, 128, seed=seq + 2)
+            copies = max(2, int(np.ceil(3 * L2_BYTES / (kb.nbytes * 2))) + 1)
+            qd = torch.from_numpy(q).cuda()
+            kd = [torch.from_numpy(kb).cuda() for _ in range(copies)]
+            vd = [torch.from_numpy(vb).cuda() for _ in range(copies)]
+            desc = P.AttnDesc(n_head_q=32, n_head_kv=8, seq_kv=seq, kv_type=kv_type)
+            ws = P.fa_workspace(desc)
+            o = torch.empty(1, 32, 1, 128, device="cuda")
+            lse = torch.empty(1, 32, 1, device="cuda")
+            reps = max(4, 64 // copies)
+            g = capture(torch, lambda: [P.fa_decode(desc, qd, kd[r % copies], vd[r % copies], o=o, lse=lse, ws=ws)
+                                        for r in range(copies * reps)])
+            time_graphs(torch, [g], 2, stream)
+            n = 10
+            us = time_graphs(torch, [g], n, stream) / (n * copies * reps) * 1e3
+            nbytes = W.fa_algorithmic_bytes(1, 32, 8, seq, 128, kv_type)
+            fa[name][str(seq)] = {"us": round(us, 3), "GB/s": round(nbytes / (us / 1e6) / 1e9, 1),
+                                  "frac": round(nbytes / (us / 1e6) / 1e9 / peak, 4)}
+            del kd, vd, g
+        conv[name] = {}
+        for d, n_kv, nh in ((64, 7680, 8), (128, 16384, 8), (256, 16384, 2), (256, 32768, 4)):
+            nb = d // 32
+            bb = P.KV_BLOCK_BYTES[kv_type]
+            src_bytes = nb * nh * n_kv * bb
+            copies = max(2, int(np.ceil(3 * L2_BYTES / (src_bytes + n_kv * nh * d * 2))) + 1)
+            srcs = [torch.randint(0, 256, (src_bytes,), dtype=torch.uint8, device="cuda") for _ in range(copies)]
+            for s_ in srcs:   # finite fp16 scales: d in [0.01, 0.02)
+                s_.view(-1, bb)[:, 1] = 0x20 + (s_.view(-1, bb)[:, 1] & 3)
+            dst = torch.empty(nh, n_kv, d, dtype=torch.float16, device="cuda")
+            args = (d, n_kv, nh, 1, nb * nh, nb, nb * nh * n_kv)
+            reps = max(8, 64 // copies)
+            g = capture(torch, lambda: [P.kv_to_f16(kv_type, srcs[r % copies], *args, out=dst)
+                                        for r in range(copies * reps)])
+            time_graphs(torch, [g], 2, stream)
+            n = 10
+            us = time_graphs(torch, [g], n, stream) / (n * copies * reps) * 1e3
+            nbytes = src_bytes + n_kv * nh * d * 2
+            conv[name][f"d{d}_kv{n_kv}_h{nh}"] = {"us": round(us, 3), "GB/s": round(nbytes / (us / 1e6) / 1e9, 1),
+                                                  "frac": round(nbytes / (us / 1e6) / 1e9 / peak, 4)}
+            del srcs, g
+    return {"fa_decode": fa, "kv_to_f16": conv}
+
+
 DECODE_MODELS = {   # BASELINE configs 4 and 5: Llama-3 8B / 70B shapes, random-init Q4_0
     "llama3-8b": dict(n_layer=32, hidden=4096, n_head=32, n_head_kv=8, head_dim=128, ffn=14336, vocab=128256,
                       ctx=4096),
@@ -605,6 +662,7 @@ def main():
     del e2e_graphs
     fa = fa_section(torch, P, stream) if rank == 0 else None
     h16 = h16_section(torch, P, stream) if rank == 0 else None
+    kvq = kv_quant_section(torch, P, stream) if rank == 0 else None
     P.check(P.device_error())
     decode = decode_section(torch, P, stream, rank, world, dist, max_over_ranks) if not args.no_decode else None
 
@@ -634,6 +692,7 @@ def main():
         "batch_sweep": batch_sweep,
         "fa_decode": fa,
         "h16_qmv": h16,
+        "quantised_kv": kvq,
         "decode": decode,
         "clocks": clocks.summary(),
         "checksum": round(checksum, 3),

@@ -31,7 +31,7 @@
 extern "C" {
 #endif
 
-#define P100_B200_ABI_VERSION 1
+#define P100_B200_ABI_VERSION 2
 
 typedef enum p100_status {
     P100_OK = 0,
@@ -44,6 +44,12 @@ typedef enum p100_status {
 
 /* Weight formats in the order of p100::qmv::Type (include/p100/qmv.h:20). */
 typedef enum p100_qtype { P100_Q4_0 = 0, P100_Q8_0 = 1, P100_Q4_K = 2 } p100_qtype;
+
+/* K/V cache element types (llama.cpp's -ctk / -ctv f16, q8_0, q4_0, the
+ * cache types the reference benchmarks: bench/phase0.sh:127).  A quantised
+ * row of d values is d/32 ggml blocks along the head dimension: q8_0
+ * {fp16 d, int8 q[32]} (34 bytes), q4_0 {fp16 d, u8 qs[16]} (18 bytes). */
+typedef enum p100_kv_type { P100_KV_F16 = 0, P100_KV_Q8_0 = 1, P100_KV_Q4_0 = 2 } p100_kv_type;
 
 /* Same type as cudaStream_t; 0 is the legacy default stream. */
 typedef struct CUstream_st* p100_stream_t;
@@ -131,7 +137,14 @@ p100_status p100_qmv_h16(int type, const void* w, int rows, int k, const void* h
  *   o   fp32 [batch][n_head_q][seq_q][d_v]
  *   lse fp32 [batch][n_head_q][seq_q]  (natural log; -inf for a fully masked row)
  *   mask fp32 [seq_q][seq_kv], additive, optional.
- * Query head h reads kv head h / (n_head_q / n_head_kv). */
+ * Query head h reads kv head h / (n_head_q / n_head_kv).
+ * With kv_type q8_0 / q4_0, k and v hold the same rows as blocks (a row of
+ * d values is d/32 blocks); strides still count values and must be
+ * multiples of 64, and the kernel reads the blocks directly, with the
+ * values dequantize_q8_0 / dequantize_q4_0 give (bench/micro/
+ * dequant_nc.cu:32-48): the result equals p100_kv_to_f16 followed by the
+ * fp16 decode bit for bit.  Quantised K/V need d 64 or 128 and 1, 2, 4 or 8
+ * query heads per kv head. */
 typedef struct p100_attn_desc {
     int batch, n_head_q, n_head_kv, seq_q, seq_kv, d_qk, d_v;
     float scale;      /* 0 means 1/sqrt(d_qk)          */
@@ -140,6 +153,7 @@ typedef struct p100_attn_desc {
     int kv_splits;    /* split-K parts per head, 0 = chosen for the device */
     long long kv_head_stride;   /* elements between kv heads, 0 = seq_kv * d */
     long long kv_batch_stride;  /* elements between batches,  0 = n_head_kv * head stride */
+    int kv_type;      /* p100_kv_type of k and v; 0 = fp16 */
 } p100_attn_desc;
 
 /* validate (attention_reference.cpp:18-32): P100_OK, or P100_ERR_INVALID with
@@ -176,6 +190,20 @@ p100_status p100_fa_decode(const p100_attn_desc* desc, const float* q, const voi
 p100_status p100_fa_decode_static(const p100_attn_desc* desc, const float* q, const void* k,
                                   const void* v, const float* mask, float* o, float* lse,
                                   p100_stream_t stream);
+
+/* Quantised K/V view -> contiguous fp16: llama.cpp's ggml_get_to_fp16_nc_cuda
+ * for q8_0 / q4_0 as FlashAttention's tile and MMA kernels call it before
+ * every attention call, replacing dequantize_block and the reference's
+ * dequantize_block_q_0_nc (bench/micro/dequant_nc.cu:53-121, patch 0002).
+ * Value i00 of row i01 of plane (i02, i03) is value i00 % 32 of block
+ * i03*s03 + i02*s02 + i01*s01 + i00/32 of src (strides in blocks, as ggml's
+ * nb / type size); dst[((i03*ne02 + i02)*ne01 + i01)*ne00 + i00] =
+ * fp16(float(q) * d) (q8_0) or fp16((float(nib) - 8) * d) (q4_0), nearest
+ * even.  ne00 % 32 == 0, ne01 * ne00 / 8 < 2^31, src 2-byte and dst 16-byte
+ * aligned. */
+p100_status p100_kv_to_f16(int kv_type, const void* src, long long ne00, long long ne01, long long ne02,
+                           long long ne03, long long s01, long long s02, long long s03, void* dst,
+                           p100_stream_t stream);
 
 /* ---------------------------------------------------- decode-step glue */
 /* The reference stops at one mat-vec and one attention call; it has no decode

@@ -33,6 +33,11 @@ TYPE_NAMES = {Q4_0: "q4_0", Q8_0: "q8_0", Q4_K: "q4_K"}
 BLOCK_ELEMS = {Q4_0: 32, Q8_0: 32, Q4_K: 256}
 BLOCK_BYTES = {Q4_0: 18, Q8_0: 34, Q4_K: 144}
 
+# K/V cache element types (kv_oracle.cpp); a quantised row of d values holds
+# d / 32 blocks of KV_BLOCK_BYTES.
+KV_F16, KV_Q8_0, KV_Q4_0 = 0, 1, 2
+KV_BLOCK_BYTES = {KV_Q8_0: 34, KV_Q4_0: 18}
+
 # p100o_act / qmv::ActivationBlock: 68 four-byte fields.
 ACT_DTYPE = np.dtype([("scale", "<f4"), ("sum", "<f4"), ("h", "<f4", (32,)),
                       ("qd", "<f4"), ("qsum", "<f4"), ("q", "<i4", (32,))])
@@ -142,6 +147,11 @@ class Oracle(_Base):
         self._swiglu = f("swiglu_q8_1", ip, vp, ip, vp)
         self._argmax = f("argmax", ip, vp, ip, vp)
         self._decode_step = f("decode_step", ip, vp, vp, vp, vp, vp, ip, ip, vp, vp)
+        ll = C.c_int64
+        self.kv_block_bytes = f("kv_block_bytes", ip, ip)
+        self._kv_to_f16 = f("kv_to_f16", ip, ip, vp, ll, ll, ll, ll, ll, ll, ll, vp)
+        self._kv_lcg = f("kv_lcg_blocks", None, ip, C.c_size_t, C.c_uint32, vp)
+        self._kv_quantize = f("kv_quantize", ip, ip, vp, C.c_size_t, vp)
 
     # ------------------------------------------------------------ seeded inputs
     def fill_normal(self, seed, n, mean=0.0, stddev=1.0, round_fp16=False):
@@ -282,6 +292,32 @@ class Oracle(_Base):
         x = np.ascontiguousarray(x, dtype=np.float32)
         val = np.zeros(1, dtype=np.float32)
         return self._argmax(_ptr(x), x.size, _ptr(val)), float(val[0])
+
+    # ------------------------------------------------------ quantised K/V cache
+    def kv_to_f16(self, kv_type, src, ne00, ne01, ne02=1, ne03=1, s01=None, s02=None, s03=None):
+        """dequantize_block over a K/V view (dequant_nc.cu:53-121): fp16
+        [ne03][ne02][ne01][ne00]; block strides default to a contiguous view."""
+        nb = ne00 // 32
+        s01 = nb if s01 is None else s01
+        s02 = nb * ne01 if s02 is None else s02
+        s03 = s02 * ne02 if s03 is None else s03
+        src = np.ascontiguousarray(src, dtype=np.uint8)
+        out = np.zeros((ne03, ne02, ne01, ne00), dtype=np.uint16)
+        self._check(self._kv_to_f16(kv_type, _ptr(src), ne00, ne01, ne02, ne03, s01, s02, s03, _ptr(out)))
+        return out.view(np.float16)
+
+    def kv_lcg_blocks(self, kv_type, nblk, seed=12345):
+        """nblk blocks from the reference's generator (dequant_nc.cu:144-149)."""
+        out = np.zeros(nblk * KV_BLOCK_BYTES[kv_type], dtype=np.uint8)
+        self._kv_lcg(kv_type, nblk, seed, _ptr(out))
+        return out
+
+    def kv_quantize(self, kv_type, x):
+        """ggml's q8_0 / q4_0 block quantiser over x (size % 32 == 0): bytes."""
+        x = np.ascontiguousarray(x, dtype=np.float32).ravel()
+        out = np.zeros(x.size // 32 * KV_BLOCK_BYTES[kv_type], dtype=np.uint8)
+        self._check(self._kv_quantize(kv_type, _ptr(x), x.size, _ptr(out)))
+        return out
 
     def decode_step(self, cfg, weights, k_cache, v_cache, rope_cs, pos, token):
         """One token of the restated decoder.  cfg: LlamaConfig; weights: dict of

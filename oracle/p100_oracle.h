@@ -168,6 +168,20 @@ int p100o_decode_step(const p100o_llama* cfg, const p100o_llama_weights* w, uint
                       uint16_t* v_cache, const float* rope_cs, int pos, int token, float* logits,
                       float* hidden_out);
 
+/* ---- quantised K/V cache (kv_oracle.cpp) */
+enum { P100O_KV_F16 = 0, P100O_KV_Q8_0 = 1, P100O_KV_Q4_0 = 2 };
+/* 34 (q8_0), 18 (q4_0), else 0. */
+int p100o_kv_block_bytes(int kv_type);
+/* dequantize_block over a K/V view (bench/micro/dequant_nc.cu:32-121):
+ * dst[((i03*ne02 + i02)*ne01 + i01)*ne00 + i00] = fp16 bits of the value
+ * i00 % 32 of block i03*s03 + i02*s02 + i01*s01 + i00/32. */
+int p100o_kv_to_f16(int kv_type, const void* src, int64_t ne00, int64_t ne01, int64_t ne02, int64_t ne03,
+                    int64_t s01, int64_t s02, int64_t s03, uint16_t* dst);
+/* nblk blocks from the reference's LCG (dequant_nc.cu:144-149). */
+void p100o_kv_lcg_blocks(int kv_type, size_t nblk, uint32_t seed, void* out);
+/* ggml's q8_0 / q4_0 block quantisers over n values (n % 32 == 0). */
+int p100o_kv_quantize(int kv_type, const float* x, size_t n, void* out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -27,6 +27,9 @@ TYPE_NAMES = {Q4_0: "q4_0", Q8_0: "q8_0", Q4_K: "q4_K"}
 TYPES = {v: k for k, v in TYPE_NAMES.items()}
 BLOCK_ELEMS = {Q4_0: 32, Q8_0: 32, Q4_K: 256}
 BLOCK_BYTES = {Q4_0: 18, Q8_0: 34, Q4_K: 144}
+# K/V cache element types (p100_kv_type) and their 32-value block bytes.
+KV_F16, KV_Q8_0, KV_Q4_0 = 0, 1, 2
+KV_BLOCK_BYTES = {KV_Q8_0: 34, KV_Q4_0: 18}
 Q8_1_BLOCK_BYTES = 36
 QMV_PDL = 1
 
@@ -55,12 +58,12 @@ class AttnDesc(C.Structure):
     _fields_ = [("batch", C.c_int), ("n_head_q", C.c_int), ("n_head_kv", C.c_int), ("seq_q", C.c_int),
                 ("seq_kv", C.c_int), ("d_qk", C.c_int), ("d_v", C.c_int), ("scale", C.c_float),
                 ("softcap", C.c_float), ("causal", C.c_int), ("kv_splits", C.c_int),
-                ("kv_head_stride", C.c_longlong), ("kv_batch_stride", C.c_longlong)]
+                ("kv_head_stride", C.c_longlong), ("kv_batch_stride", C.c_longlong), ("kv_type", C.c_int)]
 
     def __init__(self, batch=1, n_head_q=1, n_head_kv=1, seq_q=1, seq_kv=1, d_qk=128, d_v=128, scale=0.0,
-                 softcap=0.0, causal=False, kv_splits=0, kv_head_stride=0, kv_batch_stride=0):
+                 softcap=0.0, causal=False, kv_splits=0, kv_head_stride=0, kv_batch_stride=0, kv_type=0):
         super().__init__(batch, n_head_q, n_head_kv, seq_q, seq_kv, d_qk, d_v, scale, softcap, int(bool(causal)),
-                         kv_splits, kv_head_stride, kv_batch_stride)
+                         kv_splits, kv_head_stride, kv_batch_stride, kv_type)
 
 
 _lib = None
@@ -95,6 +98,7 @@ def _bind(lib):
         "p100_fa_workspace_size": (sz, [vp]),
         "p100_fa_workspace_init": (ip, [vp, sz, st]),
         "p100_fa_decode": (ip, [vp, vp, vp, vp, vp, vp, vp, vp, sz, st]),
+        "p100_kv_to_f16": (ip, [ip, vp] + [C.c_longlong] * 7 + [vp, st]),
         "p100_tp_unique_id": (ip, [vp]),
         "p100_tp_init_rank": (ip, [vp, ip, ip, ip, C.POINTER(vp)]),
         "p100_tp_create": (ip, [ip, C.POINTER(ip), C.POINTER(vp)]),
@@ -271,8 +275,24 @@ def fa_workspace(desc, device=None, stream=None):
     return torch.zeros(n, dtype=torch.uint8, device=device or "cuda")
 
 
+def kv_to_f16(kv_type, src, ne00, ne01, ne02=1, ne03=1, s01=None, s02=None, s03=None, out=None, stream=None):
+    """Quantised K/V view (uint8 blocks) -> fp16 [ne03, ne02, ne01, ne00] (p100_kv_to_f16);
+    block strides default to a contiguous view."""
+    torch = _torch()
+    nb = ne00 // 32
+    s01 = nb if s01 is None else s01
+    s02 = nb * ne01 if s02 is None else s02
+    s03 = s02 * ne02 if s03 is None else s03
+    if out is None:
+        out = torch.empty(ne03, ne02, ne01, ne00, dtype=torch.float16, device=src.device)
+    check(lib().p100_kv_to_f16(kv_type, _ptr(src), ne00, ne01, ne02, ne03, s01, s02, s03, _ptr(out),
+                               _stream(stream)))
+    return out
+
+
 def fa_decode(desc, q, k, v, mask=None, o=None, lse=None, ws=None, stream=None):
-    """Split-K FA-vec decode: q fp32 [B,Hq,1,D], k/v fp16 [B,Hkv,S,D] -> o fp32, lse fp32."""
+    """Split-K FA-vec decode: q fp32 [B,Hq,1,D], k/v fp16 [B,Hkv,S,D] (or, with desc.kv_type
+    KV_Q8_0 / KV_Q4_0, uint8 blocks of the same rows) -> o fp32, lse fp32."""
     torch = _torch()
     if o is None:
         o = torch.empty(desc.batch, desc.n_head_q, desc.seq_q, desc.d_v, dtype=torch.float32, device=q.device)

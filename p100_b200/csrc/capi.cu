@@ -555,6 +555,7 @@ struct FaPlan {
     bool auto_parts = false;   // kv_splits == 0: the split may change (fa_mma cluster merge)
     int parts_wide = 1;        // fa_mma with the workspace merge: two CTAs per SM
     int seq = 0;
+    int kv_type = P100_KV_F16;
 };
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
@@ -574,6 +575,16 @@ p100_status plan_fa(const p100_attn_desc& d, int sms, FaPlan& plan) {
     if (plan.head_stride < static_cast<long long>(d.seq_kv) * d.d_qk || plan.head_stride % 8 ||
         plan.batch_stride % 8)
         return set_error(P100_ERR_INVALID, "KV strides must cover seq_kv rows and be multiples of 8 elements");
+    if (d.kv_type != P100_KV_F16 && d.kv_type != P100_KV_Q8_0 && d.kv_type != P100_KV_Q4_0)
+        return set_error(P100_ERR_INVALID, "unknown kv_type %d", d.kv_type);
+    plan.kv_type = d.kv_type;
+    if (d.kv_type != P100_KV_F16) {
+        // fa_mma_kernel only: whole 64-value block pairs keep every row 4-byte aligned
+        if (plan.head_stride % 64 || plan.batch_stride % 64)
+            return set_error(P100_ERR_INVALID, "quantised KV strides must be multiples of 64 values");
+        if ((plan.D != 64 && plan.D != 128) || (G != 1 && G != 2 && G != 4 && G != 8))
+            return set_error(P100_ERR_UNSUPPORTED, "quantised K/V need d 64 or 128 and 1, 2, 4 or 8 query heads per kv head");
+    }
     const int heads = d.batch * d.n_head_kv;
     const int max_parts = std::max(1, d.seq_kv / fa::kTile);
     int parts = d.kv_splits;
@@ -629,10 +640,10 @@ p100_status launch_fa_t(const FaPlan& plan, const fa::Params& prm, int heads, cu
     return cuda_status(cudaLaunchKernelEx(&cfg, kern, prm), "fa_decode_kernel launch");
 }
 
-template <int D, int G>
+template <int D, int G, int KV>
 p100_status launch_fa_mma_t(const FaPlan& plan, const fa::Params& prm, int heads, cudaStream_t stream, bool pdl) {
-    auto kern = fam::fa_mma_kernel<D, G>;
-    constexpr size_t smem = fam::smem_bytes<D, G>();
+    auto kern = fam::fa_mma_kernel<D, G, KV>;
+    constexpr size_t smem = fam::smem_bytes<D, G, KV>();
     static thread_local int configured[64] = {};
     static thread_local int cluster_fits[64][5] = {};   // per log2(parts): clusters that fit, 0 unknown, -1 none
     int dev = 0;
@@ -709,13 +720,21 @@ p100_status launch_fa_mma_t(const FaPlan& plan, const fa::Params& prm, int heads
     return cuda_status(cudaLaunchKernelEx(&cfg, kern, run), "fa_mma_kernel launch");
 }
 
+template <int D, int KV>
+p100_status launch_fa_mma_kv(const FaPlan& plan, const fa::Params& prm, int heads, cudaStream_t s, bool pdl) {
+    switch (plan.G) {
+        case 1: return launch_fa_mma_t<D, 1, KV>(plan, prm, heads, s, pdl);
+        case 2: return launch_fa_mma_t<D, 2, KV>(plan, prm, heads, s, pdl);
+        case 4: return launch_fa_mma_t<D, 4, KV>(plan, prm, heads, s, pdl);
+        default: return launch_fa_mma_t<D, 8, KV>(plan, prm, heads, s, pdl);
+    }
+}
 template <int D>
 p100_status launch_fa_mma_d(const FaPlan& plan, const fa::Params& prm, int heads, cudaStream_t s, bool pdl) {
-    switch (plan.G) {
-        case 1: return launch_fa_mma_t<D, 1>(plan, prm, heads, s, pdl);
-        case 2: return launch_fa_mma_t<D, 2>(plan, prm, heads, s, pdl);
-        case 4: return launch_fa_mma_t<D, 4>(plan, prm, heads, s, pdl);
-        default: return launch_fa_mma_t<D, 8>(plan, prm, heads, s, pdl);
+    switch (plan.kv_type) {
+        case P100_KV_Q8_0: return launch_fa_mma_kv<D, P100_KV_Q8_0>(plan, prm, heads, s, pdl);
+        case P100_KV_Q4_0: return launch_fa_mma_kv<D, P100_KV_Q4_0>(plan, prm, heads, s, pdl);
+        default: return launch_fa_mma_kv<D, P100_KV_F16>(plan, prm, heads, s, pdl);
     }
 }
 
@@ -731,6 +750,8 @@ template <int D>
 p100_status launch_fa_d(const FaPlan& plan, const fa::Params& prm, int heads, cudaStream_t s, bool pdl = false) {
     if constexpr (D != 256)
         if (fa_use_mma(plan, prm)) return launch_fa_mma_d<D>(plan, prm, heads, s, pdl);
+    if (plan.kv_type != P100_KV_F16)
+        return set_error(P100_ERR_UNSUPPORTED, "quantised K/V need the tensor-core kernel (16-byte aligned K/V)");
     switch (plan.gmax) {
         case 1: return launch_fa_t<D, 1>(plan, prm, heads, s, pdl);
         case 2: return launch_fa_t<D, 2>(plan, prm, heads, s, pdl);
@@ -840,6 +861,42 @@ p100_status p100_dequantize(int type, const void* w, int rows, int k, float* out
         default: dequantize_kernel<P100_Q4_K><<<grid, 256, 0, stream>>>(wb, out, rows, k, row_bytes); break;
     }
     return launch_status("dequantize_kernel launch");
+}
+
+p100_status p100_kv_to_f16(int kv_type, const void* src, long long ne00, long long ne01, long long ne02,
+                           long long ne03, long long s01, long long s02, long long s03, void* dst,
+                           p100_stream_t stream) {
+    clear_error();
+    if (kv_type != P100_KV_Q8_0 && kv_type != P100_KV_Q4_0)
+        return set_error(P100_ERR_INVALID, "kv_type must be q8_0 or q4_0, got %d", kv_type);
+    if (ne00 <= 0 || ne00 % 32 || ne00 > (1 << 30)) return set_error(P100_ERR_INVALID, "ne00 must be a positive multiple of 32");
+    if (ne01 < 0 || ne02 < 0 || ne03 < 0 || s01 < 0 || s02 < 0 || s03 < 0)
+        return set_error(P100_ERR_INVALID, "extents and strides must be non-negative");
+    if (ne01 * (ne00 / 8) >= (1ll << 31)) return set_error(P100_ERR_INVALID, "ne01 * ne00 / 8 must be below 2^31");
+    if (ne01 == 0 || ne02 == 0 || ne03 == 0) return P100_OK;
+    if (!src || !dst) return set_error(P100_ERR_INVALID, "null buffer");
+    if (reinterpret_cast<uintptr_t>(src) % 2) return set_error(P100_ERR_INVALID, "src must be 2-byte aligned");
+    if (reinterpret_cast<uintptr_t>(dst) % 16) return set_error(P100_ERR_INVALID, "dst must be 16-byte aligned");
+    if (p100_status st = require_sm100(nullptr, nullptr)) return st;
+    kvq::ConvParams p{};
+    p.src = static_cast<const uint8_t*>(src);
+    p.dst = static_cast<__half*>(dst);
+    p.ne01 = ne01;
+    p.ne02 = ne02;
+    p.ne03 = ne03;
+    p.s01 = s01;
+    p.s02 = s02;
+    p.s03 = s03;
+    p.ne00 = static_cast<int>(ne00);
+    p.chunks = static_cast<int>(ne00 / 8);
+    p.units = static_cast<int>(ne01 * p.chunks);
+    const dim3 grid(static_cast<unsigned>((p.units + 255) / 256),
+                    static_cast<unsigned>(std::min<long long>(ne02 * ne03, 65535)));
+    if (kv_type == P100_KV_Q8_0)
+        kvq::kv_to_f16_kernel<P100_KV_Q8_0><<<grid, 256, 0, stream>>>(p);
+    else
+        kvq::kv_to_f16_kernel<P100_KV_Q4_0><<<grid, 256, 0, stream>>>(p);
+    return launch_status("kv_to_f16_kernel launch");
 }
 
 p100_status p100_qmv(int type, const void* w, int rows, int k, const void* x_q8_1, int batch, float* y,

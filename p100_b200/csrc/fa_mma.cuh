@@ -26,8 +26,18 @@
 // global workspace, or, when the parts of a kv head form one thread-block
 // cluster, through distributed shared memory: every CTA then merges its own
 // slice of the outputs (no workspace, fence, ticket or L2 round trips).
+//
+// Quantised caches (KV = q8_0 or q4_0): the ring holds the raw blocks of
+// each 64-key tile (the tile is one contiguous byte range of the head, copied
+// in 16-byte chunks from the 16-byte boundary at or below its start), and
+// each warp dequantises its own 16 rows of K and V into a private fp16 tile
+// with the values of kvq::dequant8 (rows past the part's end as zeros), then
+// runs the fp16 code on it unchanged — so the result is that of the fp16
+// kernel on the converted cache, bit for bit, from about half (q8_0) or a
+// quarter (q4_0) of the bytes.
 #pragma once
 #include "fa_decode.cuh"
+#include "kv_quant.cuh"
 
 namespace p100b {
 namespace fam {
@@ -63,6 +73,24 @@ __device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], uint32_t addr) {
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, int src_bytes) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
 }
+// 4 bytes global -> shared (both 4-byte aligned).
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint32_t lds16(uint32_t a) {
+    unsigned short v;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ void sts128(uint32_t a, uint4 v) {
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                 : "memory");
+}
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait() {
@@ -92,27 +120,59 @@ __host__ __device__ constexpr int stages() { return D >= 256 ? 2 : 3; }
 constexpr int kMaxClusterParts = 16;
 template <int D, int G>
 __host__ __device__ constexpr size_t rx_floats() { return size_t(G) * D + 2 * kMaxClusterParts * G; }
-template <int D, int G>
-__host__ __device__ constexpr size_t smem_bytes() {
-    return size_t(stages<D>()) * 2 * kTile * (D + 8) * 2 + size_t(G) * D * 4 + 256 + rx_floats<D, G>() * 4;
+// Quantised caches: bytes per key row, per raw K (or V) slot (the tile, up to
+// 15 bytes of lead before it and the dequantiser's 12-byte overread after it),
+// and as many stages (3 to 8) as leave two CTAs per SM at G = 8 beside the
+// four warps' private fp16 K and V tiles (115,712 bytes per CTA).
+template <int D, int KV>
+__host__ __device__ constexpr int raw_row_bytes() { return D / 32 * kvq::block_bytes<KV>(); }
+template <int D, int KV>
+__host__ __device__ constexpr int raw_slot_bytes() { return (kTile * raw_row_bytes<D, KV>() + 48 + 15) & ~15; }
+template <int D>
+__host__ __device__ constexpr int quant_ring_budget() {
+    return 115712 - (kWarps * 2 * 16 * (D + 8) * 2 + 8 * D * 4 + 256 + int(rx_floats<D, 8>()) * 4);
 }
+template <int D, int KV>
+__host__ __device__ constexpr int nstages() {
+    return KV == P100_KV_F16 ? stages<D>()
+           : quant_ring_budget<D>() / (2 * raw_slot_bytes<D, KV>()) < 3 ? 3
+           : quant_ring_budget<D>() / (2 * raw_slot_bytes<D, KV>()) > 8 ? 8
+                                                                        : quant_ring_budget<D>() / (2 * raw_slot_bytes<D, KV>());
+}
+template <int D, int KV>
+__host__ __device__ constexpr size_t ring_bytes() {
+    return KV == P100_KV_F16 ? size_t(stages<D>()) * 2 * kTile * (D + 8) * 2
+                             : size_t(nstages<D, KV>()) * 2 * raw_slot_bytes<D, KV>() + size_t(kWarps) * 2 * 16 * (D + 8) * 2;
+}
+template <int D, int G, int KV = P100_KV_F16>
+__host__ __device__ constexpr size_t smem_bytes() {
+    return ring_bytes<D, KV>() + size_t(G) * D * 4 + 256 + rx_floats<D, G>() * 4;
+}
+static_assert(smem_bytes<128, 8, P100_KV_Q8_0>() <= 115712 && smem_bytes<128, 8, P100_KV_Q4_0>() <= 115712 &&
+                  smem_bytes<64, 8, P100_KV_Q8_0>() <= 115712 && smem_bytes<64, 8, P100_KV_Q4_0>() <= 115712,
+              "two CTAs per SM");
 
 // Grid (parts, batch * n_kv); G = query heads per kv head (1, 2, 4 or 8);
-// D = 64 or 128.
-template <int D, int G>
+// D = 64 or 128; KV = the cache's p100_kv_type.
+template <int D, int G, int KV = P100_KV_F16>
 __global__ void __launch_bounds__(kThreads, 1) fa_mma_kernel(const fa::Params p) {
     static_assert(G == 1 || G == 2 || G == 4 || G == 8, "G");
     constexpr int RS = D + 8;        // padded row stride (halves)
-    constexpr int NS = stages<D>();
+    constexpr int NS = nstages<D, KV>();
     constexpr int KSQ = D / 16;      // k-steps of Q K^T
     constexpr int NTV = D / 8;       // n-tiles of P V
     constexpr int CHUNKS = kTile * D / 8;   // 16-byte chunks per K (or V) tile
+    constexpr bool QUANT = KV != P100_KV_F16;
+    constexpr int BB = kvq::block_bytes<KV>();
+    constexpr int RB = raw_row_bytes<D, KV>();
+    constexpr int RAW = raw_slot_bytes<D, KV>();
     extern __shared__ __align__(128) uint8_t smem[];
-    __half* ring = reinterpret_cast<__half*>(smem);                     // [NS][K|V][kTile][RS]
-    float* s_q = reinterpret_cast<float*>(smem + size_t(NS) * 2 * kTile * RS * 2);   // [G][D]
+    // fp16: [NS][K|V][kTile][RS]; quantised: [NS][K|V][RAW] then [kWarps][K|V][16][RS]
+    __half* ring = reinterpret_cast<__half*>(smem);
+    float* s_q = reinterpret_cast<float*>(smem + ring_bytes<D, KV>());   // [G][D]
     float* s_qs = s_q + G * D;                                          // [8] per-head power-of-two scale
     unsigned* s_flag = reinterpret_cast<unsigned*>(s_qs + 8);
-    float* rx = reinterpret_cast<float*>(smem + smem_bytes<D, G>() - rx_floats<D, G>() * 4);   // cluster merge
+    float* rx = reinterpret_cast<float*>(smem + smem_bytes<D, G, KV>() - rx_floats<D, G>() * 4);   // cluster merge
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, t = lane & 3;
@@ -137,6 +197,13 @@ __global__ void __launch_bounds__(kThreads, 1) fa_mma_kernel(const fa::Params p)
     const __half* kbase = p.k + b * p.batch_stride + kvh * p.head_stride;
     const __half* vbase = p.v + b * p.batch_stride + kvh * p.head_stride;
     const uint32_t ring_addr = smem_addr(ring);
+    // quantised: this head's rows (strides count values, in whole blocks)
+    const size_t qhead = size_t((b * p.batch_stride + kvh * p.head_stride) / 32) * BB;
+    const uint8_t* kq = reinterpret_cast<const uint8_t*>(p.k) + qhead;
+    const uint8_t* vq = reinterpret_cast<const uint8_t*>(p.v) + qhead;
+    // bytes before each tile's 16-byte boundary (the same for every tile: 64 rows are 256-byte multiples)
+    const int lead_k = static_cast<int>(reinterpret_cast<uintptr_t>(kq + size_t(key0) * RB) & 15);
+    const int lead_v = static_cast<int>(reinterpret_cast<uintptr_t>(vq + size_t(key0) * RB) & 15);
 
     // The raw query pairs of this group, loaded before any K/V copy is issued
     // (after the wait when they come from the previous kernel).
@@ -149,8 +216,29 @@ __global__ void __launch_bounds__(kThreads, 1) fa_mma_kernel(const fa::Params p)
         qr[j] = i < G * D / 2 ? *reinterpret_cast<const float2*>(qg + 2 * i) : make_float2(0.f, 0.f);
     }
 
+    // Raw rows [j0, j0 + n) of a quantised head into a slot: the byte range
+    // from the 16-byte boundary `lead` bytes below row j0, in 16-byte chunks
+    // while a chunk ends inside the head's p.seq rows, the rest (< 16 bytes,
+    // a multiple of 4: rows and heads start 4-byte aligned) in 4-byte copies.
+    auto copy_raw = [&](uint32_t dst, const uint8_t* head, int lead, int j0, int n) {
+        const uint8_t* src = head + size_t(j0) * RB - lead;
+        const uintptr_t end = reinterpret_cast<uintptr_t>(head + size_t(p.seq) * RB);
+        const int total = lead + n * RB;
+        int nfull = (total + 15) >> 4;
+        if (reinterpret_cast<uintptr_t>(src) + size_t(nfull) * 16 > end)
+            nfull = static_cast<int>(((end & ~uintptr_t(15)) - reinterpret_cast<uintptr_t>(src)) >> 4);
+        for (int c = tid; c < nfull; c += kThreads) cp_async16(dst + c * 16, src + c * 16, 16);
+        const int tail = (total - nfull * 16) >> 2;
+        if (tid < tail) cp_async4(dst + nfull * 16 + tid * 4, src + nfull * 16 + tid * 4);
+    };
     auto issue = [&](int tile) {
-        if (tile < ntiles) {
+        if (QUANT && tile < ntiles) {
+            const int j0 = key0 + tile * kTile;
+            const int n = min(kTile, key1 - j0);
+            const uint32_t kdst = ring_addr + uint32_t((tile % NS) * 2 * RAW);
+            copy_raw(kdst, kq, lead_k, j0, n);
+            copy_raw(kdst + RAW, vq, lead_v, j0, n);
+        } else if (tile < ntiles) {
             const int j0 = key0 + tile * kTile;
             const int n = min(kTile, key1 - j0);
             const uint32_t kdst = ring_addr + uint32_t((tile % NS) * 2 * kTile * RS * 2);
@@ -173,7 +261,31 @@ __global__ void __launch_bounds__(kThreads, 1) fa_mma_kernel(const fa::Params p)
         for (int s = 0; s < NS - 1; ++s) issue(s);   // K/V never come from the previous kernel here
     pdl_allow_dependents();
     pdl_wait_prior_grid();
-    if (p.rope_cs && pos >= 0 && part == p.parts - 1) {
+    if (QUANT && p.rope_cs && pos >= 0 && part == p.parts - 1) {
+        // the new row, quantised: warp w forms blocks w, w + 4, ... of the
+        // rotated k row then of the v row (lane = value in the block; the
+        // rotation pairs adjacent lanes) and stores them into row pos
+        const float* kr = p.q + (size_t(p.nq_total) + kvh) * D;
+        const float* vr = p.q + (size_t(p.nq_total) + p.nkv + kvh) * D;
+        for (int blk = warp; blk < 2 * (D / 32); blk += kWarps) {
+            const bool is_k = blk < D / 32;
+            const int e = (is_k ? blk : blk - D / 32) * 32 + lane;
+            float x;
+            if (is_k) {
+                const float xe = kr[e], xo = __shfl_xor_sync(0xffffffffu, xe, 1);
+                const float x0 = (lane & 1) ? xo : xe, x1 = (lane & 1) ? xe : xo;
+                const float2 t = p.rope_cs[size_t(pos) * (D / 2) + e / 2];
+                x = (lane & 1) ? __fadd_rn(__fmul_rn(x0, t.y), __fmul_rn(x1, t.x))
+                               : __fsub_rn(__fmul_rn(x0, t.x), __fmul_rn(x1, t.y));
+            } else {
+                x = vr[e];
+            }
+            uint8_t* row = const_cast<uint8_t*>(is_k ? kq : vq) + size_t(pos) * RB;
+            kvq::quantize_block_warp<KV>(x, lane, row + (e / 32) * BB);
+        }
+        __threadfence();
+        __syncthreads();
+    } else if (p.rope_cs && pos >= 0 && part == p.parts - 1) {
         // the new row: rotated k and v of this kv head into cache row pos
         // (only this part's key range reaches pos), visible before any copy
         const float* kr = p.q + (size_t(p.nq_total) + kvh) * D;
@@ -254,17 +366,52 @@ __global__ void __launch_bounds__(kThreads, 1) fa_mma_kernel(const fa::Params p)
         cp_async_wait<NS - 2>();
         __syncthreads();   // tile's copies visible to all; the slot refilled next is no longer read
         issue(tile + NS - 1);
-        const uint32_t kst = ring_addr + uint32_t((tile % NS) * 2 * kTile * RS * 2);
-        const uint32_t vst = kst + uint32_t(kTile * RS * 2);
         const int j0 = key0 + tile * kTile;
         const int n = min(kTile, key1 - j0);
+        // fp16: the stage itself, rows warp*16.. of it; quantised: this warp's
+        // private tiles, rows 0..15, dequantised from the raw stage here
+        uint32_t kst = ring_addr + uint32_t((tile % NS) * 2 * kTile * RS * 2);
+        uint32_t vst = kst + uint32_t(kTile * RS * 2);
+        int wrow = warp * 16;
+        if constexpr (QUANT) {
+            constexpr int LPR = D / 8;       // lanes per row, eight values each
+            constexpr int RPS = 32 / LPR;    // rows per step
+            const uint32_t kraw = ring_addr + uint32_t((tile % NS) * 2 * RAW), vraw = kraw + RAW;
+            kst = ring_addr + uint32_t(NS * 2 * RAW + warp * 2 * 16 * RS * 2);
+            vst = kst + uint32_t(16 * RS * 2);
+            wrow = 0;
+            const int c = lane % LPR;
+            const int boff = (c >> 2) * BB, qoff = boff + kvq::chunk_offset<KV>(c & 3);
+            const int shift = kvq::chunk_shift<KV>(c & 3);
+            auto load8 = [&](uint32_t row) -> uint4 {
+                const uint32_t a = row + qoff, a4 = a & ~3u, sh = (a & 3u) * 8;
+                const uint32_t w0 = lds32(a4), w1 = lds32(a4 + 4), w2 = lds32(a4 + 8);
+                uint32_t x0 = __funnelshift_r(w0, w1, sh), x1 = __funnelshift_r(w1, w2, sh);
+                kvq::isolate<KV>(x0, x1, shift);
+                const uint32_t d = lds16(row + boff);
+                return kvq::dequant8<KV>(x0, x1, d | (d << 16));
+            };
+            __syncwarp();   // every lane is past its reads of the previous tile
+#pragma unroll
+            for (int st = 0; st < 16 / RPS; ++st) {
+                const int rr = st * RPS + lane / LPR, r = warp * 16 + rr;
+                uint4 kv4 = make_uint4(0u, 0u, 0u, 0u), vv4 = kv4;
+                if (r < n) {
+                    kv4 = load8(kraw + uint32_t(lead_k + r * RB));
+                    vv4 = load8(vraw + uint32_t(lead_v + r * RB));
+                }
+                sts128(kst + uint32_t((rr * RS + c * 8) * 2), kv4);
+                sts128(vst + uint32_t((rr * RS + c * 8) * 2), vv4);
+            }
+            __syncwarp();
+        }
 
         // ---- S = Q K^T over this warp's 16 keys (two n-tiles of 8)
         float s[2][4];
 #pragma unroll
         for (int nt = 0; nt < 2; ++nt) {
             s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
-            const int krow = warp * 16 + nt * 8 + (lane & 7);
+            const int krow = wrow + nt * 8 + (lane & 7);
 #pragma unroll
             for (int ks = 0; ks < KSQ; ks += 2) {
                 uint32_t r[4];
@@ -342,7 +489,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_mma_kernel(const fa::Params p)
         for (int n2 = 0; n2 < NTV / 2; ++n2) {
             uint32_t r[4];
             const int m = lane >> 3;
-            const int vrow = warp * 16 + (lane & 7) + 8 * (m & 1);
+            const int vrow = wrow + (lane & 7) + 8 * (m & 1);
             ldsm_x4_trans(r, vst + uint32_t((vrow * RS + n2 * 16 + 8 * (m >> 1)) * 2));
             mma16816(o[2 * n2], pa, r[0], r[1]);
             mma16816(o[2 * n2 + 1], pa, r[2], r[3]);

@@ -70,6 +70,32 @@ def qmv_algorithmic_bytes(qtype, rows, k, batch):
     return rows * (k // BLOCK_ELEMS[qtype]) * BLOCK_BYTES[qtype] + batch * k * 4 + batch * rows * 4
 
 
-def fa_algorithmic_bytes(batch, n_head_q, n_head_kv, seq_kv, d):
-    """fp16 K and V read once + fp32 q and O (+ LSE)."""
-    return batch * n_head_kv * seq_kv * d * 2 * 2 + batch * n_head_q * d * 4 * 2 + batch * n_head_q * 4
+def fa_algorithmic_bytes(batch, n_head_q, n_head_kv, seq_kv, d, kv_type=0):
+    """K and V read once (fp16, or q8_0 / q4_0 blocks: 34 / 18 bytes per 32
+    values) + fp32 q and O (+ LSE)."""
+    kv_row = d * 2 if kv_type == 0 else d // 32 * (34 if kv_type == 1 else 18)
+    return batch * n_head_kv * seq_kv * kv_row * 2 + batch * n_head_q * d * 4 * 2 + batch * n_head_q * 4
+
+
+def kv_cache_blocks(kv_type, batch, n_head_kv, seq_kv, d, seed):
+    """A q8_0 / q4_0 K/V cache [B,Hkv,S,D/32*bb] of N(0,1)*0.5 rows for
+    benchmarks, quantised on the host by ggml's block rule (x / (max|x| / 127)
+    rounded for q8_0; trunc(x / (v / -8) + 8.5) clamped to 15, v the value of
+    largest |x|, for q4_0), vectorised with numpy; the parity tests use the
+    oracle's exact quantiser instead."""
+    rng = np.random.default_rng(seed)
+    x = (rng.standard_normal((batch * n_head_kv * seq_kv * d // 32, 32), dtype=np.float32) * 0.5)
+    if kv_type == 1:
+        dsc = np.abs(x).max(axis=1) / np.float32(127)
+        idv = np.where(dsc != 0, np.float32(1) / np.where(dsc != 0, dsc, 1), 0).astype(np.float32)
+        t = x * idv[:, None]
+        q = np.trunc(t + np.copysign(np.float32(0.5), t)).astype(np.int8).view(np.uint8)
+    else:
+        j = np.abs(x).argmax(axis=1)
+        vmax = x[np.arange(x.shape[0]), j]
+        dsc = vmax / np.float32(-8)
+        idv = np.where(dsc != 0, np.float32(1) / np.where(dsc != 0, dsc, 1), 0).astype(np.float32)
+        c = np.minimum(15, np.trunc(x * idv[:, None] + np.float32(8.5))).astype(np.uint8)
+        q = c[:, :16] | (c[:, 16:] << 4)
+    blocks = np.concatenate([dsc.astype(np.float16).view(np.uint8).reshape(-1, 2), q], axis=1)
+    return blocks.reshape(batch, n_head_kv, seq_kv, -1)

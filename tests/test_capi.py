@@ -33,7 +33,7 @@ def test_exports_every_declared_symbol(lib):
 
 
 def test_sizes_and_versions(lib):
-    assert lib.p100_abi_version() == 1
+    assert lib.p100_abi_version() == 2
     assert [lib.p100_block_elems(t) for t in (0, 1, 2, 9)] == [32, 32, 256, -1]
     assert [lib.p100_block_bytes(t) for t in (0, 1, 2, 9)] == [18, 34, 144, -1]
     assert lib.p100_weight_bytes(P.Q4_0, 14336, 4096) == 33030144
@@ -58,6 +58,16 @@ def test_invalid_arguments_use_reference_wording(lib):
     d = P.AttnDesc(seq_kv=0)
     assert lib.p100_fa_decode(C.byref(d), z, z, z, None, z, None, None, 0, None) == P.ERR_INVALID
     assert P.last_error() == "all dimensions must be positive"
+    # quantised K/V conversion: shape and type checks come before any device call
+    kv = lib.p100_kv_to_f16
+    kv.argtypes = [C.c_int, C.c_void_p] + [C.c_longlong] * 7 + [C.c_void_p, C.c_void_p]
+    assert kv(P.KV_F16, z, 128, 4, 1, 1, 4, 16, 16, z, None) == P.ERR_INVALID
+    assert kv(P.KV_Q8_0, z, 48, 4, 1, 1, 2, 8, 8, z, None) == P.ERR_INVALID
+    assert P.last_error() == "ne00 must be a positive multiple of 32"
+    assert kv(P.KV_Q4_0, z, 128, 4, 1, 1, -1, 16, 16, z, None) == P.ERR_INVALID
+    assert kv(P.KV_Q8_0, C.c_void_p(17), 128, 4, 1, 1, 4, 16, 16, z, None) == P.ERR_INVALID
+    assert P.last_error() == "src must be 2-byte aligned"
+    assert kv(P.KV_Q8_0, z, 128, 0, 1, 1, 4, 16, 16, z, None) == P.OK   # nothing to convert
     assert lib.p100_fa_workspace_size(C.byref(d)) == 0
     assert P.last_error() == "all dimensions must be positive"
 
