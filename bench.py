@@ -485,19 +485,24 @@ def kernel_only(args):
         print(json.dumps({"kernel_only": "decode llama3-8b ctx 4096", "steps": args.warmup + args.steps,
                           "position": pos, "token": tok}))
         return 0
-    if args.kernel_only in ("fa", "fa4096"):
-        seq = 32768 if args.kernel_only == "fa" else 4096
+    if args.kernel_only in ("fa", "fa4096", "faq8", "faq4"):
+        seq = 4096 if args.kernel_only == "fa4096" else 32768
+        kv_type = {"faq8": P.KV_Q8_0, "faq4": P.KV_Q4_0}.get(args.kernel_only, P.KV_F16)
         q, k, v = W.attention_inputs(1, 32, 8, seq, 128, seed=seq)
+        if kv_type != P.KV_F16:
+            k = W.kv_cache_blocks(kv_type, 1, 8, seq, 128, seed=seq + 1)
+            v = W.kv_cache_blocks(kv_type, 1, 8, seq, 128, seed=seq + 2)
         qd = torch.from_numpy(q).cuda()
         kd = [torch.from_numpy(k).cuda() for _ in range(2)]
         vd = [torch.from_numpy(v).cuda() for _ in range(2)]
-        desc = P.AttnDesc(n_head_q=32, n_head_kv=8, seq_kv=seq)
+        desc = P.AttnDesc(n_head_q=32, n_head_kv=8, seq_kv=seq, kv_type=kv_type)
         ws = P.fa_workspace(desc)
         for i in range(args.warmup + args.steps):
             P.fa_decode(desc, qd, kd[i % 2], vd[i % 2], ws=ws)
         torch.cuda.synchronize()
         P.check(P.device_error())
-        print(json.dumps({"kernel_only": f"fa_decode 32/8 heads d128 ctx {seq}", "launches": args.warmup + args.steps}))
+        print(json.dumps({"kernel_only": f"fa_decode 32/8 heads d128 ctx {seq} kv_type {kv_type}",
+                          "launches": args.warmup + args.steps}))
         return 0
     _, k, rows = TARGET
     batch = 16 if args.kernel_only == "qmvb" else 1
@@ -521,9 +526,9 @@ def main():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the 8B/70B decode section")
-    ap.add_argument("--kernel-only", choices=["qmv", "qmvb", "fa", "fa4096", "decode"],
+    ap.add_argument("--kernel-only", choices=["qmv", "qmvb", "fa", "fa4096", "faq8", "faq4", "decode"],
                     help="one kernel's launches only (ncu cases); qmvb = the target shape at batch 16, "
-                         "fa = 32768 keys, fa4096 = 4096 keys")
+                         "fa = 32768 keys, fa4096 = 4096 keys, faq8 / faq4 = 32768 keys of q8_0 / q4_0 K/V")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -595,7 +595,10 @@ p100_status plan_fa(const p100_attn_desc& d, int sms, FaPlan& plan) {
     plan.parts = std::min(std::min(parts, max_parts), 512);
     // fa_mma_kernel fits two CTAs per SM: with automatic splitting and the
     // workspace merge it runs twice the parts (the workspace covers both).
-    plan.parts_wide = plan.auto_parts ? std::min(std::min(2 * std::max(1, sms / heads), max_parts), 512) : plan.parts;
+    // (three CTAs per SM over a quantised cache: its rings hold raw blocks)
+    const int per_sm = d.kv_type == P100_KV_Q8_0 || d.kv_type == P100_KV_Q4_0 ? fam::kQuantCtasPerSm : 2;
+    plan.parts_wide =
+        plan.auto_parts ? std::min(std::min(per_sm * std::max(1, sms / heads), max_parts), 512) : plan.parts;
     plan.seq = d.seq_kv;
     const int ws_parts = std::max(plan.parts, plan.parts_wide);
     plan.nstage = d.d_qk == 256 ? 2 : 4;
@@ -890,7 +893,7 @@ p100_status p100_kv_to_f16(int kv_type, const void* src, long long ne00, long lo
     p.ne00 = static_cast<int>(ne00);
     p.chunks = static_cast<int>(ne00 / 8);
     p.units = static_cast<int>(ne01 * p.chunks);
-    const dim3 grid(static_cast<unsigned>((p.units + 255) / 256),
+    const dim3 grid(static_cast<unsigned>((p.units + 256 * kvq::kUnits - 1) / (256 * kvq::kUnits)),
                     static_cast<unsigned>(std::min<long long>(ne02 * ne03, 65535)));
     if (kv_type == P100_KV_Q8_0)
         kvq::kv_to_f16_kernel<P100_KV_Q8_0><<<grid, 256, 0, stream>>>(p);

@@ -73,28 +73,34 @@ __device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], uint32_t addr) {
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, int src_bytes) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
 }
-// 4 bytes global -> shared (both 4-byte aligned).
-__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
-}
-__device__ __forceinline__ uint32_t lds32(uint32_t a) {
-    uint32_t v;
-    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(a));
-    return v;
-}
-__device__ __forceinline__ uint32_t lds16(uint32_t a) {
-    unsigned short v;
-    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
-    return v;
-}
-__device__ __forceinline__ void sts128(uint32_t a, uint4 v) {
-    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
-                 : "memory");
-}
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait() {
     asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// 8x8 b16 transpose within the warp: lane (g, t) gets elements (2t, g) and
+// (2t+1, g) of the matrix whose (g, 2t..2t+1) it held.
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t a) {
+    uint32_t d;
+    asm("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(a));
+    return d;
+}
+// Values i and i+1 (i even, within one block) of the block at byte offset
+// `blk` of shared memory as an fp16 pair, rounded as kvq::dequant8 rounds.
+template <int KV>
+__device__ __forceinline__ uint32_t dequant_pair(const uint8_t* smem, int blk, int i, uint32_t d2) {
+    uint32_t x;
+    if (KV == P100_KV_Q8_0) {
+        x = *reinterpret_cast<const unsigned short*>(smem + blk + 2 + i) ^ 0x8080u;
+    } else {
+        const uint32_t w = *reinterpret_cast<const unsigned short*>(smem + blk + 2 + (i & 15));
+        x = (i < 16 ? w : w >> 4) & 0x0F0Fu;
+    }
+    uint32_t h = __byte_perm(x, 0x64u, 0x4140);
+    asm("sub.rn.f16x2 %0, %0, %1;" : "+r"(h) : "r"(KV == P100_KV_Q8_0 ? 0x64806480u : 0x64086408u));
+    asm("mul.rn.f16x2 %0, %0, %1;" : "+r"(h) : "r"(d2));
+    return h;
 }
 
 // Every thread of the cluster arrives; release/acquire orders the shared
@@ -120,17 +126,18 @@ __host__ __device__ constexpr int stages() { return D >= 256 ? 2 : 3; }
 constexpr int kMaxClusterParts = 16;
 template <int D, int G>
 __host__ __device__ constexpr size_t rx_floats() { return size_t(G) * D + 2 * kMaxClusterParts * G; }
-// Quantised caches: bytes per key row, per raw K (or V) slot (the tile, up to
-// 15 bytes of lead before it and the dequantiser's 12-byte overread after it),
-// and as many stages (3 to 8) as leave two CTAs per SM at G = 8 beside the
-// four warps' private fp16 K and V tiles (115,712 bytes per CTA).
+// Quantised caches: bytes per key row, per raw K (or V) slot (the tile plus
+// up to 15 bytes of lead before it, rounded up with room to spare), and as
+// many stages (3 to 8) as leave three CTAs per SM at G = 8 (76,800 bytes per
+// CTA).
 template <int D, int KV>
 __host__ __device__ constexpr int raw_row_bytes() { return D / 32 * kvq::block_bytes<KV>(); }
 template <int D, int KV>
 __host__ __device__ constexpr int raw_slot_bytes() { return (kTile * raw_row_bytes<D, KV>() + 48 + 15) & ~15; }
+constexpr int kQuantCtasPerSm = 3;
 template <int D>
 __host__ __device__ constexpr int quant_ring_budget() {
-    return 115712 - (kWarps * 2 * 16 * (D + 8) * 2 + 8 * D * 4 + 256 + int(rx_floats<D, 8>()) * 4);
+    return 76800 - (8 * D * 4 + 256 + int(rx_floats<D, 8>()) * 4);
 }
 template <int D, int KV>
 __host__ __device__ constexpr int nstages() {
@@ -142,36 +149,36 @@ __host__ __device__ constexpr int nstages() {
 template <int D, int KV>
 __host__ __device__ constexpr size_t ring_bytes() {
     return KV == P100_KV_F16 ? size_t(stages<D>()) * 2 * kTile * (D + 8) * 2
-                             : size_t(nstages<D, KV>()) * 2 * raw_slot_bytes<D, KV>() + size_t(kWarps) * 2 * 16 * (D + 8) * 2;
+                             : size_t(nstages<D, KV>()) * 2 * raw_slot_bytes<D, KV>();
 }
 template <int D, int G, int KV = P100_KV_F16>
 __host__ __device__ constexpr size_t smem_bytes() {
     return ring_bytes<D, KV>() + size_t(G) * D * 4 + 256 + rx_floats<D, G>() * 4;
 }
-static_assert(smem_bytes<128, 8, P100_KV_Q8_0>() <= 115712 && smem_bytes<128, 8, P100_KV_Q4_0>() <= 115712 &&
-                  smem_bytes<64, 8, P100_KV_Q8_0>() <= 115712 && smem_bytes<64, 8, P100_KV_Q4_0>() <= 115712,
-              "two CTAs per SM");
+static_assert(smem_bytes<128, 8, P100_KV_Q8_0>() <= 76800 && smem_bytes<128, 8, P100_KV_Q4_0>() <= 76800 &&
+                  smem_bytes<64, 8, P100_KV_Q8_0>() <= 76800 && smem_bytes<64, 8, P100_KV_Q4_0>() <= 76800,
+              "three CTAs per SM");
 
 // Grid (parts, batch * n_kv); G = query heads per kv head (1, 2, 4 or 8);
 // D = 64 or 128; KV = the cache's p100_kv_type.
 template <int D, int G, int KV = P100_KV_F16>
-__global__ void __launch_bounds__(kThreads, 1) fa_mma_kernel(const fa::Params p) {
+__global__ void __launch_bounds__(kThreads, KV == P100_KV_F16 ? 1 : kQuantCtasPerSm) fa_mma_kernel(const fa::Params p) {
     static_assert(G == 1 || G == 2 || G == 4 || G == 8, "G");
     constexpr int RS = D + 8;        // padded row stride (halves)
     constexpr int NS = nstages<D, KV>();
     constexpr int KSQ = D / 16;      // k-steps of Q K^T
     constexpr int NTV = D / 8;       // n-tiles of P V
-    constexpr int CHUNKS = kTile * D / 8;   // 16-byte chunks per K (or V) tile
     constexpr bool QUANT = KV != P100_KV_F16;
     constexpr int BB = kvq::block_bytes<KV>();
     constexpr int RB = raw_row_bytes<D, KV>();
     constexpr int RAW = raw_slot_bytes<D, KV>();
     extern __shared__ __align__(128) uint8_t smem[];
-    // fp16: [NS][K|V][kTile][RS]; quantised: [NS][K|V][RAW] then [kWarps][K|V][16][RS]
+    // fp16: [NS][K|V][kTile][RS]; quantised: [NS][K|V][RAW]
     __half* ring = reinterpret_cast<__half*>(smem);
     float* s_q = reinterpret_cast<float*>(smem + ring_bytes<D, KV>());   // [G][D]
     float* s_qs = s_q + G * D;                                          // [8] per-head power-of-two scale
     unsigned* s_flag = reinterpret_cast<unsigned*>(s_qs + 8);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(s_qs + 16);           // [NS] K/V stage barriers
     float* rx = reinterpret_cast<float*>(smem + smem_bytes<D, G, KV>() - rx_floats<D, G>() * 4);   // cluster merge
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -216,49 +223,88 @@ __global__ void __launch_bounds__(kThreads, 1) fa_mma_kernel(const fa::Params p)
         qr[j] = i < G * D / 2 ? *reinterpret_cast<const float2*>(qg + 2 * i) : make_float2(0.f, 0.f);
     }
 
-    // Raw rows [j0, j0 + n) of a quantised head into a slot: the byte range
-    // from the 16-byte boundary `lead` bytes below row j0, in 16-byte chunks
-    // while a chunk ends inside the head's p.seq rows, the rest (< 16 bytes,
-    // a multiple of 4: rows and heads start 4-byte aligned) in 4-byte copies.
-    auto copy_raw = [&](uint32_t dst, const uint8_t* head, int lead, int j0, int n) {
+    // fp16 K/V tiles: 16-byte cp.async chunks into rows padded to D + 8
+    // halves (chunk i of this thread: row crow + i * RSTEP), zero-filled past
+    // the part's end (a masked key's V then adds exactly 0); one commit group
+    // per tile.  (Per-row bulk copies, 128 per tile, measured slower.)
+    // Quantised tiles: the rows are one contiguous byte range of the head,
+    // copied by one bulk-async copy from the 16-byte boundary `lead` bytes
+    // below it, as far as 16-byte chunks stay inside the head's p.seq rows,
+    // completing on the stage's mbarrier (thread 0 arms it); the rest (< 16
+    // bytes, a multiple of 4) by plain 4-byte loads and stores, fenced
+    // against the async proxy that refills the slot later and visible to
+    // readers through the block barriers between issue and use.
+    if (tid == 0) {
+        for (int i = 0; i < NS; ++i) mbar_init(&bars[i], 1);
+        fence_barrier_init();
+    }
+    __syncthreads();
+    const uint64_t policy = l2_evict_first_policy();
+    const int crow = tid / (D / 8), ccol = tid % (D / 8);   // fp16: this thread's first chunk
+    const __half* kth = kbase + size_t(crow) * D + ccol * 8;
+    const __half* vth = vbase + size_t(crow) * D + ccol * 8;
+    const uint32_t cdst = uint32_t((crow * RS + ccol * 8) * 2);
+    // quantised: the 16-byte aligned source of rows [j0, j0 + n), its whole
+    // 16-byte chunks inside the head's rows, and the 4-byte words after them
+    auto quant_part = [&](const uint8_t* head, int lead, int j0, int n, int& nfull, int& tail) {
         const uint8_t* src = head + size_t(j0) * RB - lead;
         const uintptr_t end = reinterpret_cast<uintptr_t>(head + size_t(p.seq) * RB);
         const int total = lead + n * RB;
-        int nfull = (total + 15) >> 4;
+        nfull = (total + 15) >> 4;
         if (reinterpret_cast<uintptr_t>(src) + size_t(nfull) * 16 > end)
             nfull = static_cast<int>(((end & ~uintptr_t(15)) - reinterpret_cast<uintptr_t>(src)) >> 4);
-        for (int c = tid; c < nfull; c += kThreads) cp_async16(dst + c * 16, src + c * 16, 16);
-        const int tail = (total - nfull * 16) >> 2;
-        if (tid < tail) cp_async4(dst + nfull * 16 + tid * 4, src + nfull * 16 + tid * 4);
+        tail = (total - nfull * 16) >> 2;
+        return src;
     };
     auto issue = [&](int tile) {
-        if (QUANT && tile < ntiles) {
-            const int j0 = key0 + tile * kTile;
-            const int n = min(kTile, key1 - j0);
-            const uint32_t kdst = ring_addr + uint32_t((tile % NS) * 2 * RAW);
-            copy_raw(kdst, kq, lead_k, j0, n);
-            copy_raw(kdst + RAW, vq, lead_v, j0, n);
-        } else if (tile < ntiles) {
-            const int j0 = key0 + tile * kTile;
-            const int n = min(kTile, key1 - j0);
-            const uint32_t kdst = ring_addr + uint32_t((tile % NS) * 2 * kTile * RS * 2);
+        if (tile >= ntiles) return;
+        const int j0 = key0 + tile * kTile;
+        const int n = min(kTile, key1 - j0);
+        uint64_t* bar = &bars[tile % NS];
+        if constexpr (QUANT) {
+            uint8_t* kdst = smem + (tile % NS) * 2 * RAW;
+            uint8_t* vdst = kdst + RAW;
+            int nk, tk, nv, tv;
+            const uint8_t* ksrc = quant_part(kq, lead_k, j0, n, nk, tk);
+            const uint8_t* vsrc = quant_part(vq, lead_v, j0, n, nv, tv);
+            if (tid == 0) {
+                mbar_arrive_expect_tx(bar, uint32_t(nk + nv) * 16);
+                bulk_load(kdst, ksrc, uint32_t(nk) * 16, bar, policy);
+                bulk_load(vdst, vsrc, uint32_t(nv) * 16, bar, policy);
+            }
+            if (tk > 0 || tv > 0) {   // the head's last rows only
+                if (tid < tk)
+                    *reinterpret_cast<uint32_t*>(kdst + nk * 16 + 4 * tid) =
+                        *reinterpret_cast<const uint32_t*>(ksrc + nk * 16 + 4 * tid);
+                if (tid >= 64 && tid - 64 < tv)
+                    *reinterpret_cast<uint32_t*>(vdst + nv * 16 + 4 * (tid - 64)) =
+                        *reinterpret_cast<const uint32_t*>(vsrc + nv * 16 + 4 * (tid - 64));
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            }
+        } else {
+            constexpr int RSTEP = kThreads / (D / 8);
+            const uint32_t kdst = ring_addr + uint32_t((tile % NS) * 2 * kTile * RS * 2) + cdst;
             const uint32_t vdst = kdst + uint32_t(kTile * RS * 2);
+            const __half* ks = kth + size_t(j0) * D;
+            const __half* vs = vth + size_t(j0) * D;
+            (void)bar;
 #pragma unroll
-            for (int i = 0; i < CHUNKS / kThreads; ++i) {
-                const int c = tid + i * kThreads;
-                const int r = c / (D / 8), col = c % (D / 8);
-                const bool valid = r < n;
-                const size_t src = size_t(j0 + (valid ? r : 0)) * D + col * 8;
-                const uint32_t off = uint32_t((r * RS + col * 8) * 2);
-                cp_async16(kdst + off, kbase + src, valid ? 16 : 0);
-                cp_async16(vdst + off, vbase + src, valid ? 16 : 0);
+            for (int i = 0; i < kTile * D / 8 / kThreads; ++i) {
+                const bool valid = crow + i * RSTEP < n;
+                const int off = valid ? i * RSTEP * D : -crow * D;   // invalid: row j0 (not read)
+                cp_async16(kdst + uint32_t(i * RSTEP * RS * 2), ks + off, valid ? 16 : 0);
+                cp_async16(vdst + uint32_t(i * RSTEP * RS * 2), vs + off, valid ? 16 : 0);
             }
         }
-        cp_async_commit();   // one group per tile slot, empty past the end
+    };
+    // the commit groups count tiles (empty past the end), as the waits expect
+    auto issue_tile = [&](int tile) {
+        issue(tile);
+        if constexpr (!QUANT) cp_async_commit();
     };
 
     if (!p.len_dev)
-        for (int s = 0; s < NS - 1; ++s) issue(s);   // K/V never come from the previous kernel here
+        for (int s = 0; s < NS - 1; ++s) issue_tile(s);   // K/V never come from the previous kernel here
     pdl_allow_dependents();
     pdl_wait_prior_grid();
     if (QUANT && p.rope_cs && pos >= 0 && part == p.parts - 1) {
@@ -284,6 +330,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_mma_kernel(const fa::Params p)
             kvq::quantize_block_warp<KV>(x, lane, row + (e / 32) * BB);
         }
         __threadfence();
+        asm volatile("fence.proxy.async.global;" ::: "memory");   // the row is read by bulk copies next
         __syncthreads();
     } else if (p.rope_cs && pos >= 0 && part == p.parts - 1) {
         // the new row: rotated k and v of this kv head into cache row pos
@@ -301,10 +348,11 @@ __global__ void __launch_bounds__(kThreads, 1) fa_mma_kernel(const fa::Params p)
                 __halves2half2(__float2half_rn(vr[2 * i]), __float2half_rn(vr[2 * i + 1]));
         }
         __threadfence();
+        asm volatile("fence.proxy.async.global;" ::: "memory");   // the row is read by bulk copies next
         __syncthreads();
     }
     if (p.len_dev)
-        for (int s = 0; s < NS - 1; ++s) issue(s);
+        for (int s = 0; s < NS - 1; ++s) issue_tile(s);
 
     // ---- queries: q * scale per head, scaled by a power of two 2^e so the
     // largest |entry| lies in [2^13, 2^14)
@@ -362,62 +410,55 @@ __global__ void __launch_bounds__(kThreads, 1) fa_mma_kernel(const fa::Params p)
     for (int n = 0; n < NTV; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
     float m_run = -INFINITY, l_run = 0.f;
 
+    bool copies_ok = true;   // false once a stage wait gave up (device flag raised): stop waiting
     for (int tile = 0; tile < ntiles; ++tile) {
-        cp_async_wait<NS - 2>();
+        if constexpr (QUANT) {
+            if (copies_ok) copies_ok = mbar_wait(&bars[tile % NS], (tile / NS) & 1);
+        } else {
+            cp_async_wait<NS - 2>();
+        }
         __syncthreads();   // tile's copies visible to all; the slot refilled next is no longer read
-        issue(tile + NS - 1);
+        if (copies_ok) issue_tile(tile + NS - 1);
         const int j0 = key0 + tile * kTile;
         const int n = min(kTile, key1 - j0);
-        // fp16: the stage itself, rows warp*16.. of it; quantised: this warp's
-        // private tiles, rows 0..15, dequantised from the raw stage here
-        uint32_t kst = ring_addr + uint32_t((tile % NS) * 2 * kTile * RS * 2);
-        uint32_t vst = kst + uint32_t(kTile * RS * 2);
-        int wrow = warp * 16;
-        if constexpr (QUANT) {
-            constexpr int LPR = D / 8;       // lanes per row, eight values each
-            constexpr int RPS = 32 / LPR;    // rows per step
-            const uint32_t kraw = ring_addr + uint32_t((tile % NS) * 2 * RAW), vraw = kraw + RAW;
-            kst = ring_addr + uint32_t(NS * 2 * RAW + warp * 2 * 16 * RS * 2);
-            vst = kst + uint32_t(16 * RS * 2);
-            wrow = 0;
-            const int c = lane % LPR;
-            const int boff = (c >> 2) * BB, qoff = boff + kvq::chunk_offset<KV>(c & 3);
-            const int shift = kvq::chunk_shift<KV>(c & 3);
-            auto load8 = [&](uint32_t row) -> uint4 {
-                const uint32_t a = row + qoff, a4 = a & ~3u, sh = (a & 3u) * 8;
-                const uint32_t w0 = lds32(a4), w1 = lds32(a4 + 4), w2 = lds32(a4 + 8);
-                uint32_t x0 = __funnelshift_r(w0, w1, sh), x1 = __funnelshift_r(w1, w2, sh);
-                kvq::isolate<KV>(x0, x1, shift);
-                const uint32_t d = lds16(row + boff);
-                return kvq::dequant8<KV>(x0, x1, d | (d << 16));
-            };
-            __syncwarp();   // every lane is past its reads of the previous tile
-#pragma unroll
-            for (int st = 0; st < 16 / RPS; ++st) {
-                const int rr = st * RPS + lane / LPR, r = warp * 16 + rr;
-                uint4 kv4 = make_uint4(0u, 0u, 0u, 0u), vv4 = kv4;
-                if (r < n) {
-                    kv4 = load8(kraw + uint32_t(lead_k + r * RB));
-                    vv4 = load8(vraw + uint32_t(lead_v + r * RB));
-                }
-                sts128(kst + uint32_t((rr * RS + c * 8) * 2), kv4);
-                sts128(vst + uint32_t((rr * RS + c * 8) * 2), vv4);
-            }
-            __syncwarp();
-        }
+        // fp16: K and V fragments by ldmatrix from the stage.  Quantised:
+        // straight from the raw rows — K pairs (key, dims 2t..2t+1) are the
+        // B fragment as they stand, V pairs are transposed by movmatrix —
+        // with the values kvq::dequant8 gives; V rows past n are zeros.
+        const uint32_t kst = ring_addr + uint32_t((tile % NS) * 2 * kTile * RS * 2);
+        const uint32_t vst = kst + uint32_t(kTile * RS * 2);
+        const int kraw = (tile % NS) * 2 * RAW + lead_k, vraw = (tile % NS) * 2 * RAW + RAW + lead_v;
+        auto scale2 = [&](int off) -> uint32_t {
+            const uint32_t d = *reinterpret_cast<const unsigned short*>(smem + off);
+            return d | (d << 16);
+        };
 
         // ---- S = Q K^T over this warp's 16 keys (two n-tiles of 8)
         float s[2][4];
 #pragma unroll
         for (int nt = 0; nt < 2; ++nt) {
             s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
-            const int krow = wrow + nt * 8 + (lane & 7);
+            if constexpr (QUANT) {
+                const int row = kraw + (warp * 16 + nt * 8 + g) * RB;
+                uint32_t d2[D / 32];
 #pragma unroll
-            for (int ks = 0; ks < KSQ; ks += 2) {
-                uint32_t r[4];
-                ldsm_x4(r, kst + uint32_t((krow * RS + ks * 16 + (lane >> 3) * 8) * 2));
-                mma16816(s[nt], qa[ks], r[0], r[1]);
-                mma16816(s[nt], qa[ks + 1], r[2], r[3]);
+                for (int bk = 0; bk < D / 32; ++bk) d2[bk] = scale2(row + bk * BB);
+#pragma unroll
+                for (int ks = 0; ks < KSQ; ++ks) {
+                    const int j = ks * 16 + 2 * t;   // dims j, j+1 and j+8, j+9
+                    const uint32_t b0 = dequant_pair<KV>(smem, row + (j / 32) * BB, j % 32, d2[j / 32]);
+                    const uint32_t b1 = dequant_pair<KV>(smem, row + (j / 32) * BB, j % 32 + 8, d2[j / 32]);
+                    mma16816(s[nt], qa[ks], b0, b1);
+                }
+            } else {
+                const int krow = warp * 16 + nt * 8 + (lane & 7);
+#pragma unroll
+                for (int ks = 0; ks < KSQ; ks += 2) {
+                    uint32_t r[4];
+                    ldsm_x4(r, kst + uint32_t((krow * RS + ks * 16 + (lane >> 3) * 8) * 2));
+                    mma16816(s[nt], qa[ks], r[0], r[1]);
+                    mma16816(s[nt], qa[ks + 1], r[2], r[3]);
+                }
             }
         }
         // hi + lo rows -> the head's scores for keys (nt, 2t + e)
@@ -477,26 +518,58 @@ __global__ void __launch_bounds__(kThreads, 1) fa_mma_kernel(const fa::Params p)
                                         : pack_half2(pr[1][0], pr[1][1]);
             pa[1] = pa[3] = 0u;
         }
-        // ---- O = O * alpha + P V
+        // ---- O = O * alpha + P V (no rows' maximum moved: alpha is 1 everywhere)
+        if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll
-        for (int nv = 0; nv < NTV; ++nv) {
-            o[nv][0] *= alpha;
-            o[nv][1] *= alpha;
-            o[nv][2] *= alpha;
-            o[nv][3] *= alpha;
+            for (int nv = 0; nv < NTV; ++nv) {
+                o[nv][0] *= alpha;
+                o[nv][1] *= alpha;
+                o[nv][2] *= alpha;
+                o[nv][3] *= alpha;
+            }
         }
+        if constexpr (QUANT) {
+            // rows g and g + 8 of this warp's 16 keys; pairs (key, dims) -> (dims, key)
+            const int r0 = warp * 16 + g;
+            const bool ok0 = r0 < n, ok1 = r0 + 8 < n;
+            const int row0 = vraw + r0 * RB, row1 = row0 + 8 * RB;
+            uint32_t d0[D / 32], d1[D / 32];
 #pragma unroll
-        for (int n2 = 0; n2 < NTV / 2; ++n2) {
-            uint32_t r[4];
-            const int m = lane >> 3;
-            const int vrow = wrow + (lane & 7) + 8 * (m & 1);
-            ldsm_x4_trans(r, vst + uint32_t((vrow * RS + n2 * 16 + 8 * (m >> 1)) * 2));
-            mma16816(o[2 * n2], pa, r[0], r[1]);
-            mma16816(o[2 * n2 + 1], pa, r[2], r[3]);
+            for (int bk = 0; bk < D / 32; ++bk) {
+                d0[bk] = scale2(row0 + bk * BB);
+                d1[bk] = scale2(row1 + bk * BB);
+            }
+            if (n == kTile) {
+#pragma unroll
+                for (int nv = 0; nv < NTV; ++nv) {
+                    const int j = nv * 8 + 2 * t, bk = j / 32;
+                    const uint32_t h0 = dequant_pair<KV>(smem, row0 + bk * BB, j % 32, d0[bk]);
+                    const uint32_t h1 = dequant_pair<KV>(smem, row1 + bk * BB, j % 32, d1[bk]);
+                    mma16816(o[nv], pa, movmatrix_trans(h0), movmatrix_trans(h1));
+                }
+            } else {
+#pragma unroll
+                for (int nv = 0; nv < NTV; ++nv) {
+                    const int j = nv * 8 + 2 * t, bk = j / 32;
+                    const uint32_t h0 = dequant_pair<KV>(smem, row0 + bk * BB, j % 32, d0[bk]);
+                    const uint32_t h1 = dequant_pair<KV>(smem, row1 + bk * BB, j % 32, d1[bk]);
+                    mma16816(o[nv], pa, movmatrix_trans(ok0 ? h0 : 0u), movmatrix_trans(ok1 ? h1 : 0u));
+                }
+            }
+        } else {
+#pragma unroll
+            for (int n2 = 0; n2 < NTV / 2; ++n2) {
+                uint32_t r[4];
+                const int m = lane >> 3;
+                const int vrow = warp * 16 + (lane & 7) + 8 * (m & 1);
+                ldsm_x4_trans(r, vst + uint32_t((vrow * RS + n2 * 16 + 8 * (m >> 1)) * 2));
+                mma16816(o[2 * n2], pa, r[0], r[1]);
+                mma16816(o[2 * n2 + 1], pa, r[2], r[3]);
+            }
         }
     }
-    cp_async_wait<0>();
-    __syncthreads();   // every copy landed and every warp is done with the ring
+    if constexpr (!QUANT) cp_async_wait<0>();
+    __syncthreads();   // every copy landed (each issued tile was waited for) and every warp is done with the ring
 
     // ---- hi + lo rows of O; then merge the four warps through shared memory
     float* s_wm = reinterpret_cast<float*>(smem);          // [kWarps][8]

@@ -73,26 +73,43 @@ struct ConvParams {
     int units;             // ne01 * chunks per plane
 };
 
-// One thread per 8 consecutive outputs: four 2-byte loads of its code bytes
-// (blocks are only 2-byte aligned), one of d, one 16-byte store; a warp's
-// stores cover 512 contiguous bytes.  Grid (units / 256, planes).
+// One thread per 8 consecutive outputs of kUnits rows-chunks (a CTA covers
+// 256 * kUnits consecutive (row, chunk) units of a plane): all their loads —
+// four 2-byte loads of the code bytes (blocks are only 2-byte aligned) and
+// one of d each — are issued before any conversion, then one 16-byte store
+// each; a warp's stores cover 512 contiguous bytes.  Grid (units / (256 *
+// kUnits), planes).
+constexpr int kUnits = 4;
 template <int KV>
 __global__ void __launch_bounds__(256) kv_to_f16_kernel(const ConvParams p) {
     constexpr int BB = block_bytes<KV>();
-    const int u = blockIdx.x * 256 + threadIdx.x;
-    if (u >= p.units) return;
-    const int i01 = u / p.chunks, ch = u - i01 * p.chunks;
-    const int c = ch & 3;
+    const int u0 = blockIdx.x * 256 * kUnits + threadIdx.x;
+    int i01[kUnits], ch[kUnits];
+#pragma unroll
+    for (int j = 0; j < kUnits; ++j) {
+        const int u = min(u0 + j * 256, p.units - 1);
+        i01[j] = u / p.chunks;
+        ch[j] = u - i01[j] * p.chunks;
+    }
     for (long long plane = blockIdx.y; plane < p.ne02 * p.ne03; plane += gridDim.y) {
         const long long i03 = plane / p.ne02, i02 = plane - i03 * p.ne02;
-        const uint8_t* blk = p.src + (i03 * p.s03 + i02 * p.s02 + i01 * p.s01 + (ch >> 2)) * BB;
-        const unsigned short* q = reinterpret_cast<const unsigned short*>(blk + chunk_offset<KV>(c));
-        uint32_t x0 = uint32_t(__ldg(q)) | (uint32_t(__ldg(q + 1)) << 16);
-        uint32_t x1 = uint32_t(__ldg(q + 2)) | (uint32_t(__ldg(q + 3)) << 16);
-        isolate<KV>(x0, x1, chunk_shift<KV>(c));
-        const uint32_t d = __ldg(reinterpret_cast<const unsigned short*>(blk));
-        const uint4 v = dequant8<KV>(x0, x1, d | (d << 16));
-        *reinterpret_cast<uint4*>(p.dst + (plane * p.ne01 + i01) * p.ne00 + ch * 8) = v;
+        const uint8_t* base = p.src + (i03 * p.s03 + i02 * p.s02) * BB;
+        uint32_t x0[kUnits], x1[kUnits], d[kUnits];
+#pragma unroll
+        for (int j = 0; j < kUnits; ++j) {
+            const uint8_t* blk = base + (i01[j] * p.s01 + (ch[j] >> 2)) * BB;
+            const unsigned short* q = reinterpret_cast<const unsigned short*>(blk + chunk_offset<KV>(ch[j] & 3));
+            x0[j] = uint32_t(__ldg(q)) | (uint32_t(__ldg(q + 1)) << 16);
+            x1[j] = uint32_t(__ldg(q + 2)) | (uint32_t(__ldg(q + 3)) << 16);
+            d[j] = __ldg(reinterpret_cast<const unsigned short*>(blk));
+        }
+#pragma unroll
+        for (int j = 0; j < kUnits; ++j) {
+            if (u0 + j * 256 >= p.units) break;
+            isolate<KV>(x0[j], x1[j], chunk_shift<KV>(ch[j] & 3));
+            const uint4 v = dequant8<KV>(x0[j], x1[j], d[j] | (d[j] << 16));
+            *reinterpret_cast<uint4*>(p.dst + (plane * p.ne01 + i01[j]) * p.ne00 + ch[j] * 8) = v;
+        }
     }
 }
 

@@ -114,12 +114,27 @@ def test_decode_equals_converted_fp16(cuda, orc, kv_type, d, hq, hkv):
 
 
 @pytest.mark.parametrize("kv_type", KV_TYPES)
-@pytest.mark.parametrize("seq", [1, 2, 63, 64, 65, 129, 4096, 20000])
-def test_ragged_and_long_contexts(cuda, orc, kv_type, seq):
-    """Short tails, the cluster merge (<= 16K keys) and the wide workspace merge."""
+@pytest.mark.parametrize("seq", [1, 2, 63, 64, 65, 129, 4096, 16384])
+def test_ragged_and_contexts_to_16k(cuda, orc, kv_type, seq):
+    """Short tails and the cluster merge (automatic split up to 16K keys, the
+    same split as the fp16 decode)."""
     o, lse, o16, lse16, *_ = run_pair(cuda, orc, kv_type, 1, 32, 8, seq, 128, seed=seq)
     assert np.array_equal(o.view(np.uint32), o16.view(np.uint32))
     assert np.array_equal(lse.view(np.uint32), lse16.view(np.uint32))
+
+
+@pytest.mark.parametrize("kv_type", KV_TYPES)
+def test_long_context_workspace_merge(cuda, orc, kv_type):
+    """Past 16K keys the automatic split differs (a quantised ring fits three
+    CTAs per SM, fp16 two), so: bit-exact at an explicit common split, and the
+    automatic split within the attention tolerance of attention_reference."""
+    seq = 20000
+    o, lse, o16, lse16, *_ = run_pair(cuda, orc, kv_type, 1, 32, 8, seq, 128, splits=48, seed=seq)
+    assert np.array_equal(o.view(np.uint32), o16.view(np.uint32))
+    o, lse, _, _, q, kf, vf = run_pair(cuda, orc, kv_type, 1, 32, 8, seq, 128, seed=seq)
+    p = oracle.Attn(n_head_q=32, n_head_kv=8, seq_kv=seq, d_qk=128, d_v=128)
+    ref_o, ref_lse, _ = orc.attention_reference_threaded(p, q, kf, vf, oracle.host_cores())
+    check_attention(o, lse, ref_o, ref_lse)
 
 
 @pytest.mark.parametrize("kv_type", KV_TYPES)
