@@ -42,8 +42,11 @@ typedef enum p100_status {
     P100_ERR_UNSUPPORTED = 5   /* no sm_100 device, or a shape this build does not handle     */
 } p100_status;
 
-/* Weight formats in the order of p100::qmv::Type (include/p100/qmv.h:20). */
-typedef enum p100_qtype { P100_Q4_0 = 0, P100_Q8_0 = 1, P100_Q4_K = 2 } p100_qtype;
+/* Weight formats in the order of p100::qmv::Type (include/p100/qmv.h:20),
+ * then ggml's Q5_K (176-byte) and Q6_K (210-byte) super-blocks of 256 values,
+ * which the reference does not have (the Q4_K_M GGUF mix keeps some tensors
+ * in them): p100_dequantize and p100_qmv only, on a general kernel. */
+typedef enum p100_qtype { P100_Q4_0 = 0, P100_Q8_0 = 1, P100_Q4_K = 2, P100_Q5_K = 3, P100_Q6_K = 4 } p100_qtype;
 
 /* K/V cache element types (llama.cpp's -ctk / -ctv f16, q8_0, q4_0, the
  * cache types the reference benchmarks: bench/phase0.sh:127).  A quantised
@@ -259,7 +262,10 @@ p100_status p100_argmax(const float* x, int n, int batch, int* idx, float* val, 
 /* --------------------------------------------------- batch-1 decoder */
 /* A Llama-3-shaped model with synthetic weights, decoded one token per
  * p100_decoder_step.  No reference counterpart (see above).  Every linear
- * weight and the embedding use wtype; norms are fp32; the KV cache is fp16.
+ * weight and the embedding use wtype; norms are fp32; the KV cache is fp16,
+ * or q8_0 / q4_0 blocks with kv_type (head_dim 64 or 128 and 1, 2, 4 or 8
+ * query heads per kv head: the new rows are quantised inside the attention
+ * kernel, as ggml quantises them for a quantised cache).
  * With a tensor-parallel handle the decoder holds that rank's slices: q/k/v
  * and gate/up split by output rows, o and down along K with an NCCL
  * all-reduce after each, the LM head by vocabulary rows with an all-gather of
@@ -271,6 +277,7 @@ typedef struct p100_llama_config {
     float rope_theta, norm_eps;
     int wtype;
     int flags;   /* P100_DEC_* (0: defaults) */
+    int kv_type; /* p100_kv_type of the cache (0: fp16) */
 } p100_llama_config;
 /* Run each RMSNorm inside the mat-vec that consumes it (p100_qmv_rmsnorm;
  * hidden 4096 or 8192, no peer-memory all-reduce): the same bits with one

@@ -28,10 +28,10 @@ HERE = pathlib.Path(__file__).resolve().parent
 LIB = HERE / "lib" / "libp100_oracle.so"
 REF_LIB = HERE / "_ref" / "libp100_ref.so"
 
-Q4_0, Q8_0, Q4_K = 0, 1, 2
-TYPE_NAMES = {Q4_0: "q4_0", Q8_0: "q8_0", Q4_K: "q4_K"}
-BLOCK_ELEMS = {Q4_0: 32, Q8_0: 32, Q4_K: 256}
-BLOCK_BYTES = {Q4_0: 18, Q8_0: 34, Q4_K: 144}
+Q4_0, Q8_0, Q4_K, Q5_K, Q6_K = 0, 1, 2, 3, 4
+TYPE_NAMES = {Q4_0: "q4_0", Q8_0: "q8_0", Q4_K: "q4_K"}   # the reference's types (its golden tables)
+BLOCK_ELEMS = {Q4_0: 32, Q8_0: 32, Q4_K: 256, Q5_K: 256, Q6_K: 256}
+BLOCK_BYTES = {Q4_0: 18, Q8_0: 34, Q4_K: 144, Q5_K: 176, Q6_K: 210}
 
 # K/V cache element types (kv_oracle.cpp); a quantised row of d values holds
 # d / 32 blocks of KV_BLOCK_BYTES.
@@ -147,6 +147,7 @@ class Oracle(_Base):
         self._swiglu = f("swiglu_q8_1", ip, vp, ip, vp)
         self._argmax = f("argmax", ip, vp, ip, vp)
         self._decode_step = f("decode_step", ip, vp, vp, vp, vp, vp, ip, ip, vp, vp)
+        self._decode_step_kv = f("decode_step_kv", ip, vp, vp, ip, ip, vp, vp, vp, ip, ip, vp, vp)
         ll = C.c_int64
         self.kv_block_bytes = f("kv_block_bytes", ip, ip)
         self._kv_to_f16 = f("kv_to_f16", ip, ip, vp, ll, ll, ll, ll, ll, ll, ll, vp)
@@ -319,12 +320,13 @@ class Oracle(_Base):
         self._check(self._kv_quantize(kv_type, _ptr(x), x.size, _ptr(out)))
         return out
 
-    def decode_step(self, cfg, weights, k_cache, v_cache, rope_cs, pos, token):
+    def decode_step(self, cfg, weights, k_cache, v_cache, rope_cs, pos, token, kv_type=KV_F16, append=True):
         """One token of the restated decoder.  cfg: LlamaConfig; weights: dict of
         host numpy arrays named as the decoder's tensors ('embed', 'attn_norm'
         [per layer], 'wqkv', 'wo', 'ffn_norm', 'wgu', 'wdown', 'out_norm',
-        'lm_head').  Caches (uint16 fp16 bits) are updated in place.  Returns
-        (next token, logits, final residual)."""
+        'lm_head').  Caches (uint16 fp16 bits, or uint8 q8_0 / q4_0 blocks with
+        kv_type) are updated in place; append=False keeps a quantised cache's
+        row pos as given.  Returns (next token, logits, final residual)."""
         L = cfg.n_layer
         keep = []
 
@@ -344,9 +346,9 @@ class Oracle(_Base):
                          C.cast(table("wdown"), C.c_void_p), arr(weights["out_norm"]), arr(weights["lm_head"]))
         logits = np.zeros(cfg.vocab, dtype=np.float32)
         hidden = np.zeros(cfg.hidden, dtype=np.float32)
-        tok = self._decode_step(C.byref(cfg), C.byref(w), _ptr(k_cache), _ptr(v_cache),
-                                _ptr(np.ascontiguousarray(rope_cs, dtype=np.float32)), pos, token, _ptr(logits),
-                                _ptr(hidden))
+        tok = self._decode_step_kv(C.byref(cfg), C.byref(w), kv_type, int(bool(append)), _ptr(k_cache), _ptr(v_cache),
+                                   _ptr(np.ascontiguousarray(rope_cs, dtype=np.float32)), pos, token, _ptr(logits),
+                                   _ptr(hidden))
         if tok < 0:
             raise ValueError("decode_step rejected its arguments")
         return tok, logits, hidden

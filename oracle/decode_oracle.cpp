@@ -168,6 +168,19 @@ int p100o_argmax(const float* x, int n, float* val) {
 
 int p100o_decode_step(const p100o_llama* c, const p100o_llama_weights* w, uint16_t* k_cache, uint16_t* v_cache,
                       const float* rope_cs, int pos, int token, float* logits, float* hidden_out) {
+    return p100o_decode_step_kv(c, w, P100O_KV_F16, 1, k_cache, v_cache, rope_cs, pos, token, logits, hidden_out);
+}
+
+// With a q8_0 / q4_0 cache ([layer][n_head_kv][max_ctx][head_dim/32 blocks]):
+// q and k rotated as p100o_rope_kv_append rotates them, the rotated k row and
+// the v row of each kv head quantised into cache row pos (p100o_kv_quantize:
+// ggml's block quantisers), attention over the rows converted to fp16
+// (p100o_kv_to_f16), in FP64 as for an fp16 cache.  append = 0 (quantised
+// caches only) leaves row pos as the caller gave it: a test then attends over
+// the device's own new rows, whose codes can sit one rounding step away from
+// these (the two sides' k and v differ in the last bits).
+int p100o_decode_step_kv(const p100o_llama* c, const p100o_llama_weights* w, int kv_type, int append, void* k_cache,
+                         void* v_cache, const float* rope_cs, int pos, int token, float* logits, float* hidden_out) {
     const int t = c->wtype, hd = c->head_dim, H = c->hidden;
     const int nq = c->n_head, nkv = c->n_head_kv, F = c->ffn;
     if (pos < 0 || pos >= c->max_ctx || token < 0 || token >= c->vocab) return -1;
@@ -186,18 +199,55 @@ int p100o_decode_step(const p100o_llama* c, const p100o_llama_weights* w, uint16
                            nullptr);
         if (qmv(w->wqkv[l], (nq + 2 * nkv) * hd, H, qkv.data())) return -1;
         const size_t layer_off = size_t(l) * nkv * hs;
-        p100o_rope_kv_append(qkv.data(), nq, nkv, hd, rope_cs, c->max_ctx, pos, k_cache + layer_off,
-                             v_cache + layer_off, hs);
-        // attention over rows [0, pos] of this layer's cache, in FP64
         const int seq = pos + 1;
         std::vector<float> kf(size_t(nkv) * seq * hd), vf(size_t(nkv) * seq * hd);
-        for (int h = 0; h < nkv; ++h)
-            for (int j = 0; j < seq; ++j)
-                for (int e = 0; e < hd; ++e) {
-                    const size_t src = layer_off + size_t(h) * hs + size_t(j) * hd + e;
-                    kf[(size_t(h) * seq + j) * hd + e] = half_value(k_cache[src]);
-                    vf[(size_t(h) * seq + j) * hd + e] = half_value(v_cache[src]);
+        if (kv_type == P100O_KV_F16) {
+            uint16_t* kc = static_cast<uint16_t*>(k_cache);
+            uint16_t* vc = static_cast<uint16_t*>(v_cache);
+            p100o_rope_kv_append(qkv.data(), nq, nkv, hd, rope_cs, c->max_ctx, pos, kc + layer_off, vc + layer_off,
+                                 hs);
+            for (int h = 0; h < nkv; ++h)
+                for (int j = 0; j < seq; ++j)
+                    for (int e = 0; e < hd; ++e) {
+                        const size_t src = layer_off + size_t(h) * hs + size_t(j) * hd + e;
+                        kf[(size_t(h) * seq + j) * hd + e] = half_value(kc[src]);
+                        vf[(size_t(h) * seq + j) * hd + e] = half_value(vc[src]);
+                    }
+        } else {
+            const int bb = p100o_kv_block_bytes(kv_type);
+            if (!bb || hd % 32) return -1;
+            const size_t rb = size_t(hd / 32) * bb, hsb = size_t(c->max_ctx) * rb;
+            uint8_t* kc = static_cast<uint8_t*>(k_cache) + size_t(l) * nkv * hsb;
+            uint8_t* vc = static_cast<uint8_t*>(v_cache) + size_t(l) * nkv * hsb;
+            std::vector<float> kr(static_cast<size_t>(hd));
+            for (int h = 0; h < nq + nkv; ++h) {
+                float* v = qkv.data() + size_t(h) * hd;
+                for (int i = 0; i < hd / 2; ++i) {
+                    const float x0 = v[2 * i], x1 = v[2 * i + 1];
+                    const float cs = rope_cs[(size_t(pos) * (hd / 2) + i) * 2];
+                    const float sn = rope_cs[(size_t(pos) * (hd / 2) + i) * 2 + 1];
+                    float* out = h < nq ? v : kr.data();
+                    out[2 * i] = x0 * cs - x1 * sn;
+                    out[2 * i + 1] = x0 * sn + x1 * cs;
                 }
+                if (h >= nq && append) {
+                    const int kh = h - nq;
+                    p100o_kv_quantize(kv_type, kr.data(), size_t(hd), kc + kh * hsb + size_t(pos) * rb);
+                    p100o_kv_quantize(kv_type, qkv.data() + size_t(nq + nkv + kh) * hd, size_t(hd),
+                                      vc + kh * hsb + size_t(pos) * rb);
+                }
+            }
+            std::vector<uint16_t> k16(size_t(seq) * hd), v16(size_t(seq) * hd);
+            for (int h = 0; h < nkv; ++h) {
+                p100o_kv_to_f16(kv_type, kc + h * hsb, hd, seq, 1, 1, hd / 32, 0, 0, k16.data());
+                p100o_kv_to_f16(kv_type, vc + h * hsb, hd, seq, 1, 1, hd / 32, 0, 0, v16.data());
+                for (size_t i = 0; i < k16.size(); ++i) {
+                    kf[size_t(h) * seq * hd + i] = half_value(k16[i]);
+                    vf[size_t(h) * seq * hd + i] = half_value(v16[i]);
+                }
+            }
+        }
+        // attention over rows [0, pos] of this layer's cache, in FP64
         p100o_attn ap = {1, nq, nkv, 1, seq, hd, hd, 0.0f, 0.0f, 0};
         if (p100o_attention_reference(&ap, qkv.data(), kf.data(), vf.data(), nullptr, attn.data(), nullptr))
             return -1;

@@ -80,9 +80,14 @@ float fp16_round_d(double x) {
 }
 
 // ---------------------------------------------------------------- formats
-int elems_of(int t) { return t == P100O_Q4_K ? 256 : 32; }            // qmv_model.cpp:12
-int bytes_of(int t) { return t == P100O_Q4_0 ? 18 : t == P100O_Q8_0 ? 34 : 144; }  // :13
-bool known_type(int t) { return t == P100O_Q4_0 || t == P100O_Q8_0 || t == P100O_Q4_K; }
+// Q5_K (176 bytes) and Q6_K (210 bytes) are ggml's published super-block
+// formats; the reference's contract has the first three only.
+int elems_of(int t) { return t == P100O_Q4_0 || t == P100O_Q8_0 ? 32 : 256; }   // qmv_model.cpp:12
+int bytes_of(int t) {                                                           // :13
+    return t == P100O_Q4_0 ? 18 : t == P100O_Q8_0 ? 34 : t == P100O_Q4_K ? 144 : t == P100O_Q5_K ? 176 : 210;
+}
+bool ref_type(int t) { return t == P100O_Q4_0 || t == P100O_Q8_0 || t == P100O_Q4_K; }
+bool known_type(int t) { return ref_type(t) || t == P100O_Q5_K || t == P100O_Q6_K; }
 
 // 0,2,1,3 order inside each group of four (qmv_model.cpp:64).
 inline int lane_order(int i) { return (i & ~3) | ((i & 1) << 1) | ((i & 2) >> 1); }
@@ -99,10 +104,12 @@ float butterfly_sum(const float* in) {
     return a[0];
 }
 
-// One 32-value slab of a weight block: the record of qmv_model.cpp:78-91.
+// One 32-value slab of a weight block: the record of qmv_model.cpp:78-91
+// (value d*sc*q - m*mn); Q6_K scales each 16 values, so sc2 is the scale of
+// values 16..31 (equal to sc for every other type).
 struct Slab {
     float d = 0, m = 0;
-    int sc = 1, mn = 0;
+    int sc = 1, mn = 0, sc2 = 1;
     int q[32];
 };
 
@@ -127,20 +134,47 @@ Slab slab_of(int t, const uint8_t* block, int sub) {
         for (int i = 0; i < 32; ++i) s.q[i] = ((block[2 + (i & 15)] >> ((i >> 4) * 4)) & 15) - 8;
     } else if (t == P100O_Q8_0) {
         for (int i = 0; i < 32; ++i) s.q[i] = static_cast<int8_t>(block[2 + i]);
-    } else {
+    } else if (t == P100O_Q4_K) {
         uint16_t dmin;
         std::memcpy(&dmin, block + 2, 2);
         s.m = half_to_float(dmin);
         q4k_scale_min(block + 4, sub, s.sc, s.mn);
         const uint8_t* qs = block + 16 + (sub / 2) * 32;
         for (int i = 0; i < 32; ++i) s.q[i] = (qs[i] >> ((sub % 2) * 4)) & 15;
+    } else if (t == P100O_Q5_K) {
+        // {d, dmin, scales[12], qh[32], qs[128]} (ggml block_q5_K): the Q4_K
+        // nibble of slab `sub` plus 16 * bit `sub` of qh[i]
+        uint16_t dmin;
+        std::memcpy(&dmin, block + 2, 2);
+        s.m = half_to_float(dmin);
+        q4k_scale_min(block + 4, sub, s.sc, s.mn);
+        const uint8_t* qh = block + 16;
+        const uint8_t* qs = block + 48 + (sub / 2) * 32;
+        for (int i = 0; i < 32; ++i) s.q[i] = ((qs[i] >> ((sub % 2) * 4)) & 15) | (((qh[i] >> sub) & 1) << 4);
+    } else {
+        // {ql[128], qh[64], int8 scales[16], d} (ggml block_q6_K): slab sub =
+        // 4h + c of half h; low 4 bits from ql[64h + 32(c&1) + i] (high
+        // nibble when c >= 2), bits 4-5 from qh[32h + i] >> 2c, minus 32;
+        // scale scales[8h + 2c + i/16]
+        uint16_t d;
+        std::memcpy(&d, block + 208, 2);
+        s.d = half_to_float(d);
+        const int h = sub / 4, c = sub % 4;
+        const uint8_t* ql = block + 64 * h + 32 * (c & 1);
+        const uint8_t* qh = block + 128 + 32 * h;
+        const int8_t* sc = reinterpret_cast<const int8_t*>(block + 192 + 8 * h + 2 * c);
+        s.sc = sc[0];
+        s.sc2 = sc[1];
+        for (int i = 0; i < 32; ++i) s.q[i] = (((ql[i] >> ((c >> 1) * 4)) & 15) | (((qh[i] >> (2 * c)) & 3) << 4)) - 32;
+        return s;
     }
+    s.sc2 = s.sc;
     return s;
 }
 
 // Dequantised value in double, qmv_model.cpp:143.
 inline double slab_value(const Slab& s, int i) {
-    return double(s.d) * s.sc * s.q[i] - double(s.m) * s.mn;
+    return double(s.d) * (i < 16 ? s.sc : s.sc2) * s.q[i] - double(s.m) * s.mn;
 }
 
 // h16 FP64 dot, qmv_model.cpp:92-99.
@@ -183,6 +217,33 @@ float h16_model(int t, const uint8_t* w, int k, const p100o_act* acts, int chain
 float q81_row(int t, const uint8_t* w, int k, const p100o_act* acts) {
     float r = 0;
     const int bs = elems_of(t), bb = bytes_of(t);
+    if (!ref_type(t)) {
+        // Q5_K / Q6_K, per 32-value slab against its Q8_1 block, in the
+        // library's slab arithmetic (qmv.cuh slab_dot): Q5_K as Q4_K,
+        // fma(d, qd * (dot * sc), -dmin * (qd * (sum(q8) * mn))); Q6_K
+        // (d * qd) * (sc * dot(values 0..15) + sc2 * dot(values 16..31))
+        for (int b = 0; b < k / bs; ++b)
+            for (int sub = 0; sub < 8; ++sub) {
+                const Slab s = slab_of(t, w + size_t(b) * bb, sub);
+                const p100o_act& a = acts[b * 8 + sub];
+                if (t == P100O_Q5_K) {
+                    int dot = 0, sum = 0;
+                    for (int i = 0; i < 32; ++i) {
+                        dot += s.q[i] * a.q[i];
+                        sum += a.q[i];
+                    }
+                    r += std::fma(s.d, a.qd * float(dot * s.sc), -s.m * (a.qd * float(sum * s.mn)));
+                } else {
+                    int lo = 0, hi = 0;
+                    for (int i = 0; i < 16; ++i) {
+                        lo += s.q[i] * a.q[i];
+                        hi += s.q[i + 16] * a.q[i + 16];
+                    }
+                    r += (s.d * a.qd) * float(s.sc * lo + s.sc2 * hi);
+                }
+            }
+        return r;
+    }
     for (int b = 0; b < k / bs; ++b) {
         const uint8_t* block = w + b * bb;
         if (t != P100O_Q4_K) {
@@ -380,8 +441,8 @@ int p100o_random_row(int type, int k, void* rng, uint8_t* out) {
         uint8_t* p = out + size_t(b) * bb;
         for (int i = 0; i < bb; ++i) p[i] = static_cast<uint8_t>(byte(g));
         const uint16_t d = half_from_double(scale(g));
-        std::memcpy(p, &d, 2);
-        if (type == P100O_Q4_K) {
+        std::memcpy(p + (type == P100O_Q6_K ? 208 : 0), &d, 2);
+        if (type == P100O_Q4_K || type == P100O_Q5_K) {
             const uint16_t m = half_from_double(scale(g));
             std::memcpy(p + 2, &m, 2);
         }
@@ -446,8 +507,10 @@ int p100o_evaluate(int type, const void* w_row, const float* x, int k, const p10
     }
     r.q81 = q81_row(type, w, k, acts);
     r.weight_norm = std::sqrt(r.weight_norm);
-    r.h8 = h16_model(type, w, k, acts, 8);
-    r.h16 = h16_model(type, w, k, acts, 16);
+    // the h16 model (one scale per 32 values) covers the reference's types
+    r.h8 = ref_type(type) ? h16_model(type, w, k, acts, 8) : NAN;
+    r.h16 = ref_type(type) ? h16_model(type, w, k, acts, 16) : NAN;
+    if (!ref_type(type)) r.h16_exact = NAN;
     *out = r;
     return 0;
 }
@@ -458,6 +521,7 @@ int p100o_qmv_h16(int type, const void* w, int rows, int k, const p100o_act* act
     if (!check_qmv_shape(type, k)) return -1;
     if (rows < 0 || batch <= 0) return fail("rows must be non-negative and batch positive");
     if (chain != 8 && chain != 16) return fail("invalid h16 shape/chain");   // qmv_model.cpp:122
+    if (!ref_type(type)) return fail("the h16 path covers Q4_0, Q8_0 and Q4_K");
     const size_t rb = size_t(k / elems_of(type)) * bytes_of(type);
     const uint8_t* wb = static_cast<const uint8_t*>(w);
     for (int c = 0; c < batch; ++c)

@@ -25,8 +25,10 @@
 extern "C" {
 #endif
 
-/* Weight formats, in the order of p100::qmv::Type (include/p100/qmv.h:20). */
-enum { P100O_Q4_0 = 0, P100O_Q8_0 = 1, P100O_Q4_K = 2 };
+/* Weight formats, in the order of p100::qmv::Type (include/p100/qmv.h:20),
+ * then ggml's Q5_K and Q6_K super-blocks (not in the reference's contract:
+ * dequantisation and the q81 dot only; no h16 model). */
+enum { P100O_Q4_0 = 0, P100O_Q8_0 = 1, P100O_Q4_K = 2, P100O_Q5_K = 3, P100O_Q6_K = 4 };
 
 /* Thread-local description of the last failure (status -1). */
 const char* p100o_last_error(void);
@@ -170,6 +172,14 @@ int p100o_decode_step(const p100o_llama* cfg, const p100o_llama_weights* w, uint
 
 /* ---- quantised K/V cache (kv_oracle.cpp) */
 enum { P100O_KV_F16 = 0, P100O_KV_Q8_0 = 1, P100O_KV_Q4_0 = 2 };
+/* p100o_decode_step over a cache of kv_type: fp16 bits as above, or q8_0 /
+ * q4_0 blocks [layer][n_head_kv][max_ctx][head_dim/32]; the new rows are the
+ * rotated k and the v of each kv head quantised by p100o_kv_quantize (append
+ * = 1; with 0 a quantised cache's row pos is used as given), the attention
+ * reads every row converted by p100o_kv_to_f16. */
+int p100o_decode_step_kv(const p100o_llama* cfg, const p100o_llama_weights* w, int kv_type, int append,
+                         void* k_cache, void* v_cache, const float* rope_cs, int pos, int token, float* logits,
+                         float* hidden_out);
 /* 34 (q8_0), 18 (q4_0), else 0. */
 int p100o_kv_block_bytes(int kv_type);
 /* dequantize_block over a K/V view (bench/micro/dequant_nc.cu:32-121):

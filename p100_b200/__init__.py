@@ -22,11 +22,11 @@ HERE = pathlib.Path(__file__).resolve().parent
 LIB_PATH = HERE / "lib" / "libp100_b200.so"
 CSRC = HERE / "csrc"
 
-Q4_0, Q8_0, Q4_K = 0, 1, 2
-TYPE_NAMES = {Q4_0: "q4_0", Q8_0: "q8_0", Q4_K: "q4_K"}
+Q4_0, Q8_0, Q4_K, Q5_K, Q6_K = 0, 1, 2, 3, 4
+TYPE_NAMES = {Q4_0: "q4_0", Q8_0: "q8_0", Q4_K: "q4_K", Q5_K: "q5_K", Q6_K: "q6_K"}
 TYPES = {v: k for k, v in TYPE_NAMES.items()}
-BLOCK_ELEMS = {Q4_0: 32, Q8_0: 32, Q4_K: 256}
-BLOCK_BYTES = {Q4_0: 18, Q8_0: 34, Q4_K: 144}
+BLOCK_ELEMS = {Q4_0: 32, Q8_0: 32, Q4_K: 256, Q5_K: 256, Q6_K: 256}
+BLOCK_BYTES = {Q4_0: 18, Q8_0: 34, Q4_K: 144, Q5_K: 176, Q6_K: 210}
 # K/V cache element types (p100_kv_type) and their 32-value block bytes.
 KV_F16, KV_Q8_0, KV_Q4_0 = 0, 1, 2
 KV_BLOCK_BYTES = {KV_Q8_0: 34, KV_Q4_0: 18}
@@ -406,12 +406,13 @@ class LlamaConfig(C.Structure):
     """p100_llama_config."""
     _fields_ = [("n_layer", C.c_int), ("hidden", C.c_int), ("n_head", C.c_int), ("n_head_kv", C.c_int),
                 ("head_dim", C.c_int), ("ffn", C.c_int), ("vocab", C.c_int), ("max_ctx", C.c_int),
-                ("rope_theta", C.c_float), ("norm_eps", C.c_float), ("wtype", C.c_int), ("flags", C.c_int)]
+                ("rope_theta", C.c_float), ("norm_eps", C.c_float), ("wtype", C.c_int), ("flags", C.c_int),
+                ("kv_type", C.c_int)]
 
     def __init__(self, n_layer, hidden, n_head, n_head_kv, head_dim, ffn, vocab, max_ctx, rope_theta=500000.0,
-                 norm_eps=1e-5, wtype=0, flags=0):
+                 norm_eps=1e-5, wtype=0, flags=0, kv_type=0):
         super().__init__(n_layer, hidden, n_head, n_head_kv, head_dim, ffn, vocab, max_ctx, rope_theta, norm_eps,
-                         wtype, flags)
+                         wtype, flags, kv_type)
 
 
 DEC_FUSED_NORM = 1   # P100_DEC_FUSED_NORM

@@ -78,9 +78,14 @@ p100_status require_sm100(int* device_out, int* sm_count_out) {
 
 namespace {
 
-bool known_type(int t) { return t == P100_Q4_0 || t == P100_Q8_0 || t == P100_Q4_K; }
-int elems_of(int t) { return t == P100_Q4_K ? 256 : 32; }
-int bytes_of(int t) { return t == P100_Q4_0 ? 18 : t == P100_Q8_0 ? 34 : 144; }
+// the reference's three formats (every kernel) and ggml's Q5_K / Q6_K (the
+// general mat-vec and dequantisation kernels)
+bool ref_type(int t) { return t == P100_Q4_0 || t == P100_Q8_0 || t == P100_Q4_K; }
+bool known_type(int t) { return ref_type(t) || t == P100_Q5_K || t == P100_Q6_K; }
+int elems_of(int t) { return t == P100_Q4_0 || t == P100_Q8_0 ? 32 : 256; }
+int bytes_of(int t) {
+    return t == P100_Q4_0 ? 18 : t == P100_Q8_0 ? 34 : t == P100_Q4_K ? 144 : t == P100_Q5_K ? 176 : 210;
+}
 
 p100_status launch_status(const char* what) { return cuda_status(cudaGetLastError(), what); }
 
@@ -103,6 +108,7 @@ size_t round128(size_t x) { return (x + 127) & ~size_t(127); }
 constexpr size_t kStageTarget = 16 * 1024;
 
 bool plan_bulk(int type, const void* w, int rows, int k, int batch, int sms, QmvPlan& plan) {
+    if (!ref_type(type)) return false;
     const size_t row_bytes = size_t(k / elems_of(type)) * bytes_of(type);
     if (reinterpret_cast<uintptr_t>(w) % 16 || row_bytes % 16 || k % 256) return false;
     const int rps = int(std::max<size_t>(1, std::min<size_t>(qmv::kMaxRows, (kStageTarget + row_bytes / 2) / row_bytes)));
@@ -182,6 +188,7 @@ struct TeamPlan {
 // The batch-1 kernel: a lane per 256-weight column group, one row per team
 // per stage.  Needs 16-byte aligned weights and activations and k % 256 == 0.
 bool plan_team(int type, const void* w, const void* xq, int rows, int k, int batch, int sms, TeamPlan& plan) {
+    if (!ref_type(type)) return false;
     if (batch != 1 || k % 256 || reinterpret_cast<uintptr_t>(w) % 16 || reinterpret_cast<uintptr_t>(xq) % 16)
         return false;
     const int ngroups = k / 256;
@@ -344,6 +351,7 @@ struct MmaPlan {
 // consumer warps, whose per-warp share of blocks is compiled in and whose
 // layout fits: two ring slots ahead of the activations.
 bool plan_mma(int type, const void* w, const void* xq, int rows, int k, int batch, int sms, MmaPlan& plan) {
+    if (!ref_type(type)) return false;
     if (batch < 2 || batch > 16 || !known_type(type)) return false;
     if (reinterpret_cast<uintptr_t>(w) % 16 || reinterpret_cast<uintptr_t>(xq) % 16 || k % 256) return false;
     const int nb = k / 32;
@@ -494,7 +502,9 @@ p100_status run_qmv(int type, const void* w, int rows, int k, const void* xq, in
     switch (type) {
         case P100_Q4_0: qmv::qmv_generic_kernel<P100_Q4_0><<<grid, 256, 0, stream>>>(wb, xb, y, rows, k, batch, row_bytes); break;
         case P100_Q8_0: qmv::qmv_generic_kernel<P100_Q8_0><<<grid, 256, 0, stream>>>(wb, xb, y, rows, k, batch, row_bytes); break;
-        default: qmv::qmv_generic_kernel<P100_Q4_K><<<grid, 256, 0, stream>>>(wb, xb, y, rows, k, batch, row_bytes); break;
+        case P100_Q4_K: qmv::qmv_generic_kernel<P100_Q4_K><<<grid, 256, 0, stream>>>(wb, xb, y, rows, k, batch, row_bytes); break;
+        case P100_Q5_K: qmv::qmv_generic_kernel<P100_Q5_K><<<grid, 256, 0, stream>>>(wb, xb, y, rows, k, batch, row_bytes); break;
+        default: qmv::qmv_generic_kernel<P100_Q6_K><<<grid, 256, 0, stream>>>(wb, xb, y, rows, k, batch, row_bytes); break;
     }
     return launch_status("qmv_generic_kernel launch");
 }
@@ -861,7 +871,9 @@ p100_status p100_dequantize(int type, const void* w, int rows, int k, float* out
     switch (type) {
         case P100_Q4_0: dequantize_kernel<P100_Q4_0><<<grid, 256, 0, stream>>>(wb, out, rows, k, row_bytes); break;
         case P100_Q8_0: dequantize_kernel<P100_Q8_0><<<grid, 256, 0, stream>>>(wb, out, rows, k, row_bytes); break;
-        default: dequantize_kernel<P100_Q4_K><<<grid, 256, 0, stream>>>(wb, out, rows, k, row_bytes); break;
+        case P100_Q4_K: dequantize_kernel<P100_Q4_K><<<grid, 256, 0, stream>>>(wb, out, rows, k, row_bytes); break;
+        case P100_Q5_K: dequantize_kernel<P100_Q5_K><<<grid, 256, 0, stream>>>(wb, out, rows, k, row_bytes); break;
+        default: dequantize_kernel<P100_Q6_K><<<grid, 256, 0, stream>>>(wb, out, rows, k, row_bytes); break;
     }
     return launch_status("dequantize_kernel launch");
 }
@@ -1023,6 +1035,7 @@ extern "C" p100_status p100_qmv_h16(int type, const void* w, int rows, int k, co
                                     int chain, float* y, p100_stream_t stream) {
     clear_error();
     if (!known_type(type)) return set_error(P100_ERR_INVALID, "unknown weight type %d", type);
+    if (!ref_type(type)) return set_error(P100_ERR_UNSUPPORTED, "the h16 path covers Q4_0, Q8_0 and Q4_K");
     if (k <= 0 || k % elems_of(type)) return set_error(P100_ERR_INVALID, "whole weight blocks required");
     if (chain != 8 && chain != 16) return set_error(P100_ERR_INVALID, "invalid h16 shape/chain");
     if (rows < 0 || batch <= 0) return set_error(P100_ERR_INVALID, "rows must be non-negative and batch positive");

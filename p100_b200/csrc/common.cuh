@@ -126,6 +126,13 @@ __device__ __forceinline__ float half_hi(uint32_t w) {
 // Bytes 2..5 of the 8-byte pair (lo, hi): realigns a 2-byte-offset word.
 __device__ __forceinline__ uint32_t shift2(uint32_t lo, uint32_t hi) { return __byte_perm(lo, hi, 0x5432); }
 
+// fp16 of v (nearest even) into the 2-byte aligned p with one 16-bit store.
+// (Writing its two bytes as two 8-bit stores lost the low byte in this
+// sm_100a build, measured: every scale came out with a zero low byte.)
+__device__ __forceinline__ void store_half_bits(uint8_t* p, float v) {
+    *reinterpret_cast<unsigned short*>(p) = __half_as_ushort(__float2half_rn(v));
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);

@@ -22,6 +22,7 @@
 #pragma once
 #include "common.cuh"
 #include "quant.cuh"
+#include "kv_quant.cuh"
 
 namespace p100b {
 namespace dec {
@@ -436,11 +437,7 @@ __device__ __forceinline__ float normal_from(uint64_t h) {   // Box-Muller
     const float u1 = unit_float(h), u2 = unit_float(mix64(h));
     return sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2);
 }
-__device__ __forceinline__ void store_half(uint8_t* p, float v) {
-    const unsigned short b = __half_as_ushort(__float2half_rn(v));
-    p[0] = uint8_t(b & 0xff);
-    p[1] = uint8_t(b >> 8);
-}
+__device__ __forceinline__ void store_half(uint8_t* p, float v) { store_half_bits(p, v); }
 
 // Weight blocks of a rows x blocks matrix slice whose (row, block) (0, 0)
 // sits at global (row0, block0).  Q4_0: d = |N(0,1)| * dscale, codes
@@ -495,6 +492,25 @@ __global__ void init_kv_kernel(__half* __restrict__ c, int heads, int npos, int 
     const long long e = id % per_head;
     const uint64_t g = (uint64_t(head0 + h) << 40) ^ uint64_t(e);
     c[h * head_stride + e] = __float2half_rn(normal_from(mix64(key ^ mix64(g))) * scale);
+}
+
+// The same values as init_kv_kernel (before its fp16 rounding), quantised
+// to q8_0 / q4_0 blocks with kvq::quantize_block_warp: one warp per block,
+// lane = value; row (h, pos) at c + (h * max_ctx + pos) * hd/32 blocks.
+template <int KV>
+__global__ void init_kv_quant_kernel(uint8_t* __restrict__ c, int heads, int npos, int hd, int max_ctx, uint64_t key,
+                                     int head0, float scale) {
+    const long long blk = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    const long long per_head = static_cast<long long>(npos) * (hd / 32);
+    if (blk >= per_head * heads) return;   // warp-uniform
+    const int h = static_cast<int>(blk / per_head);
+    const long long e = (blk % per_head) * 32 + lane;   // value index within the head's rows
+    const uint64_t g = (uint64_t(head0 + h) << 40) ^ uint64_t(e);
+    const float x = normal_from(mix64(key ^ mix64(g))) * scale;
+    const long long pos = e / hd;
+    uint8_t* row = c + (static_cast<long long>(h) * max_ctx + pos) * (hd / 32) * kvq::block_bytes<KV>();
+    kvq::quantize_block_warp<KV>(x, lane, row + ((e % hd) / 32) * kvq::block_bytes<KV>());
 }
 
 }  // namespace dec

@@ -45,7 +45,8 @@ struct Decoder {
     size_t arena_bytes = 0;
     std::vector<DecTensor> attn_norm, wqkv, wo, ffn_norm, wgu, wdown;
     DecTensor embed, out_norm, lm_head;
-    __half *kcache = nullptr, *vcache = nullptr;   // [layer][nkv][max_ctx][hd]
+    __half *kcache = nullptr, *vcache = nullptr;   // [layer][nkv][max_ctx][hd] (fp16, or blocks)
+    size_t kv_row_bytes = 0;                       // one cache row: hd * 2, or hd/32 blocks
     float *x = nullptr, *delta = nullptr, *qkv = nullptr, *attn = nullptr, *gu = nullptr, *logits = nullptr;
     // P100_DEC_FUSED_NORM: the RMSNorms run inside the next mat-vec (team
     // kernel); the residual alternates between x2 and x, ending in x (2 per
@@ -95,6 +96,12 @@ const char* config_reason(const p100_llama_config& c, int nranks) {
     if (c.n_head % c.n_head_kv) return "n_head must be divisible by n_head_kv";
     if (c.head_dim != 64 && c.head_dim != 128 && c.head_dim != 256) return "head_dim must be 64, 128 or 256";
     if (c.n_head / c.n_head_kv > 8) return "at most 8 query heads per kv head";
+    if (c.kv_type != P100_KV_F16 && c.kv_type != P100_KV_Q8_0 && c.kv_type != P100_KV_Q4_0) return "unknown kv_type";
+    if (c.kv_type != P100_KV_F16) {
+        const int g = c.n_head / c.n_head_kv;
+        if (c.head_dim == 256 || (g != 1 && g != 2 && g != 4 && g != 8))
+            return "a quantised KV cache needs head_dim 64 or 128 and 1, 2, 4 or 8 query heads per kv head";
+    }
     if (c.n_head % nranks || c.n_head_kv % nranks) return "heads must split evenly over the ranks";
     const int blk = elems_of(c.wtype);
     if (c.hidden % blk || c.hidden % 32) return "hidden must be whole weight blocks";
@@ -139,8 +146,11 @@ p100_status dec_alloc(Decoder& d) {
     tensor(d.embed, c.vocab, c.hidden, dec_weight_bytes(t, c.vocab, c.hidden));
     tensor(d.out_norm, c.hidden, 1, size_t(c.hidden) * 4);
     tensor(d.lm_head, d.vocab_n, c.hidden, dec_weight_bytes(t, d.vocab_n, c.hidden));
-    const size_t kv_elems = size_t(L) * d.nkv * c.max_ctx * hd;
-    const size_t at_k = take(kv_elems * 2), at_v = take(kv_elems * 2);
+    d.kv_row_bytes = c.kv_type == P100_KV_Q8_0   ? size_t(hd / 32) * 34
+                     : c.kv_type == P100_KV_Q4_0 ? size_t(hd / 32) * 18
+                                                 : size_t(hd) * 2;
+    const size_t kv_bytes = size_t(L) * d.nkv * c.max_ctx * d.kv_row_bytes;
+    const size_t at_k = take(kv_bytes), at_v = take(kv_bytes);
     const int xq_k = std::max(c.hidden, std::max(d.nq * hd, d.ffn));
     const size_t at_x = take(size_t(c.hidden) * 4), at_delta = take(size_t(c.hidden) * 4);
     const size_t at_x2 = take(size_t(c.hidden) * 4);
@@ -158,6 +168,7 @@ p100_status dec_alloc(Decoder& d) {
     ad.seq_kv = c.max_ctx;
     ad.d_qk = ad.d_v = hd;
     ad.kv_head_stride = static_cast<long long>(c.max_ctx) * hd;
+    ad.kv_type = c.kv_type;
     if (p100_status st = plan_fa(ad, d.sms, d.fa_plan)) return st;
     const size_t at_ws = take(std::max<size_t>(d.fa_plan.ws_total, 256));
     d.arena_bytes = off;
@@ -266,12 +277,22 @@ p100_status dec_fill_kv(Decoder& d, int npos, uint64_t seed, float scale) {
     const long long hs = static_cast<long long>(c.max_ctx) * hd;
     const long long n = static_cast<long long>(d.nkv) * npos * hd;
     for (int l = 0; l < c.n_layer && n > 0; ++l) {
-        const size_t layer_off = size_t(l) * d.nkv * hs;
-        const unsigned grid = unsigned((n + 255) / 256);
-        dec::init_kv_kernel<<<grid, 256>>>(d.kcache + layer_off, d.nkv, npos, hd, hs, dec_key(seed, l, 100),
-                                           d.rank * d.nkv, scale);
-        dec::init_kv_kernel<<<grid, 256>>>(d.vcache + layer_off, d.nkv, npos, hd, hs, dec_key(seed, l, 101),
-                                           d.rank * d.nkv, scale);
+        const size_t layer_bytes = size_t(l) * d.nkv * c.max_ctx * d.kv_row_bytes;
+        uint8_t* kl = reinterpret_cast<uint8_t*>(d.kcache) + layer_bytes;
+        uint8_t* vl = reinterpret_cast<uint8_t*>(d.vcache) + layer_bytes;
+        if (c.kv_type == P100_KV_F16) {
+            const unsigned grid = unsigned((n + 255) / 256);
+            dec::init_kv_kernel<<<grid, 256>>>(reinterpret_cast<__half*>(kl), d.nkv, npos, hd, hs,
+                                               dec_key(seed, l, 100), d.rank * d.nkv, scale);
+            dec::init_kv_kernel<<<grid, 256>>>(reinterpret_cast<__half*>(vl), d.nkv, npos, hd, hs,
+                                               dec_key(seed, l, 101), d.rank * d.nkv, scale);
+        } else {
+            const unsigned grid = unsigned((n / 32 + 7) / 8);   // a warp per block
+            auto kern = c.kv_type == P100_KV_Q8_0 ? dec::init_kv_quant_kernel<P100_KV_Q8_0>
+                                                  : dec::init_kv_quant_kernel<P100_KV_Q4_0>;
+            kern<<<grid, 256>>>(kl, d.nkv, npos, hd, c.max_ctx, dec_key(seed, l, 100), d.rank * d.nkv, scale);
+            kern<<<grid, 256>>>(vl, d.nkv, npos, hd, c.max_ctx, dec_key(seed, l, 101), d.rank * d.nkv, scale);
+        }
         if (p100_status st = launch_status("init_kv_kernel launch")) return st;
     }
     return cuda_status(cudaDeviceSynchronize(), "KV fill");
@@ -334,14 +355,16 @@ p100_status dec_record_step(Decoder& d, cudaStream_t s) {
         return e;
     };
     for (int l = 0; l < c.n_layer && !st; ++l) {
-        const size_t layer_off = size_t(l) * d.nkv * hs;
+        const size_t layer_bytes = size_t(l) * d.nkv * c.max_ctx * d.kv_row_bytes;
+        const __half* kl = reinterpret_cast<const __half*>(reinterpret_cast<const uint8_t*>(d.kcache) + layer_bytes);
+        const __half* vl = reinterpret_cast<const __half*>(reinterpret_cast<const uint8_t*>(d.vcache) + layer_bytes);
         st = norm_qmv(l == 0 ? nullptr : d.delta, d.attn_norm[l], d.wqkv[l], d.wqkv[l].rows, d.qkv);
         if (!st) {
             fa::Params prm = {};
             const FaPlan& plan = d.fa_plan;
             prm.q = d.qkv;
-            prm.k = d.kcache + layer_off;
-            prm.v = d.vcache + layer_off;
+            prm.k = kl;
+            prm.v = vl;
             prm.o = d.attn;
             prm.ws_o = plan.parts > 1 ? reinterpret_cast<float*>(d.fa_ws) : nullptr;
             prm.ws_ml = plan.parts > 1 ? reinterpret_cast<float*>(d.fa_ws + plan.ws_o) : nullptr;
@@ -358,6 +381,10 @@ p100_status dec_record_step(Decoder& d, cudaStream_t s) {
             prm.len_dev = d.pos;
             prm.len_add = 1;   // the row appended at pos is part of the context
             const bool fused = fa_use_mma(plan, prm);
+            if (!fused && c.kv_type != P100_KV_F16) {
+                st = set_error(P100_ERR_UNSUPPORTED, "a quantised KV cache needs the fused attention kernel");
+                break;
+            }
             if (fused) {
                 // RoPE, the KV append and the Q8_1 of the output run inside
                 // the attention kernel (fa::Params, fused decode step)
@@ -368,7 +395,7 @@ p100_status dec_record_step(Decoder& d, cudaStream_t s) {
                 st = launch_glue(dec::rope_kv_append_kernel, dim3(d.nq + 2 * d.nkv), dim3(hd / 2), s,
                                  "rope_kv_append_kernel launch", d.qkv, d.nq, d.nkv, hd,
                                  reinterpret_cast<const float2*>(d.rope), c.max_ctx, static_cast<const int*>(d.pos),
-                                 d.kcache + layer_off, d.vcache + layer_off, hs);
+                                 const_cast<__half*>(kl), const_cast<__half*>(vl), hs);
             }
             if (!st) {
                 switch (hd) {
@@ -772,7 +799,7 @@ p100_status p100_decoder_buffer(p100_decoder* h, int which, void** ptr, size_t* 
     clear_error();
     if (!h) return set_error(P100_ERR_INVALID, "null decoder");
     p100b::Decoder& d = h->d;
-    const size_t kv = size_t(d.cfg.n_layer) * d.nkv * d.cfg.max_ctx * d.cfg.head_dim * 2;
+    const size_t kv = size_t(d.cfg.n_layer) * d.nkv * d.cfg.max_ctx * d.kv_row_bytes;
     void* p = nullptr;
     size_t n = 0;
     switch (which) {

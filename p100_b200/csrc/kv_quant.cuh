@@ -115,7 +115,7 @@ __global__ void __launch_bounds__(256) kv_to_f16_kernel(const ConvParams p) {
 
 // ------------------------------------------------------------ quantisation
 // One 32-value block per warp, lane j holding value j; writes the block at
-// blk (2-byte aligned).  ggml's block quantisers as llama.cpp runs them for a
+// blk (2-byte aligned, as every block of a row of blocks is).  ggml's block quantisers as llama.cpp runs them for a
 // quantised cache (cpy-utils.cuh quantize_f32_q8_0_block /
 // quantize_f32_q4_0_block):
 //   q8_0: d = max|x| / 127, q = roundf(x * (d ? 1/d : 0));
@@ -149,11 +149,7 @@ __device__ __forceinline__ void quantize_block_warp(float x, int lane, uint8_t* 
         const int hi = __shfl_down_sync(0xffffffffu, q, 16);
         if (lane < 16) blk[2 + lane] = static_cast<uint8_t>(q | (hi << 4));
     }
-    if (lane == 0) {
-        const unsigned short h = __half_as_ushort(__float2half_rn(d));
-        blk[0] = static_cast<uint8_t>(h & 255);
-        blk[1] = static_cast<uint8_t>(h >> 8);
-    }
+    if (lane == 0) store_half_bits(blk, d);
 }
 
 }  // namespace kvq

@@ -1,4 +1,5 @@
-// qmv.cuh — quantised mat-vec y = W x for Q4_0 / Q8_0 / Q4_K weights against
+// qmv.cuh — quantised mat-vec y = W x for Q4_0 / Q8_0 / Q4_K (and, on the
+// generic kernel only, Q5_K / Q6_K) weights against
 // Q8_1 activations, batch 1..16, on CUDA cores (int8 dp4a).
 //
 // Bulk path (16-byte aligned rows, k % 256 == 0), warp-specialised:
@@ -341,21 +342,41 @@ __device__ __forceinline__ float slab_dot(const uint8_t* __restrict__ row, int j
 #pragma unroll
         for (int i = 0; i < 32; ++i) dot += static_cast<int8_t>(blk[2 + i]) * q[i];
         return (d * dx) * float(dot);
-    } else {
-        const uint8_t* blk = row + size_t(j / 8) * 144;
+    } else if (TYPE == P100_Q4_K || TYPE == P100_Q5_K) {
+        constexpr int BB = TYPE == P100_Q4_K ? 144 : 176;
+        const uint8_t* blk = row + size_t(j / 8) * BB;
         const int sub = j % 8;
         const float d = load_half_bytes(blk), dmin = load_half_bytes(blk + 2);
         int sc, mn;
         q4k_scale_min(blk + 4, sub, sc, mn);
-        const uint8_t* qs = blk + 16 + (sub / 2) * 32;
+        const uint8_t* qs = blk + (TYPE == P100_Q4_K ? 16 : 48) + (sub / 2) * 32;
+        const uint8_t* qh = blk + 16;   // Q5_K: bit `sub` of qh[i] is the code's 16
         const int shift = (sub % 2) * 4;
         int dot = 0, sumq = 0;
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-            dot += ((qs[i] >> shift) & 15) * q[i];
+            int w = (qs[i] >> shift) & 15;
+            if (TYPE == P100_Q5_K) w |= ((qh[i] >> sub) & 1) << 4;
+            dot += w * q[i];
             sumq += q[i];
         }
         return fmaf(d, dx * float(dot * sc), -dmin * (dx * float(sumq * mn)));
+    } else {
+        // Q6_K: (d * dx) * (sc0 * dot(values 0..15) + sc1 * dot(values 16..31))
+        const uint8_t* blk = row + size_t(j / 8) * 210;
+        const int sub = j % 8, h = sub / 4, c = sub % 4;
+        const float d = load_half_bytes(blk + 208);
+        const uint8_t* ql = blk + 64 * h + 32 * (c & 1);
+        const uint8_t* qh = blk + 128 + 32 * h;
+        const int8_t* sc = reinterpret_cast<const int8_t*>(blk + 192 + 8 * h + 2 * c);
+        const int nshift = (c >> 1) * 4, hshift = 2 * c;
+        int lo = 0, hi = 0;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            lo += ((((ql[i] >> nshift) & 15) | (((qh[i] >> hshift) & 3) << 4)) - 32) * q[i];
+            hi += ((((ql[i + 16] >> nshift) & 15) | (((qh[i + 16] >> hshift) & 3) << 4)) - 32) * q[i + 16];
+        }
+        return (d * dx) * float(sc[0] * lo + sc[1] * hi);
     }
 }
 

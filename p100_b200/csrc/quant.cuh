@@ -56,16 +56,12 @@ __device__ __forceinline__ float load_half_bytes(const uint8_t* p) {
     return __half2float(__ushort_as_half(static_cast<unsigned short>(p[0] | (p[1] << 8))));
 }
 
-// One thread per 32-value slab (a Q4_0/Q8_0 block, or one Q4_K sub-block).
-// Values: Q4_0 d*(nib-8), Q8_0 d*q, Q4_K fma(d*sc, q, -(dmin*mn)).  Each is the
-// exact value rounded once to FP32, as float(double(...)) is in the model: the
-// products are exact in FP32 and the double difference is exact for any fp16
-// d/dmin, so a single fused rounding gives the same bits.
-// The 32 values of slab j (a Q4_0/Q8_0 block, or one Q4_K sub-block) of a
-// weight row: Q4_0 d*(nib-8), Q8_0 d*q, Q4_K fma(d*sc, q, -(dmin*mn)).  Each
-// is the exact value rounded once to FP32, as float(double(...)) is in the
-// model: the products are exact in FP32 and the double difference is exact
-// for any fp16 d/dmin, so a single fused rounding gives the same bits.
+// The 32 values of slab j (a Q4_0/Q8_0 block, or one 32-value sub-block of
+// a Q4_K/Q5_K/Q6_K super-block) of a weight row: Q4_0 d*(nib-8), Q8_0 d*q,
+// Q4_K/Q5_K fma(d*sc, q, -(dmin*mn)), Q6_K (d*sc)*q.  Each is the exact value
+// rounded once to FP32, as float(double(...)) is in the model: the products
+// are exact in FP32 and the double difference is exact for any fp16 d/dmin,
+// so a single fused rounding gives the same bits.
 template <int TYPE>
 __device__ __forceinline__ void dequant_slab(const uint8_t* __restrict__ row, int j, float (&vals)[32]) {
     if (TYPE == P100_Q4_0) {
@@ -82,7 +78,7 @@ __device__ __forceinline__ void dequant_slab(const uint8_t* __restrict__ row, in
         const float d = load_half_bytes(blk);
 #pragma unroll
         for (int i = 0; i < 32; ++i) vals[i] = d * float(static_cast<int8_t>(blk[2 + i]));
-    } else {
+    } else if (TYPE == P100_Q4_K) {
         const uint8_t* blk = row + size_t(j / 8) * 144;
         const int sub = j % 8;
         const float d = load_half_bytes(blk), dmin = load_half_bytes(blk + 2);
@@ -93,6 +89,38 @@ __device__ __forceinline__ void dequant_slab(const uint8_t* __restrict__ row, in
         const int shift = (sub % 2) * 4;
 #pragma unroll
         for (int i = 0; i < 32; ++i) vals[i] = fmaf(ds, float((qs[i] >> shift) & 15), -ms);
+    } else if (TYPE == P100_Q5_K) {
+        // Q4_K's nibble plus 16 * bit `sub` of qh[i]; d*sc*q (<= 22 bits) and
+        // dmin*mn are exact in FP32, so one fused rounding again
+        const uint8_t* blk = row + size_t(j / 8) * 176;
+        const int sub = j % 8;
+        const float d = load_half_bytes(blk), dmin = load_half_bytes(blk + 2);
+        int sc, mn;
+        q4k_scale_min(blk + 4, sub, sc, mn);
+        const float ds = d * float(sc), ms = dmin * float(mn);
+        const uint8_t* qh = blk + 16;
+        const uint8_t* qs = blk + 48 + (sub / 2) * 32;
+        const int shift = (sub % 2) * 4;
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+            vals[i] = fmaf(ds, float(((qs[i] >> shift) & 15) | (((qh[i] >> sub) & 1) << 4)), -ms);
+    } else {
+        // Q6_K slab 4h + c: ql[64h + 32(c&1) + i] nibble (c >= 2: high), bits
+        // 4-5 from qh[32h + i] >> 2c, minus 32, times d * scales[8h + 2c + i/16];
+        // d * sc (18 bits) times q (6 bits) is exact in FP32
+        const uint8_t* blk = row + size_t(j / 8) * 210;
+        const int sub = j % 8, h = sub / 4, c = sub % 4;
+        const float d = load_half_bytes(blk + 208);
+        const uint8_t* ql = blk + 64 * h + 32 * (c & 1);
+        const uint8_t* qh = blk + 128 + 32 * h;
+        const int8_t* sc = reinterpret_cast<const int8_t*>(blk + 192 + 8 * h + 2 * c);
+        const float ds0 = d * float(sc[0]), ds1 = d * float(sc[1]);
+        const int nshift = (c >> 1) * 4, hshift = 2 * c;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            const int q = (((ql[i] >> nshift) & 15) | (((qh[i] >> hshift) & 3) << 4)) - 32;
+            vals[i] = (i < 16 ? ds0 : ds1) * float(q);
+        }
     }
 }
 

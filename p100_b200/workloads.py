@@ -10,15 +10,18 @@ in for model weights, activations and a prefilled KV cache.
 * Q8_0: d as above, codes uniform in -127..127.
 * Q4_K: d, dmin = fp16(|N(0,1)| * 0.02), 12 packed scale bytes uniform in
   0..255 (so every 6-bit scale/min is uniform), 128 nibble bytes uniform.
+* Q5_K: as Q4_K, plus the 32 high-bit bytes uniform.
+* Q6_K: the 128 low-nibble, 64 high-bit and 16 int8 scale bytes uniform,
+  d = fp16(|N(0,1)| * 0.02).
 * activations ~ N(0,1) fp32; K/V cache fp16 N(0,1) * 0.5; q ~ N(0,1).
 """
 from __future__ import annotations
 
 import numpy as np
 
-Q4_0, Q8_0, Q4_K = 0, 1, 2
-BLOCK_ELEMS = {Q4_0: 32, Q8_0: 32, Q4_K: 256}
-BLOCK_BYTES = {Q4_0: 18, Q8_0: 34, Q4_K: 144}
+Q4_0, Q8_0, Q4_K, Q5_K, Q6_K = 0, 1, 2, 3, 4
+BLOCK_ELEMS = {Q4_0: 32, Q8_0: 32, Q4_K: 256, Q5_K: 256, Q6_K: 256}
+BLOCK_BYTES = {Q4_0: 18, Q8_0: 34, Q4_K: 144, Q5_K: 176, Q6_K: 210}
 
 # Llama-3-8B layer shapes of the mat-vec sweep, (name, k, rows).
 LLAMA3_8B_SHAPES = [("q/o", 4096, 4096), ("k/v", 4096, 1024), ("gate/up", 4096, 14336), ("down", 14336, 4096)]
@@ -44,11 +47,16 @@ def weights(qtype, rows, k, seed):
         out = np.empty((rows, nb, 34), np.uint8)
         out[..., :2] = _scales(rng, (rows, nb)).view(np.uint8).reshape(rows, nb, 2)
         out[..., 2:] = rng.integers(-127, 128, (rows, nb, 32), dtype=np.int8).view(np.uint8)
-    else:
-        out = np.empty((rows, nb, 144), np.uint8)
+    elif qtype in (Q4_K, Q5_K):
+        bb = BLOCK_BYTES[qtype]
+        out = np.empty((rows, nb, bb), np.uint8)
         out[..., 0:2] = _scales(rng, (rows, nb)).view(np.uint8).reshape(rows, nb, 2)
         out[..., 2:4] = _scales(rng, (rows, nb)).view(np.uint8).reshape(rows, nb, 2)
-        out[..., 4:] = rng.integers(0, 256, (rows, nb, 140), dtype=np.uint8)
+        out[..., 4:] = rng.integers(0, 256, (rows, nb, bb - 4), dtype=np.uint8)
+    else:   # Q6_K: ql, qh, int8 scales uniform; d last
+        out = np.empty((rows, nb, 210), np.uint8)
+        out[..., :208] = rng.integers(0, 256, (rows, nb, 208), dtype=np.uint8)
+        out[..., 208:] = _scales(rng, (rows, nb)).view(np.uint8).reshape(rows, nb, 2)
     return out.reshape(-1)
 
 

@@ -214,6 +214,73 @@ def test_decoder_matches_restated_steps(cuda, orc, wtype, shape):
         dec.close()
 
 
+def dequantised_rows(orc, kv_type, raw, hd):
+    """A quantised cache (uint8, rows of hd/32 blocks) as float32 rows."""
+    rb = hd // 32 * P.KV_BLOCK_BYTES[kv_type]
+    rows = raw.size // rb
+    return orc.kv_to_f16(kv_type, raw, hd, rows).astype(np.float32).reshape(rows, hd)
+
+
+@pytest.mark.parametrize("kv_type", [P.KV_Q8_0, P.KV_Q4_0], ids=["kv-q8_0", "kv-q4_0"])
+@pytest.mark.parametrize("shape", [TINY, dict(TINY, head_dim=128, hidden=512, n_head=8, n_head_kv=2)],
+                         ids=["d64", "d128"])
+def test_decoder_quantised_cache_matches_restated_steps(cuda, orc, kv_type, shape):
+    """A q8_0 / q4_0 cache: the fused attention kernel quantises the new rows
+    (ggml's block rule) and reads the blocks; the restated step quantises the
+    same rotated rows and attends over the rows converted to fp16."""
+    cfg = P.LlamaConfig(**shape, wtype=P.Q4_0, kv_type=kv_type)
+    ocfg = oracle.LlamaConfig(*[getattr(cfg, f) for f, _ in oracle.LlamaConfig._fields_])
+    hd = cfg.head_dim
+    dec = P.Decoder(cfg)
+    try:
+        dec.init_random(99 + kv_type)
+        npos = 150
+        dec.fill_kv(npos, 5, 0.5)
+        dec.set_state(npos, 3)
+        w = read_model(dec, cfg)
+        cs = dec.read(*dec.buffer(P.B_ROPE)).view(np.float32)
+        tok = 3
+        for step in range(4):
+            pos = npos + step
+            kc = dec.read(*dec.buffer(P.B_KCACHE)).copy()
+            vc = dec.read(*dec.buffer(P.B_VCACHE)).copy()
+            assert kc.size == cfg.n_layer * cfg.n_head_kv * cfg.max_ctx * hd // 32 * P.KV_BLOCK_BYTES[kv_type]
+            # the restated append on a copy: the new rows within one code step
+            # of the device's (the two sides' k and v differ in the last bits)
+            okc, ovc = kc.copy(), vc.copy()
+            orc.decode_step(ocfg, w, okc, ovc, cs, pos, tok, kv_type=kv_type)
+            dec.step(1)
+            assert dec.state()[0] == pos + 1
+            gkc = dec.read(*dec.buffer(P.B_KCACHE)).copy()
+            gvc = dec.read(*dec.buffer(P.B_VCACHE)).copy()
+            for g, o in ((gkc, okc), (gvc, ovc)):
+                gr, orow = dequantised_rows(orc, kv_type, g, hd), dequantised_rows(orc, kv_type, o, hd)
+                assert np.max(np.abs(gr - orow)) <= 0.02 * max(1.0, np.max(np.abs(orow))), step
+            # the step itself, teacher-forced on the device's new rows
+            otok, ologits, ohidden = orc.decode_step(ocfg, w, gkc.copy(), gvc.copy(), cs, pos, tok,
+                                                     kv_type=kv_type, append=False)
+            glogits = dec.read(*dec.buffer(P.B_LOGITS)).view(np.float32)
+            ghidden = dec.read(*dec.buffer(P.B_HIDDEN)).view(np.float32)
+            err = np.max(np.abs(glogits - ologits))
+            herr = np.max(np.abs(ghidden - ohidden)) / np.max(np.abs(ohidden))
+            assert herr <= DECODE_HIDDEN_TOL, (step, herr)
+            assert err <= DECODE_LOGIT_TOL * np.max(np.abs(ologits)), (step, err)
+            gtok = dec.state()[1]
+            assert gtok == int(np.argmax(glogits))
+            tok = gtok
+        assert P.device_error() == P.OK
+    finally:
+        dec.close()
+
+
+def test_decoder_rejects_unfusable_quantised_cache(cuda):
+    for shape in (TINY_D256, dict(TINY, n_head=6, n_head_kv=2)):
+        with pytest.raises(P.InvalidArgument):
+            P.Decoder(P.LlamaConfig(**shape, kv_type=P.KV_Q8_0))
+    with pytest.raises(P.InvalidArgument):
+        P.Decoder(P.LlamaConfig(**TINY, kv_type=7))
+
+
 # Hidden 4096 (the 8B head geometry) with P100_DEC_FUSED_NORM: the RMSNorms
 # run inside the following mat-vecs.  The restatement comparison above stays
 # on the tiny model: with 4096-wide normalised activations of O(1) feeding a

@@ -1,0 +1,55 @@
+"""ggml's Q5_K and Q6_K weights on B200 (p100_dequantize, p100_qmv on the
+general mat-vec kernel) against the CPU restatement (oracle/p100_oracle.cpp,
+itself checked against ggml's dequantisation loops in
+tests/test_oracle_ktypes.py).  Dequantisation is bit-exact; the mat-vec is
+within the reference's normalised q81 tolerance of the oracle's q81 dot (and
+of the exact FP64 dot)."""
+import numpy as np
+import pytest
+
+from conftest import QMV_NORM_TOL
+from test_qmv_gpu import assert_qmv_close, dev, q81_reference, row_norms
+
+import p100_b200 as P
+from p100_b200 import workloads as W
+
+pytestmark = pytest.mark.gpu
+KTYPES = [P.Q5_K, P.Q6_K]
+
+
+@pytest.mark.parametrize("qtype", KTYPES)
+@pytest.mark.parametrize("rows,k", [(7, 256), (300, 4096), (64, 14336)])
+def test_dequantize_bit_exact(cuda, orc, qtype, rows, k):
+    w = W.weights(qtype, rows, k, seed=rows + k + qtype)
+    got = P.dequantize(qtype, dev(cuda, w), rows, k).cpu().numpy()
+    want = orc.dequantize(qtype, w, rows, k)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+@pytest.mark.parametrize("qtype", KTYPES)
+@pytest.mark.parametrize("rows,k,batch", [(1024, 4096, 1), (333, 4096, 3), (256, 14336, 16), (40, 256, 2)])
+def test_qmv_within_tolerance(cuda, orc, qtype, rows, k, batch):
+    w = W.weights(qtype, rows, k, seed=11 * qtype + k)
+    x = W.activations(batch, k, seed=k + batch)
+    xq = P.q8_1_quantize(dev(cuda, x))
+    y = P.qmv(qtype, dev(cuda, w), rows, k, xq, batch).cpu().numpy()
+    wn = row_norms(orc, qtype, w, rows, k)
+    err = assert_qmv_close(y, q81_reference(orc, qtype, w, rows, k, x).astype(np.float64), wn, x)
+    assert err <= 1e-5, err   # the same slab arithmetic, summed in another order
+    exact = x.astype(np.float64) @ orc.dequantize(qtype, w, rows, k).astype(np.float64).T
+    assert_qmv_close(y, exact, wn, x, tol=QMV_NORM_TOL)
+    assert P.device_error() == P.OK
+
+
+@pytest.mark.parametrize("qtype", KTYPES)
+def test_h16_and_whole_blocks(cuda, qtype):
+    w = cuda.zeros(1 << 16, dtype=cuda.uint8, device="cuda")
+    h = cuda.zeros(4096, dtype=cuda.float16, device="cuda")
+    ss = cuda.zeros(512, device="cuda")
+    y = cuda.zeros(64, device="cuda")
+    with pytest.raises(P.P100Error) as e:
+        P.qmv_h16(qtype, w, 8, 256, h, ss, 1, 16, y=y)
+    assert e.value.status == P.ERR_UNSUPPORTED
+    xq = cuda.zeros(4096, dtype=cuda.uint8, device="cuda")
+    with pytest.raises(P.InvalidArgument):
+        P.qmv(qtype, w, 8, 128, xq, 1, y=y)     # a super-block is 256 values
