@@ -356,6 +356,7 @@ __global__ void __launch_bounds__(kThreads, KV == P100_KV_F16 ? 1 : kQuantCtasPe
 
     // ---- queries: q * scale per head, scaled by a power of two 2^e so the
     // largest |entry| lies in [2^13, 2^14)
+    float2 qv2[QPT];   // this thread's pairs, rotated and scaled
 #pragma unroll
     for (int j = 0; j < QPT; ++j) {
         const int i = tid + j * kThreads;
@@ -364,12 +365,13 @@ __global__ void __launch_bounds__(kThreads, KV == P100_KV_F16 ? 1 : kQuantCtasPe
         if (p.rope_cs) {   // rotate the raw q pair (rope_kv_append_kernel's arithmetic)
             const int pr = pos >= 0 ? pos : 0;
             const float2 t = p.rope_cs[size_t(pr) * (D / 2) + i % (D / 2)];
-            s_q[2 * i] = __fsub_rn(__fmul_rn(x0, t.x), __fmul_rn(x1, t.y)) * p.scale;
-            s_q[2 * i + 1] = __fadd_rn(__fmul_rn(x0, t.y), __fmul_rn(x1, t.x)) * p.scale;
+            qv2[j] = make_float2(__fsub_rn(__fmul_rn(x0, t.x), __fmul_rn(x1, t.y)) * p.scale,
+                                 __fadd_rn(__fmul_rn(x0, t.y), __fmul_rn(x1, t.x)) * p.scale);
         } else {
-            s_q[2 * i] = x0 * p.scale;
-            s_q[2 * i + 1] = x1 * p.scale;
+            qv2[j] = make_float2(x0 * p.scale, x1 * p.scale);
         }
+        s_q[2 * i] = qv2[j].x;
+        s_q[2 * i + 1] = qv2[j].y;
     }
     __syncthreads();
     for (int h = warp; h < G; h += kWarps) {
@@ -377,27 +379,47 @@ __global__ void __launch_bounds__(kThreads, KV == P100_KV_F16 ? 1 : kQuantCtasPe
         for (int d = lane; d < D; d += 32) m = fmaxf(m, fabsf(s_q[h * D + d]));
         m = warp_max(m);
         if (lane == 0) {
-            int e = 0;   // clamped so 2^e and 2^-e stay normal floats
-            if (m > 0.f && m < INFINITY) e = max(-120, min(120, 13 - ilogbf(m)));
-            s_qs[h] = ldexpf(1.0f, e);
+            // e = 13 - ilogb(m), clamped so 2^e and 2^-e stay normal floats;
+            // from the exponent bits (a subnormal m clamps to 120 either way)
+            int e = 0;
+            if (m > 0.f && m < INFINITY) e = max(-120, min(120, 13 - (((__float_as_int(m) >> 23) & 255) - 127)));
+            s_qs[h] = __int_as_float((e + 127) << 23);
         }
+    }
+    __syncthreads();
+    // Each thread splits its own pairs x = q * 2^e into hi = fp16(x) and
+    // lo = fp16(x - hi), over s_q (whose values were all read above): the A
+    // fragments then load as fp16 pairs.
+    __half2* s_hi = reinterpret_cast<__half2*>(s_q);   // [G * D / 2]
+    __half2* s_lo = s_hi + G * D / 2;                   // [G * D / 2]
+#pragma unroll
+    for (int j = 0; j < QPT; ++j) {
+        const int i = tid + j * kThreads;
+        if (i >= G * D / 2) break;
+        const float sc = s_qs[2 * i / D];
+        const float x0 = qv2[j].x * sc, x1 = qv2[j].y * sc;
+        const __half h0 = __float2half_rn(x0), h1 = __float2half_rn(x1);
+        s_hi[i] = __halves2half2(h0, h1);
+        s_lo[i] = __halves2half2(__float2half_rn(x0 - __half2float(h0)), __float2half_rn(x1 - __half2float(h1)));
     }
     __syncthreads();
     // A fragments: row r < G -> hi of head r, G <= r < 2G -> lo of head r - G
     uint32_t qa[KSQ][4];
     {
-        auto qv = [&](int r, int d) -> float {
-            if (r < G) return __half2float(__float2half_rn(s_q[r * D + d] * s_qs[r]));
-            if (r < 2 * G) return half_rest(s_q[(r - G) * D + d] * s_qs[r - G]);
-            return 0.f;
+        const uint32_t* hi32 = reinterpret_cast<const uint32_t*>(s_hi);
+        const uint32_t* lo32 = reinterpret_cast<const uint32_t*>(s_lo);
+        auto frag = [&](int r, int d) -> uint32_t {   // elements (r, d), (r, d + 1), d even
+            if (r < G) return hi32[(r * D + d) / 2];
+            if (r < 2 * G) return lo32[((r - G) * D + d) / 2];
+            return 0u;
         };
 #pragma unroll
         for (int ks = 0; ks < KSQ; ++ks) {
             const int d0 = ks * 16 + 2 * t;
-            qa[ks][0] = pack_half2(qv(g, d0), qv(g, d0 + 1));
-            qa[ks][1] = pack_half2(qv(g + 8, d0), qv(g + 8, d0 + 1));
-            qa[ks][2] = pack_half2(qv(g, d0 + 8), qv(g, d0 + 9));
-            qa[ks][3] = pack_half2(qv(g + 8, d0 + 8), qv(g + 8, d0 + 9));
+            qa[ks][0] = frag(g, d0);
+            qa[ks][1] = frag(g + 8, d0);
+            qa[ks][2] = frag(g, d0 + 8);
+            qa[ks][3] = frag(g + 8, d0 + 8);
         }
     }
     // this lane's head (rows g and, for G = 8, g + 8 belong to head g mod G)
@@ -643,22 +665,21 @@ __global__ void __launch_bounds__(kThreads, KV == P100_KV_F16 ? 1 : kQuantCtasPe
         float* s_gm = s_w + np * G;       // [G]
         float* s_den = s_gm + G;          // [G]
         float* s_out = s_den + G;         // [per] this CTA's merged outputs
-        if (tid < G) {
-            float gmax = -INFINITY;
-            for (int q = 0; q < np; ++q) gmax = fmaxf(gmax, rx_m[q * G + tid]);
-            float den = 0.f;
-            for (int q = 0; q < np; ++q) {
-                const float l = rx_l[q * G + tid];
-                den += l == 0.f ? 0.f : expf(rx_m[q * G + tid] - gmax) * l;
+        // one warp per head, one lane per part (np <= 16): the global max,
+        // the parts' weights exp(m_q - M) and den = sum of weight * l_q
+        for (int h = warp; h < G; h += kWarps) {
+            const bool has = lane < np;
+            const float mq = has ? rx_m[lane * G + h] : -INFINITY;
+            const float lq = has ? rx_l[lane * G + h] : 0.f;
+            const float gmax = warp_max(mq);
+            const float wq = lq == 0.f ? 0.f : expf(mq - gmax);
+            const float den = warp_sum(wq * lq);
+            if (has) s_w[lane * G + h] = wq;
+            if (lane == 0) {
+                s_gm[h] = gmax;
+                s_den[h] = den;
+                if (part == 0 && p.lse) p.lse[row0 + h] = den == 0.f ? -INFINITY : gmax + logf(den);
             }
-            s_gm[tid] = gmax;
-            s_den[tid] = den;
-            if (part == 0 && p.lse) p.lse[row0 + tid] = den == 0.f ? -INFINITY : gmax + logf(den);
-        }
-        __syncthreads();
-        for (int i = tid; i < np * G; i += kThreads) {
-            const int h = i % G;
-            s_w[i] = rx_l[i] == 0.f ? 0.f : expf(rx_m[i] - s_gm[h]);
         }
         __syncthreads();
         for (int i = tid; i < per; i += kThreads) {
