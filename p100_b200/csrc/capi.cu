@@ -558,6 +558,8 @@ const char* attn_reason(const p100_attn_desc& d) {
     return nullptr;
 }
 
+constexpr int kFaWideSeq = 8192;
+
 struct FaPlan {
     int D = 0, G = 0, gmax = 0, parts = 1, nstage = 0;
     long long head_stride = 0, batch_stride = 0;
@@ -603,9 +605,10 @@ p100_status plan_fa(const p100_attn_desc& d, int sms, FaPlan& plan) {
     // at most 512 parts: the last-CTA merge keeps every part's (m, l) and
     // weight in shared memory (2 * parts * G floats, inside the idle ring)
     plan.parts = std::min(std::min(parts, max_parts), 512);
-    // fa_mma_kernel fits two CTAs per SM: with automatic splitting and the
-    // workspace merge it runs twice the parts (the workspace covers both).
-    // (three CTAs per SM over a quantised cache: its rings hold raw blocks)
+    // The 4-warp fa_mma_kernel fits two CTAs per SM (three over a quantised
+    // cache: its rings hold raw blocks): with automatic splitting and the
+    // workspace merge it runs that many times the parts (the workspace covers
+    // both); the 8-warp shape runs plan.parts, one CTA per SM.
     const int per_sm = d.kv_type == P100_KV_Q8_0 || d.kv_type == P100_KV_Q4_0 ? fam::kQuantCtasPerSm : 2;
     plan.parts_wide =
         plan.auto_parts ? std::min(std::min(per_sm * std::max(1, sms / heads), max_parts), 512) : plan.parts;
@@ -653,10 +656,10 @@ p100_status launch_fa_t(const FaPlan& plan, const fa::Params& prm, int heads, cu
     return cuda_status(cudaLaunchKernelEx(&cfg, kern, prm), "fa_decode_kernel launch");
 }
 
-template <int D, int G, int KV>
+template <int D, int G, int KV, int NW>
 p100_status launch_fa_mma_t(const FaPlan& plan, const fa::Params& prm, int heads, cudaStream_t stream, bool pdl) {
-    auto kern = fam::fa_mma_kernel<D, G, KV>;
-    constexpr size_t smem = fam::smem_bytes<D, G, KV>();
+    auto kern = fam::fa_mma_kernel<D, G, KV, NW>;
+    constexpr size_t smem = fam::smem_bytes<D, G, KV, NW>();
     static thread_local int configured[64] = {};
     static thread_local int cluster_fits[64][5] = {};   // per log2(parts): clusters that fit, 0 unknown, -1 none
     int dev = 0;
@@ -674,7 +677,7 @@ p100_status launch_fa_mma_t(const FaPlan& plan, const fa::Params& prm, int heads
     // merge and run twice the parts instead (two CTAs per SM).
     fa::Params run = prm;
     int np = 0;
-    if (plan.auto_parts && plan.parts >= 2 && plan.seq <= 16384) {
+    if (NW == 4 && plan.auto_parts && plan.parts >= 2 && plan.seq <= kFaWideSeq) {
         np = 1;
         while (np * 2 <= std::min(16, plan.parts) && np * 2 <= G * D / 32) np *= 2;
         if (np < 2 || 2 * np < plan.parts) np = 0;
@@ -684,7 +687,7 @@ p100_status launch_fa_mma_t(const FaPlan& plan, const fa::Params& prm, int heads
     if (np && cluster_fits[dev][lg] == 0) {
         cudaLaunchConfig_t q = {};
         q.gridDim = dim3(np, 1);
-        q.blockDim = dim3(fam::kThreads);
+        q.blockDim = dim3(NW * 32);
         q.dynamicSmemBytes = smem;
         cudaLaunchAttribute ca[1];
         ca[0].id = cudaLaunchAttributeClusterDimension;
@@ -706,12 +709,12 @@ p100_status launch_fa_mma_t(const FaPlan& plan, const fa::Params& prm, int heads
     if (np) {
         run.parts = np;
         run.cluster_merge = 1;
-    } else if (run.parts > 1) {
-        run.parts = plan.parts_wide;
+    } else if (run.parts > 1 && NW == 4) {
+        run.parts = plan.parts_wide;   // the 8-warp shape keeps plan.parts: one CTA per SM
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(run.parts, heads);
-    cfg.blockDim = dim3(fam::kThreads);
+    cfg.blockDim = dim3(NW * 32);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[2];
@@ -733,14 +736,21 @@ p100_status launch_fa_mma_t(const FaPlan& plan, const fa::Params& prm, int heads
     return cuda_status(cudaLaunchKernelEx(&cfg, kern, run), "fa_mma_kernel launch");
 }
 
+template <int D, int KV, int NW>
+p100_status launch_fa_mma_nw(const FaPlan& plan, const fa::Params& prm, int heads, cudaStream_t s, bool pdl) {
+    switch (plan.G) {
+        case 1: return launch_fa_mma_t<D, 1, KV, NW>(plan, prm, heads, s, pdl);
+        case 2: return launch_fa_mma_t<D, 2, KV, NW>(plan, prm, heads, s, pdl);
+        case 4: return launch_fa_mma_t<D, 4, KV, NW>(plan, prm, heads, s, pdl);
+        default: return launch_fa_mma_t<D, 8, KV, NW>(plan, prm, heads, s, pdl);
+    }
+}
+// The 8-warp shape for automatic splits of more than kFaWideSeq keys (their
+// measured crossover lies between 4K and 16K keys), the 4-warp shape else.
 template <int D, int KV>
 p100_status launch_fa_mma_kv(const FaPlan& plan, const fa::Params& prm, int heads, cudaStream_t s, bool pdl) {
-    switch (plan.G) {
-        case 1: return launch_fa_mma_t<D, 1, KV>(plan, prm, heads, s, pdl);
-        case 2: return launch_fa_mma_t<D, 2, KV>(plan, prm, heads, s, pdl);
-        case 4: return launch_fa_mma_t<D, 4, KV>(plan, prm, heads, s, pdl);
-        default: return launch_fa_mma_t<D, 8, KV>(plan, prm, heads, s, pdl);
-    }
+    if (plan.auto_parts && plan.seq > kFaWideSeq) return launch_fa_mma_nw<D, KV, 8>(plan, prm, heads, s, pdl);
+    return launch_fa_mma_nw<D, KV, 4>(plan, prm, heads, s, pdl);
 }
 template <int D>
 p100_status launch_fa_mma_d(const FaPlan& plan, const fa::Params& prm, int heads, cudaStream_t s, bool pdl) {

@@ -42,9 +42,14 @@
 namespace p100b {
 namespace fam {
 
-constexpr int kWarps = 4;
-constexpr int kThreads = kWarps * 32;
-constexpr int kTile = 64;   // keys per tile: 16 per warp
+// Two shapes, chosen per call by the host: 4 warps over 64-key tiles (two
+// or three CTAs per SM, the cluster merge up to 8K keys), or 8 warps over
+// 128-key tiles (one CTA per SM with deeper rings, longer contexts: twice the
+// warps per CTA hide the per-tile chain better than a second CTA does, and a
+// split of one part per SM keeps the workspace merge short).  Each warp owns
+// 16 keys of every tile.
+template <int NW>
+__host__ __device__ constexpr int tile_keys() { return 16 * NW; }
 
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
     return uint32_t(__half_as_ushort(__float2half_rn(lo))) | (uint32_t(__half_as_ushort(__float2half_rn(hi))) << 16);
@@ -115,9 +120,9 @@ __device__ __forceinline__ void st_cluster(float* local, int rank, float v) {
     asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(remote), "f"(v) : "memory");
 }
 
-// Three 64-key stages (107 KB of shared memory at D = 128): two CTAs fit an SM,
-// so a cluster of 16 parts per kv head fits a GPC (7 such clusters fit the
-// GPU at four stages, 14 at three).
+// Three stages: 64-key ones (107 KB of shared memory at D = 128) let two CTAs
+// fit an SM, so a cluster of 16 parts per kv head fits a GPC (7 such clusters
+// fit the GPU at four stages, 14 at three); 128-key ones take 218 KB.
 template <int D>
 __host__ __device__ constexpr int stages() { return D >= 256 ? 2 : 3; }
 // Cluster-merge receive area: [16 parts][G][D] slices of O (G*D floats in
@@ -128,58 +133,65 @@ template <int D, int G>
 __host__ __device__ constexpr size_t rx_floats() { return size_t(G) * D + 2 * kMaxClusterParts * G; }
 // Quantised caches: bytes per key row, per raw K (or V) slot (the tile plus
 // up to 15 bytes of lead before it, rounded up with room to spare), and as
-// many stages (3 to 8) as leave three CTAs per SM at G = 8 (76,800 bytes per
-// CTA).
+// many stages (3 to 8) as leave three 4-warp CTAs per SM at G = 8 (76,800
+// bytes per CTA), or fill one SM for the 8-warp shape (232,448 bytes).
 template <int D, int KV>
 __host__ __device__ constexpr int raw_row_bytes() { return D / 32 * kvq::block_bytes<KV>(); }
-template <int D, int KV>
-__host__ __device__ constexpr int raw_slot_bytes() { return (kTile * raw_row_bytes<D, KV>() + 48 + 15) & ~15; }
-constexpr int kQuantCtasPerSm = 3;
-template <int D>
+template <int D, int KV, int NW>
+__host__ __device__ constexpr int raw_slot_bytes() { return (tile_keys<NW>() * raw_row_bytes<D, KV>() + 48 + 15) & ~15; }
+constexpr int kQuantCtasPerSm = 3;   // 4-warp shape over a quantised cache
+template <int NW>
+__host__ __device__ constexpr int ctas_per_sm(int kv) { return NW == 8 ? 1 : kv == P100_KV_F16 ? 2 : kQuantCtasPerSm; }
+template <int D, int NW>
 __host__ __device__ constexpr int quant_ring_budget() {
-    return 76800 - (8 * D * 4 + 256 + int(rx_floats<D, 8>()) * 4);
+    return (NW == 8 ? 232448 : 76800) - (8 * D * 4 + 256 + int(rx_floats<D, 8>()) * 4);
 }
-template <int D, int KV>
+template <int D, int KV, int NW>
 __host__ __device__ constexpr int nstages() {
     return KV == P100_KV_F16 ? stages<D>()
-           : quant_ring_budget<D>() / (2 * raw_slot_bytes<D, KV>()) < 3 ? 3
-           : quant_ring_budget<D>() / (2 * raw_slot_bytes<D, KV>()) > 8 ? 8
-                                                                        : quant_ring_budget<D>() / (2 * raw_slot_bytes<D, KV>());
+           : quant_ring_budget<D, NW>() / (2 * raw_slot_bytes<D, KV, NW>()) < 3 ? 3
+           : quant_ring_budget<D, NW>() / (2 * raw_slot_bytes<D, KV, NW>()) > 8 ? 8
+                                                                                : quant_ring_budget<D, NW>() / (2 * raw_slot_bytes<D, KV, NW>());
 }
-template <int D, int KV>
+template <int D, int KV, int NW>
 __host__ __device__ constexpr size_t ring_bytes() {
-    return KV == P100_KV_F16 ? size_t(stages<D>()) * 2 * kTile * (D + 8) * 2
-                             : size_t(nstages<D, KV>()) * 2 * raw_slot_bytes<D, KV>();
+    return KV == P100_KV_F16 ? size_t(stages<D>()) * 2 * tile_keys<NW>() * (D + 8) * 2
+                             : size_t(nstages<D, KV, NW>()) * 2 * raw_slot_bytes<D, KV, NW>();
 }
-template <int D, int G, int KV = P100_KV_F16>
+template <int D, int G, int KV = P100_KV_F16, int NW = 4>
 __host__ __device__ constexpr size_t smem_bytes() {
-    return ring_bytes<D, KV>() + size_t(G) * D * 4 + 256 + rx_floats<D, G>() * 4;
+    return ring_bytes<D, KV, NW>() + size_t(G) * D * 4 + 256 + rx_floats<D, G>() * 4;
 }
 static_assert(smem_bytes<128, 8, P100_KV_Q8_0>() <= 76800 && smem_bytes<128, 8, P100_KV_Q4_0>() <= 76800 &&
                   smem_bytes<64, 8, P100_KV_Q8_0>() <= 76800 && smem_bytes<64, 8, P100_KV_Q4_0>() <= 76800,
-              "three CTAs per SM");
+              "three 4-warp CTAs per SM");
+static_assert(smem_bytes<128, 8, P100_KV_F16, 8>() <= 232448 && smem_bytes<128, 8, P100_KV_Q8_0, 8>() <= 232448 &&
+                  smem_bytes<128, 8, P100_KV_Q4_0, 8>() <= 232448,
+              "one 8-warp CTA per SM");
 
 // Grid (parts, batch * n_kv); G = query heads per kv head (1, 2, 4 or 8);
-// D = 64 or 128; KV = the cache's p100_kv_type.
-template <int D, int G, int KV = P100_KV_F16>
-__global__ void __launch_bounds__(kThreads, KV == P100_KV_F16 ? 1 : kQuantCtasPerSm) fa_mma_kernel(const fa::Params p) {
+// D = 64 or 128; KV = the cache's p100_kv_type; NW = 4 or 8 warps.
+template <int D, int G, int KV = P100_KV_F16, int NW = 4>
+__global__ void __launch_bounds__(NW * 32, ctas_per_sm<NW>(KV)) fa_mma_kernel(const fa::Params p) {
     static_assert(G == 1 || G == 2 || G == 4 || G == 8, "G");
+    static_assert(NW == 4 || NW == 8, "NW");
+    constexpr int kWarps = NW, kThreads = NW * 32, kTile = tile_keys<NW>();
     constexpr int RS = D + 8;        // padded row stride (halves)
-    constexpr int NS = nstages<D, KV>();
+    constexpr int NS = nstages<D, KV, NW>();
     constexpr int KSQ = D / 16;      // k-steps of Q K^T
     constexpr int NTV = D / 8;       // n-tiles of P V
     constexpr bool QUANT = KV != P100_KV_F16;
     constexpr int BB = kvq::block_bytes<KV>();
     constexpr int RB = raw_row_bytes<D, KV>();
-    constexpr int RAW = raw_slot_bytes<D, KV>();
+    constexpr int RAW = raw_slot_bytes<D, KV, NW>();
     extern __shared__ __align__(128) uint8_t smem[];
     // fp16: [NS][K|V][kTile][RS]; quantised: [NS][K|V][RAW]
     __half* ring = reinterpret_cast<__half*>(smem);
-    float* s_q = reinterpret_cast<float*>(smem + ring_bytes<D, KV>());   // [G][D]
+    float* s_q = reinterpret_cast<float*>(smem + ring_bytes<D, KV, NW>());   // [G][D]
     float* s_qs = s_q + G * D;                                          // [8] per-head power-of-two scale
     unsigned* s_flag = reinterpret_cast<unsigned*>(s_qs + 8);
     uint64_t* bars = reinterpret_cast<uint64_t*>(s_qs + 16);           // [NS] K/V stage barriers
-    float* rx = reinterpret_cast<float*>(smem + smem_bytes<D, G, KV>() - rx_floats<D, G>() * 4);   // cluster merge
+    float* rx = reinterpret_cast<float*>(smem + smem_bytes<D, G, KV, NW>() - rx_floats<D, G>() * 4);   // cluster merge
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, t = lane & 3;

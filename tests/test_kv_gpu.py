@@ -124,15 +124,28 @@ def test_ragged_and_contexts_to_16k(cuda, orc, kv_type, seq):
 
 
 @pytest.mark.parametrize("kv_type", KV_TYPES)
-def test_long_context_workspace_merge(cuda, orc, kv_type):
-    """Past 16K keys the automatic split differs (a quantised ring fits three
-    CTAs per SM, fp16 two), so: bit-exact at an explicit common split, and the
-    automatic split within the attention tolerance of attention_reference."""
-    seq = 20000
-    o, lse, o16, lse16, *_ = run_pair(cuda, orc, kv_type, 1, 32, 8, seq, 128, splits=48, seed=seq)
+@pytest.mark.parametrize("seq", [8192, 8193, 20000, 32768])
+def test_long_contexts(cuda, orc, kv_type, seq):
+    """Past 8K keys the automatic split runs the 8-warp shape (128-key tiles,
+    one part per SM, workspace merge) for both caches: bit-exact, and within
+    the attention tolerance of attention_reference; at 8192 keys the 4-warp
+    cluster merge still runs."""
+    o, lse, o16, lse16, q, kf, vf = run_pair(cuda, orc, kv_type, 1, 32, 8, seq, 128, seed=seq)
     assert np.array_equal(o.view(np.uint32), o16.view(np.uint32))
-    o, lse, _, _, q, kf, vf = run_pair(cuda, orc, kv_type, 1, 32, 8, seq, 128, seed=seq)
-    p = oracle.Attn(n_head_q=32, n_head_kv=8, seq_kv=seq, d_qk=128, d_v=128)
+    assert np.array_equal(lse.view(np.uint32), lse16.view(np.uint32))
+    if seq == 20000:
+        p = oracle.Attn(n_head_q=32, n_head_kv=8, seq_kv=seq, d_qk=128, d_v=128)
+        ref_o, ref_lse, _ = orc.attention_reference_threaded(p, q, kf, vf, oracle.host_cores())
+        check_attention(o, lse, ref_o, ref_lse)
+
+
+@pytest.mark.parametrize("kv_type", KV_TYPES)
+@pytest.mark.parametrize("hq,hkv,d", [(64, 8, 64), (8, 8, 128), (16, 2, 64)])
+def test_long_contexts_other_groups(cuda, orc, kv_type, hq, hkv, d):
+    """The 8-warp shape with d 64 and groups of 8, 1 and 8 query heads, batch 2."""
+    o, lse, o16, lse16, q, kf, vf = run_pair(cuda, orc, kv_type, 2, hq, hkv, 9000, d, seed=hq + d)
+    assert np.array_equal(o.view(np.uint32), o16.view(np.uint32))
+    p = oracle.Attn(batch=2, n_head_q=hq, n_head_kv=hkv, seq_kv=9000, d_qk=d, d_v=d)
     ref_o, ref_lse, _ = orc.attention_reference_threaded(p, q, kf, vf, oracle.host_cores())
     check_attention(o, lse, ref_o, ref_lse)
 
