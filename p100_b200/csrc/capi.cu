@@ -14,6 +14,8 @@
 #include <utility>
 #include <vector>
 
+#include <cudaTypedefs.h>
+
 #include "common.cuh"
 #include "fa_decode.cuh"
 #include "fa_mma.cuh"
@@ -656,6 +658,38 @@ p100_status launch_fa_t(const FaPlan& plan, const fa::Params& prm, int heads, cu
     return cuda_status(cudaLaunchKernelEx(&cfg, kern, prm), "fa_decode_kernel launch");
 }
 
+// cuTensorMapEncodeTiled from the driver the runtime loaded (no link to libcuda).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess) {
+            (void)cudaGetLastError();
+            f = nullptr;
+        }
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    }();
+    return fn;
+}
+
+// The fp16 K or V cache as a 4-d tensor (d, rows [0, seq), kv heads, batch)
+// in boxes of 64 values x `rows` rows with the 128-byte swizzle.
+p100_status kv_tensor_map(CUtensorMap* map, const void* base, int d, int seq, int nkv, int batch,
+                          long long head_stride, long long batch_stride, int rows) {
+    PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+    if (!encode) return set_error(P100_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
+    const cuuint64_t dims[4] = {cuuint64_t(d), cuuint64_t(seq), cuuint64_t(nkv), cuuint64_t(batch)};
+    const cuuint64_t strides[3] = {cuuint64_t(d) * 2, cuuint64_t(head_stride) * 2, cuuint64_t(batch_stride) * 2};
+    const cuuint32_t box[4] = {64, cuuint32_t(rows), 1, 1};
+    const cuuint32_t elem[4] = {1, 1, 1, 1};
+    const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(base), dims, strides, box, elem,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(P100_ERR_INVALID, "K/V tensor map rejected (error %d): strides or extents", int(r));
+    return P100_OK;
+}
+
 template <int D, int G, int KV, int NW>
 p100_status launch_fa_mma_t(const FaPlan& plan, const fa::Params& prm, int heads, cudaStream_t stream, bool pdl) {
     auto kern = fam::fa_mma_kernel<D, G, KV, NW>;
@@ -676,6 +710,15 @@ p100_status launch_fa_mma_t(const FaPlan& plan, const fa::Params& prm, int heads
     // keeps at least half the parts.  Longer contexts amortise the workspace
     // merge and run twice the parts instead (two CTAs per SM).
     fa::Params run = prm;
+    if (KV == P100_KV_F16) {
+        const int batch = heads / prm.nkv;
+        if (p100_status st = kv_tensor_map(&run.tmk, prm.k, D, prm.seq, prm.nkv, batch, prm.head_stride,
+                                           prm.batch_stride, fam::tile_keys<NW>()))
+            return st;
+        if (p100_status st = kv_tensor_map(&run.tmv, prm.v, D, prm.seq, prm.nkv, batch, prm.head_stride,
+                                           prm.batch_stride, fam::tile_keys<NW>()))
+            return st;
+    }
     int np = 0;
     if (NW == 4 && plan.auto_parts && plan.parts >= 2 && plan.seq <= kFaWideSeq) {
         np = 1;

@@ -109,6 +109,20 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
         : "memory");
 }
 
+// Tiled tensor copy global -> this CTA's shared memory, completing on `bar`:
+// the box of the 4-d tensor map at coordinates (c0, c1, c2, c3), elements
+// outside the tensor read as zero.  c0 * element size must be a multiple of
+// 16 bytes and no coordinate negative; dst aligned as the map's swizzle wants
+// (1024 bytes for the 128-byte swizzle).  One destination CTA.
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* tmap, int c0, int c1, int c2, int c3,
+                                            uint64_t* bar, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(dst),
+        "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_addr(bar)), "l"(policy)
+        : "memory");
+}
+
 // ------------------------------------------------------------ programmatic dependent launch
 // Both are no-ops for a kernel launched without the PDL attribute.
 __device__ __forceinline__ void pdl_wait_prior_grid() { asm volatile("griddepcontrol.wait;" ::: "memory"); }

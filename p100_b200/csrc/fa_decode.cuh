@@ -18,6 +18,8 @@
 // the parts: global max M, weights exp(m_p - M), one division, LSE = M +
 // log(den) (attention_tiled_model.cpp:183-222, fattn-common.cuh:963-977).
 #pragma once
+#include <cuda.h>
+
 #include "common.cuh"
 #include "quant.cuh"
 
@@ -60,6 +62,10 @@ struct Params {
     // cluster (gridDim.x == parts <= 16) and merge through distributed shared
     // memory instead of ws_o / ws_ml / tickets.
     int cluster_merge;
+    // fa_mma_kernel over an fp16 cache: 4-d tensor maps (d, rows [0, seq),
+    // kv heads, batch) of k and v, boxes of 64 values x one tile of rows,
+    // 128-byte swizzle (set by the launcher).
+    CUtensorMap tmk, tmv;
 };
 
 __device__ __forceinline__ void half8_to_float(const uint4 v, float (&f)[8]) {

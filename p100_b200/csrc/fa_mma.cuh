@@ -74,16 +74,6 @@ __device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], uint32_t addr) {
                  : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
                  : "r"(addr));
 }
-// 16 bytes global -> shared; src_bytes 0 writes zeros (src is not read).
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, int src_bytes) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-
 // 8x8 b16 transpose within the warp: lane (g, t) gets elements (2t, g) and
 // (2t+1, g) of the matrix whose (g, 2t..2t+1) it held.
 __device__ __forceinline__ uint32_t movmatrix_trans(uint32_t a) {
@@ -153,9 +143,11 @@ __host__ __device__ constexpr int nstages() {
            : quant_ring_budget<D, NW>() / (2 * raw_slot_bytes<D, KV, NW>()) > 8 ? 8
                                                                                 : quant_ring_budget<D, NW>() / (2 * raw_slot_bytes<D, KV, NW>());
 }
+// fp16 stages hold [K|V][D/64 boxes][tile rows][128 B], 128-byte swizzled,
+// from a 1024-byte boundary (the slack is the last 1024 bytes).
 template <int D, int KV, int NW>
 __host__ __device__ constexpr size_t ring_bytes() {
-    return KV == P100_KV_F16 ? size_t(stages<D>()) * 2 * tile_keys<NW>() * (D + 8) * 2
+    return KV == P100_KV_F16 ? size_t(stages<D>()) * 2 * tile_keys<NW>() * D * 2 + 1024
                              : size_t(nstages<D, KV, NW>()) * 2 * raw_slot_bytes<D, KV, NW>();
 }
 template <int D, int G, int KV = P100_KV_F16, int NW = 4>
@@ -172,11 +164,10 @@ static_assert(smem_bytes<128, 8, P100_KV_F16, 8>() <= 232448 && smem_bytes<128, 
 // Grid (parts, batch * n_kv); G = query heads per kv head (1, 2, 4 or 8);
 // D = 64 or 128; KV = the cache's p100_kv_type; NW = 4 or 8 warps.
 template <int D, int G, int KV = P100_KV_F16, int NW = 4>
-__global__ void __launch_bounds__(NW * 32, ctas_per_sm<NW>(KV)) fa_mma_kernel(const fa::Params p) {
+__global__ void __launch_bounds__(NW * 32, ctas_per_sm<NW>(KV)) fa_mma_kernel(const __grid_constant__ fa::Params p) {
     static_assert(G == 1 || G == 2 || G == 4 || G == 8, "G");
     static_assert(NW == 4 || NW == 8, "NW");
     constexpr int kWarps = NW, kThreads = NW * 32, kTile = tile_keys<NW>();
-    constexpr int RS = D + 8;        // padded row stride (halves)
     constexpr int NS = nstages<D, KV, NW>();
     constexpr int KSQ = D / 16;      // k-steps of Q K^T
     constexpr int NTV = D / 8;       // n-tiles of P V
@@ -185,8 +176,9 @@ __global__ void __launch_bounds__(NW * 32, ctas_per_sm<NW>(KV)) fa_mma_kernel(co
     constexpr int RB = raw_row_bytes<D, KV>();
     constexpr int RAW = raw_slot_bytes<D, KV, NW>();
     extern __shared__ __align__(128) uint8_t smem[];
-    // fp16: [NS][K|V][kTile][RS]; quantised: [NS][K|V][RAW]
-    __half* ring = reinterpret_cast<__half*>(smem);
+    // fp16: [NS][K|V][D/64][kTile][128 B] from the first 1024-byte boundary;
+    // quantised: [NS][K|V][RAW] from the start
+    uint8_t* ring = smem + (QUANT ? 0u : (1024u - (smem_addr(smem) & 1023u)) & 1023u);
     float* s_q = reinterpret_cast<float*>(smem + ring_bytes<D, KV, NW>());   // [G][D]
     float* s_qs = s_q + G * D;                                          // [8] per-head power-of-two scale
     unsigned* s_flag = reinterpret_cast<unsigned*>(s_qs + 8);
@@ -252,10 +244,6 @@ __global__ void __launch_bounds__(NW * 32, ctas_per_sm<NW>(KV)) fa_mma_kernel(co
     }
     __syncthreads();
     const uint64_t policy = l2_evict_first_policy();
-    const int crow = tid / (D / 8), ccol = tid % (D / 8);   // fp16: this thread's first chunk
-    const __half* kth = kbase + size_t(crow) * D + ccol * 8;
-    const __half* vth = vbase + size_t(crow) * D + ccol * 8;
-    const uint32_t cdst = uint32_t((crow * RS + ccol * 8) * 2);
     // quantised: the 16-byte aligned source of rows [j0, j0 + n), its whole
     // 16-byte chunks inside the head's rows, and the 4-byte words after them
     auto quant_part = [&](const uint8_t* head, int lead, int j0, int n, int& nfull, int& tail) {
@@ -293,27 +281,22 @@ __global__ void __launch_bounds__(NW * 32, ctas_per_sm<NW>(KV)) fa_mma_kernel(co
                         *reinterpret_cast<const uint32_t*>(vsrc + nv * 16 + 4 * (tid - 64));
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             }
-        } else {
-            constexpr int RSTEP = kThreads / (D / 8);
-            const uint32_t kdst = ring_addr + uint32_t((tile % NS) * 2 * kTile * RS * 2) + cdst;
-            const uint32_t vdst = kdst + uint32_t(kTile * RS * 2);
-            const __half* ks = kth + size_t(j0) * D;
-            const __half* vs = vth + size_t(j0) * D;
-            (void)bar;
+        } else if (tid == 0) {
+            // D/64 boxes of 64 values x kTile rows each for K and V; rows past
+            // the tensor's p.seq read as zeros, rows of the next part are
+            // read and masked (their V rows are zeroed after the wait)
+            (void)n;
+            const uint32_t kdst = ring_addr + uint32_t((tile % NS) * 2 * kTile * D * 2);
+            const uint32_t vdst = kdst + uint32_t(kTile * D * 2);
+            mbar_arrive_expect_tx(bar, uint32_t(2 * kTile * D * 2));
 #pragma unroll
-            for (int i = 0; i < kTile * D / 8 / kThreads; ++i) {
-                const bool valid = crow + i * RSTEP < n;
-                const int off = valid ? i * RSTEP * D : -crow * D;   // invalid: row j0 (not read)
-                cp_async16(kdst + uint32_t(i * RSTEP * RS * 2), ks + off, valid ? 16 : 0);
-                cp_async16(vdst + uint32_t(i * RSTEP * RS * 2), vs + off, valid ? 16 : 0);
+            for (int bx = 0; bx < D / 64; ++bx) {
+                tma_load_4d(kdst + uint32_t(bx * kTile * 128), &p.tmk, bx * 64, j0, kvh, b, bar, policy);
+                tma_load_4d(vdst + uint32_t(bx * kTile * 128), &p.tmv, bx * 64, j0, kvh, b, bar, policy);
             }
         }
     };
-    // the commit groups count tiles (empty past the end), as the waits expect
-    auto issue_tile = [&](int tile) {
-        issue(tile);
-        if constexpr (!QUANT) cp_async_commit();
-    };
+    auto issue_tile = [&](int tile) { issue(tile); };
 
     if (!p.len_dev)
         for (int s = 0; s < NS - 1; ++s) issue_tile(s);   // K/V never come from the previous kernel here
@@ -446,21 +429,29 @@ __global__ void __launch_bounds__(NW * 32, ctas_per_sm<NW>(KV)) fa_mma_kernel(co
 
     bool copies_ok = true;   // false once a stage wait gave up (device flag raised): stop waiting
     for (int tile = 0; tile < ntiles; ++tile) {
-        if constexpr (QUANT) {
-            if (copies_ok) copies_ok = mbar_wait(&bars[tile % NS], (tile / NS) & 1);
-        } else {
-            cp_async_wait<NS - 2>();
+        const int j0 = key0 + tile * kTile;
+        const int n = min(kTile, key1 - j0);
+        // fp16: the stage's K and V boxes (128-byte swizzled: the 16-byte
+        // chunk c of row r sits at chunk c ^ (r % 8))
+        const uint32_t kst = ring_addr + uint32_t((tile % NS) * 2 * kTile * D * 2);
+        const uint32_t vst = kst + uint32_t(kTile * D * 2);
+        if (copies_ok) copies_ok = mbar_wait(&bars[tile % NS], (tile / NS) & 1);
+        if (!QUANT && n < kTile) {
+            // V rows past the part's end hold the next keys (or zeros past
+            // the tensor): make them zeros so a masked key adds exactly 0
+            for (int i = tid; i < (kTile - n) * (D / 8); i += kThreads) {
+                const int r = n + i / (D / 8), c = i % (D / 8);
+                *reinterpret_cast<uint4*>(ring + (vst - ring_addr) + (c >> 3) * kTile * 128 + r * 128 + (c & 7) * 16) =
+                    make_uint4(0u, 0u, 0u, 0u);
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // the slot is refilled by TMA later
         }
         __syncthreads();   // tile's copies visible to all; the slot refilled next is no longer read
         if (copies_ok) issue_tile(tile + NS - 1);
-        const int j0 = key0 + tile * kTile;
-        const int n = min(kTile, key1 - j0);
         // fp16: K and V fragments by ldmatrix from the stage.  Quantised:
         // straight from the raw rows — K pairs (key, dims 2t..2t+1) are the
         // B fragment as they stand, V pairs are transposed by movmatrix —
         // with the values kvq::dequant8 gives; V rows past n are zeros.
-        const uint32_t kst = ring_addr + uint32_t((tile % NS) * 2 * kTile * RS * 2);
-        const uint32_t vst = kst + uint32_t(kTile * RS * 2);
         const int kraw = (tile % NS) * 2 * RAW + lead_k, vraw = (tile % NS) * 2 * RAW + RAW + lead_v;
         auto scale2 = [&](int off) -> uint32_t {
             const uint32_t d = *reinterpret_cast<const unsigned short*>(smem + off);
@@ -489,7 +480,8 @@ __global__ void __launch_bounds__(NW * 32, ctas_per_sm<NW>(KV)) fa_mma_kernel(co
 #pragma unroll
                 for (int ks = 0; ks < KSQ; ks += 2) {
                     uint32_t r[4];
-                    ldsm_x4(r, kst + uint32_t((krow * RS + ks * 16 + (lane >> 3) * 8) * 2));
+                    const int cidx = 2 * ks + (lane >> 3);   // 16-byte chunk of the row
+                    ldsm_x4(r, kst + uint32_t((cidx >> 3) * kTile * 128 + krow * 128 + (((cidx & 7) ^ (krow & 7)) << 4)));
                     mma16816(s[nt], qa[ks], r[0], r[1]);
                     mma16816(s[nt], qa[ks + 1], r[2], r[3]);
                 }
@@ -596,13 +588,13 @@ __global__ void __launch_bounds__(NW * 32, ctas_per_sm<NW>(KV)) fa_mma_kernel(co
                 uint32_t r[4];
                 const int m = lane >> 3;
                 const int vrow = warp * 16 + (lane & 7) + 8 * (m & 1);
-                ldsm_x4_trans(r, vst + uint32_t((vrow * RS + n2 * 16 + 8 * (m >> 1)) * 2));
+                const int cidx = 2 * n2 + (m >> 1);
+                ldsm_x4_trans(r, vst + uint32_t((cidx >> 3) * kTile * 128 + vrow * 128 + (((cidx & 7) ^ (vrow & 7)) << 4)));
                 mma16816(o[2 * n2], pa, r[0], r[1]);
                 mma16816(o[2 * n2 + 1], pa, r[2], r[3]);
             }
         }
     }
-    if constexpr (!QUANT) cp_async_wait<0>();
     __syncthreads();   // every copy landed (each issued tile was waited for) and every warp is done with the ring
 
     // ---- hi + lo rows of O; then merge the four warps through shared memory
