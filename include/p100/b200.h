@@ -31,7 +31,7 @@
 extern "C" {
 #endif
 
-#define P100_B200_ABI_VERSION 2
+#define P100_B200_ABI_VERSION 3
 
 typedef enum p100_status {
     P100_OK = 0,
@@ -278,7 +278,20 @@ typedef struct p100_llama_config {
     int wtype;
     int flags;   /* P100_DEC_* (0: defaults) */
     int kv_type; /* p100_kv_type of the cache (0: fp16) */
+    /* Per-tensor weight formats, or NULL for wtype everywhere: an array of
+     * P100_DEC_TENSOR_TYPES(n_layer) p100_qtype values indexed by
+     * P100_TT_EMBED, P100_TT_LM_HEAD and P100_TT_LAYER(layer, P100_TT_Q ..
+     * P100_TT_DOWN), read during p100_decoder_create only.  llama.cpp's
+     * Q4_K_M files, for one, keep attn_v, ffn_down and output in Q6_K in
+     * some layers and Q4_K elsewhere.  A fused matrix (q|k|v, gate|up) then
+     * holds each range's rows in its own format, one range after the other;
+     * its mat-vec runs one launch per run of equal formats. */
+    const int* tensor_types;
 } p100_llama_config;
+enum { P100_TT_EMBED = 0, P100_TT_LM_HEAD = 1 };
+enum { P100_TT_Q = 0, P100_TT_K, P100_TT_V, P100_TT_O, P100_TT_GATE, P100_TT_UP, P100_TT_DOWN };
+#define P100_TT_LAYER(layer, part) (2 + 7 * (layer) + (part))
+#define P100_DEC_TENSOR_TYPES(n_layer) (2 + 7 * (n_layer))
 /* Run each RMSNorm inside the mat-vec that consumes it (p100_qmv_rmsnorm;
  * hidden 4096 or 8192, no peer-memory all-reduce): the same bits with one
  * launch less per norm.  Off by default: on B200 at batch 1 it measured
@@ -290,7 +303,7 @@ typedef struct p100_llama_config {
 typedef struct p100_decoder p100_decoder;
 /* Tensor ids (per layer where it applies). */
 enum {
-    P100_T_EMBED = 0,     /* [vocab][hidden] wtype                          */
+    P100_T_EMBED = 0,     /* [vocab][hidden] wtype (or its tensor type)     */
     P100_T_ATTN_NORM,     /* [hidden] fp32                                  */
     P100_T_WQKV,          /* rows [q heads | k heads | v heads] x hidden    */
     P100_T_WO,            /* [hidden] x (this rank's q heads * head_dim)    */
@@ -307,8 +320,9 @@ enum { P100_B_HIDDEN = 0, P100_B_LOGITS, P100_B_KCACHE, P100_B_VCACHE, P100_B_RO
 p100_status p100_decoder_create(const p100_llama_config* cfg, p100_tp* tp, p100_decoder** out);
 /* Synthetic weights from seed: block scales d = |N(0,1)| * 0.02 *
  * sqrt(256 / K) (K the unsplit matrix's input width, so activations keep
- * their scale at any width and depth), codes uniform; norms uniform in
- * [0.9, 1.1].
+ * their scale at any width and depth), codes uniform, d divided per format
+ * by 1 (Q4_0), 16 (Q8_0), 64 (Q4_K), 128 (Q5_K) or 256 (Q6_K) so that every
+ * format's values have about the same RMS; norms uniform in [0.9, 1.1].
  * Every value is a function of (seed, tensor, global coordinates), so the
  * slices of a tensor-parallel rank equal the unsplit model's. */
 p100_status p100_decoder_init_random(p100_decoder* d, unsigned long long seed);

@@ -358,7 +358,17 @@ class LlamaConfig(C.Structure):
     """p100o_llama, the same fields as p100_llama_config."""
     _fields_ = [("n_layer", C.c_int), ("hidden", C.c_int), ("n_head", C.c_int), ("n_head_kv", C.c_int),
                 ("head_dim", C.c_int), ("ffn", C.c_int), ("vocab", C.c_int), ("max_ctx", C.c_int),
-                ("rope_theta", C.c_float), ("norm_eps", C.c_float), ("wtype", C.c_int)]
+                ("rope_theta", C.c_float), ("norm_eps", C.c_float), ("wtype", C.c_int),
+                ("tensor_types", C.POINTER(C.c_int))]
+
+    def __init__(self, *args, tensor_types=None, **kw):
+        """tensor_types: None, or 2 + 7 * n_layer formats (embed, lm_head, then
+        q k v o gate up down per layer), as the decoder's config takes them."""
+        super().__init__(*args, **kw)
+        self._tt = None
+        if tensor_types is not None:
+            self._tt = (C.c_int * len(tensor_types))(*[int(t) for t in tensor_types])
+            self.tensor_types = C.cast(self._tt, C.POINTER(C.c_int))
 
 
 class LlamaWeights(C.Structure):

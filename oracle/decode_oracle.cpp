@@ -15,6 +15,8 @@
 #include <cmath>
 #include <cstdint>
 #include <cstring>
+#include <initializer_list>
+#include <utility>
 #include <vector>
 
 #include "p100_oracle.h"
@@ -181,23 +183,36 @@ int p100o_decode_step(const p100o_llama* c, const p100o_llama_weights* w, uint16
 // these (the two sides' k and v differ in the last bits).
 int p100o_decode_step_kv(const p100o_llama* c, const p100o_llama_weights* w, int kv_type, int append, void* k_cache,
                          void* v_cache, const float* rope_cs, int pos, int token, float* logits, float* hidden_out) {
-    const int t = c->wtype, hd = c->head_dim, H = c->hidden;
+    const int hd = c->head_dim, H = c->hidden;
     const int nq = c->n_head, nkv = c->n_head_kv, F = c->ffn;
     if (pos < 0 || pos >= c->max_ctx || token < 0 || token >= c->vocab) return -1;
     const long long hs = static_cast<long long>(c->max_ctx) * hd;
-    const size_t rb_h = size_t(H / p100o_block_elems(t)) * p100o_block_bytes(t);
+    // format of tensor id i: 0 embed, 1 lm_head, 2 + 7 * layer + {q k v o gate up down}
+    auto tt = [&](int i) { return c->tensor_types ? c->tensor_types[i] : c->wtype; };
+    auto lt = [&](int l, int part) { return tt(2 + 7 * l + part); };
+    const int te = tt(0);
+    const size_t rb_h = size_t(H / p100o_block_elems(te)) * p100o_block_bytes(te);
     std::vector<float> x(static_cast<size_t>(H)), delta(static_cast<size_t>(H));
     std::vector<uint8_t> xq(size_t(std::max(H, std::max(nq * hd, F)) / 32) * 36);
     std::vector<float> qkv(size_t(nq + 2 * nkv) * hd), attn(size_t(nq) * hd), gu(size_t(2) * F);
-    p100o_dequantize(t, static_cast<const uint8_t*>(w->embed) + size_t(token) * rb_h, 1, H, x.data());
-    auto qmv = [&](const void* m, int rows, int k, float* y) {
+    if (p100o_dequantize(te, static_cast<const uint8_t*>(w->embed) + size_t(token) * rb_h, 1, H, x.data()))
+        return -1;
+    // y = m . xq (k inputs) over row ranges {format, rows} stored one after the other
+    auto qmv = [&](const void* m, std::initializer_list<std::pair<int, int>> ranges, int k, float* y) {
         const std::vector<p100o_act> acts = unpack_q8_1(xq.data(), k);
-        return p100o_qmv_q81(t, m, rows, k, acts.data(), 1, y);
+        const uint8_t* p = static_cast<const uint8_t*>(m);
+        for (const auto& r : ranges) {
+            if (p100o_qmv_q81(r.first, p, r.second, k, acts.data(), 1, y)) return -1;
+            p += size_t(r.second) * size_t(k / p100o_block_elems(r.first)) * p100o_block_bytes(r.first);
+            y += r.second;
+        }
+        return 0;
     };
     for (int l = 0; l < c->n_layer; ++l) {
         p100o_rmsnorm_q8_1(x.data(), l == 0 ? nullptr : delta.data(), w->attn_norm[l], c->norm_eps, H, xq.data(),
                            nullptr);
-        if (qmv(w->wqkv[l], (nq + 2 * nkv) * hd, H, qkv.data())) return -1;
+        if (qmv(w->wqkv[l], {{lt(l, 0), nq * hd}, {lt(l, 1), nkv * hd}, {lt(l, 2), nkv * hd}}, H, qkv.data()))
+            return -1;
         const size_t layer_off = size_t(l) * nkv * hs;
         const int seq = pos + 1;
         std::vector<float> kf(size_t(nkv) * seq * hd), vf(size_t(nkv) * seq * hd);
@@ -252,15 +267,15 @@ int p100o_decode_step_kv(const p100o_llama* c, const p100o_llama_weights* w, int
         if (p100o_attention_reference(&ap, qkv.data(), kf.data(), vf.data(), nullptr, attn.data(), nullptr))
             return -1;
         if (p100o_quantize_q8_1(attn.data(), nq * hd, 1, xq.data())) return -1;
-        if (qmv(w->wo[l], H, nq * hd, delta.data())) return -1;
+        if (qmv(w->wo[l], {{lt(l, 3), H}}, nq * hd, delta.data())) return -1;
         p100o_rmsnorm_q8_1(x.data(), delta.data(), w->ffn_norm[l], c->norm_eps, H, xq.data(), nullptr);
-        if (qmv(w->wgu[l], 2 * F, H, gu.data())) return -1;
+        if (qmv(w->wgu[l], {{lt(l, 4), F}, {lt(l, 5), F}}, H, gu.data())) return -1;
         p100o_swiglu_q8_1(gu.data(), F, xq.data());
-        if (qmv(w->wdown[l], H, F, delta.data())) return -1;
+        if (qmv(w->wdown[l], {{lt(l, 6), H}}, F, delta.data())) return -1;
     }
     p100o_rmsnorm_q8_1(x.data(), delta.data(), w->out_norm, c->norm_eps, H, xq.data(), nullptr);
     if (hidden_out) std::memcpy(hidden_out, x.data(), size_t(H) * 4);
-    if (qmv(w->lm_head, c->vocab, H, logits)) return -1;
+    if (qmv(w->lm_head, {{tt(1), c->vocab}}, H, logits)) return -1;
     return p100o_argmax(logits, c->vocab, nullptr);
 }
 

@@ -150,6 +150,10 @@ typedef struct p100o_llama {
     int n_layer, hidden, n_head, n_head_kv, head_dim, ffn, vocab, max_ctx;
     float rope_theta, norm_eps;
     int wtype;
+    /* NULL, or per-tensor formats indexed as p100_llama_config's
+     * tensor_types (embed, lm_head, then q k v o gate up down per layer);
+     * fused matrices hold their ranges one after the other */
+    const int* tensor_types;
 } p100o_llama;
 /* Host copies of the unsplit model, laid out as the GPU decoder's tensors. */
 typedef struct p100o_llama_weights {

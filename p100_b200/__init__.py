@@ -407,15 +407,46 @@ class LlamaConfig(C.Structure):
     _fields_ = [("n_layer", C.c_int), ("hidden", C.c_int), ("n_head", C.c_int), ("n_head_kv", C.c_int),
                 ("head_dim", C.c_int), ("ffn", C.c_int), ("vocab", C.c_int), ("max_ctx", C.c_int),
                 ("rope_theta", C.c_float), ("norm_eps", C.c_float), ("wtype", C.c_int), ("flags", C.c_int),
-                ("kv_type", C.c_int)]
+                ("kv_type", C.c_int), ("tensor_types", C.POINTER(C.c_int))]
 
     def __init__(self, n_layer, hidden, n_head, n_head_kv, head_dim, ffn, vocab, max_ctx, rope_theta=500000.0,
-                 norm_eps=1e-5, wtype=0, flags=0, kv_type=0):
+                 norm_eps=1e-5, wtype=0, flags=0, kv_type=0, tensor_types=None):
+        """tensor_types: None (wtype everywhere) or DEC_TENSOR_TYPES(n_layer)
+        formats indexed by TT_EMBED, TT_LM_HEAD and tt_layer(l, TT_Q ..)."""
         super().__init__(n_layer, hidden, n_head, n_head_kv, head_dim, ffn, vocab, max_ctx, rope_theta, norm_eps,
                          wtype, flags, kv_type)
+        self.set_tensor_types(tensor_types)
+
+    def set_tensor_types(self, types):
+        if types is None:
+            self._tt = None
+            self.tensor_types = None
+            return
+        types = [int(t) for t in types]
+        if len(types) != dec_tensor_types(self.n_layer):
+            raise ValueError(f"tensor_types needs {dec_tensor_types(self.n_layer)} entries, got {len(types)}")
+        self._tt = (C.c_int * len(types))(*types)   # kept alive with the config
+        self.tensor_types = C.cast(self._tt, C.POINTER(C.c_int))
+
+    def types(self):
+        """The format of every tensor id (wtype where tensor_types is None)."""
+        if self._tt is None:
+            return [self.wtype] * dec_tensor_types(self.n_layer)
+        return list(self._tt)
 
 
 DEC_FUSED_NORM = 1   # P100_DEC_FUSED_NORM
+# tensor ids of LlamaConfig.tensor_types (P100_TT_*)
+TT_EMBED, TT_LM_HEAD = 0, 1
+TT_Q, TT_K, TT_V, TT_O, TT_GATE, TT_UP, TT_DOWN = range(7)
+
+
+def tt_layer(layer, part):
+    return 2 + 7 * layer + part
+
+
+def dec_tensor_types(n_layer):
+    return 2 + 7 * n_layer
 
 
 T_EMBED, T_ATTN_NORM, T_WQKV, T_WO, T_FFN_NORM, T_WGATE_UP, T_WDOWN, T_OUT_NORM, T_LM_HEAD = range(9)

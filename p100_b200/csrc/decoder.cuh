@@ -33,6 +33,12 @@ struct DecTensor {
     uint8_t* ptr = nullptr;
     size_t bytes = 0;
     int rows = 0, cols = 0;   // cols in elements (weights) or 1 (vectors)
+    // A weight matrix as runs of rows in one format each, stored one after
+    // the other (q | k | v or gate | up ranges of equal format merged): part
+    // p is prows[p] rows of ptype[p] at byte poff[p].
+    int nparts = 0;
+    int ptype[3] = {}, prows[3] = {};
+    size_t poff[3] = {};
 };
 
 struct Decoder {
@@ -40,7 +46,7 @@ struct Decoder {
     p100_tp* tp = nullptr;
     int rank = 0, nranks = 1, device = 0, sms = 0;
     int nq = 0, nkv = 0, ffn = 0, vocab0 = 0, vocab_n = 0;   // this rank's slice
-    size_t row_bytes_h = 0;                                  // one hidden-K weight row
+    std::vector<int> ttypes;                                 // P100_TT_* -> weight format
     uint8_t* arena = nullptr;
     size_t arena_bytes = 0;
     std::vector<DecTensor> attn_norm, wqkv, wo, ffn_norm, wgu, wdown;
@@ -87,11 +93,20 @@ p100_status launch_glue(void (*kern)(Exp...), dim3 grid, dim3 block, cudaStream_
     return cuda_status(cudaLaunchKernelEx(&cfg, kern, std::forward<Act>(args)...), what);
 }
 
-const char* config_reason(const p100_llama_config& c, int nranks) {
+// The format of tensor id i (P100_TT_*).
+int dec_ttype(const Decoder& d, int i) { return d.ttypes[size_t(i)]; }
+
+const char* config_reason(const p100_llama_config& c, int nranks, const std::vector<int>& tt) {
     if (c.n_layer <= 0 || c.hidden <= 0 || c.n_head <= 0 || c.n_head_kv <= 0 || c.head_dim <= 0 || c.ffn <= 0 ||
         c.vocab <= 0 || c.max_ctx <= 0)
         return "all model dimensions must be positive";
-    if (c.wtype != P100_Q4_0 && c.wtype != P100_Q8_0 && c.wtype != P100_Q4_K) return "unknown weight type";
+    if (tt.size() != size_t(P100_DEC_TENSOR_TYPES(c.n_layer))) return "n_layer above 2^20";
+    if (!known_type(c.wtype)) return "unknown weight type";
+    int blk = 1;
+    for (int t : tt) {
+        if (!known_type(t)) return "unknown weight type in tensor_types";
+        blk = std::max(blk, elems_of(t));
+    }
     if (c.flags & ~P100_DEC_FUSED_NORM) return "unknown decoder flags";
     if (c.n_head % c.n_head_kv) return "n_head must be divisible by n_head_kv";
     if (c.head_dim != 64 && c.head_dim != 128 && c.head_dim != 256) return "head_dim must be 64, 128 or 256";
@@ -103,7 +118,6 @@ const char* config_reason(const p100_llama_config& c, int nranks) {
             return "a quantised KV cache needs head_dim 64 or 128 and 1, 2, 4 or 8 query heads per kv head";
     }
     if (c.n_head % nranks || c.n_head_kv % nranks) return "heads must split evenly over the ranks";
-    const int blk = elems_of(c.wtype);
     if (c.hidden % blk || c.hidden % 32) return "hidden must be whole weight blocks";
     if (c.hidden > dec::kNormMaxK) return "hidden above the RMSNorm kernel's limit (16384)";
     if ((c.n_head / nranks) * c.head_dim % blk) return "a rank's attention slice must be whole weight blocks";
@@ -116,13 +130,12 @@ const char* config_reason(const p100_llama_config& c, int nranks) {
 
 p100_status dec_alloc(Decoder& d) {
     const p100_llama_config& c = d.cfg;
-    const int t = c.wtype, hd = c.head_dim, L = c.n_layer;
+    const int hd = c.head_dim, L = c.n_layer;
     d.nq = c.n_head / d.nranks;
     d.nkv = c.n_head_kv / d.nranks;
     d.ffn = c.ffn / d.nranks;
     d.vocab0 = static_cast<int>(static_cast<long long>(c.vocab) * d.rank / d.nranks);
     d.vocab_n = static_cast<int>(static_cast<long long>(c.vocab) * (d.rank + 1) / d.nranks) - d.vocab0;
-    d.row_bytes_h = dec_weight_bytes(t, 1, c.hidden);
     size_t off = 0;
     auto take = [&](size_t bytes) { const size_t at = off; off += align256(bytes); return at; };
     struct Req { DecTensor* t; size_t at; };
@@ -133,19 +146,39 @@ p100_status dec_alloc(Decoder& d) {
         dt.bytes = bytes;
         reqs.push_back({&dt, take(bytes)});
     };
+    // a weight matrix of cols inputs from row ranges {format, rows}
+    auto weight = [&](DecTensor& dt, int cols, std::initializer_list<std::pair<int, int>> ranges) {
+        int rows = 0;
+        size_t bytes = 0;
+        dt.nparts = 0;
+        for (const auto& r : ranges) {
+            if (dt.nparts > 0 && dt.ptype[dt.nparts - 1] == r.first) {
+                dt.prows[dt.nparts - 1] += r.second;
+            } else {
+                dt.ptype[dt.nparts] = r.first;
+                dt.prows[dt.nparts] = r.second;
+                dt.poff[dt.nparts] = bytes;
+                ++dt.nparts;
+            }
+            rows += r.second;
+            bytes += dec_weight_bytes(r.first, r.second, cols);
+        }
+        tensor(dt, rows, cols, bytes);
+    };
+    auto tt = [&](int l, int part) { return dec_ttype(d, P100_TT_LAYER(l, part)); };
     d.attn_norm.resize(L); d.wqkv.resize(L); d.wo.resize(L); d.ffn_norm.resize(L); d.wgu.resize(L); d.wdown.resize(L);
     for (int l = 0; l < L; ++l) {
-        const int qkv_rows = (d.nq + 2 * d.nkv) * hd;
         tensor(d.attn_norm[l], c.hidden, 1, size_t(c.hidden) * 4);
-        tensor(d.wqkv[l], qkv_rows, c.hidden, dec_weight_bytes(t, qkv_rows, c.hidden));
-        tensor(d.wo[l], c.hidden, d.nq * hd, dec_weight_bytes(t, c.hidden, d.nq * hd));
+        weight(d.wqkv[l], c.hidden,
+               {{tt(l, P100_TT_Q), d.nq * hd}, {tt(l, P100_TT_K), d.nkv * hd}, {tt(l, P100_TT_V), d.nkv * hd}});
+        weight(d.wo[l], d.nq * hd, {{tt(l, P100_TT_O), c.hidden}});
         tensor(d.ffn_norm[l], c.hidden, 1, size_t(c.hidden) * 4);
-        tensor(d.wgu[l], 2 * d.ffn, c.hidden, dec_weight_bytes(t, 2 * d.ffn, c.hidden));
-        tensor(d.wdown[l], c.hidden, d.ffn, dec_weight_bytes(t, c.hidden, d.ffn));
+        weight(d.wgu[l], c.hidden, {{tt(l, P100_TT_GATE), d.ffn}, {tt(l, P100_TT_UP), d.ffn}});
+        weight(d.wdown[l], d.ffn, {{tt(l, P100_TT_DOWN), c.hidden}});
     }
-    tensor(d.embed, c.vocab, c.hidden, dec_weight_bytes(t, c.vocab, c.hidden));
+    weight(d.embed, c.hidden, {{dec_ttype(d, P100_TT_EMBED), c.vocab}});
     tensor(d.out_norm, c.hidden, 1, size_t(c.hidden) * 4);
-    tensor(d.lm_head, d.vocab_n, c.hidden, dec_weight_bytes(t, d.vocab_n, c.hidden));
+    weight(d.lm_head, c.hidden, {{dec_ttype(d, P100_TT_LM_HEAD), d.vocab_n}});
     d.kv_row_bytes = c.kv_type == P100_KV_Q8_0   ? size_t(hd / 32) * 34
                      : c.kv_type == P100_KV_Q4_0 ? size_t(hd / 32) * 18
                                                  : size_t(hd) * 2;
@@ -225,7 +258,9 @@ p100_status dec_init_matrix(int t, uint8_t* w, size_t row_bytes, int rows, int c
     switch (t) {
         case P100_Q4_0: return dec_init_w<P100_Q4_0>(w, row_bytes, rows, blocks, key, row0, block0, dscale);
         case P100_Q8_0: return dec_init_w<P100_Q8_0>(w, row_bytes, rows, blocks, key, row0, block0, dscale);
-        default: return dec_init_w<P100_Q4_K>(w, row_bytes, rows, blocks, key, row0, block0, dscale);
+        case P100_Q4_K: return dec_init_w<P100_Q4_K>(w, row_bytes, rows, blocks, key, row0, block0, dscale);
+        case P100_Q5_K: return dec_init_w<P100_Q5_K>(w, row_bytes, rows, blocks, key, row0, block0, dscale);
+        default: return dec_init_w<P100_Q6_K>(w, row_bytes, rows, blocks, key, row0, block0, dscale);
     }
 }
 
@@ -239,34 +274,37 @@ p100_status dec_init_vector(float* v, long long n, uint64_t key) {
 // positions of this rank's heads / FFN slice; LM head rows are vocabulary ids.
 p100_status dec_init_random(Decoder& d, uint64_t seed) {
     const p100_llama_config& c = d.cfg;
-    const int t = c.wtype, hd = c.head_dim;
-    const size_t rb_h = d.row_bytes_h;
+    const int hd = c.head_dim, H = c.hidden;
     enum { K_NORM1, K_Q, K_K, K_V, K_O, K_NORM2, K_GATE, K_UP, K_DOWN, K_EMB, K_NORM3, K_LM };
+    // rows [row0, row0 + rows) of a range of format t stored at w
+    auto range = [&](uint8_t* w, int t, int rows, int cols, uint64_t key, long long row0, long long col0,
+                     int k_global) {
+        return dec_init_matrix(t, w, dec_weight_bytes(t, 1, cols), rows, cols, key, row0, col0, k_global);
+    };
     for (int l = 0; l < c.n_layer; ++l) {
         p100_status st = P100_OK;
+        const int tq = dec_ttype(d, P100_TT_LAYER(l, P100_TT_Q)), tk = dec_ttype(d, P100_TT_LAYER(l, P100_TT_K));
+        const int tv = dec_ttype(d, P100_TT_LAYER(l, P100_TT_V)), tg = dec_ttype(d, P100_TT_LAYER(l, P100_TT_GATE));
         uint8_t* w = d.wqkv[l].ptr;
+        uint8_t* wk = w + dec_weight_bytes(tq, d.nq * hd, H);
+        uint8_t* wv = wk + dec_weight_bytes(tk, d.nkv * hd, H);
         const long long q0 = static_cast<long long>(d.rank) * d.nq * hd, kv0 = static_cast<long long>(d.rank) * d.nkv * hd;
-        if (!st) st = dec_init_vector(reinterpret_cast<float*>(d.attn_norm[l].ptr), c.hidden, dec_key(seed, l, K_NORM1));
-        if (!st) st = dec_init_matrix(t, w, rb_h, d.nq * hd, c.hidden, dec_key(seed, l, K_Q), q0, 0, c.hidden);
-        if (!st) st = dec_init_matrix(t, w + size_t(d.nq * hd) * rb_h, rb_h, d.nkv * hd, c.hidden, dec_key(seed, l, K_K),
-                                      kv0, 0, c.hidden);
-        if (!st) st = dec_init_matrix(t, w + size_t((d.nq + d.nkv) * hd) * rb_h, rb_h, d.nkv * hd, c.hidden,
-                                      dec_key(seed, l, K_V), kv0, 0, c.hidden);
-        if (!st) st = dec_init_matrix(t, d.wo[l].ptr, dec_weight_bytes(t, 1, d.nq * hd), c.hidden, d.nq * hd,
-                                      dec_key(seed, l, K_O), 0, q0, c.n_head * hd);
-        if (!st) st = dec_init_vector(reinterpret_cast<float*>(d.ffn_norm[l].ptr), c.hidden, dec_key(seed, l, K_NORM2));
         const long long f0 = static_cast<long long>(d.rank) * d.ffn;
-        if (!st) st = dec_init_matrix(t, d.wgu[l].ptr, rb_h, d.ffn, c.hidden, dec_key(seed, l, K_GATE), f0, 0, c.hidden);
-        if (!st) st = dec_init_matrix(t, d.wgu[l].ptr + size_t(d.ffn) * rb_h, rb_h, d.ffn, c.hidden, dec_key(seed, l, K_UP),
-                                      f0, 0, c.hidden);
-        if (!st) st = dec_init_matrix(t, d.wdown[l].ptr, dec_weight_bytes(t, 1, d.ffn), c.hidden, d.ffn,
-                                      dec_key(seed, l, K_DOWN), 0, f0, c.ffn);
+        if (!st) st = dec_init_vector(reinterpret_cast<float*>(d.attn_norm[l].ptr), H, dec_key(seed, l, K_NORM1));
+        if (!st) st = range(w, tq, d.nq * hd, H, dec_key(seed, l, K_Q), q0, 0, H);
+        if (!st) st = range(wk, tk, d.nkv * hd, H, dec_key(seed, l, K_K), kv0, 0, H);
+        if (!st) st = range(wv, tv, d.nkv * hd, H, dec_key(seed, l, K_V), kv0, 0, H);
+        if (!st) st = range(d.wo[l].ptr, d.wo[l].ptype[0], H, d.nq * hd, dec_key(seed, l, K_O), 0, q0, c.n_head * hd);
+        if (!st) st = dec_init_vector(reinterpret_cast<float*>(d.ffn_norm[l].ptr), H, dec_key(seed, l, K_NORM2));
+        if (!st) st = range(d.wgu[l].ptr, tg, d.ffn, H, dec_key(seed, l, K_GATE), f0, 0, H);
+        if (!st) st = range(d.wgu[l].ptr + dec_weight_bytes(tg, d.ffn, H), dec_ttype(d, P100_TT_LAYER(l, P100_TT_UP)),
+                            d.ffn, H, dec_key(seed, l, K_UP), f0, 0, H);
+        if (!st) st = range(d.wdown[l].ptr, d.wdown[l].ptype[0], H, d.ffn, dec_key(seed, l, K_DOWN), 0, f0, c.ffn);
         if (st) return st;
     }
-    p100_status st = dec_init_matrix(t, d.embed.ptr, rb_h, c.vocab, c.hidden, dec_key(seed, -1, K_EMB), 0, 0, c.hidden);
-    if (!st) st = dec_init_vector(reinterpret_cast<float*>(d.out_norm.ptr), c.hidden, dec_key(seed, -1, K_NORM3));
-    if (!st) st = dec_init_matrix(t, d.lm_head.ptr, rb_h, d.vocab_n, c.hidden, dec_key(seed, -1, K_LM), d.vocab0, 0,
-                                  c.hidden);
+    p100_status st = range(d.embed.ptr, d.embed.ptype[0], c.vocab, H, dec_key(seed, -1, K_EMB), 0, 0, H);
+    if (!st) st = dec_init_vector(reinterpret_cast<float*>(d.out_norm.ptr), H, dec_key(seed, -1, K_NORM3));
+    if (!st) st = range(d.lm_head.ptr, d.lm_head.ptype[0], d.vocab_n, H, dec_key(seed, -1, K_LM), d.vocab0, 0, H);
     if (!st) st = cuda_status(cudaDeviceSynchronize(), "decoder initialisation");
     return st;
 }
@@ -302,8 +340,20 @@ template <int T>
 p100_status dec_embed_t(Decoder& d, cudaStream_t s) {
     const int slabs = d.cfg.hidden / 32;
     return launch_glue(dec::embed_kernel<T>, dim3((slabs + 255) / 256), dim3(256), s, "embed_kernel launch",
-                       static_cast<const uint8_t*>(d.embed.ptr), d.row_bytes_h, d.cfg.vocab, d.cfg.hidden,
+                       static_cast<const uint8_t*>(d.embed.ptr), dec_weight_bytes(T, 1, d.cfg.hidden), d.cfg.vocab,
+                       d.cfg.hidden,
                        static_cast<const int*>(d.token), d.fuse_norm ? d.x2 : d.x);
+}
+
+// y = w . xq (k inputs), one mat-vec launch per part of w.
+p100_status dec_qmv(const DecTensor& w, int k, const uint8_t* xq, float* y, cudaStream_t s) {
+    int row = 0;
+    for (int p = 0; p < w.nparts; ++p) {
+        if (p100_status st = run_qmv(w.ptype[p], w.ptr + w.poff[p], w.prows[p], k, xq, 1, y + row, P100_QMV_PDL, s))
+            return st;
+        row += w.prows[p];
+    }
+    return P100_OK;
 }
 
 // x += delta (or, with peer_reduce, += the peer all-reduce of this epoch),
@@ -331,13 +381,15 @@ p100_status dec_allreduce(Decoder& d, cudaStream_t s) {
 // One token, recorded into stream s (a capture stream).
 p100_status dec_record_step(Decoder& d, cudaStream_t s) {
     const p100_llama_config& c = d.cfg;
-    const int t = c.wtype, hd = c.head_dim;
+    const int hd = c.head_dim;
     const long long hs = static_cast<long long>(c.max_ctx) * hd;
     p100_status st = P100_OK;
-    switch (t) {
+    switch (d.embed.ptype[0]) {
         case P100_Q4_0: st = dec_embed_t<P100_Q4_0>(d, s); break;
         case P100_Q8_0: st = dec_embed_t<P100_Q8_0>(d, s); break;
-        default: st = dec_embed_t<P100_Q4_K>(d, s); break;
+        case P100_Q4_K: st = dec_embed_t<P100_Q4_K>(d, s); break;
+        case P100_Q5_K: st = dec_embed_t<P100_Q5_K>(d, s); break;
+        default: st = dec_embed_t<P100_Q6_K>(d, s); break;
     }
     // With the fused norms, cur is the residual stream and each norm writes
     // the updated stream to the other buffer.
@@ -345,11 +397,11 @@ p100_status dec_record_step(Decoder& d, cudaStream_t s) {
     auto norm_qmv = [&](const float* delta, const DecTensor& nw, const DecTensor& w, int rows, float* y) {
         if (!d.fuse_norm) {
             p100_status e = dec_rmsnorm(d, delta, nw, s, delta != nullptr && d.peer_ar);
-            if (!e) e = run_qmv(t, w.ptr, rows, c.hidden, d.xq, 1, y, P100_QMV_PDL, s);
+            if (!e) e = dec_qmv(w, c.hidden, d.xq, y, s);
             return e;
         }
         float* next = cur == d.x ? d.x2 : d.x;
-        const p100_status e = run_qmv_norm(t, w.ptr, rows, c.hidden, cur, delta, next,
+        const p100_status e = run_qmv_norm(w.ptype[0], w.ptr, rows, c.hidden, cur, delta, next,
                                            reinterpret_cast<const float*>(nw.ptr), c.norm_eps, y, P100_QMV_PDL, s);
         cur = next;
         return e;
@@ -410,13 +462,13 @@ p100_status dec_record_step(Decoder& d, cudaStream_t s) {
                                  "q8_1_quantize_kernel launch", static_cast<const float*>(d.attn), d.xq, k_o, k_o / 32);
             }
         }
-        if (!st) st = run_qmv(t, d.wo[l].ptr, c.hidden, d.nq * hd, d.xq, 1, d.delta, P100_QMV_PDL, s);
+        if (!st) st = dec_qmv(d.wo[l], d.nq * hd, d.xq, d.delta, s);
         if (!st) st = dec_allreduce(d, s);
         if (!st) st = norm_qmv(d.delta, d.ffn_norm[l], d.wgu[l], 2 * d.ffn, d.gu);
         if (!st)
             st = launch_glue(dec::swiglu_q8_1_kernel, dim3((d.ffn / 32 + 7) / 8, 1), dim3(256), s,
                              "swiglu_q8_1_kernel launch", static_cast<const float*>(d.gu), d.ffn, d.xq);
-        if (!st) st = run_qmv(t, d.wdown[l].ptr, c.hidden, d.ffn, d.xq, 1, d.delta, P100_QMV_PDL, s);
+        if (!st) st = dec_qmv(d.wdown[l], d.ffn, d.xq, d.delta, s);
         if (!st) st = dec_allreduce(d, s);
     }
     if (!st) st = norm_qmv(d.delta, d.out_norm, d.lm_head, d.vocab_n, d.logits);
@@ -674,7 +726,12 @@ p100_status p100_decoder_create(const p100_llama_config* cfg, p100_tp* tp, p100_
     if (!cfg || !out) return set_error(P100_ERR_INVALID, "null argument");
     *out = nullptr;
     const int nranks = tp ? p100_tp_size(tp) : 1;
-    if (const char* why = config_reason(*cfg, nranks)) return set_error(P100_ERR_INVALID, "%s", why);
+    std::vector<int> tt;
+    if (cfg->n_layer > 0 && cfg->n_layer <= (1 << 20)) {
+        tt.assign(size_t(P100_DEC_TENSOR_TYPES(cfg->n_layer)), cfg->wtype);
+        if (cfg->tensor_types) tt.assign(cfg->tensor_types, cfg->tensor_types + tt.size());
+    }
+    if (const char* why = config_reason(*cfg, nranks, tt)) return set_error(P100_ERR_INVALID, "%s", why);
     int dev = 0;
     if (tp) {
         dev = p100_tp_device(tp);
@@ -686,6 +743,8 @@ p100_status p100_decoder_create(const p100_llama_config* cfg, p100_tp* tp, p100_
     if (p100_status st = require_sm100(nullptr, &sms)) return st;
     auto* h = new p100_decoder();
     h->d.cfg = *cfg;
+    h->d.cfg.tensor_types = nullptr;   // read here only: the caller's array need not outlive this call
+    h->d.ttypes = std::move(tt);
     h->d.tp = tp;
     h->d.rank = tp ? p100_tp_rank(tp) : 0;
     h->d.nranks = nranks;
@@ -699,7 +758,11 @@ p100_status p100_decoder_create(const p100_llama_config* cfg, p100_tp* tp, p100_
         // all-reduce keeps its reduce inside the separate RMSNorm kernel.
         Decoder& d = h->d;
         const int t = d.cfg.wtype, k = d.cfg.hidden;
-        d.fuse_norm = (d.cfg.flags & P100_DEC_FUSED_NORM) && !d.peer_ar && qmv_norm_applies(t, d.wqkv[0].ptr, d.wqkv[0].rows, k, d.x2, d.x) &&
+        bool uniform = true;
+        for (size_t i = 0; i < d.ttypes.size(); ++i)
+            if (i != P100_TT_EMBED && d.ttypes[i] != t) uniform = false;
+        d.fuse_norm = (d.cfg.flags & P100_DEC_FUSED_NORM) && uniform && !d.peer_ar &&
+                      qmv_norm_applies(t, d.wqkv[0].ptr, d.wqkv[0].rows, k, d.x2, d.x) &&
                       qmv_norm_applies(t, d.wgu[0].ptr, 2 * d.ffn, k, d.x, d.x2) &&
                       qmv_norm_applies(t, d.lm_head.ptr, d.vocab_n, k, d.x2, d.x);
         clear_error();

@@ -15,10 +15,10 @@ names llama.cpp writes) into a `Decoder`: q, k and v rows are stacked into
 the decoder's fused QKV matrix and gate / up into its gate-up matrix, sliced
 per rank under tensor parallelism.  llama.cpp stores q and k rows in the
 order its RoPE of adjacent pairs expects, which is the decoder's RoPE, so no
-rows are permuted.  The decoder keeps every linear weight and the embedding
-in one format (Q4_0, Q8_0 or Q4_K): a file that mixes formats (a Q4_K_M
-file keeps some tensors in Q6_K) is rejected with the offending tensor
-named.
+rows are permuted.  Every matrix keeps its file format (Q4_0, Q8_0, Q4_K,
+Q5_K or Q6_K, per tensor: a Q4_K_M file, for one, holds attn_v, ffn_down
+and output in Q6_K in some layers), passed to the decoder as its
+tensor_types; a tensor in any other format is rejected with its name.
 """
 from __future__ import annotations
 
@@ -232,7 +232,7 @@ def _meta(g, key, default=None):
 
 def llama_config(g, max_ctx=None, kv_type=0, flags=0):
     """The decoder configuration of a llama GGUF file: (LlamaConfig kwargs,
-    p100 weight type)."""
+    the embedding's ggml type, whose format is the config's wtype)."""
     arch = g.metadata.get("general.architecture", "llama")
     if arch != "llama":
         raise GGUFError(f"{g.path}: architecture {arch!r} (llama is loaded)")
@@ -248,8 +248,9 @@ def llama_config(g, max_ctx=None, kv_type=0, flags=0):
     vocab = int(emb.dims[1])
     ctx = int(_meta(g, "context_length", 4096))
     wt = emb.ggml_type
-    if wt not in (GGML_Q4_0, GGML_Q8_0, GGML_Q4_K):
-        raise GGUFError(f"{g.path}: token_embd.weight is {GGML_NAMES.get(wt, wt)}; the decoder reads Q4_0, Q8_0 or Q4_K")
+    if wt not in P100_TYPE:
+        raise GGUFError(f"{g.path}: token_embd.weight is {GGML_NAMES.get(wt, wt)}; the decoder reads "
+                        + ", ".join(GGML_NAMES[t] for t in P100_TYPE))
     cfg = dict(n_layer=int(_meta(g, "block_count")), hidden=hidden, n_head=n_head, n_head_kv=n_head_kv,
                head_dim=head_dim, ffn=int(_meta(g, "feed_forward_length")), vocab=vocab,
                max_ctx=int(max_ctx or min(ctx, 4096)), rope_theta=float(_meta(g, "rope.freq_base", 10000.0)),
@@ -259,36 +260,47 @@ def llama_config(g, max_ctx=None, kv_type=0, flags=0):
 
 
 def _check(g, name, gt, dims):
+    """The bytes of tensor name after checking its dims and its format: gt, or
+    any format the decoder's mat-vec reads when gt is None."""
     t = g.tensors.get(name)
     if t is None:
         raise GGUFError(f"{g.path}: no tensor {name}")
-    if t.ggml_type != gt:
+    if gt is None and t.ggml_type not in P100_TYPE:
+        raise GGUFError(f"{g.path}: tensor {name} is {GGML_NAMES.get(t.ggml_type, t.ggml_type)}, the decoder "
+                        "reads " + ", ".join(GGML_NAMES[x] for x in P100_TYPE))
+    if gt is not None and t.ggml_type != gt:
         raise GGUFError(f"{g.path}: tensor {name} is {GGML_NAMES.get(t.ggml_type, t.ggml_type)}, "
-                        f"the decoder needs {GGML_NAMES.get(gt, gt)} for every weight of this model")
+                        f"the decoder needs {GGML_NAMES.get(gt, gt)}")
     if tuple(t.dims) != tuple(dims):
         raise GGUFError(f"{g.path}: tensor {name} has dims {t.dims}, expected {tuple(dims)}")
     return g.tensor_bytes(name)
 
 
-def llama_tensors(g, cfg, wt):
+# Per-layer matrices in the order of the decoder's tensor_types (P100_TT_Q .. P100_TT_DOWN).
+LAYER_MATRICES = ("attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate", "ffn_up", "ffn_down")
+
+
+def llama_tensors(g, cfg):
     """Check every tensor the decoder reads (name, format, dims) before any
     device work; returns the name of the LM head tensor (`output.weight`, or
-    `token_embd.weight` when the two are tied)."""
+    `token_embd.weight` when the two are tied) and the tensor_types list
+    (p100 formats: embedding, LM head, then each layer's LAYER_MATRICES)."""
     H, hd, F, V = cfg["hidden"], cfg["head_dim"], cfg["ffn"], cfg["vocab"]
     nq, nkv = cfg["n_head"], cfg["n_head_kv"]
-    need = [("token_embd.weight", wt, (H, V)), ("output_norm.weight", GGML_F32, (H,))]
     lm = "output.weight" if "output.weight" in g.tensors else "token_embd.weight"
-    need.append((lm, wt, (H, V)))
+    need = [("token_embd.weight", None, (H, V)), (lm, None, (H, V)), ("output_norm.weight", GGML_F32, (H,))]
+    dims = {"attn_q": (H, nq * hd), "attn_k": (H, nkv * hd), "attn_v": (H, nkv * hd), "attn_output": (nq * hd, H),
+            "ffn_gate": (H, F), "ffn_up": (H, F), "ffn_down": (F, H)}
     for l in range(cfg["n_layer"]):
         b = f"blk.{l}."
-        need += [(b + "attn_norm.weight", GGML_F32, (H,)), (b + "ffn_norm.weight", GGML_F32, (H,)),
-                 (b + "attn_q.weight", wt, (H, nq * hd)), (b + "attn_k.weight", wt, (H, nkv * hd)),
-                 (b + "attn_v.weight", wt, (H, nkv * hd)), (b + "attn_output.weight", wt, (nq * hd, H)),
-                 (b + "ffn_gate.weight", wt, (H, F)), (b + "ffn_up.weight", wt, (H, F)),
-                 (b + "ffn_down.weight", wt, (F, H))]
-    for name, gt, dims in need:
-        _check(g, name, gt, dims)
-    return lm
+        need += [(b + "attn_norm.weight", GGML_F32, (H,)), (b + "ffn_norm.weight", GGML_F32, (H,))]
+        need += [(b + m + ".weight", None, dims[m]) for m in LAYER_MATRICES]
+    for name, gt, d in need:
+        _check(g, name, gt, d)
+    types = [P100_TYPE[g.tensors[n].ggml_type] for n in ("token_embd.weight", lm)]
+    for l in range(cfg["n_layer"]):
+        types += [P100_TYPE[g.tensors[f"blk.{l}.{m}.weight"].ggml_type] for m in LAYER_MATRICES]
+    return lm, types
 
 
 def load_llama(path, tp=None, max_ctx=None, kv_type=0, flags=0):
@@ -299,10 +311,10 @@ def load_llama(path, tp=None, max_ctx=None, kv_type=0, flags=0):
         T_WGATE_UP, T_WO, T_WQKV
     from .tp import k_shard, row_shard, split_range
     with GGUFFile(path) as g:
-        kw, wt = llama_config(g, max_ctx, kv_type, flags)
-        lm = llama_tensors(g, kw, wt)
-        c = LlamaConfig(**kw)
-        qt = P100_TYPE[wt]
+        kw, _ = llama_config(g, max_ctx, kv_type, flags)
+        lm, types = llama_tensors(g, kw)
+        uniform = all(t == types[0] for t in types)
+        c = LlamaConfig(**kw, tensor_types=None if uniform else types)
         H, hd, F, V = c.hidden, c.head_dim, c.ffn, c.vocab
         nq, nkv = c.n_head, c.n_head_kv
         ntp = tp.size if tp is not None else 1
@@ -316,11 +328,15 @@ def load_llama(path, tp=None, max_ctx=None, kv_type=0, flags=0):
                     raise GGUFError(f"{path}: {data.size} bytes for a decoder tensor of {nbytes}")
                 dec.write(ptr, data)
 
-            put(T_EMBED, 0, _check(g, "token_embd.weight", wt, (H, V)))
+            def mat(name, dims):
+                """(bytes, p100 format) of a matrix tensor, checked."""
+                return _check(g, name, None, dims), P100_TYPE[g.tensors[name].ggml_type]
+
+            put(T_EMBED, 0, _check(g, "token_embd.weight", None, (H, V)))
             put(T_OUT_NORM, 0, _check(g, "output_norm.weight", GGML_F32, (H,)))
             v0 = dec.vocab_offset
             vn = dec.tensor(T_LM_HEAD)[2]
-            put(T_LM_HEAD, 0, row_shard(_check(g, lm, wt, (H, V)), qt, V, H, v0, v0 + vn))
+            put(T_LM_HEAD, 0, row_shard(*mat(lm, (H, V)), V, H, v0, v0 + vn))
             q0, q1 = split_range(nq * hd, ntp, rank, hd)
             k0, k1 = split_range(nkv * hd, ntp, rank, hd)
             f0, f1 = split_range(F, ntp, rank, 256 if ntp > 1 else 1)
@@ -328,15 +344,16 @@ def load_llama(path, tp=None, max_ctx=None, kv_type=0, flags=0):
                 b = f"blk.{l}."
                 put(T_ATTN_NORM, l, _check(g, b + "attn_norm.weight", GGML_F32, (H,)))
                 put(T_FFN_NORM, l, _check(g, b + "ffn_norm.weight", GGML_F32, (H,)))
-                wq = row_shard(_check(g, b + "attn_q.weight", wt, (H, nq * hd)), qt, nq * hd, H, q0, q1)
-                wk = row_shard(_check(g, b + "attn_k.weight", wt, (H, nkv * hd)), qt, nkv * hd, H, k0, k1)
-                wv = row_shard(_check(g, b + "attn_v.weight", wt, (H, nkv * hd)), qt, nkv * hd, H, k0, k1)
+                # fused matrices: each range in its own format, one after the other
+                wq = row_shard(*mat(b + "attn_q.weight", (H, nq * hd)), nq * hd, H, q0, q1)
+                wk = row_shard(*mat(b + "attn_k.weight", (H, nkv * hd)), nkv * hd, H, k0, k1)
+                wv = row_shard(*mat(b + "attn_v.weight", (H, nkv * hd)), nkv * hd, H, k0, k1)
                 put(T_WQKV, l, np.concatenate([wq, wk, wv]))
-                put(T_WO, l, k_shard(_check(g, b + "attn_output.weight", wt, (nq * hd, H)), qt, H, nq * hd, q0, q1))
-                wg = row_shard(_check(g, b + "ffn_gate.weight", wt, (H, F)), qt, F, H, f0, f1)
-                wu = row_shard(_check(g, b + "ffn_up.weight", wt, (H, F)), qt, F, H, f0, f1)
+                put(T_WO, l, k_shard(*mat(b + "attn_output.weight", (nq * hd, H)), H, nq * hd, q0, q1))
+                wg = row_shard(*mat(b + "ffn_gate.weight", (H, F)), F, H, f0, f1)
+                wu = row_shard(*mat(b + "ffn_up.weight", (H, F)), F, H, f0, f1)
                 put(T_WGATE_UP, l, np.concatenate([wg, wu]))
-                put(T_WDOWN, l, k_shard(_check(g, b + "ffn_down.weight", wt, (F, H)), qt, H, F, f0, f1))
+                put(T_WDOWN, l, k_shard(*mat(b + "ffn_down.weight", (F, H)), H, F, f0, f1))
         except BaseException:
             dec.close()
             raise

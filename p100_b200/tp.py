@@ -21,8 +21,8 @@ from __future__ import annotations
 
 from dataclasses import dataclass
 
-BLOCK_ELEMS = {0: 32, 1: 32, 2: 256}
-BLOCK_BYTES = {0: 18, 1: 34, 2: 144}
+BLOCK_ELEMS = {0: 32, 1: 32, 2: 256, 3: 256, 4: 256}
+BLOCK_BYTES = {0: 18, 1: 34, 2: 144, 3: 176, 4: 210}
 
 
 def split_range(total, parts, rank, align=1):

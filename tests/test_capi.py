@@ -33,7 +33,7 @@ def test_exports_every_declared_symbol(lib):
 
 
 def test_sizes_and_versions(lib):
-    assert lib.p100_abi_version() == 2
+    assert lib.p100_abi_version() == 3
     assert [lib.p100_block_elems(t) for t in (0, 1, 2, 3, 4, 9)] == [32, 32, 256, 256, 256, -1]
     assert [lib.p100_block_bytes(t) for t in (0, 1, 2, 3, 4, 9)] == [18, 34, 144, 176, 210, -1]
     assert lib.p100_weight_bytes(P.Q4_0, 14336, 4096) == 33030144

@@ -1,7 +1,9 @@
 """GGUF files (p100_b200/gguf.py) on CPU: the writer and reader agree on
 every metadata type, tensor bytes and the data alignment; a llama file
-yields the decoder configuration; malformed or mixed-format files are
-rejected with the reason."""
+yields the decoder configuration and each matrix's format (files that mix
+formats, as llama.cpp's Q4_K_M files do, included); malformed files and
+matrices in formats the decoder does not read are rejected with the
+reason."""
 import struct
 
 import numpy as np
@@ -77,8 +79,9 @@ def test_llama_config(tmp_path, qtype):
         assert cfg == dict(n_layer=2, hidden=512, n_head=8, n_head_kv=2, head_dim=64, ffn=512, vocab=300,
                            max_ctx=1024, rope_theta=500000.0, norm_eps=pytest.approx(1e-5), wtype=qtype, flags=0,
                            kv_type=0)
-        lm = gguf.llama_tensors(g, cfg, wt)
+        lm, types = gguf.llama_tensors(g, cfg)
         assert lm == ("token_embd.weight" if qtype == W.Q8_0 else "output.weight")
+        assert wt == gguf.GGML_OF_P100[qtype] and types == [qtype] * (2 + 7 * 2)
 
 
 def test_rejections(tmp_path):
@@ -92,16 +95,49 @@ def test_rejections(tmp_path):
     (tmp_path / "cut.gguf").write_bytes(data[:len(data) // 2])
     with pytest.raises(gguf.GGUFError, match="past the end|truncated"):
         gguf.GGUFFile(str(tmp_path / "cut.gguf"))
-    # a Q4_K_M-style mix: one tensor in Q6_K
+    # a matrix in a format the mat-vec does not read (F16)
     meta, t = llama_tensors(W.Q4_K)
-    t = [(n, gguf.GGML_Q6_K, d, W.weights(W.Q6_K, d[1], d[0], seed=5)) if n == "blk.1.ffn_down.weight"
+    t = [(n, gguf.GGML_F16, d, np.zeros(d[0] * d[1], np.float16)) if n == "blk.1.ffn_down.weight"
          else (n, gt, d, x) for n, gt, d, x in t]
     gguf.write_gguf(p, meta, t)
     with gguf.GGUFFile(str(p)) as g:
         cfg, wt = gguf.llama_config(g)
-        with pytest.raises(gguf.GGUFError, match="blk.1.ffn_down.weight is Q6_K"):
-            gguf.llama_tensors(g, cfg, wt)
+        with pytest.raises(gguf.GGUFError, match="blk.1.ffn_down.weight is F16"):
+            gguf.llama_tensors(g, cfg)
     meta["general.architecture"] = "qwen2"
     gguf.write_gguf(p, meta, t)
     with gguf.GGUFFile(str(p)) as g, pytest.raises(gguf.GGUFError, match="architecture"):
         gguf.llama_config(g)
+
+
+def test_mixed_formats(tmp_path):
+    """A Q4_K_M-style file: Q4_K, with attn_v and ffn_down of layer 1 and the
+    output matrix in Q6_K and one ffn_up in Q5_K: each matrix's format lands
+    at its tensor_types index."""
+    meta, t = llama_tensors(W.Q4_K)
+    swap = {"blk.1.attn_v.weight": W.Q6_K, "blk.1.ffn_down.weight": W.Q6_K, "output.weight": W.Q6_K,
+            "blk.0.ffn_up.weight": W.Q5_K}
+    t = [(n, gguf.GGML_OF_P100[swap[n]], d, W.weights(swap[n], d[1], d[0], seed=5)) if n in swap
+         else (n, gt, d, x) for n, gt, d, x in t]
+    p = tmp_path / "mixed.gguf"
+    gguf.write_gguf(p, meta, t)
+    with gguf.GGUFFile(str(p)) as g:
+        cfg, wt = gguf.llama_config(g)
+        assert wt == gguf.GGML_Q4_K and cfg["wtype"] == W.Q4_K
+        lm, types = gguf.llama_tensors(g, cfg)
+    want = [W.Q4_K] * (2 + 7 * 2)
+    want[1] = W.Q6_K                                           # output
+    want[2 + 7 * 0 + gguf.LAYER_MATRICES.index("ffn_up")] = W.Q5_K
+    want[2 + 7 * 1 + gguf.LAYER_MATRICES.index("attn_v")] = W.Q6_K
+    want[2 + 7 * 1 + gguf.LAYER_MATRICES.index("ffn_down")] = W.Q6_K
+    assert lm == "output.weight" and types == want
+
+
+def test_tp_shards_of_k_quants():
+    """Row and K slices of Q5_K / Q6_K matrices fall on their 256-value blocks."""
+    from p100_b200 import tp
+    for qt, bb in ((W.Q5_K, 176), (W.Q6_K, 210)):
+        w = W.weights(qt, 4, 1024, seed=2)
+        assert tp.row_shard(w, qt, 4, 1024, 1, 3).size == 2 * 4 * bb
+        ks = tp.k_shard(w, qt, 4, 1024, 256, 768).reshape(4, 2 * bb)
+        assert np.array_equal(ks, w.reshape(4, 4 * bb)[:, bb:3 * bb])
