@@ -365,10 +365,55 @@ def kv_quant_section(torch, P, stream):
 DECODE_MODELS = {   # BASELINE configs 4 and 5: Llama-3 8B / 70B shapes, random-init Q4_0
     "llama3-8b": dict(n_layer=32, hidden=4096, n_head=32, n_head_kv=8, head_dim=128, ffn=14336, vocab=128256,
                       ctx=4096),
+    # the 8B shape with llama.cpp's Q4_K_M format mix (q4_k_m_types)
+    "llama3-8b-q4_k_m": dict(n_layer=32, hidden=4096, n_head=32, n_head_kv=8, head_dim=128, ffn=14336,
+                             vocab=128256, ctx=4096, mix="q4_k_m"),
     "llama3-70b": dict(n_layer=80, hidden=8192, n_head=64, n_head_kv=8, head_dim=128, ffn=28672, vocab=128256,
                        ctx=8192),
 }
 DECODE_STEPS, DECODE_WARMUP = 48, 4
+
+
+def q4_k_m_types(P, n_layer):
+    """Per-tensor formats of a llama.cpp Q4_K_M file: Q4_K, with attn_v and
+    ffn_down in Q6_K in the first and last eighth of the layers and in every
+    third layer between, and the output matrix in Q6_K."""
+    t = [P.Q4_K] * P.dec_tensor_types(n_layer)
+    t[P.TT_LM_HEAD] = P.Q6_K
+    e = n_layer // 8
+    for l in range(n_layer):
+        if l < e or l >= n_layer - e or (l - e) % 3 == 2:
+            t[P.tt_layer(l, P.TT_V)] = P.Q6_K
+            t[P.tt_layer(l, P.TT_DOWN)] = P.Q6_K
+    return t
+
+
+def ktypes_section(torch, P, stream):
+    """Batch-1 mat-vec of the K-quant formats (the team kernel) at the 8B
+    decode shapes: GB/s of weight + activation bytes per launch, launches
+    chained with PDL over weight copies rotating beyond 3x L2."""
+    peak = peak_gbs()[0]
+    out = {}
+    shapes = (("gate_up", 4096, 28672), ("down", 14336, 4096), ("lm_head", 4096, 128256))
+    for qt, qname in ((P.Q4_K, "q4_k"), (P.Q5_K, "q5_k"), (P.Q6_K, "q6_k")):
+        out[qname] = {}
+        for name, k, rows in shapes:
+            nbytes_w = rows * (k // P.BLOCK_ELEMS[qt]) * P.BLOCK_BYTES[qt]
+            copies = max(2, int(np.ceil(3 * L2_BYTES / nbytes_w)) + 1)
+            ws = [torch.randint(0, 256, (nbytes_w,), dtype=torch.uint8, device="cuda") for _ in range(copies)]
+            xq = P.q8_1_quantize(torch.from_numpy(W.activations(1, k, seed=k)).cuda())
+            y = torch.empty(1, rows, device="cuda")
+            reps = max(4, 32 // copies)
+            g = capture(torch, lambda: [P.qmv(qt, ws[r % copies], rows, k, xq, 1, y=y, flags=P.QMV_PDL)
+                                        for r in range(copies * reps)])
+            time_graphs(torch, [g], 2, stream)
+            n = 10
+            us = time_graphs(torch, [g], n, stream) / (n * copies * reps) * 1e3
+            nbytes = W.qmv_algorithmic_bytes(qt, rows, k, 1)
+            out[qname][f"{name} {k}x{rows}"] = {"us": round(us, 3), "GB/s": round(nbytes / (us / 1e6) / 1e9, 1),
+                                                "frac": round(nbytes / (us / 1e6) / 1e9 / peak, 4)}
+            del ws, g
+    return out
 
 
 def decode_section(torch, P, stream, rank, world, dist, max_over_ranks):
@@ -388,8 +433,10 @@ def decode_section(torch, P, stream, rank, world, dist, max_over_ranks):
     try:
         for name, m in DECODE_MODELS.items():
             ctx = m["ctx"]
+            mix = q4_k_m_types(P, m["n_layer"]) if m.get("mix") == "q4_k_m" else None
             cfg = P.LlamaConfig(m["n_layer"], m["hidden"], m["n_head"], m["n_head_kv"], m["head_dim"], m["ffn"],
-                                m["vocab"], ctx + DECODE_WARMUP + 2 * DECODE_STEPS + 8)
+                                m["vocab"], ctx + DECODE_WARMUP + 2 * DECODE_STEPS + 8,
+                                wtype=P.Q4_K if mix else P.Q4_0, tensor_types=mix)
             dec = P.Decoder(cfg, tp)
             try:
                 dec.init_random(20261201)
@@ -668,6 +715,7 @@ def main():
     fa = fa_section(torch, P, stream) if rank == 0 else None
     h16 = h16_section(torch, P, stream) if rank == 0 else None
     kvq = kv_quant_section(torch, P, stream) if rank == 0 else None
+    kq = ktypes_section(torch, P, stream) if rank == 0 else None
     P.check(P.device_error())
     decode = decode_section(torch, P, stream, rank, world, dist, max_over_ranks) if not args.no_decode else None
 
@@ -698,6 +746,7 @@ def main():
         "fa_decode": fa,
         "h16_qmv": h16,
         "quantised_kv": kvq,
+        "ktypes_qmv": kq,
         "decode": decode,
         "clocks": clocks.summary(),
         "checksum": round(checksum, 3),

@@ -190,20 +190,23 @@ struct TeamPlan {
 // The batch-1 kernel: a lane per 256-weight column group, one row per team
 // per stage.  Needs 16-byte aligned weights and activations and k % 256 == 0.
 bool plan_team(int type, const void* w, const void* xq, int rows, int k, int batch, int sms, TeamPlan& plan) {
-    if (!ref_type(type)) return false;
+    if (!known_type(type)) return false;
     if (batch != 1 || k % 256 || reinterpret_cast<uintptr_t>(w) % 16 || reinterpret_cast<uintptr_t>(xq) % 16)
         return false;
     const int ngroups = k / 256;
     const int team = qmvt::team_lanes(ngroups);
     if (team > qmvt::kConsumers * 32) return false;
     const size_t row_bytes = size_t(k / elems_of(type)) * bytes_of(type);
+    if (row_bytes % 16) return false;   // stages are 16-byte bulk copies (Q6_K: k a multiple of 2048)
+    // Q6_K groups are read as aligned words that run up to 6 bytes past the group
+    const size_t tail = type == P100_Q6_K ? 16 : 0;
     const int teams = qmvt::kConsumers * 32 / team;
     const size_t slot = round128(size_t(teams) * row_bytes);
     const size_t part_off = 384;   // 2 x 8 ring mbarriers + the activation one; the fused norm's partials at 256
     const size_t act_off = part_off + round128(size_t(2) * teams * std::max(1, team / 32) * 4);
     const size_t ring_off = act_off + round128(size_t(k / 32) * 36);   // the Q8_1 row
-    if (ring_off + 2 * slot > size_t(qmvt::kSmemLimit)) return false;
-    const int nslot = int(std::min<size_t>(qmvt::kMaxSlots, (qmvt::kSmemLimit - ring_off) / slot));
+    if (ring_off + 2 * slot + tail > size_t(qmvt::kSmemLimit)) return false;
+    const int nslot = int(std::min<size_t>(qmvt::kMaxSlots, (qmvt::kSmemLimit - ring_off - tail) / slot));
     plan.p.rows = rows;
     plan.p.k = k;
     plan.p.row_bytes = int(row_bytes);
@@ -215,7 +218,7 @@ bool plan_team(int type, const void* w, const void* xq, int rows, int k, int bat
     plan.p.part_off = int(part_off);
     plan.p.act_off = int(act_off);
     plan.p.ring_off = int(ring_off);
-    plan.smem = ring_off + size_t(nslot) * slot;
+    plan.smem = ring_off + size_t(nslot) * slot + tail;
     plan.grid = std::max(1, std::min(sms, (rows + teams - 1) / teams));
     return true;
 }
@@ -466,7 +469,9 @@ p100_status run_qmv(int type, const void* w, int rows, int k, const void* xq, in
         switch (type) {
             case P100_Q4_0: return launch_team_type<P100_Q4_0>(tplan, batch, pdl, stream);
             case P100_Q8_0: return launch_team_type<P100_Q8_0>(tplan, batch, pdl, stream);
-            default: return launch_team_type<P100_Q4_K>(tplan, batch, pdl, stream);
+            case P100_Q4_K: return launch_team_type<P100_Q4_K>(tplan, batch, pdl, stream);
+            case P100_Q5_K: return launch_team_type<P100_Q5_K>(tplan, batch, pdl, stream);
+            default: return launch_team_type<P100_Q6_K>(tplan, batch, pdl, stream);
         }
     }
     MmaPlan mplan;
@@ -544,7 +549,9 @@ p100_status run_qmv_norm(int type, const void* w, int rows, int k, const float* 
     switch (type) {
         case P100_Q4_0: return launch_team_type<P100_Q4_0>(plan, 1, pdl, stream);
         case P100_Q8_0: return launch_team_type<P100_Q8_0>(plan, 1, pdl, stream);
-        default: return launch_team_type<P100_Q4_K>(plan, 1, pdl, stream);
+        case P100_Q4_K: return launch_team_type<P100_Q4_K>(plan, 1, pdl, stream);
+        case P100_Q5_K: return launch_team_type<P100_Q5_K>(plan, 1, pdl, stream);
+        default: return launch_team_type<P100_Q6_K>(plan, 1, pdl, stream);
     }
 }
 

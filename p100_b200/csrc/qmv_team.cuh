@@ -76,7 +76,8 @@ __device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
 struct GroupAct {
     int q[64];     // int8 codes, four per word, block-major
     float dx[8];   // fp16 block scale
-    float m[8];    // Q4_0: -8 * fp16 block sum;  Q4_K: sum of the block's codes;  Q8_0: unused
+    float m[8];    // Q4_0: -8 * fp16 block sum;  Q4_K, Q5_K: sum of the block's codes;  Q8_0: unused
+    int s16[16];   // Q6_K: sums of the codes of each 16 values (its scales are per 16)
 };
 
 struct Params {
@@ -181,14 +182,83 @@ __device__ __forceinline__ void load_group_act(const uint8_t* xs, int g, GroupAc
             sumq = __dp4a(a.q[8 * b + i], 0x01010101, sumq);
         }
         a.dx[b] = half_lo(u[9 * b]);
-        a.m[b] = TYPE == P100_Q4_0 ? -8.0f * half_hi(u[9 * b]) : TYPE == P100_Q4_K ? float(sumq) : 0.f;
+        a.m[b] = TYPE == P100_Q4_0                         ? -8.0f * half_hi(u[9 * b])
+                 : TYPE == P100_Q4_K || TYPE == P100_Q5_K ? float(sumq)
+                                                          : 0.f;
+        if (TYPE == P100_Q6_K) {
+            int lo = 0, hi = 0;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                lo = __dp4a(a.q[8 * b + i], 0x01010101, lo);
+                hi = __dp4a(a.q[8 * b + 4 + i], 0x01010101, hi);
+            }
+            a.s16[2 * b] = lo;
+            a.s16[2 * b + 1] = hi;
+        }
     }
+}
+
+// Bytes of one 256-value group in a row: eight Q4_0 / Q8_0 blocks or one
+// K-quant super-block.
+template <int TYPE>
+__host__ __device__ constexpr int group_bytes() {
+    return TYPE == P100_Q4_0 ? 144 : TYPE == P100_Q8_0 ? 272 : TYPE == P100_Q4_K ? 144 : TYPE == P100_Q5_K ? 176 : 210;
+}
+
+// Q6_K super-block (ggml block_q6_K: ql[128], qh[64], int8 scales[16], fp16
+// d) dotted with its group's activations.  A group starts 2-byte aligned
+// only (210-byte stride), so it is read as 54 aligned words from the word
+// boundary at or below it and re-aligned with a funnel shift; the last word
+// read ends at most 6 bytes past the group (the ring keeps 16 bytes of slack
+// after its last slot).  Value v of half n (v = 128n + 32c + l, c = 0..3,
+// l = 0..31) has code (nibble c>>1 of ql[64n + 32(c&1) + l]) | (bits 2c..2c+1
+// of qh[32n + l]) << 4, minus 32, and scale scales[v / 16]; per 32-value
+// block b the integer sum sc_lo*(dot_lo - 32 s_lo) + sc_hi*(dot_hi - 32
+// s_hi) is exact, then scaled by dx_b and finally by d.
+__device__ __forceinline__ float group_dot_q6k(const uint8_t* __restrict__ grp, const GroupAct& a, float acc) {
+    const uintptr_t addr = reinterpret_cast<uintptr_t>(grp);
+    const uint32_t* base = reinterpret_cast<const uint32_t*>(addr & ~uintptr_t(3));
+    const uint32_t sh = static_cast<uint32_t>(addr & 3) * 8;   // 0 or 16
+    uint32_t w[53];
+    uint32_t prev = base[0];
+#pragma unroll
+    for (int i = 0; i < 53; ++i) {
+        const uint32_t next = base[i + 1];
+        w[i] = __funnelshift_r(prev, next, sh);
+        prev = next;
+    }
+    // words: ql 0..31, qh 32..47, scales 48..51, d = low half of word 52
+    float sd = 0.f;
+#pragma unroll
+    for (int n = 0; n < 2; ++n) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const int b = 4 * n + c;   // the 32-value block
+            int lo = 0, hi = 0;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const uint32_t ql = w[16 * n + 8 * (c & 1) + i], qh = w[32 + 8 * n + i];
+                const uint32_t code = ((ql >> (4 * (c >> 1))) & 0x0f0f0f0fu) | (((qh >> (2 * c)) & 0x03030303u) << 4);
+                if (i < 4) lo = __dp4a(static_cast<int>(code), a.q[8 * b + i], lo);
+                else hi = __dp4a(static_cast<int>(code), a.q[8 * b + i], hi);
+            }
+            const uint32_t scw = w[48 + 2 * n + (c >> 1)];   // scales 8n + 2c, 8n + 2c + 1
+            const int sc_lo = static_cast<int8_t>((scw >> (16 * (c & 1))) & 255);
+            const int sc_hi = static_cast<int8_t>((scw >> (16 * (c & 1) + 8)) & 255);
+            const int isum = sc_lo * (lo - 32 * a.s16[2 * b]) + sc_hi * (hi - 32 * a.s16[2 * b + 1]);
+            sd = fmaf(a.dx[b], float(isum), sd);
+        }
+    }
+    return fmaf(half_lo(w[52]), sd, acc);
 }
 
 // acc += (row's group at grp) . (the group's activations)
 template <int TYPE>
 __device__ __forceinline__ float group_dot(const uint8_t* __restrict__ grp, const GroupAct& a, float acc) {
-    constexpr int kWords = TYPE == P100_Q8_0 ? 68 : 36;
+    if constexpr (TYPE == P100_Q6_K) {
+        return group_dot_q6k(grp, a, acc);
+    } else {
+    constexpr int kWords = group_bytes<TYPE>() / 4;
     uint32_t w[kWords];
 #pragma unroll
     for (int i = 0; i < kWords / 4; ++i) {
@@ -237,7 +307,10 @@ __device__ __forceinline__ float group_dot(const uint8_t* __restrict__ grp, cons
         }
     } else {
         // One super-block: w[0] = d | dmin, w[1..3] = twelve 6-bit scale/min
-        // bytes, w[4 + 8q + i] = nibbles of sub-blocks 2q (low) and 2q+1 (high).
+        // bytes, then (Q4_K) w[4 + 8q + i] = nibbles of sub-blocks 2q (low)
+        // and 2q+1 (high); Q5_K puts qh[32] at words 4..11 (bit j of qh[l]
+        // is the 16 of value l of sub-block j) and the nibbles at 12 + 8q + i.
+        constexpr int kQs = TYPE == P100_Q5_K ? 12 : 4;
         float sd = 0.f, sm = 0.f;
 #pragma unroll
         for (int qq = 0; qq < 4; ++qq) {
@@ -259,22 +332,36 @@ __device__ __forceinline__ float group_dot(const uint8_t* __restrict__ grp, cons
             int l0 = 0, l1 = 0, h0 = 0, h1 = 0;
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                const uint32_t n0 = w[4 + 8 * qq + i], n1 = w[8 + 8 * qq + i];
-                l0 = __dp4a(static_cast<int>(n0 & 0x0f0f0f0fu), a.q[8 * j0 + i], l0);
-                l1 = __dp4a(static_cast<int>(n1 & 0x0f0f0f0fu), a.q[8 * j0 + 4 + i], l1);
-                h0 = dp4a_us(n0 & 0xf0f0f0f0u, a.q[8 * j1 + i], h0);
-                h1 = dp4a_us(n1 & 0xf0f0f0f0u, a.q[8 * j1 + 4 + i], h1);
+                const uint32_t n0 = w[kQs + 8 * qq + i], n1 = w[kQs + 4 + 8 * qq + i];
+                if constexpr (TYPE == P100_Q5_K) {
+                    // five-bit codes: nibble | (bit j of qh[l]) << 4
+                    const uint32_t b0 = w[4 + i], b1 = w[8 + i];
+                    const uint32_t c00 = (n0 & 0x0f0f0f0fu) | (((b0 >> j0) & 0x01010101u) << 4);
+                    const uint32_t c01 = (n1 & 0x0f0f0f0fu) | (((b1 >> j0) & 0x01010101u) << 4);
+                    const uint32_t c10 = ((n0 >> 4) & 0x0f0f0f0fu) | (((b0 >> j1) & 0x01010101u) << 4);
+                    const uint32_t c11 = ((n1 >> 4) & 0x0f0f0f0fu) | (((b1 >> j1) & 0x01010101u) << 4);
+                    l0 = __dp4a(static_cast<int>(c00), a.q[8 * j0 + i], l0);
+                    l1 = __dp4a(static_cast<int>(c01), a.q[8 * j0 + 4 + i], l1);
+                    h0 = __dp4a(static_cast<int>(c10), a.q[8 * j1 + i], h0);
+                    h1 = __dp4a(static_cast<int>(c11), a.q[8 * j1 + 4 + i], h1);
+                } else {
+                    l0 = __dp4a(static_cast<int>(n0 & 0x0f0f0f0fu), a.q[8 * j0 + i], l0);
+                    l1 = __dp4a(static_cast<int>(n1 & 0x0f0f0f0fu), a.q[8 * j0 + 4 + i], l1);
+                    h0 = dp4a_us(n0 & 0xf0f0f0f0u, a.q[8 * j1 + i], h0);
+                    h1 = dp4a_us(n1 & 0xf0f0f0f0u, a.q[8 * j1 + 4 + i], h1);
+                }
             }
             // sum_j dx_j * (dot_j * sc_j) and sum_j dx_j * (sumq_j * mn_j)
             // (qmv_model.cpp:175-178)
             sd = fmaf(a.dx[j0], float((l0 + l1) * sc0), sd);
-            sd = fmaf(a.dx[j1], float(((h0 + h1) >> 4) * sc1), sd);
+            sd = fmaf(a.dx[j1], float(((h0 + h1) >> (TYPE == P100_Q5_K ? 0 : 4)) * sc1), sd);
             sm = fmaf(a.dx[j0], a.m[j0] * float(mn0), sm);
             sm = fmaf(a.dx[j1], a.m[j1] * float(mn1), sm);
         }
         acc = fmaf(half_lo(w[0]), sd, fmaf(-half_hi(w[0]), sm, acc));
     }
     return acc;
+    }
 }
 
 // NG = k / 256 when compiled for one hidden size, 0 for any (runtime shape).
@@ -285,7 +372,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_team_kernel(const Params p) {
     uint64_t* empty = full + kMaxSlots;
     float* partial = reinterpret_cast<float*>(smem + p.part_off);   // [2][teams][warps per team]
     uint8_t* ring = smem + p.ring_off;
-    constexpr int kGroupBytes = TYPE == P100_Q8_0 ? 272 : 144;
+    constexpr int kGroupBytes = group_bytes<TYPE>();
     const int ngroups = NG > 0 ? NG : p.ngroups;
     const int team_size = NG > 0 ? team_lanes(NG) : p.team;
     const int teams = NG > 0 ? kConsumers * 32 / team_lanes(NG) : p.teams;

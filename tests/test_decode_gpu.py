@@ -50,7 +50,7 @@ def test_rmsnorm_q8_1_bit_exact(cuda, orc, k, batch, with_delta):
         assert np.array_equal(got_q[b], oq)
 
 
-@pytest.mark.parametrize("qtype", [P.Q4_0, P.Q8_0, P.Q4_K])
+@pytest.mark.parametrize("qtype", [P.Q4_0, P.Q8_0, P.Q4_K, P.Q5_K, P.Q6_K])
 @pytest.mark.parametrize("k,rows,with_delta", [(4096, 6144, True), (8192, 1000, True), (4096, 300, False)])
 def test_qmv_rmsnorm_equals_two_calls(cuda, qtype, k, rows, with_delta):
     """The RMSNorm fused into the mat-vec (p100_qmv_rmsnorm) gives the bytes of

@@ -1,5 +1,6 @@
-"""ggml's Q5_K and Q6_K weights on B200 (p100_dequantize, p100_qmv on the
-general mat-vec kernel) against the CPU restatement (oracle/p100_oracle.cpp,
+"""ggml's Q5_K and Q6_K weights on B200 (p100_dequantize, p100_qmv: the team
+kernel at batch 1 where a row is whole 16-byte units, the general mat-vec
+kernel otherwise) against the CPU restatement (oracle/p100_oracle.cpp,
 itself checked against ggml's dequantisation loops in
 tests/test_oracle_ktypes.py).  Dequantisation is bit-exact; the mat-vec is
 within the reference's normalised q81 tolerance of the oracle's q81 dot (and
@@ -38,6 +39,25 @@ def test_qmv_within_tolerance(cuda, orc, qtype, rows, k, batch):
     assert err <= 1e-5, err   # the same slab arithmetic, summed in another order
     exact = x.astype(np.float64) @ orc.dequantize(qtype, w, rows, k).astype(np.float64).T
     assert_qmv_close(y, exact, wn, x, tol=QMV_NORM_TOL)
+    assert P.device_error() == P.OK
+
+
+# Batch 1 on the team kernel: k = 4096 / 8192 / 14336 / 28672 (compiled
+# group counts 16, 32, 56, 112; teams of 16 and 32 lanes, of 2 and 4 warps),
+# 6144 (the runtime-shaped variant), row counts that leave a partial last
+# stage; and shapes that fall back to the general kernel (Q6_K rows of k =
+# 1280 are 1050 bytes, not whole 16-byte units).
+@pytest.mark.parametrize("qtype", KTYPES)
+@pytest.mark.parametrize("rows,k", [(4099, 4096), (1000, 8192), (777, 14336), (301, 28672), (515, 6144),
+                                    (20000, 4096), (33, 1280)])
+def test_qmv_batch1_team_kernel(cuda, orc, qtype, rows, k):
+    w = W.weights(qtype, rows, k, seed=5 * qtype + rows)
+    x = W.activations(1, k, seed=rows)
+    xq = P.q8_1_quantize(dev(cuda, x))
+    y = P.qmv(qtype, dev(cuda, w), rows, k, xq, 1).cpu().numpy()
+    wn = row_norms(orc, qtype, w, rows, k)
+    err = assert_qmv_close(y, q81_reference(orc, qtype, w, rows, k, x).astype(np.float64), wn, x)
+    assert err <= 1e-5, err
     assert P.device_error() == P.OK
 
 
