@@ -113,6 +113,22 @@ p100_status p100_qmv(int type, const void* w, int rows, int k, const void* x_q8_
                             by it.  Activations are read only after it ends. */
 p100_status p100_qmv_ex(int type, const void* w, int rows, int k, const void* x_q8_1,
                         int batch, float* y, unsigned flags, p100_stream_t stream);
+/* p100_q8_1_quantize with P100_QMV_PDL available: the quantiser launched as
+ * a programmatic dependent of the previous kernel (it reads x after that
+ * kernel ends), so its launch overlaps that kernel's tail. */
+p100_status p100_q8_1_quantize_ex(const float* x, void* x_q8_1, int k, int batch, unsigned flags,
+                                  p100_stream_t stream);
+/* y = W . Q8_1(x) from fp32 activations x [batch][k], the bits of
+ * p100_q8_1_quantize followed by p100_qmv_ex.  With x_q8_1
+ * (p100_q8_1_bytes(k, batch)): the quantiser (flags apply to it) writes the
+ * Q8_1 rows there and the mat-vec runs as its programmatic dependent.  With
+ * x_q8_1 NULL: one launch, the quantisation inside the mat-vec (every CTA
+ * quantises the row), at batch 1 on the team kernel only (16-byte aligned w
+ * and x, rows of whole 16-byte units; else P100_ERR_UNSUPPORTED).  No
+ * counterpart in the reference, whose callers quantise (prepare) before each
+ * mat-vec. */
+p100_status p100_qmv_f32(int type, const void* w, int rows, int k, const float* x, int batch,
+                         void* x_q8_1, float* y, unsigned flags, p100_stream_t stream);
 
 /* ---------------------------------------------------- h16 activation path */
 /* The FP16-activation mat-vec, qmv::h16_model (qmv_model.cpp:53-71,92-133;

@@ -92,6 +92,8 @@ def _bind(lib):
         "p100_dequantize": (ip, [ip, vp, ip, ip, vp, st]),
         "p100_qmv": (ip, [ip, vp, ip, ip, vp, ip, vp, st]),
         "p100_qmv_ex": (ip, [ip, vp, ip, ip, vp, ip, vp, C.c_uint, st]),
+        "p100_qmv_f32": (ip, [ip, vp, ip, ip, vp, ip, vp, vp, C.c_uint, st]),
+        "p100_q8_1_quantize_ex": (ip, [vp, vp, ip, ip, C.c_uint, st]),
         "p100_h16_prepare": (ip, [vp, vp, vp, ip, ip, st]),
         "p100_qmv_h16": (ip, [ip, vp, ip, ip, vp, vp, ip, ip, vp, st]),
         "p100_attn_validate": (ip, [vp, C.c_char_p, sz]),
@@ -204,15 +206,19 @@ def q8_1_bytes(k, batch=1):
     return lib().p100_q8_1_bytes(k, batch)
 
 
-def q8_1_quantize(x, out=None, stream=None):
-    """Q8_1 blocks of x (fp32 [batch, k] on the GPU) -> uint8 [batch * k/32 * 36]."""
+def q8_1_quantize(x, out=None, stream=None, flags=0):
+    """Q8_1 blocks of x (fp32 [batch, k] on the GPU) -> uint8 [batch * k/32 * 36]
+    (p100_q8_1_quantize, or p100_q8_1_quantize_ex with flags)."""
     torch = _torch()
     x = x.contiguous()
     k = x.shape[-1]
     batch = x.numel() // k
     if out is None:
         out = torch.empty(batch * (k // 32) * Q8_1_BLOCK_BYTES, dtype=torch.uint8, device=x.device)
-    check(lib().p100_q8_1_quantize(_ptr(x), _ptr(out), k, batch, _stream(stream)))
+    if flags:
+        check(lib().p100_q8_1_quantize_ex(_ptr(x), _ptr(out), k, batch, flags, _stream(stream)))
+    else:
+        check(lib().p100_q8_1_quantize(_ptr(x), _ptr(out), k, batch, _stream(stream)))
     return out
 
 
@@ -253,6 +259,18 @@ def qmv(qtype, w, rows, k, x_q8_1, batch=1, y=None, flags=0, stream=None):
     if y is None:
         y = torch.empty(batch, rows, dtype=torch.float32, device=w.device)
     check(lib().p100_qmv_ex(qtype, _ptr(w), rows, k, _ptr(x_q8_1), batch, _ptr(y), flags, _stream(stream)))
+    return y
+
+
+def qmv_f32(qtype, w, rows, k, x, batch=1, y=None, x_q8_1=None, flags=0, stream=None):
+    """y[batch, rows] = W . Q8_1(x) for fp32 x (p100_qmv_f32): with x_q8_1,
+    the quantiser into it and the mat-vec as its programmatic dependent;
+    without, one fused launch (batch 1 on the team kernel only)."""
+    torch = _torch()
+    if y is None:
+        y = torch.empty(batch, rows, dtype=torch.float32, device=w.device)
+    check(lib().p100_qmv_f32(qtype, _ptr(w), rows, k, _ptr(x), batch, _ptr(x_q8_1), _ptr(y), flags,
+                             _stream(stream)))
     return y
 
 

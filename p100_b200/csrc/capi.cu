@@ -903,16 +903,30 @@ size_t p100_q8_1_bytes(int k, int batch) {
 }
 
 p100_status p100_q8_1_quantize(const float* x, void* x_q8_1, int k, int batch, p100_stream_t stream) {
+    return p100_q8_1_quantize_ex(x, x_q8_1, k, batch, 0u, stream);
+}
+
+p100_status p100_q8_1_quantize_ex(const float* x, void* x_q8_1, int k, int batch, unsigned flags,
+                                  p100_stream_t stream) {
     clear_error();
+    if (flags & ~P100_QMV_PDL) return set_error(P100_ERR_INVALID, "unknown flags 0x%x", flags);
     if (k <= 0 || k % 32) return set_error(P100_ERR_INVALID, "whole activation blocks required");
     if (batch <= 0 || batch > 65535) return set_error(P100_ERR_INVALID, "batch must be in 1..65535");
     if (!x || !x_q8_1) return set_error(P100_ERR_INVALID, "null buffer");
     if (reinterpret_cast<uintptr_t>(x_q8_1) % 4) return set_error(P100_ERR_INVALID, "x_q8_1 must be 4-byte aligned");
     if (p100_status st = require_sm100(nullptr, nullptr)) return st;
     const int blocks = k / 32;
-    q8_1_quantize_kernel<<<dim3((blocks + 7) / 8, batch), 256, 0, stream>>>(x, static_cast<uint8_t*>(x_q8_1), k,
-                                                                             blocks);
-    return launch_status("q8_1_quantize_kernel launch");
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((blocks + 7) / 8, batch);
+    cfg.blockDim = dim3(256);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = (flags & P100_QMV_PDL) ? 1 : 0;
+    return cuda_status(cudaLaunchKernelEx(&cfg, q8_1_quantize_kernel, x, static_cast<uint8_t*>(x_q8_1), k, blocks),
+                       "q8_1_quantize_kernel launch");
 }
 
 p100_status p100_dequantize(int type, const void* w, int rows, int k, float* out, p100_stream_t stream) {
@@ -978,6 +992,43 @@ p100_status p100_qmv(int type, const void* w, int rows, int k, const void* x_q8_
                      p100_stream_t stream) {
     clear_error();
     return run_qmv(type, w, rows, k, x_q8_1, batch, y, 0u, stream);
+}
+
+p100_status p100_qmv_f32(int type, const void* w, int rows, int k, const float* x, int batch, void* x_q8_1,
+                         float* y, unsigned flags, p100_stream_t stream) {
+    clear_error();
+    if (flags & ~P100_QMV_PDL) return set_error(P100_ERR_INVALID, "unknown flags 0x%x", flags);
+    if (!known_type(type)) return set_error(P100_ERR_INVALID, "unknown weight type %d", type);
+    if (k <= 0 || k % elems_of(type)) return set_error(P100_ERR_INVALID, "whole weight blocks required");
+    if (rows < 0) return set_error(P100_ERR_INVALID, "rows must be non-negative");
+    if (batch < 1 || batch > 16) return set_error(P100_ERR_INVALID, "batch must be in 1..16");
+    if (rows == 0) return P100_OK;
+    if (!w || !x || !y) return set_error(P100_ERR_INVALID, "null buffer");
+    if (reinterpret_cast<uintptr_t>(w) % 2) return set_error(P100_ERR_INVALID, "weights must be 2-byte aligned");
+    int sms = 0;
+    if (p100_status st = require_sm100(nullptr, &sms)) return st;
+    TeamPlan plan;
+    if (!x_q8_1 && plan_team(type, w, x, rows, k, batch, sms, plan)) {
+        plan.p.w = static_cast<const uint8_t*>(w);
+        plan.p.xq = nullptr;
+        plan.p.y = y;
+        plan.p.col0 = 0;
+        plan.p.x_f32 = x;
+        const bool pdl = (flags & P100_QMV_PDL) != 0;
+        switch (type) {
+            case P100_Q4_0: return launch_team_type<P100_Q4_0>(plan, 1, pdl, stream);
+            case P100_Q8_0: return launch_team_type<P100_Q8_0>(plan, 1, pdl, stream);
+            case P100_Q4_K: return launch_team_type<P100_Q4_K>(plan, 1, pdl, stream);
+            case P100_Q5_K: return launch_team_type<P100_Q5_K>(plan, 1, pdl, stream);
+            default: return launch_team_type<P100_Q6_K>(plan, 1, pdl, stream);
+        }
+    }
+    if (!x_q8_1)
+        return set_error(P100_ERR_UNSUPPORTED,
+                         "without x_q8_1 the quantisation is fused, which needs batch 1 on the team kernel "
+                         "(16-byte aligned w and x, rows of whole 16-byte units)");
+    if (p100_status st = p100_q8_1_quantize_ex(x, x_q8_1, k, batch, flags, stream)) return st;
+    return run_qmv(type, w, rows, k, x_q8_1, batch, y, flags | P100_QMV_PDL, stream);
 }
 
 p100_status p100_qmv_ex(int type, const void* w, int rows, int k, const void* x_q8_1, int batch, float* y,

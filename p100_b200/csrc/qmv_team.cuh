@@ -100,7 +100,26 @@ struct Params {
     float* x_out;
     const float* norm_w;
     float eps;
+    // Fused quantisation (x_f32 not null, norm_w null): the Q8_1 row is
+    // built from these fp32 activations (16-byte aligned) instead of read.
+    const float* x_f32;
 };
+
+// The Q8_1 row of p.x_f32 into xs by the 8 consumer warps: float4 chunk c
+// (values 4c..4c+3, block c / 8) by lane c % 8 of an octet; octet_q8_1_block
+// repeats q8_1_quantize_kernel's butterfly, so the bytes are that kernel's.
+__device__ __forceinline__ void quantize_row(const Params& p, uint8_t* xs) {
+    const int nc = p.k / 4;
+    const float4* xr = reinterpret_cast<const float4*>(p.x_f32);
+    for (int c0 = 0; c0 < nc; c0 += kConsumers * 32) {   // every consumer thread runs every pass
+        const int c = c0 + static_cast<int>(threadIdx.x);
+        const bool live = c < nc;
+        const float4 x = live ? xr[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float v[4] = {x.x, x.y, x.z, x.w};
+        dec::octet_q8_1_block(v, c & 7, live ? xs + size_t(c >> 3) * 36 : nullptr);
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(kConsumers * 32) : "memory");   // the whole row is written
+}
 
 // The fused RMSNorm prologue: the Q8_1 row of rmsnorm(x_in + delta) * w into
 // xs, by the 8 consumer warps (256 threads), bit-identical to
@@ -410,9 +429,11 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_team_kernel(const Params p) {
                           policy);
             }
             // the activations may come from the previous kernel (with the
-            // fused norm the consumers build them and the barrier is unused)
+            // fused norm or quantisation the consumers build them and the
+            // barrier is unused)
             pdl_wait_prior_grid();
-            if (!p.norm_w) {
+            const bool act_copy = !p.norm_w && !p.x_f32;
+            if (act_copy) {
                 asm volatile("fence.proxy.async.global;" ::: "memory");
                 const uint32_t abytes = static_cast<uint32_t>(p.k / 32 * 36);
                 mbar_arrive_expect_tx(act_bar, abytes);
@@ -434,7 +455,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_team_kernel(const Params p) {
             }
             // no copy may still be writing shared memory when the block exits
             // (normally everything has landed: the consumers needed it)
-            if (!p.norm_w) mbar_wait(act_bar, 0);
+            if (act_copy) mbar_wait(act_bar, 0);
             for (int s = max(0, issued - p.nslot); s < issued; ++s) mbar_wait(&full[s % p.nslot], (s / p.nslot) & 1);
         }
         return;
@@ -452,7 +473,11 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_team_kernel(const Params p) {
             fused_norm_row<NG>(p, smem + p.act_off, reinterpret_cast<float*>(smem + kNormScratchOff));
         }
     }
-    if (!p.norm_w) {
+    if (!p.norm_w && p.x_f32) {
+        pdl_wait_prior_grid();   // x may come from an earlier kernel
+        quantize_row(p, smem + p.act_off);
+    }
+    if (!p.norm_w && !p.x_f32) {
         const bool ok = mbar_wait(act_bar, 0);
         int any_timeout;
         if (team_size <= 32) {

@@ -219,3 +219,53 @@ def test_qmv_invalid_arguments(cuda):
         P.qmv(P.Q4_0, w, 1, 32, xq, 17)
     with pytest.raises(P.InvalidArgument, match="unknown weight type"):
         P.qmv(7, w, 1, 32, xq, 1)
+
+
+# ------------------------------------------------- fp32 activations
+@pytest.mark.parametrize("qtype", [W.Q4_0, W.Q8_0, W.Q4_K, W.Q5_K, W.Q6_K])
+@pytest.mark.parametrize("rows,k", [(4096, 4096), (1031, 14336), (333, 6144), (257, 28672), (64, 256)])
+def test_qmv_f32_equals_quantize_then_qmv(cuda, qtype, rows, k):
+    """p100_qmv_f32 gives the bits of p100_q8_1_quantize followed by p100_qmv,
+    on two calls in a row: with scratch (the quantiser then the mat-vec as
+    its programmatic dependent; the scratch holds the Q8_1 row) and without
+    (the quantisation fused into the team kernel; Q6_K rows of k = 256 are
+    210 bytes, which that kernel does not take, and are refused)."""
+    w = dev(cuda, W.weights(qtype, rows, k, seed=rows + k + qtype))
+    x = dev(cuda, W.activations(1, k, seed=k + qtype))
+    xq = P.q8_1_quantize(x)
+    want = P.qmv(qtype, w, rows, k, xq, 1).cpu().numpy()
+    scratch = cuda.full((P.q8_1_bytes(k, 1),), 7, dtype=cuda.uint8, device="cuda")
+    for flags in (0, P.QMV_PDL):
+        got = P.qmv_f32(qtype, w, rows, k, x, x_q8_1=scratch, flags=flags).cpu().numpy()
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+        assert np.array_equal(scratch.cpu().numpy(), xq.cpu().numpy())
+    if qtype == W.Q6_K and k == 256:
+        with pytest.raises(P.P100Error) as e:
+            P.qmv_f32(qtype, w, rows, k, x)
+        assert e.value.status == P.ERR_UNSUPPORTED
+    else:
+        for flags in (0, P.QMV_PDL):
+            got = P.qmv_f32(qtype, w, rows, k, x, flags=flags).cpu().numpy()
+            assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    assert P.device_error() == P.OK
+
+
+def test_qmv_f32_batches_and_rejections(cuda):
+    k, rows, b = 4096, 500, 4
+    w = dev(cuda, W.weights(W.Q4_0, rows, k, seed=3))
+    x = dev(cuda, W.activations(b, k, seed=4))
+    want = P.qmv(W.Q4_0, w, rows, k, P.q8_1_quantize(x), b).cpu().numpy()
+    scratch = cuda.empty(P.q8_1_bytes(k, b), dtype=cuda.uint8, device="cuda")
+    got = P.qmv_f32(W.Q4_0, w, rows, k, x, batch=b, x_q8_1=scratch).cpu().numpy()
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    with pytest.raises(P.P100Error) as e:          # batch 4 without scratch
+        P.qmv_f32(W.Q4_0, w, rows, k, x, batch=b)
+    assert e.value.status == P.ERR_UNSUPPORTED
+    xs = cuda.zeros(k + 1, device="cuda")[1:]       # 4-byte aligned only: not fused
+    with pytest.raises(P.P100Error) as e:
+        P.qmv_f32(W.Q4_0, w, rows, k, xs)
+    assert e.value.status == P.ERR_UNSUPPORTED
+    with pytest.raises(P.InvalidArgument):
+        P.qmv_f32(W.Q4_0, w, rows, k, x[:1], flags=8)
+    with pytest.raises(P.InvalidArgument):
+        P.q8_1_quantize(x, flags=8)
