@@ -197,11 +197,17 @@ bool plan_team(int type, const void* w, const void* xq, int rows, int k, int bat
     const int team = qmvt::team_lanes(ngroups);
     if (team > qmvt::kConsumers * 32) return false;
     const size_t row_bytes = size_t(k / elems_of(type)) * bytes_of(type);
-    if (row_bytes % 16) return false;   // stages are 16-byte bulk copies (Q6_K: k a multiple of 2048)
+    // Stages are 16-byte bulk copies: rows of whole 16-byte units, or (Q6_K,
+    // whose groups are read on the 2-byte grid) a matrix that ends on the
+    // grid, each stage widened to it (up to 14 bytes before its first row and
+    // 14 after its last, and the last group's reads 6 past it: 32 more bytes
+    // per slot).
+    const bool ragged = row_bytes % 16 != 0;
+    if (ragged && (type != P100_Q6_K || (size_t(rows) * row_bytes) % 16)) return false;
     // Q6_K groups are read as aligned words that run up to 6 bytes past the group
     const size_t tail = type == P100_Q6_K ? 16 : 0;
     const int teams = qmvt::kConsumers * 32 / team;
-    const size_t slot = round128(size_t(teams) * row_bytes);
+    const size_t slot = round128(size_t(teams) * row_bytes + (ragged ? 32 : 0));
     const size_t part_off = 384;   // 2 x 8 ring mbarriers + the activation one; the fused norm's partials at 256
     const size_t act_off = part_off + round128(size_t(2) * teams * std::max(1, team / 32) * 4);
     const size_t ring_off = act_off + round128(size_t(k / 32) * 36);   // the Q8_1 row

@@ -383,6 +383,19 @@ __device__ __forceinline__ float group_dot(const uint8_t* __restrict__ grp, cons
     }
 }
 
+// The bytes one stage copies: rows [first, first + nrows) widened to the
+// 16-byte grid (bulk copies move whole 16-byte units).  Rows of Q4_0, Q8_0,
+// Q4_K and Q5_K are whole units, so this is exactly those rows; Q6_K rows of
+// k not a multiple of 2048 (tensor-parallel slices) start anywhere on the
+// 2-byte grid, the stage then begins (first * row_bytes) % 16 bytes into its
+// slot, and the host plan requires the matrix to end on the grid (so no copy
+// reads past it).  src: the byte offset of the copy in w.
+__device__ __forceinline__ uint32_t stage_span(const Params& p, int first, int nrows, size_t& src) {
+    const size_t off = size_t(first) * p.row_bytes;
+    src = off & ~size_t(15);
+    return static_cast<uint32_t>(((off + size_t(nrows) * p.row_bytes + 15) & ~size_t(15)) - src);
+}
+
 // NG = k / 256 when compiled for one hidden size, 0 for any (runtime shape).
 template <int TYPE, int NG>
 __global__ void __launch_bounds__(kThreads, 1) qmv_team_kernel(const Params p) {
@@ -423,9 +436,10 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_team_kernel(const Params p) {
             const int pre = min(look, nst);
             for (int s = 0; s < pre; ++s) {
                 const int first = r0 + s * teams;
-                const uint32_t bytes = static_cast<uint32_t>(min(teams, r1 - first)) * p.row_bytes;
+                size_t src;
+                const uint32_t bytes = stage_span(p, first, min(teams, r1 - first), src);
                 mbar_arrive_expect_tx(&full[s], bytes);
-                bulk_load(ring + size_t(s) * p.slot_bytes, p.w + size_t(first) * p.row_bytes, bytes, &full[s],
+                bulk_load(ring + size_t(s) * p.slot_bytes, p.w + src, bytes, &full[s],
                           policy);
             }
             // the activations may come from the previous kernel (with the
@@ -447,9 +461,10 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_team_kernel(const Params p) {
                 if (!mbar_wait(&full[(s - look) % p.nslot], ((s - look) / p.nslot) & 1)) break;
                 if (s >= p.nslot && !mbar_wait(&empty[slot], ((s / p.nslot) - 1) & 1)) break;
                 const int first = r0 + s * teams;
-                const uint32_t bytes = static_cast<uint32_t>(min(teams, r1 - first)) * p.row_bytes;
+                size_t src;
+                const uint32_t bytes = stage_span(p, first, min(teams, r1 - first), src);
                 mbar_arrive_expect_tx(&full[slot], bytes);
-                bulk_load(ring + size_t(slot) * p.slot_bytes, p.w + size_t(first) * p.row_bytes, bytes, &full[slot],
+                bulk_load(ring + size_t(slot) * p.slot_bytes, p.w + src, bytes, &full[slot],
                           policy);
                 issued = s + 1;
             }
@@ -528,7 +543,8 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_team_kernel(const Params p) {
         const int nr = min(teams, r1 - first);
         float acc = 0.f;
         if (team < nr && has_group)
-            acc = group_dot<TYPE>(stage + size_t(team) * p.row_bytes + size_t(tl) * kGroupBytes, act, acc);
+            acc = group_dot<TYPE>(stage + ((size_t(first) * p.row_bytes) & 15) + size_t(team) * p.row_bytes +
+                                      size_t(tl) * kGroupBytes, act, acc);
         // the stage's words are in registers: hand the slot back
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[slot]);

@@ -16,11 +16,16 @@ import numpy as np
 import pytest
 
 import p100_b200 as P
-from test_decode_gpu import DECODE_LOGIT_TOL, TINY
+from test_decode_gpu import DECODE_LOGIT_TOL, TINY, mixed_types
 
 pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
 
 SEED, NPOS, STEPS, TOKEN = 99, 100, 3, 7
+# Per-tensor formats (five of them; a rank's Q6_K ffn_down slice has rows of
+# 420 bytes, off the 16-byte grid) on a shape whose TP=2 slices are whole
+# 256-value blocks.
+SHAPES = {"tiny": TINY,
+          "mixed": dict(TINY, hidden=512, n_head=8, n_head_kv=4, ffn=1024, tensor_types=mixed_types())}
 
 
 def _free_port():
@@ -43,7 +48,7 @@ def _run(dec):
     return out
 
 
-def _rank(rank, world, port, q, allreduce):
+def _rank(rank, world, port, q, allreduce, shape):
     import datetime
     import torch
     import torch.distributed as dist
@@ -56,7 +61,7 @@ def _rank(rank, world, port, q, allreduce):
         box = [P.tp_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(box, src=0)
         tp = P.TP(box[0], world, rank, rank)
-        dec = P.Decoder(P.LlamaConfig(**TINY), tp)
+        dec = P.Decoder(P.LlamaConfig(**SHAPES[shape]), tp)
         out = _run(dec)
         q.put((rank, dec.vocab_offset, [(p, t, l.tolist()) for p, t, l in out]))
     except Exception as e:  # noqa: BLE001
@@ -69,8 +74,9 @@ def _rank(rank, world, port, q, allreduce):
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("shape", ["tiny", "mixed"])
 @pytest.mark.parametrize("allreduce", ["peer", "nccl"])
-def test_tp2_matches_tp1(cuda, allreduce):
+def test_tp2_matches_tp1(cuda, allreduce, shape):
     """allreduce: 'peer' = the one-shot all-reduce over NVLink peer memory
     (push kernel + reduce inside the next RMSNorm), 'nccl' = ncclAllReduce."""
     if cuda.cuda.device_count() < 2:
@@ -79,7 +85,7 @@ def test_tp2_matches_tp1(cuda, allreduce):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, 2, port, q, allreduce)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, q, allreduce, shape)) for r in range(2)]
     for p in procs:
         p.start()
     res = sorted([q.get(timeout=300) for _ in range(2)], key=lambda r: r[0])
@@ -89,14 +95,14 @@ def test_tp2_matches_tp1(cuda, allreduce):
     for r in res:
         assert r[1] != "error", r
     with cuda.cuda.device(0):
-        dec = P.Decoder(P.LlamaConfig(**TINY))
+        dec = P.Decoder(P.LlamaConfig(**SHAPES[shape]))
         try:
             ref = _run(dec)
         finally:
             dec.close()
     for step in range(STEPS):
         pos1, tok1, logits1 = ref[step]
-        full = np.zeros(TINY["vocab"], dtype=np.float32)
+        full = np.zeros(SHAPES[shape]["vocab"], dtype=np.float32)
         for rank, off, out in res:
             pos, tok, logits = out[step]
             assert pos == pos1

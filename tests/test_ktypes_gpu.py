@@ -45,11 +45,13 @@ def test_qmv_within_tolerance(cuda, orc, qtype, rows, k, batch):
 # Batch 1 on the team kernel: k = 4096 / 8192 / 14336 / 28672 (compiled
 # group counts 16, 32, 56, 112; teams of 16 and 32 lanes, of 2 and 4 warps),
 # 6144 (the runtime-shaped variant), row counts that leave a partial last
-# stage; and shapes that fall back to the general kernel (Q6_K rows of k =
-# 1280 are 1050 bytes, not whole 16-byte units).
+# stage; Q6_K rows that are not whole 16-byte units (k = 7168 and 3584, the
+# down slices of tensor parallelism 2 and 4; k = 1280: 1050-byte rows), whose
+# stages start off the 16-byte grid; and a shape that falls back to the
+# general kernel (33 Q6_K rows of 1050 bytes do not end on the grid).
 @pytest.mark.parametrize("qtype", KTYPES)
 @pytest.mark.parametrize("rows,k", [(4099, 4096), (1000, 8192), (777, 14336), (301, 28672), (515, 6144),
-                                    (20000, 4096), (33, 1280)])
+                                    (20000, 4096), (4096, 7168), (1000, 3584), (40, 1280), (33, 1280)])
 def test_qmv_batch1_team_kernel(cuda, orc, qtype, rows, k):
     w = W.weights(qtype, rows, k, seed=5 * qtype + rows)
     x = W.activations(1, k, seed=rows)

@@ -223,13 +223,13 @@ def test_qmv_invalid_arguments(cuda):
 
 # ------------------------------------------------- fp32 activations
 @pytest.mark.parametrize("qtype", [W.Q4_0, W.Q8_0, W.Q4_K, W.Q5_K, W.Q6_K])
-@pytest.mark.parametrize("rows,k", [(4096, 4096), (1031, 14336), (333, 6144), (257, 28672), (64, 256)])
+@pytest.mark.parametrize("rows,k", [(4096, 4096), (1031, 14336), (333, 6144), (257, 28672), (64, 256), (63, 256)])
 def test_qmv_f32_equals_quantize_then_qmv(cuda, qtype, rows, k):
     """p100_qmv_f32 gives the bits of p100_q8_1_quantize followed by p100_qmv,
     on two calls in a row: with scratch (the quantiser then the mat-vec as
     its programmatic dependent; the scratch holds the Q8_1 row) and without
-    (the quantisation fused into the team kernel; Q6_K rows of k = 256 are
-    210 bytes, which that kernel does not take, and are refused)."""
+    (the quantisation fused into the team kernel; 63 Q6_K rows of 210 bytes
+    end off the 16-byte grid, which that kernel does not take: refused)."""
     w = dev(cuda, W.weights(qtype, rows, k, seed=rows + k + qtype))
     x = dev(cuda, W.activations(1, k, seed=k + qtype))
     xq = P.q8_1_quantize(x)
@@ -239,7 +239,7 @@ def test_qmv_f32_equals_quantize_then_qmv(cuda, qtype, rows, k):
         got = P.qmv_f32(qtype, w, rows, k, x, x_q8_1=scratch, flags=flags).cpu().numpy()
         assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
         assert np.array_equal(scratch.cpu().numpy(), xq.cpu().numpy())
-    if qtype == W.Q6_K and k == 256:
+    if qtype == W.Q6_K and rows * (k // 256 * 210) % 16:
         with pytest.raises(P.P100Error) as e:
             P.qmv_f32(qtype, w, rows, k, x)
         assert e.value.status == P.ERR_UNSUPPORTED
