@@ -75,3 +75,25 @@ def test_h16_and_whole_blocks(cuda, qtype):
     xq = cuda.zeros(4096, dtype=cuda.uint8, device="cuda")
     with pytest.raises(P.InvalidArgument):
         P.qmv(qtype, w, 8, 128, xq, 1, y=y)     # a super-block is 256 values
+
+
+@pytest.mark.parametrize("qtype", KTYPES)
+@pytest.mark.parametrize("rows,k,batch", [(4096, 4096, 2), (515, 14336, 5), (40, 1280, 16), (33, 1280, 3)])
+def test_qmv_batches_equal_columns(cuda, orc, qtype, rows, k, batch):
+    """Batch 2..16 of Q5_K / Q6_K: one team-kernel launch per column where the
+    team kernel takes the matrix (the general kernel for 33 Q6_K rows of 1050
+    bytes), the bits of batch-1 calls column by column, and within the q81
+    tolerance of the oracle."""
+    w = dev(cuda, W.weights(qtype, rows, k, seed=7 * qtype + rows))
+    x = W.activations(batch, k, seed=batch + k)
+    xq = P.q8_1_quantize(dev(cuda, x))
+    y = P.qmv(qtype, w, rows, k, xq, batch).cpu().numpy()
+    cb = P.q8_1_bytes(k, 1)
+    for c in range(batch):
+        yc = P.qmv(qtype, w, rows, k, xq[c * cb:(c + 1) * cb], 1).cpu().numpy()
+        assert np.array_equal(y[c].view(np.uint32), yc[0].view(np.uint32)), c
+    wh = w.cpu().numpy()
+    err = assert_qmv_close(y, q81_reference(orc, qtype, wh, rows, k, x).astype(np.float64),
+                           row_norms(orc, qtype, wh, rows, k), x)
+    assert err <= 1e-5, err
+    assert P.device_error() == P.OK
