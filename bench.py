@@ -553,6 +553,17 @@ def kernel_only(args):
         return 0
     _, k, rows = TARGET
     batch = 16 if args.kernel_only == "qmvb" else 1
+    if args.kernel_only == "h16":
+        # the h16 path (HFMA2 chain 16) on the target shape, 5 copies (165 MB > L2)
+        ws = [torch.from_numpy(W.weights(W.Q4_0, rows, k, seed=s_)).cuda() for s_ in range(5)]
+        h, ss = P.h16_prepare(torch.from_numpy(W.activations(1, k, seed=2)).cuda())
+        y = torch.empty(1, rows, device="cuda")
+        for i in range(args.warmup + args.steps):
+            P.qmv_h16(W.Q4_0, ws[i % 5], rows, k, h, ss, 1, 16, y=y)
+        torch.cuda.synchronize()
+        P.check(P.device_error())
+        print(json.dumps({"kernel_only": f"qmv_h16 Q4_0 {k}x{rows} chain 16", "launches": args.warmup + args.steps}))
+        return 0
     if args.kernel_only == "qmv6k":
         # the Q6_K LM head of a Q4_K_M 8B model: 4096 x 128256, 431 MB > L2
         k, rows = 4096, 128256
@@ -585,8 +596,9 @@ def main():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the 8B/70B decode section")
-    ap.add_argument("--kernel-only", choices=["qmv", "qmvb", "qmv6k", "fa", "fa4096", "faq8", "faq4", "decode"],
+    ap.add_argument("--kernel-only", choices=["qmv", "qmvb", "qmv6k", "h16", "fa", "fa4096", "faq8", "faq4", "decode"],
                     help="one kernel's launches only (ncu cases); qmvb = the target shape at batch 16, "
+                         "h16 = the target shape on the h16 path, "
                          "qmv6k = a Q6_K 4096x128256 LM head at batch 1, "
                          "fa = 32768 keys, fa4096 = 4096 keys, faq8 / faq4 = 32768 keys of q8_0 / q4_0 K/V")
     args = ap.parse_args()
