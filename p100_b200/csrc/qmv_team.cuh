@@ -3,7 +3,7 @@
 // The decode mat-vec streams every weight byte once, so its instruction cost
 // per byte of HBM is what matters:
 //   * A lane owns one fixed 256-weight column group of every row (eight Q4_0 /
-//     Q8_0 blocks or one Q4_K super-block), so its Q8_1 activations for that
+//     Q8_0 blocks or one Q4_K / Q5_K / Q6_K super-block), so its Q8_1 activations for that
 //     group live in registers for the whole launch (loaded once, 16-byte
 //     loads); no activation traffic in the inner loop.
 //   * A team of T lanes (T = k/256 rounded up to a power of two, or to whole
@@ -27,8 +27,13 @@
 //     hidden sizes, which turns the team geometry and the activation
 //     addressing into constants; 0 selects the runtime-shaped variant.
 //   * A group is read with 128-bit shared loads at a 144- or 272-byte lane
-//     stride (bank-conflict free); high nibbles are multiplied in place by an
-//     unsigned x signed dp4a and the 16x factor removed by one shift.
+//     stride (bank-conflict free; Q5_K 176 bytes); high nibbles are
+//     multiplied in place by an unsigned x signed dp4a and the 16x factor
+//     removed by one shift.  Q6_K groups (210 bytes) sit on the 2-byte grid
+//     and are read as aligned 32-bit words re-aligned by a funnel shift
+//     (group_dot_q6k).
+//   * Batch > 1 of Q5_K / Q6_K (no tensor-core form) is one launch per
+//     column (Params.col0) by the host.
 //   * Rows are finished by an XOR butterfly inside the team (and, for teams of
 //     several warps, a fixed-order add of the warps' partials), so the result
 //     is deterministic.
