@@ -31,6 +31,10 @@
 extern "C" {
 #endif
 
+/* Raised when a struct below changes layout: 2 added p100_attn_desc's
+ * kv_type (p100_llama_config's kv_type followed within 2), 3
+ * p100_llama_config's tensor_types.  A binding compares it with
+ * p100_abi_version(). */
 #define P100_B200_ABI_VERSION 3
 
 typedef enum p100_status {
