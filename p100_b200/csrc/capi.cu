@@ -591,6 +591,10 @@ const char* attn_reason(const p100_attn_desc& d) {
 }
 
 constexpr int kFaWideSeq = 8192;
+// ... and at least this many (sequence, kv head) pairs: with fewer, one
+// 16-CTA cluster per head (cluster merge) beats one part per SM merged
+// through the workspace by the last CTA, at any context length.
+constexpr int kFaWideHeads = 8;
 
 struct FaPlan {
     int D = 0, G = 0, gmax = 0, parts = 1, nstage = 0;
@@ -750,10 +754,13 @@ p100_status launch_fa_mma_t(const FaPlan& plan, const fa::Params& prm, int heads
             return st;
     }
     int np = 0;
-    if (NW == 4 && plan.auto_parts && plan.parts >= 2 && plan.seq <= kFaWideSeq) {
+    if (NW == 4 && plan.auto_parts && plan.parts >= 2 && (plan.seq <= kFaWideSeq || heads < kFaWideHeads)) {
         np = 1;
         while (np * 2 <= std::min(16, plan.parts) && np * 2 <= G * D / 32) np *= 2;
-        if (np < 2 || 2 * np < plan.parts) np = 0;
+        // A full 16-CTA cluster stays on the cluster merge however many parts
+        // the SM count would allow (few kv heads: one cluster per head beats
+        // a wide split merged through the workspace by the last CTA).
+        if (np < 2 || (2 * np < plan.parts && np < 16)) np = 0;
     }
     int lg = 0;
     while (np && (1 << lg) < np) ++lg;
@@ -818,11 +825,13 @@ p100_status launch_fa_mma_nw(const FaPlan& plan, const fa::Params& prm, int head
         default: return launch_fa_mma_t<D, 8, KV, NW>(plan, prm, heads, s, pdl);
     }
 }
-// The 8-warp shape for automatic splits of more than kFaWideSeq keys (their
-// measured crossover lies between 4K and 16K keys), the 4-warp shape else.
+// The 8-warp shape for automatic splits of more than kFaWideSeq keys over
+// at least kFaWideHeads heads (their measured crossover lies between 4K and
+// 16K keys), the 4-warp shape else.
 template <int D, int KV>
 p100_status launch_fa_mma_kv(const FaPlan& plan, const fa::Params& prm, int heads, cudaStream_t s, bool pdl) {
-    if (plan.auto_parts && plan.seq > kFaWideSeq) return launch_fa_mma_nw<D, KV, 8>(plan, prm, heads, s, pdl);
+    if (plan.auto_parts && plan.seq > kFaWideSeq && heads >= kFaWideHeads)
+        return launch_fa_mma_nw<D, KV, 8>(plan, prm, heads, s, pdl);
     return launch_fa_mma_nw<D, KV, 4>(plan, prm, heads, s, pdl);
 }
 template <int D>
@@ -1218,7 +1227,35 @@ namespace p100b {
 static __device__ __align__(256) unsigned char g_fa_static_scratch[P100_FA_STATIC_SCRATCH_BYTES];
 namespace {
 std::mutex g_static_mutex;
-void* g_static_scratch_ptr[64];   // the array's device address, per device ordinal
+// The array's device address per device ordinal, valid for the context whose
+// unique id is beside it: a cudaDeviceReset or a recreated primary context
+// gets a new id, and the address is looked up again.
+void* g_static_scratch_ptr[64];
+unsigned long long g_static_scratch_ctx[64];
+
+// Unique id of the calling thread's current context (0 if unavailable), from
+// the driver the runtime loaded.
+unsigned long long current_context_id() {
+    static const auto fns = [] {
+        std::pair<PFN_cuCtxGetCurrent_v4000, PFN_cuCtxGetId_v12000> r{nullptr, nullptr};
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            r.first = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(f);
+        f = nullptr;
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            r.second = reinterpret_cast<PFN_cuCtxGetId_v12000>(f);
+        (void)cudaGetLastError();
+        return r;
+    }();
+    CUcontext ctx = nullptr;
+    unsigned long long id = 0;
+    if (!fns.first || !fns.second || fns.first(&ctx) != CUDA_SUCCESS || !ctx || fns.second(ctx, &id) != CUDA_SUCCESS)
+        return 0;
+    return id;
+}
 }  // namespace
 }  // namespace p100b
 
@@ -1240,14 +1277,18 @@ extern "C" p100_status p100_fa_decode_static(const p100_attn_desc* desc, const f
     if (plan.ws_total) {
         {
             // Host code cannot use the array's name as a device address: look
-            // the address up once per device, with that device current.
+            // the address up once per device and context, with that device
+            // current.  The lookup creates the context if there is none yet,
+            // so its id is read after it.
             std::lock_guard<std::mutex> lock(g_static_mutex);
-            if (!g_static_scratch_ptr[dev]) {
+            const unsigned long long ctx = current_context_id();
+            if (!g_static_scratch_ptr[dev] || ctx == 0 || g_static_scratch_ctx[dev] != ctx) {
                 void* ptr = nullptr;
                 if (p100_status st = cuda_status(cudaGetSymbolAddress(&ptr, g_fa_static_scratch),
                                                  "cudaGetSymbolAddress(static scratch)"))
                     return st;
                 g_static_scratch_ptr[dev] = ptr;
+                g_static_scratch_ctx[dev] = current_context_id();
             }
             scratch = g_static_scratch_ptr[dev];
         }
