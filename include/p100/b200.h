@@ -320,6 +320,13 @@ enum { P100_TT_Q = 0, P100_TT_K, P100_TT_V, P100_TT_O, P100_TT_GATE, P100_TT_UP,
  * separate one-block norm kernel fits beside the previous mat-vec and starts
  * the moment it ends. */
 #define P100_DEC_FUSED_NORM 1
+/* Decode with the persistent step kernel (one cooperative launch a token,
+ * see p100_decoder_path) where it applies, instead of the graph of separate
+ * kernels.  Off by default: on B200 it measured slower than the graph
+ * (Llama-3-8B shape at context 4096: 396 against 663 tokens/s on one GPU;
+ * its grid barriers cost as much as the kernel boundaries they replace, and
+ * its FP32 SIMT attention is latency-bound at eight warps per SM). */
+#define P100_DEC_STEP 2
 typedef struct p100_decoder p100_decoder;
 /* Tensor ids (per layer where it applies). */
 enum {
@@ -351,10 +358,27 @@ p100_status p100_decoder_fill_kv(p100_decoder* d, int n_pos, unsigned long long 
 p100_status p100_decoder_set_state(p100_decoder* d, int pos, int token);
 /* Synchronises the device, then reads the position and the last token. */
 p100_status p100_decoder_state(p100_decoder* d, int* pos, int* token);
-/* n_steps tokens on stream.  The first call captures one step as a CUDA
- * graph (on a stream of its own, so make it outside any capture); every step
- * replays it.  With tp, every rank must call it the same number of times. */
+/* n_steps tokens on stream.  On the step path (p100_decoder_path) each token
+ * is one cooperative launch of the persistent step kernel.  On the graph path
+ * the first call captures one step as a CUDA graph (on a stream of its own,
+ * so make it outside any capture) and every step replays it.  With tp, every
+ * rank must call it the same number of times.  After a device-side wait ran
+ * out (p100_device_error() == P100_ERR_TIMEOUT) the step path returns at once
+ * from later launches: destroy and recreate the decoder. */
 p100_status p100_decoder_step(p100_decoder* d, int n_steps, p100_stream_t stream);
+/* Which kernels p100_decoder_step runs.  P100_DEC_PATH_STEP (with
+ * P100_DEC_STEP in flags): the whole token
+ * as one persistent kernel (one CTA per SM, phases meeting at grid barriers,
+ * a producer warp streaming every weight matrix and K/V tile through a
+ * shared-memory ring; the tensor-parallel all-reduce over NVLink peer memory
+ * inside it).  It applies when every layer matrix and the LM head share one
+ * of Q4_0, Q8_0 or Q4_K, the cache is fp16, head_dim is 64 or 128 with 1,
+ * 2, 4 or 8 query heads per kv head, every
+ * matrix's k is a multiple of 256, flags do not hold P100_DEC_FUSED_NORM,
+ * and, with tp, every pair of ranks has peer access.  P100_DEC_PATH_GRAPH
+ * (the default): one CUDA graph of separate kernels a token. */
+enum { P100_DEC_PATH_GRAPH = 0, P100_DEC_PATH_STEP = 1 };
+int p100_decoder_path(const p100_decoder* d);
 /* Device address and size of a tensor or buffer (for tests and tools). */
 p100_status p100_decoder_tensor(p100_decoder* d, int layer, int which, void** ptr, size_t* bytes, int* rows,
                                 int* cols);

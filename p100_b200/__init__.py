@@ -132,6 +132,7 @@ def _bind(lib):
         "p100_decoder_tensor": (ip, [vp, ip, ip, C.POINTER(vp), C.POINTER(sz), C.POINTER(ip), C.POINTER(ip)]),
         "p100_decoder_buffer": (ip, [vp, ip, C.POINTER(vp), C.POINTER(sz)]),
         "p100_decoder_vocab_offset": (ip, [vp]),
+        "p100_decoder_path": (ip, [vp]),
         "p100_decoder_weight_bytes_per_token": (sz, [vp]),
         "p100_decoder_destroy": (ip, [vp]),
     }
@@ -454,6 +455,8 @@ class LlamaConfig(C.Structure):
 
 
 DEC_FUSED_NORM = 1   # P100_DEC_FUSED_NORM
+DEC_STEP = 2         # P100_DEC_STEP: the persistent step kernel where it applies (opt-in)
+DEC_PATH_GRAPH, DEC_PATH_STEP = 0, 1   # p100_decoder_path
 # tensor ids of LlamaConfig.tensor_types (P100_TT_*)
 TT_EMBED, TT_LM_HEAD = 0, 1
 TT_Q, TT_K, TT_V, TT_O, TT_GATE, TT_UP, TT_DOWN = range(7)
@@ -508,6 +511,11 @@ class Decoder:
         ptr, n = C.c_void_p(), C.c_size_t()
         check(lib().p100_decoder_buffer(self.handle, which, C.byref(ptr), C.byref(n)))
         return ptr.value, n.value
+
+    @property
+    def path(self):
+        """DEC_PATH_STEP (one persistent kernel a token) or DEC_PATH_GRAPH."""
+        return lib().p100_decoder_path(self.handle)
 
     @property
     def vocab_offset(self):

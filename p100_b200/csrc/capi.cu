@@ -195,7 +195,10 @@ bool plan_team(int type, const void* w, const void* xq, int rows, int k, int bat
         return false;
     const int ngroups = k / 256;
     const int team = qmvt::team_lanes(ngroups);
-    if (team > qmvt::kConsumers * 32) return false;
+    // teams of several warps meet at a named barrier of team lanes: every
+    // consumer lane must belong to a whole team (a team of 96 lanes would
+    // leave 64 lanes waiting at a barrier that never fills)
+    if (team > qmvt::kConsumers * 32 || (qmvt::kConsumers * 32) % team) return false;
     const size_t row_bytes = size_t(k / elems_of(type)) * bytes_of(type);
     // Stages are 16-byte bulk copies: rows of whole 16-byte units, or (Q6_K,
     // whose groups are read on the 2-byte grid) a matrix that ends on the

@@ -25,6 +25,7 @@
 // its slices from global coordinates, so TP=N holds the same model as TP=1.
 #pragma once
 #include "decode.cuh"
+#include "step.cuh"
 
 namespace p100b {
 namespace {
@@ -72,6 +73,14 @@ struct Decoder {
     void* ar_peer[dec::kArMaxRanks] = {};    // IPC mappings of the other ranks' arenas
     int* ar_epoch = nullptr;                 // completed-epoch counter (in the arena above)
     dec::PeerAr ar{};
+    // the persistent step kernel (step.cuh): one cooperative launch a token
+    bool step_region = false;   // the arena holds its buffers (the config allows it)
+    bool use_step = false;      // p100_decoder_step launches it
+    uint8_t* st = nullptr;      // its buffers: layer table, attention partials, counters
+    size_t st_layers = 0, st_ws_o = 0, st_ws_ml = 0, st_tickets = 0, st_cand = 0, st_ctr = 0;
+    stp::Params sp{};
+    size_t step_smem = 0;
+    int step_type = 0;
 };
 
 size_t dec_weight_bytes(int type, int rows, int cols) {
@@ -107,7 +116,7 @@ const char* config_reason(const p100_llama_config& c, int nranks, const std::vec
         if (!known_type(t)) return "unknown weight type in tensor_types";
         blk = std::max(blk, elems_of(t));
     }
-    if (c.flags & ~P100_DEC_FUSED_NORM) return "unknown decoder flags";
+    if (c.flags & ~(P100_DEC_FUSED_NORM | P100_DEC_STEP)) return "unknown decoder flags";
     if (c.n_head % c.n_head_kv) return "n_head must be divisible by n_head_kv";
     if (c.head_dim != 64 && c.head_dim != 128 && c.head_dim != 256) return "head_dim must be 64, 128 or 256";
     if (c.n_head / c.n_head_kv > 8) return "at most 8 query heads per kv head";
@@ -126,6 +135,25 @@ const char* config_reason(const p100_llama_config& c, int nranks, const std::vec
     if (c.vocab < nranks) return "vocab smaller than the number of ranks";
     if (!(c.norm_eps >= 0.0f) || !(c.rope_theta > 0.0f)) return "norm_eps must be >= 0 and rope_theta > 0";
     return nullptr;
+}
+
+// Whether the configuration suits the persistent step kernel: one weight
+// format (Q4_0, Q8_0 or Q4_K) for every layer matrix and the LM head (the
+// embedding may differ), an fp16 cache, head_dim 64 or 128, and matrices of
+// whole 256-value groups (the team mat-vec).  Set in d.step_type.
+bool dec_step_config_ok(Decoder& d) {
+    const p100_llama_config& c = d.cfg;
+    if (!(c.flags & P100_DEC_STEP) || (c.flags & P100_DEC_FUSED_NORM)) return false;
+    if (c.kv_type != P100_KV_F16 || (c.head_dim != 64 && c.head_dim != 128)) return false;
+    const int G = c.n_head / c.n_head_kv;
+    if (d.nranks > stp::kMaxRanks || (G != 1 && G != 2 && G != 4 && G != 8)) return false;
+    const int t = d.ttypes[P100_TT_LM_HEAD];
+    if (t != P100_Q4_0 && t != P100_Q8_0 && t != P100_Q4_K) return false;
+    for (size_t i = 0; i < d.ttypes.size(); ++i)
+        if (i != P100_TT_EMBED && d.ttypes[i] != t) return false;
+    if (c.hidden % 256 || (d.nq * c.head_dim) % 256 || d.ffn % 256) return false;
+    d.step_type = t;
+    return true;
 }
 
 p100_status dec_alloc(Decoder& d) {
@@ -204,6 +232,20 @@ p100_status dec_alloc(Decoder& d) {
     ad.kv_type = c.kv_type;
     if (p100_status st = plan_fa(ad, d.sms, d.fa_plan)) return st;
     const size_t at_ws = take(std::max<size_t>(d.fa_plan.ws_total, 256));
+    // the persistent step kernel's buffers, when the configuration allows it
+    d.step_region = dec_step_config_ok(d);
+    size_t at_st = 0;
+    if (d.step_region) {
+        const int G = c.n_head / c.n_head_kv;
+        const size_t st0 = off;
+        at_st = take(size_t(L) * sizeof(stp::Layer));
+        d.st_ws_o = take(size_t(d.nkv) * stp::kMaxParts * G * hd * 4) - st0;
+        d.st_ws_ml = take(size_t(d.nkv) * stp::kMaxParts * G * 8) - st0;
+        d.st_tickets = take(size_t(d.nkv) * 4) - st0;
+        d.st_cand = take(size_t(std::max(d.sms, 1)) * 8) - st0;
+        d.st_ctr = take(256) - st0;   // grid barrier counter, two bases, abort word
+        d.st_layers = 0;
+    }
     d.arena_bytes = off;
     if (p100_status st = cuda_status(cudaMalloc(&d.arena, d.arena_bytes), "cudaMalloc(decoder)")) return st;
     for (const Req& r : reqs) r.t->ptr = d.arena + r.at;
@@ -223,6 +265,7 @@ p100_status dec_alloc(Decoder& d) {
     d.pos = reinterpret_cast<int*>(d.arena + at_pos);
     d.token = reinterpret_cast<int*>(d.arena + at_token);
     d.fa_ws = d.arena + at_ws;
+    if (d.step_region) d.st = d.arena + at_st;
     if (p100_status st = cuda_status(cudaMemset(d.arena, 0, d.arena_bytes), "cudaMemset(decoder)")) return st;
     std::vector<float> table(size_t(c.max_ctx) * (hd / 2) * 2);
     p100_rope_table(table.data(), c.max_ctx, hd, c.rope_theta);
@@ -519,96 +562,308 @@ p100_status dec_capture(Decoder& d) {
     return st;
 }
 
-// One-shot all-reduce setup: every rank allocates its arena, the IPC handles
-// go round an NCCL all-gather (as raw bytes in floats), and every rank maps
-// the others'.  Used only if every pair of ranks' GPUs has peer access (an
-// NCCL all-reduce of the verdict keeps all ranks on the same path) and
-// P100_TP_ALLREDUCE is not "nccl".  Collective: every rank calls it.
+// Device scratch of the create-time exchanges (a gather's input and output
+// and an agreement word).  A static array, so every rank has it even where a
+// local allocation failed and still enters every collective.
+static __device__ float g_setup_scratch[16 + 16 * dec::kArMaxRanks + 4];
+
+// The create-time exchanges of a tensor-parallel decoder.  Every rank calls
+// every exchange, in the same order, whatever its local state: a local
+// failure is carried into the next agreement (an all-reduce of failure
+// counts) instead of skipping a collective, so no rank is ever left waiting
+// in one.
+struct SetupComm {
+    Decoder& d;
+    cudaStream_t s = nullptr;
+    float* buf = nullptr;
+    p100_status err = P100_OK;   // the first local error
+    explicit SetupComm(Decoder& dd) : d(dd) {
+        void* p = nullptr;
+        note(cuda_status(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "setup stream"));
+        note(cuda_status(cudaGetSymbolAddress(&p, g_setup_scratch), "setup scratch"));
+        buf = static_cast<float*>(p);
+    }
+    ~SetupComm() {
+        if (s) cudaStreamDestroy(s);
+    }
+    void note(p100_status st) {
+        if (st && !err) err = st;
+    }
+    bool usable() const { return s && buf; }
+    // every rank's `count` floats from `mine` into out (rank-major)
+    void gather(const float* mine, int count, float* out) {
+        const int world = d.nranks;
+        if (usable()) {
+            note(cuda_status(cudaMemcpyAsync(buf, mine, sizeof(float) * count, cudaMemcpyHostToDevice, s), "gather in"));
+            note(p100_tp_allgather(d.tp, buf, buf + 16, size_t(count), s));
+            note(cuda_status(cudaMemcpyAsync(out, buf + 16, sizeof(float) * count * world, cudaMemcpyDeviceToHost, s),
+                             "gather out"));
+            note(cuda_status(cudaStreamSynchronize(s), "gather sync"));
+        } else {
+            std::fill(out, out + size_t(count) * world, 0.f);
+        }
+    }
+    // Agreement over the ranks (every rank gets the same): how many ranks
+    // had a local error so far (errors) and how many passed ok = false.
+    struct Votes {
+        int errors = 0, declines = 0;
+    };
+    Votes agree(bool ok) {
+        const float mine = (err ? 1000.f : 0.f) + (ok ? 0.f : 1.f);
+        float all = 1000.f * d.nranks;
+        if (usable()) {
+            const int at = 16 + 16 * dec::kArMaxRanks;
+            note(cuda_status(cudaMemcpyAsync(buf + at, &mine, sizeof(float), cudaMemcpyHostToDevice, s), "agree in"));
+            note(p100_tp_allreduce_sum(d.tp, buf + at, 1, s));
+            note(cuda_status(cudaMemcpyAsync(&all, buf + at, sizeof(float), cudaMemcpyDeviceToHost, s), "agree out"));
+            note(cuda_status(cudaStreamSynchronize(s), "agree sync"));
+        }
+        const int v = static_cast<int>(all + 0.5f);
+        return Votes{v / 1000, v % 1000};
+    }
+    // The status every rank returns after an agreement that saw errors.
+    p100_status fail(const char* what) {
+        if (err) return set_error(err, "%s: %s", what, t_error.c_str());
+        return set_error(P100_ERR_CUDA, "%s: another rank failed", what);
+    }
+};
+
+// Peer-memory exchange setup (tensor parallelism): every rank allocates an
+// arena, the IPC handles go round an all-gather, and every rank maps the
+// others'.  Used only if every pair of ranks' GPUs has peer access and
+// P100_TP_ALLREDUCE is not "nccl", all ranks having agreed.  The arena holds
+//   [2][world][hidden] fp32 slots (the one-shot all-reduce of the graph
+//   decoder and the step kernel's exchange), [2][world][kArBlocks] flags,
+//   the graph decoder's epoch, the step kernel's argmax candidates
+//   [world][2] and its 64-bit exchange counter.
+// Collective: every rank calls it.  Returns an error only when the ranks
+// agree that one of them failed; a declined or failed peer path leaves
+// d.peer_ar false on every rank (NCCL carries the exchanges then).
 p100_status dec_setup_peer_ar(Decoder& d) {
     const int world = d.nranks;
     if (!d.tp || world < 2 || world > dec::kArMaxRanks) return P100_OK;
     const char* mode = std::getenv("P100_TP_ALLREDUCE");
     const bool want = !(mode && std::strcmp(mode, "nccl") == 0);
     const int n = d.cfg.hidden;
-    if (n % (4 * dec::kArBlocks)) return P100_OK;
-    cudaStream_t s = nullptr;
-    if (p100_status st = cuda_status(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "stream")) return st;
-    // scratch: a gather's input (up to 16 floats) and output (16 per rank), then the verdict
-    const int verdict_at = 16 + 16 * world;
-    float* scratch = nullptr;
-    p100_status st = cuda_status(cudaMalloc(&scratch, sizeof(float) * (verdict_at + 2)), "cudaMalloc(ar scratch)");
-    auto gather = [&](const float* mine, int count, float* out_host) -> p100_status {
-        p100_status r = cuda_status(cudaMemcpyAsync(scratch, mine, sizeof(float) * count, cudaMemcpyHostToDevice, s),
-                                    "ar gather in");
-        if (!r) r = p100_tp_allgather(d.tp, scratch, scratch + count, size_t(count), s);
-        if (!r) r = cuda_status(cudaMemcpyAsync(out_host, scratch + count, sizeof(float) * count * world,
-                                                cudaMemcpyDeviceToHost, s), "ar gather out");
-        if (!r) r = cuda_status(cudaStreamSynchronize(s), "ar gather sync");
-        return r;
-    };
-    // 1. device ids -> peer access verdict, agreed by all ranks
-    std::vector<float> devs(world);
-    if (!st) {
-        const float me = float(d.device);
-        st = gather(&me, 1, devs.data());
-    }
-    float ok = want ? 1.f : 0.f;
-    for (int r = 0; r < world && !st && ok > 0.f; ++r) {
+    const bool shape_ok = n % (4 * dec::kArBlocks) == 0;   // the same on every rank
+    SetupComm sc(d);
+    // 1. (device, SM count) of every rank -> the verdict, agreed by all ranks
+    std::vector<float> info(size_t(world) * 2);
+    const float mine[2] = {float(d.device), float(d.sms)};
+    sc.gather(mine, 2, info.data());
+    bool ok = want && shape_ok;
+    for (int r = 0; r < world && ok; ++r) {
+        if (int(info[size_t(r) * 2 + 1]) != d.sms) ok = false;   // the step kernel's grids must match
         if (r == d.rank) continue;
         int can = 0;
-        cudaDeviceCanAccessPeer(&can, d.device, int(devs[r]));
-        if (!can) ok = 0.f;
+        if (cudaDeviceCanAccessPeer(&can, d.device, int(info[size_t(r) * 2])) != cudaSuccess || !can) ok = false;
     }
-    if (!st) st = cuda_status(cudaMemcpyAsync(scratch + verdict_at, &ok, sizeof(float), cudaMemcpyHostToDevice, s), "v");
-    if (!st) st = p100_tp_allreduce_sum(d.tp, scratch + verdict_at, 1, s);
-    float votes = 0.f;
-    if (!st) st = cuda_status(cudaMemcpyAsync(&votes, scratch + verdict_at, sizeof(float), cudaMemcpyDeviceToHost, s), "v");
-    if (!st) st = cuda_status(cudaStreamSynchronize(s), "verdict sync");
-    if (!st && votes == float(world)) {
-        // 2. arenas: slots [2][world][n] fp32, flags [2][world][kArBlocks] u32, epoch
-        const size_t slot_bytes = size_t(2) * world * n * 4;
-        const size_t flag_bytes = size_t(2) * world * dec::kArBlocks * 4;
-        st = cuda_status(cudaMalloc(&d.ar_arena, slot_bytes + flag_bytes + 256), "cudaMalloc(ar arena)");
-        if (!st) st = cuda_status(cudaMemset(d.ar_arena, 0, slot_bytes + flag_bytes + 256), "cudaMemset(ar arena)");
-        if (!st) st = cuda_status(cudaDeviceSynchronize(), "ar arena sync");
-        cudaIpcMemHandle_t h;
-        if (!st) st = cuda_status(cudaIpcGetMemHandle(&h, d.ar_arena), "cudaIpcGetMemHandle");
-        std::vector<float> mine(16), all(size_t(world) * 16);
-        static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
-        std::memcpy(mine.data(), &h, 64);
-        if (!st) st = gather(mine.data(), 16, all.data());
-        for (int r = 0; r < world && !st; ++r) {
-            uint8_t* base = nullptr;
-            if (r == d.rank) {
-                base = d.ar_arena;
-            } else {
-                cudaIpcMemHandle_t hr;
-                std::memcpy(&hr, all.data() + size_t(r) * 16, 64);
-                void* p = nullptr;
-                st = cuda_status(cudaIpcOpenMemHandle(&p, hr, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
-                d.ar_peer[r] = p;
-                base = static_cast<uint8_t*>(p);
+    (void)cudaGetLastError();
+    SetupComm::Votes v = sc.agree(ok);
+    if (v.errors) return sc.fail("peer exchange setup");
+    if (v.declines) return P100_OK;
+    // 2. arenas and their IPC handles
+    const size_t slot_bytes = size_t(2) * world * n * 4;
+    const size_t flag_bytes = size_t(2) * world * dec::kArBlocks * 4;
+    const size_t arena_bytes = slot_bytes + flag_bytes + 768;   // epoch | candidates | counter, 256 B each
+    cudaIpcMemHandle_t h{};
+    p100_status st = cuda_status(cudaMalloc(&d.ar_arena, arena_bytes), "cudaMalloc(ar arena)");
+    if (!st) st = cuda_status(cudaMemset(d.ar_arena, 0, arena_bytes), "cudaMemset(ar arena)");
+    if (!st) st = cuda_status(cudaDeviceSynchronize(), "ar arena sync");
+    if (!st) st = cuda_status(cudaIpcGetMemHandle(&h, d.ar_arena), "cudaIpcGetMemHandle");
+    auto release = [&]() {
+        for (int r = 0; r < dec::kArMaxRanks; ++r)
+            if (d.ar_peer[r]) {
+                cudaIpcCloseMemHandle(d.ar_peer[r]);
+                d.ar_peer[r] = nullptr;
             }
-            if (!st) {
-                d.ar.slots[r] = reinterpret_cast<float*>(base);
-                d.ar.flags[r] = reinterpret_cast<unsigned*>(base + slot_bytes);
-            }
+        if (d.ar_arena) cudaFree(d.ar_arena);
+        d.ar_arena = nullptr;
+    };
+    sc.note(st);
+    v = sc.agree(true);
+    if (v.errors) {
+        release();
+        return sc.fail("peer exchange setup");
+    }
+    // 3. every rank's handle; map the peers'
+    std::vector<float> hmine(16), hall(size_t(world) * 16);
+    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+    std::memcpy(hmine.data(), &h, 64);
+    sc.gather(hmine.data(), 16, hall.data());
+    st = sc.err;
+    for (int r = 0; r < world && !st; ++r) {
+        uint8_t* base = nullptr;
+        if (r == d.rank) {
+            base = d.ar_arena;
+        } else {
+            cudaIpcMemHandle_t hr;
+            std::memcpy(&hr, hall.data() + size_t(r) * 16, 64);
+            void* p = nullptr;
+            st = cuda_status(cudaIpcOpenMemHandle(&p, hr, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+            d.ar_peer[r] = p;
+            base = static_cast<uint8_t*>(p);
         }
         if (!st) {
-            d.ar_epoch = reinterpret_cast<int*>(d.ar_arena + slot_bytes + flag_bytes);
-            d.ar.world = world;
-            d.ar.rank = d.rank;
-            d.ar.n = n;
-            d.ar.epoch = d.ar_epoch;
-            // every rank's arena is zeroed and mapped before any rank pushes
-            st = p100_tp_allreduce_sum(d.tp, scratch, 1, s);
-            if (!st) st = cuda_status(cudaStreamSynchronize(s), "ar setup barrier");
-            d.peer_ar = !st;
+            d.ar.slots[r] = reinterpret_cast<float*>(base);
+            d.ar.flags[r] = reinterpret_cast<unsigned*>(base + slot_bytes);
+            d.sp.slots[r] = reinterpret_cast<float*>(base);
+            d.sp.cslots[r] = reinterpret_cast<float*>(base + slot_bytes + flag_bytes + 256);
+            d.sp.xcount[r] = reinterpret_cast<unsigned long long*>(base + slot_bytes + flag_bytes + 512);
         }
     }
-    if (scratch) cudaFree(scratch);
-    cudaStreamDestroy(s);
-    return st;
+    // 4. every rank's arena is zeroed and mapped before any rank pushes
+    sc.note(st);
+    v = sc.agree(true);
+    if (v.errors) {
+        release();
+        return sc.fail("peer exchange setup");
+    }
+    d.ar_epoch = reinterpret_cast<int*>(d.ar_arena + slot_bytes + flag_bytes);
+    d.ar.world = world;
+    d.ar.rank = d.rank;
+    d.ar.n = n;
+    d.ar.epoch = d.ar_epoch;
+    d.peer_ar = true;
+    return P100_OK;
+}
+
+// The step kernel for the decoder's format.
+using StepKernel = void (*)(stp::Params);
+StepKernel step_kernel_of(int type) {
+    switch (type) {
+        case P100_Q4_0: return stp::step_kernel<P100_Q4_0>;
+        case P100_Q8_0: return stp::step_kernel<P100_Q8_0>;
+        default: return stp::step_kernel<P100_Q4_K>;
+    }
+}
+
+stp::Mat step_mat(const DecTensor& t, int type) {
+    stp::Mat m;
+    m.w = t.ptr;
+    m.rows = t.rows;
+    m.k = t.cols;
+    m.row_bytes = static_cast<int>(dec_weight_bytes(type, 1, t.cols));
+    m.ngroups = t.cols / 256;
+    m.team = qmvt::team_lanes(m.ngroups);
+    m.teams = stp::kCThreads / m.team;
+    return m;
+}
+
+// Fills the step kernel's parameters and layer table and decides whether
+// p100_decoder_step uses it: the arena holds its buffers, the device runs
+// cooperative launches with one CTA of it per SM, and with several ranks the
+// peer exchange is set up (every rank decides alike: same configuration,
+// same verdict, same SM count).
+p100_status dec_setup_step(Decoder& d) {
+    d.use_step = false;
+    if (!d.step_region || (d.nranks > 1 && !d.peer_ar)) return P100_OK;
+    const p100_llama_config& c = d.cfg;
+    const int T = d.step_type, hd = c.head_dim, L = c.n_layer;
+    stp::Params& p = d.sp;
+    std::vector<stp::Layer> layers(static_cast<size_t>(L));
+    size_t stage_max = size_t(2) * stp::kTile * hd * 2;   // a K and a V tile
+    int act_max = 0;
+    bool whole_teams = true;   // every consumer lane in a whole team (see plan_team)
+    auto note_mat = [&](const stp::Mat& m) {
+        stage_max = std::max(stage_max, size_t(m.teams) * m.row_bytes);
+        act_max = std::max(act_max, m.k / 32 * 36);
+        if (m.team > stp::kCThreads || stp::kCThreads % m.team) whole_teams = false;
+    };
+    const size_t kv_layer = size_t(d.nkv) * c.max_ctx * hd;
+    for (int l = 0; l < L; ++l) {
+        stp::Layer& y = layers[size_t(l)];
+        y.qkv = step_mat(d.wqkv[l], T);
+        y.o = step_mat(d.wo[l], T);
+        y.gu = step_mat(d.wgu[l], T);
+        y.down = step_mat(d.wdown[l], T);
+        y.attn_norm = reinterpret_cast<const float*>(d.attn_norm[l].ptr);
+        y.ffn_norm = reinterpret_cast<const float*>(d.ffn_norm[l].ptr);
+        y.kc = d.kcache + size_t(l) * kv_layer;
+        y.vc = d.vcache + size_t(l) * kv_layer;
+        for (const stp::Mat* m : {&y.qkv, &y.o, &y.gu, &y.down}) note_mat(*m);
+    }
+    p.lm = step_mat(d.lm_head, T);
+    note_mat(p.lm);
+    if (!whole_teams) return P100_OK;
+    const size_t act_bytes = std::max<size_t>(size_t(act_max), size_t(stp::kAttnFloats) * 4);
+    p.ring_off = static_cast<int>(stp::kActOff + round128(act_bytes));
+    p.slot_bytes = static_cast<int>(round128(stage_max));
+    p.nslot = std::min(stp::kMaxSlots, (stp::kSmemLimit - p.ring_off) / p.slot_bytes);
+    if (p.nslot < 2) return P100_OK;
+    d.step_smem = size_t(p.ring_off) + size_t(p.nslot) * p.slot_bytes;
+    StepKernel kern = step_kernel_of(T);
+    int coop = 0, per_sm = 0;
+    if (cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, d.device) != cudaSuccess || !coop ||
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, stp::kSmemLimit) != cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, stp::kThreads, d.step_smem) != cudaSuccess ||
+        per_sm < 1) {
+        (void)cudaGetLastError();
+        return P100_OK;
+    }
+    p.layers = reinterpret_cast<const stp::Layer*>(d.st + d.st_layers);
+    p.n_layer = L;
+    p.out_norm = reinterpret_cast<const float*>(d.out_norm.ptr);
+    p.embed = d.embed.ptr;
+    p.embed_type = d.embed.ptype[0];
+    p.embed_row_bytes = dec_weight_bytes(p.embed_type, 1, c.hidden);
+    p.hidden = c.hidden;
+    p.nq = d.nq;
+    p.nkv = d.nkv;
+    p.G = c.n_head / c.n_head_kv;
+    p.hd = hd;
+    p.ffn = d.ffn;
+    p.vocab = c.vocab;
+    p.vocab0 = d.vocab0;
+    p.max_ctx = c.max_ctx;
+    p.eps = c.norm_eps;
+    p.scale = 1.0f / std::sqrt(float(hd));
+    p.rope = reinterpret_cast<const float2*>(d.rope);
+    p.x0 = d.x2;
+    p.x1 = d.x;
+    p.delta = d.delta;
+    p.qkv = d.qkv;
+    p.attn_q81 = d.xq;
+    p.gu = d.gu;
+    p.ffn_q81 = d.xq;
+    p.logits = d.logits;
+    p.ws_o = reinterpret_cast<float*>(d.st + d.st_ws_o);
+    p.ws_ml = reinterpret_cast<float*>(d.st + d.st_ws_ml);
+    p.tickets = reinterpret_cast<unsigned*>(d.st + d.st_tickets);
+    p.cand = reinterpret_cast<float*>(d.st + d.st_cand);
+    p.bar = reinterpret_cast<unsigned long long*>(d.st + d.st_ctr);
+    p.base = p.bar + 1;
+    p.abort_flag = reinterpret_cast<int*>(d.st + d.st_ctr + 32);
+    p.pos = d.pos;
+    p.token = d.token;
+    p.world = d.nranks;
+    p.rank = d.rank;
+    if (d.nranks == 1) {
+        p.slots[0] = nullptr;
+        p.cslots[0] = nullptr;
+        p.xcount[0] = nullptr;
+    }
+    if (p100_status st = cuda_status(cudaMemcpy(d.st + d.st_layers, layers.data(), layers.size() * sizeof(stp::Layer),
+                                                cudaMemcpyHostToDevice),
+                                     "copy step layer table"))
+        return st;
+    d.use_step = true;
+    return P100_OK;
+}
+
+// One token of the step kernel on stream s: a cooperative launch, one CTA per SM.
+p100_status dec_launch_step(Decoder& d, cudaStream_t s) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(d.sms);
+    cfg.blockDim = dim3(stp::kThreads);
+    cfg.dynamicSmemBytes = d.step_smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cuda_status(cudaLaunchKernelEx(&cfg, step_kernel_of(d.step_type), d.sp), "step_kernel launch");
 }
 
 // Collective: no rank unmaps or frees its arena before every rank's work is
@@ -751,7 +1006,16 @@ p100_status p100_decoder_create(const p100_llama_config* cfg, p100_tp* tp, p100_
     h->d.device = dev;
     h->d.sms = sms;
     p100_status st = dec_alloc(h->d);
+    if (tp) {
+        // every rank learns whether every rank allocated before any rank
+        // enters the exchanges below (a rank that returned here would leave
+        // the others waiting in them)
+        SetupComm sc(h->d);
+        sc.note(st);
+        if (sc.agree(true).errors) st = sc.fail("decoder allocation");
+    }
     if (!st) st = dec_setup_peer_ar(h->d);
+    if (!st) st = dec_setup_step(h->d);
     if (!st) {
         // P100_DEC_FUSED_NORM: RMSNorm inside the following mat-vec where
         // the team kernel has it (hidden 4096 or 8192); the one-shot peer
@@ -823,6 +1087,11 @@ p100_status p100_decoder_step(p100_decoder* h, int n_steps, p100_stream_t stream
     if (!h) return set_error(P100_ERR_INVALID, "null decoder");
     if (n_steps < 0) return set_error(P100_ERR_INVALID, "n_steps must be >= 0");
     DeviceGuard guard(h->d.device);
+    if (h->d.use_step) {
+        for (int i = 0; i < n_steps; ++i)
+            if (p100_status st = dec_launch_step(h->d, stream)) return st;
+        return P100_OK;
+    }
     if (!h->d.graph_exec)
         if (p100_status st = dec_capture(h->d)) return st;
     for (int i = 0; i < n_steps; ++i)
@@ -879,6 +1148,9 @@ p100_status p100_decoder_buffer(p100_decoder* h, int which, void** ptr, size_t* 
 }
 
 int p100_decoder_vocab_offset(const p100_decoder* h) { return h ? h->d.vocab0 : 0; }
+int p100_decoder_path(const p100_decoder* h) {
+    return h && h->d.use_step ? P100_DEC_PATH_STEP : P100_DEC_PATH_GRAPH;
+}
 size_t p100_decoder_weight_bytes_per_token(const p100_decoder* h) {
     if (!h) return 0;
     const p100b::Decoder& d = h->d;

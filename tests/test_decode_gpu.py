@@ -183,14 +183,22 @@ def mixed_types():
 TINY_MIXED = dict(TINY, tensor_types=mixed_types())
 
 
-@pytest.mark.parametrize("wtype,shape", [(P.Q4_0, TINY), (P.Q8_0, TINY), (P.Q4_K, TINY), (P.Q4_0, TINY_D256),
-                                         (P.Q4_K, TINY_MIXED)],
-                         ids=["q4_0", "q8_0", "q4_k", "q4_0-d256-unfused", "mixed"])
-def test_decoder_matches_restated_steps(cuda, orc, wtype, shape):
-    cfg = P.LlamaConfig(**shape, wtype=wtype)
+# The graph of separate kernels is the default path; the persistent step
+# kernel (one launch a token, P100_DEC_STEP) serves one-format models with an
+# fp16 cache and head_dim 64/128 on request, and the graph serves the rest.
+@pytest.mark.parametrize("wtype,shape,flags,path", [
+    (P.Q4_0, TINY, P.DEC_STEP, P.DEC_PATH_STEP), (P.Q8_0, TINY, P.DEC_STEP, P.DEC_PATH_STEP),
+    (P.Q4_K, TINY, P.DEC_STEP, P.DEC_PATH_STEP), (P.Q4_0, TINY, 0, P.DEC_PATH_GRAPH),
+    (P.Q8_0, TINY, 0, P.DEC_PATH_GRAPH), (P.Q4_K, TINY, 0, P.DEC_PATH_GRAPH),
+    (P.Q4_0, TINY_D256, P.DEC_STEP, P.DEC_PATH_GRAPH), (P.Q4_K, TINY_MIXED, P.DEC_STEP, P.DEC_PATH_GRAPH)],
+    ids=["q4_0-step", "q8_0-step", "q4_k-step", "q4_0-graph", "q8_0-graph", "q4_k-graph", "q4_0-d256-unfused",
+         "mixed"])
+def test_decoder_matches_restated_steps(cuda, orc, wtype, shape, flags, path):
+    cfg = P.LlamaConfig(**shape, wtype=wtype, flags=flags)
     ocfg = oracle.LlamaConfig(*[getattr(cfg, f) for f, _ in oracle.LlamaConfig._fields_])
     dec = P.Decoder(cfg)
     try:
+        assert dec.path == path
         dec.init_random(1234 + wtype)
         npos = 200
         dec.fill_kv(npos, 77, 0.5)
@@ -382,3 +390,35 @@ def test_mixed_tensor_layout(cuda):
     bad[P.tt_layer(1, P.TT_GATE)] = 9
     with pytest.raises(P.InvalidArgument):
         P.Decoder(P.LlamaConfig(**dict(TINY, tensor_types=bad)))
+
+
+@pytest.mark.parametrize("wtype,shape", [(P.Q4_0, dict(H4096, n_head=32, n_head_kv=8)),
+                                         (P.Q4_K, dict(H4096, n_head=64, n_head_kv=8, head_dim=64))],
+                         ids=["q4_0-g4-d128", "q4_k-g8-d64"])
+def test_step_kernel_tracks_graph_decoder(cuda, wtype, shape):
+    """The persistent step kernel (P100_DEC_STEP) against the graph decoder on
+    the 8B head geometry, 8 free-running steps from the same state: the same
+    tokens, logits within the decode bound.  The two differ only in the
+    attention arithmetic (FP32 SIMT against tensor-core hi/lo), which the
+    Q8_1 rounding of the attention output absorbs almost always."""
+    runs = []
+    for flags in (P.DEC_STEP, 0):
+        dec = P.Decoder(P.LlamaConfig(**shape, wtype=wtype, flags=flags))
+        try:
+            assert dec.path == (P.DEC_PATH_STEP if flags else P.DEC_PATH_GRAPH)
+            dec.init_random(77 + wtype)
+            dec.fill_kv(300, 3, 0.5)
+            dec.set_state(300, 11)
+            toks = []
+            for _ in range(8):
+                dec.step(1)
+                toks.append(dec.state())
+            runs.append((toks, dec.read(*dec.buffer(P.B_LOGITS)).view(np.float32).copy(),
+                         dec.read(*dec.buffer(P.B_HIDDEN)).view(np.float32).copy()))
+            assert P.device_error() == P.OK
+        finally:
+            dec.close()
+    (ta, la, ha), (tb, lb, hb) = runs
+    assert ta == tb
+    assert np.abs(la - lb).max() <= DECODE_LOGIT_TOL * np.abs(lb).max()
+    assert np.abs(ha - hb).max() <= 5e-2 * np.abs(hb).max()
