@@ -11,24 +11,30 @@ and multiply it by a Q4_0 weight matrix (8 kernel launches).  Successive steps
 rotate over distinct weight copies totalling more than 3x the 126 MB L2, so
 every step streams its weights from HBM.
 
-value   = algorithmic bytes (weights + fp32 x + fp32 y, bin/mm-gbps.py:51-57)
-          of all ranks / device time of the K steps (CUDA events, max over
-          ranks), in GB/s.
-e2e     = the same metric through the C-ABI with host buffers: each step
+value   = algorithmic bytes of the step (weights + fp32 x + fp32 y,
+          bin/mm-gbps.py:51-57) / device time (CUDA events, max over ranks),
+          in GB/s: the median over interleaved rounds of K steps each, the
+          rounds repeated until they span at least a second (`rounds`).
+          N = 1: the whole step on one GPU.  N > 1 (torchrun, one rank per
+          GPU): the same layer step split over the ranks, strong scaling —
+          q/o and down along k (partial sums, an NCCL all-reduce each inside
+          the timed region), k/v and gate/up by rows; `replicated` keeps the
+          weak-scaling figure (every rank the whole shapes, no collective).
+e2e     = the headline's step through the C-ABI with host buffers: each step
           copies its activations from pinned host memory, runs, copies y back
           and synchronises before the host reads it.
 roofline: the gate/up mat-vec (4096 x 14336, the target shape) timed alone
-          over back-to-back launches; achieved = its algorithmic bytes per
-          launch / average launch time, against MEASURED_PEAKS.json hbm_gbs.
-Multi-GPU (torchrun, one rank per GPU): weak scaling.  Each rank streams the
-row shards of an N-times wider layer stack — the same per-GPU shapes — with
-no collective on the data path (row-split mat-vecs exchange nothing).
+          over back-to-back launches in every round; achieved = its
+          algorithmic bytes per launch / median launch time, against
+          MEASURED_PEAKS.json hbm_gbs.
 --impl reference times the reference's own CPU path (prepare + evaluate per
 row, oracle/_ref) on the host cores over a bounded sample of the same rows.
 decode  = configs 4/5: batch-1 decode tokens/s of the Llama-3 8B and 70B
           shapes (random-init Q4_0, KV prefilled to 4096 / 8192), split over
           the ranks (TP = N), with each GPU's bytes per token against the HBM
-          roofline.
+          roofline; at N > 1 the 8B model's tp_parity against the unsplit
+          model and the exchange's cost per layer, and `collective` (NCCL
+          all-reduce latency and bus bandwidth at the exchange sizes).
 """
 from __future__ import annotations
 
@@ -416,34 +422,80 @@ def ktypes_section(torch, P, stream):
     return out
 
 
-def decode_section(torch, P, stream, rank, world, dist, max_over_ranks):
+def stats(values):
+    """Median, min and max of a measurement repeated over rounds."""
+    return {"median": round(statistics.median(values), 4), "min": round(min(values), 4),
+            "max": round(max(values), 4), "rounds": len(values)}
+
+
+DECODE_ROUNDS = 3
+PARITY_STEPS = 8
+
+
+def decode_parity(torch, P, m, cfg_kwargs, dec, stream, world, dist):
+    """TP=N against TP=1 in the same run: every rank also builds the unsplit
+    model (one GPU holds it beside its slice), both start from the same state
+    and run PARITY_STEPS steps; each step the TP decoder is fed the TP=1
+    token.  Reports whether every step picked the same token and the largest
+    logit difference (each rank its vocabulary slice, max over ranks)
+    relative to the TP=1 logits' largest magnitude."""
+    ctx = m["ctx"]
+    ref = P.Decoder(P.LlamaConfig(**cfg_kwargs), None)
+    try:
+        for d in (ref, dec):
+            d.init_random(20261201)
+            d.fill_kv(ctx, 7, 0.5)
+            d.set_state(ctx, 1)
+        off = dec.vocab_offset
+        equal, worst = True, 0.0
+        for _ in range(PARITY_STEPS):
+            ref.step(1, stream)
+            dec.step(1, stream)
+            rpos, rtok = ref.state()
+            pos, tok = dec.state()
+            rl = ref.read(*ref.buffer(P.B_LOGITS)).view(np.float32)
+            gl = dec.read(*dec.buffer(P.B_LOGITS)).view(np.float32)
+            worst = max(worst, float(np.abs(gl - rl[off:off + gl.size]).max() / np.abs(rl).max()))
+            equal = equal and tok == rtok and pos == rpos
+            if tok != rtok:
+                dec.set_state(pos, rtok)   # teacher-forced: the next step starts from the same token
+    finally:
+        ref.close()
+    t = torch.tensor([worst, 0.0 if equal else 1.0], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return {"steps": PARITY_STEPS, "tokens_equal": t[1].item() == 0.0, "max_logit_diff": round(t[0].item(), 8),
+            "bound": 1e-2, "against": "the unsplit model on one GPU (every rank), same state, teacher-forced tokens"}
+
+
+def decode_section(torch, P, stream, rank, world, dist, max_over_ranks, tp):
     """Configs 4/5: batch-1 decode tokens/s of the 8B and 70B shapes, the model
-    row-split over the `world` ranks (TP=world, NCCL all-reduce after o and
-    down).  KV prefilled to the config's context (N(0,1)*0.5 fp16); each step
-    appends one row and attends over the whole cache, one CUDA graph per token
-    replayed back to back; CUDA events, max over ranks.  e2e additionally
-    reads every token on the host (4 bytes per step)."""
+    row-split over the `world` ranks (TP=world; o and down all-reduced
+    through NVLink peer memory, pushed from the mat-vec's epilogue).  KV
+    prefilled to the config's context (N(0,1)*0.5 fp16); each step appends
+    one row and attends over the whole cache, one CUDA graph per token
+    replayed back to back; CUDA events, max over ranks, DECODE_ROUNDS rounds
+    (median, min, max).  e2e additionally reads every token on the host.
+    With world > 1 the 8B model also reports tp_parity (against the unsplit
+    model) and the exchange's cost (the step minus the same slice shapes
+    decoded alone on one GPU, per layer)."""
     out = {}
     peak, _ = peak_gbs()
-    tp = None
-    if world > 1:
-        box = [P.tp_unique_id() if rank == 0 else None]
-        dist.broadcast_object_list(box, src=0)
-        tp = P.TP(box[0], world, rank, torch.cuda.current_device())
-    try:
-        for name, m in DECODE_MODELS.items():
-            ctx = m["ctx"]
-            mix = q4_k_m_types(P, m["n_layer"]) if m.get("mix") == "q4_k_m" else None
-            cfg = P.LlamaConfig(m["n_layer"], m["hidden"], m["n_head"], m["n_head_kv"], m["head_dim"], m["ffn"],
-                                m["vocab"], ctx + DECODE_WARMUP + 2 * DECODE_STEPS + 8,
-                                wtype=P.Q4_K if mix else P.Q4_0, tensor_types=mix)
-            dec = P.Decoder(cfg, tp)
-            try:
-                dec.init_random(20261201)
-                dec.fill_kv(ctx, 7, 0.5)
-                dec.set_state(ctx, 1)
-                dec.step(DECODE_WARMUP, stream)
-                torch.cuda.synchronize()
+    for name, m in DECODE_MODELS.items():
+        ctx = m["ctx"]
+        mix = q4_k_m_types(P, m["n_layer"]) if m.get("mix") == "q4_k_m" else None
+        cfg_kwargs = dict(n_layer=m["n_layer"], hidden=m["hidden"], n_head=m["n_head"], n_head_kv=m["n_head_kv"],
+                          head_dim=m["head_dim"], ffn=m["ffn"], vocab=m["vocab"],
+                          max_ctx=ctx + DECODE_WARMUP + (DECODE_ROUNDS + 2) * DECODE_STEPS + PARITY_STEPS + 8,
+                          wtype=P.Q4_K if mix else P.Q4_0, tensor_types=mix)
+        dec = P.Decoder(P.LlamaConfig(**cfg_kwargs), tp)
+        try:
+            dec.init_random(20261201)
+            dec.fill_kv(ctx, 7, 0.5)
+            dec.set_state(ctx, 1)
+            dec.step(DECODE_WARMUP, stream)
+            torch.cuda.synchronize()
+            per = []
+            for _ in range(DECODE_ROUNDS):
                 if dist is not None:
                     dist.barrier()
                 a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -451,27 +503,73 @@ def decode_section(torch, P, stream, rank, world, dist, max_over_ranks):
                 dec.step(DECODE_STEPS, stream)
                 b.record(stream)
                 b.synchronize()
-                ms = max_over_ranks(a.elapsed_time(b)) / DECODE_STEPS
-                t0 = time.perf_counter()
-                for _ in range(DECODE_STEPS):
-                    dec.step(1, stream)
-                    dec.state()               # synchronises and reads the token on the host
-                e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1e3) / DECODE_STEPS
-                pos, tok = dec.state()
-                kv_rank = m["n_layer"] * 2 * (m["n_head_kv"] // world) * m["head_dim"] * 2 * (ctx + DECODE_WARMUP
-                                                                                            + DECODE_STEPS)
-                rank_bytes = dec.weight_bytes_per_token + kv_rank
-                out[name] = {"tok_s": round(1e3 / ms, 2), "ms_per_token": round(ms, 4), "context": ctx,
-                             "tp": world, "bytes_per_token_per_gpu": rank_bytes,
-                             "hbm_frac_per_gpu": round(rank_bytes / (ms / 1e3) / 1e9 / peak, 4),
-                             "e2e_tok_s": round(1e3 / e2e_ms, 2), "last_token": tok, "position": pos}
-            finally:
-                dec.close()   # releases the graph (and its NCCL calls) before the communicator
-            P.check(P.device_error())
-    finally:
-        if tp is not None:
-            tp.close()
+                per.append(max_over_ranks(a.elapsed_time(b)) / DECODE_STEPS)
+            ms = statistics.median(per)
+            t0 = time.perf_counter()
+            for _ in range(DECODE_STEPS):
+                dec.step(1, stream)
+                dec.state()               # synchronises and reads the token on the host
+            e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1e3) / DECODE_STEPS
+            pos, tok = dec.state()
+            kv_rank = m["n_layer"] * 2 * (m["n_head_kv"] // world) * m["head_dim"] * 2 * (ctx + DECODE_WARMUP
+                                                                                        + DECODE_STEPS)
+            rank_bytes = dec.weight_bytes_per_token + kv_rank
+            row = {"tok_s": round(1e3 / ms, 2), "ms_per_token": round(ms, 4),
+                   "tok_s_rounds": stats([1e3 / v for v in per]), "context": ctx, "tp": world,
+                   "bytes_per_token_per_gpu": rank_bytes,
+                   "hbm_frac_per_gpu": round(rank_bytes / (ms / 1e3) / 1e9 / peak, 4),
+                   "e2e_tok_s": round(1e3 / e2e_ms, 2), "last_token": tok, "position": pos,
+                   "exchange": ("peer memory, pushed from the o/down mat-vec epilogue" if world > 1 else "none")}
+            if world > 1 and name == "llama3-8b":
+                row["tp_parity"] = decode_parity(torch, P, m, cfg_kwargs, dec, stream, world, dist)
+                row["exchange_us_per_layer"] = exchange_cost(torch, P, m, ms, stream, world, max_over_ranks)
+            out[name] = row
+        finally:
+            dec.close()   # releases the graph (and any NCCL calls in it) before the communicator
+        P.check(P.device_error())
     return out
+
+
+def exchange_cost(torch, P, m, ms_tp, stream, world, max_over_ranks):
+    """Per layer: the TP=world step minus the same slice shapes (n_head/N,
+    n_head_kv/N, ffn/N, vocab/N) decoded alone on this GPU with no exchange."""
+    cfg = P.LlamaConfig(m["n_layer"], m["hidden"], m["n_head"] // world, m["n_head_kv"] // world, m["head_dim"],
+                        m["ffn"] // world, m["vocab"] // world, m["ctx"] + DECODE_WARMUP + DECODE_STEPS + 8)
+    dec = P.Decoder(cfg, None)
+    try:
+        dec.init_random(3)
+        dec.fill_kv(m["ctx"], 7, 0.5)
+        dec.set_state(m["ctx"], 1)
+        dec.step(DECODE_WARMUP, stream)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        dec.step(DECODE_STEPS, stream)
+        b.record(stream)
+        b.synchronize()
+        ms_slice = max_over_ranks(a.elapsed_time(b)) / DECODE_STEPS
+    finally:
+        dec.close()
+    return {"slice_alone_ms": round(ms_slice, 4), "tp_ms": round(ms_tp, 4),
+            "us_per_layer": round((ms_tp - ms_slice) * 1e3 / m["n_layer"], 3)}
+
+
+def collective_section(torch, P, tp, stream, world):
+    """NCCL all-reduce (p100_tp_allreduce_sum, fp32 sum) of the per-layer
+    exchange sizes, 64 calls captured in a graph: latency per call and bus
+    bandwidth 2 (N-1)/N x bytes / time (the analogue of the reference's
+    p2p_bandwidth benchmark for this layout's only collective)."""
+    out = {}
+    for nbytes in (16384, 32768, 65536):
+        buf = torch.ones(nbytes // 4, device="cuda")
+        g = capture(torch, lambda: [tp.allreduce_sum(buf, stream=stream) for _ in range(64)])
+        time_graphs(torch, [g], 3, stream)
+        per = [time_graphs(torch, [g], 5, stream) / (5 * 64) * 1e3 for _ in range(3)]
+        us = statistics.median(per)
+        out[f"{nbytes // 1024}KB"] = {"us": round(us, 3), "busbw_GBs": round(2 * (world - 1) / world * nbytes / us / 1e3, 3),
+                                      "us_rounds": stats(per)}
+        del g
+    return {"nccl_allreduce": out}
 
 
 def c2_grid(torch, P, stream):
@@ -617,15 +715,33 @@ def main():
 
     torch.cuda.set_device(local)
     dist = None
+    tp = None
     if world > 1:
         import datetime
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
     P.check(P.device_check(local))
     stream = torch.cuda.current_stream()
+    if world > 1:
+        box = [P.tp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(box, src=0)
+        tp = P.TP(box[0], world, rank, local)
 
-    # Weights: one host-generated set per shape, replicated on the device into
-    # `copies` copies so successive steps rotate through more than 3x L2.
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if dist is None:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.item()
+
+    # The full layer step (every rank the whole shapes; at N > 1 the
+    # replicated weak-scaling figure): one host-generated set per shape,
+    # replicated on the device into `copies` copies so successive steps
+    # rotate through more than 3x L2.
     per_copy = sum(W.weights(W.Q4_0, 1, k, 0).size * rows for _, k, rows in SHAPES)
     copies = max(4, int(np.ceil(3 * L2_BYTES / per_copy)) + 1)
     wdev = []
@@ -647,71 +763,138 @@ def main():
         for si, (name, k, rows) in enumerate(SHAPES):
             P.qmv_f32(W.Q4_0, wdev[si][c], rows, k, xs[si], x_q8_1=xqs[si], y=ys[si], flags=P.QMV_PDL)
 
-    def barrier():
-        if dist is not None:
-            dist.barrier()
-
-    def max_over_ranks(v):
-        if dist is None:
-            return v
-        t = torch.tensor([v], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return t.item()
-
-    # One graph per weight copy: step i replays graph i % copies.
     graphs = [capture(torch, lambda c=c: step_body(c)) for c in range(copies)]
+
+    # N > 1: the same global layer step split over the ranks (the headline,
+    # strong scaling): q/o and down split along k (their outputs are partial
+    # sums, all-reduced in the timed region), k/v and gate/up by rows.
+    split_graphs, split_copies, split_launches = None, 0, 0
+    if world > 1:
+        plan = []
+        for si, (name, k, rows) in enumerate(SHAPES):
+            ksplit = name in ("q/o", "down")
+            plan.append((ksplit, k // world if ksplit else k, rows if ksplit else rows // world))
+        split_per_copy = sum(W.weights(W.Q4_0, 1, lk, 0).size * lr for _, lk, lr in plan)
+        split_copies = max(4, int(np.ceil(3 * L2_BYTES / split_per_copy)) + 1)
+        sw, sx, sq, sy = [], [], [], []
+        for si, (ksplit, lk, lr) in enumerate(plan):
+            base = torch.from_numpy(W.weights(W.Q4_0, lr, lk, seed=5000 + si + 17 * rank)).cuda()
+            sw.append([base] + [base.clone() for _ in range(split_copies - 1)])
+            sx.append(torch.from_numpy(W.activations(1, lk, seed=6000 + si + 17 * rank)).cuda())
+            sq.append(torch.empty(P.q8_1_bytes(lk, 1), dtype=torch.uint8, device="cuda"))
+            sy.append(torch.empty(1, lr, dtype=torch.float32, device="cuda"))
+
+        def split_body(c):
+            for si, (ksplit, lk, lr) in enumerate(plan):
+                P.qmv_f32(W.Q4_0, sw[si][c], lr, lk, sx[si], x_q8_1=sq[si], y=sy[si], flags=P.QMV_PDL)
+                if ksplit:
+                    tp.allreduce_sum(sy[si], stream=stream)
+
+        split_graphs = [capture(torch, lambda c=c: split_body(c)) for c in range(split_copies)]
+        split_launches = 2 * len(SHAPES)
+
+    # The target shape alone (the roofline): a graph of 4*copies back-to-back
+    # launches over the rotating copies, chained with PDL and isolated.
+    ti = [i for i, sh in enumerate(SHAPES) if sh == TARGET][0]
+    P.q8_1_quantize(xs[ti], out=xqs[ti])
+    n_in_graph = 4 * copies
+    target_graphs = {}
+    for mode, flags in (("chained", P.QMV_PDL), ("isolated", 0)):
+        target_graphs[mode] = capture(torch, lambda flags=flags: [
+            P.qmv(W.Q4_0, wdev[ti][r % copies], TARGET[2], TARGET[1], xqs[ti], 1, y=ys[ti], flags=flags)
+            for r in range(n_in_graph)])
+    head_graphs = split_graphs if split_graphs else graphs
     time_graphs(torch, graphs, args.warmup, stream)
+    if split_graphs:
+        time_graphs(torch, split_graphs, args.warmup, stream)
+    for g in target_graphs.values():
+        time_graphs(torch, [g], 3, stream)
     barrier()
     torch.cuda.synchronize()
-    with ClockSampler(local) as clocks:
-        ms = time_graphs(torch, graphs, args.steps, stream)
-    ms = max_over_ranks(ms)
-    barrier()
-    per_step = step_bytes()
-    value = per_step * world * args.steps / (ms / 1e3) / 1e9
 
-    # Each shape alone: a graph of 4*copies back-to-back launches over the
-    # rotating copies, chained with PDL (each launch's weights stream in while
-    # the previous one finishes) and, for comparison, isolated.
-    shape_gbs, target_us, target_us_isolated = {}, None, None
+    # Interleaved rounds: each round times exactly --steps steps of the
+    # headline (barrier and synchronisation on both sides, max over ranks),
+    # then the replicated step (N > 1) and the target shape chained and
+    # isolated; rounds repeat until the window covers a second (at least 3).
+    head_ms, rep_ms, chained_us, isolated_us = [], [], [], []
+    reps = 10
+    t_start = time.perf_counter()
+    with ClockSampler(local) as clocks:
+        while True:
+            barrier()
+            torch.cuda.synchronize()
+            head_ms.append(max_over_ranks(time_graphs(torch, head_graphs, args.steps, stream)))
+            barrier()
+            if split_graphs:
+                rep_ms.append(max_over_ranks(time_graphs(torch, graphs, args.steps, stream)))
+            chained_us.append(time_graphs(torch, [target_graphs["chained"]], reps, stream) / (reps * n_in_graph) * 1e3)
+            isolated_us.append(time_graphs(torch, [target_graphs["isolated"]], reps, stream) / (reps * n_in_graph) * 1e3)
+            window = max_over_ranks(time.perf_counter() - t_start)
+            if len(head_ms) >= 3 and (window >= 1.0 or len(head_ms) >= 200):
+                break
+    window_s = time.perf_counter() - t_start
+    del target_graphs
+    per_step = step_bytes()
+    ms = statistics.median(head_ms)
+    value = per_step * args.steps / (ms / 1e3) / 1e9 if split_graphs else per_step * world * args.steps / (ms / 1e3) / 1e9
+    head_gbs = [per_step * (1 if split_graphs else world) * args.steps / (v / 1e3) / 1e9 for v in head_ms]
+    replicated = None
+    if split_graphs:
+        rgbs = [per_step * world * args.steps / (v / 1e3) / 1e9 for v in rep_ms]
+        replicated = {"value": round(statistics.median(rgbs), 2), "unit": "GB/s", "scaling": "weak",
+                      "rounds": stats(rgbs),
+                      "form": "every rank streams the full layer shapes (its own weights), no data-path collective"}
+    target_us, target_us_isolated = statistics.median(chained_us), statistics.median(isolated_us)
+
+    # Each shape alone (chained and isolated), for the record.
+    shape_gbs = {}
     for si, (name, k, rows) in enumerate(SHAPES):
         P.q8_1_quantize(xs[si], out=xqs[si])
-        n_in_graph = 4 * copies
         per = {}
         for mode, flags in (("chained", P.QMV_PDL), ("isolated", 0)):
             g = capture(torch, lambda si=si, k=k, rows=rows, flags=flags: [
                 P.qmv(W.Q4_0, wdev[si][r % copies], rows, k, xqs[si], 1, y=ys[si], flags=flags)
                 for r in range(n_in_graph)])
             time_graphs(torch, [g], 3, stream)
-            reps = 20
-            per[mode] = time_graphs(torch, [g], reps, stream) / (reps * n_in_graph) * 1e3
+            per[mode] = time_graphs(torch, [g], 20, stream) / (20 * n_in_graph) * 1e3
+            del g
         nbytes = W.qmv_algorithmic_bytes(W.Q4_0, rows, k, 1)
         shape_gbs[f"{name} {k}x{rows}"] = {
             "us": round(per["chained"], 3), "GB/s": round(nbytes / (per["chained"] / 1e6) / 1e9, 1),
             "us_isolated": round(per["isolated"], 3),
             "GB/s_isolated": round(nbytes / (per["isolated"] / 1e6) / 1e9, 1)}
-        if (name, k, rows) == TARGET:
-            target_us, target_us_isolated = per["chained"], per["isolated"]
 
     batch_sweep = c2_grid(torch, P, stream) if rank == 0 else None
 
-    # End to end through the C-ABI with host buffers: each step copies its
-    # activations in from pinned memory, runs, copies y out and synchronises
-    # before the host reads the result.  "graph": the calls captured once and
-    # replayed (a decode loop's form); "eager": the calls issued every step.
-    xh = [torch.from_numpy(W.activations(1, k, seed=3000 + si)).pin_memory() for si, (_, k, _) in enumerate(SHAPES)]
-    yh = [torch.empty(1, rows, dtype=torch.float32).pin_memory() for _, _, rows in SHAPES]
-    xd = [torch.empty(1, k, dtype=torch.float32, device="cuda") for _, k, _ in SHAPES]
+    # End to end through the C-ABI with host buffers, on the headline's step
+    # (the split step at N > 1): each step copies its activations in from
+    # pinned memory, runs (with its all-reduces), copies y out and
+    # synchronises before the host reads the result.  "graph": the calls
+    # captured once and replayed (a decode loop's form); "eager": the calls
+    # issued every step.  Three rounds, the median.
+    if split_graphs:
+        e_plan = [(sw[si], lk, lr, ksplit) for si, (ksplit, lk, lr) in enumerate(plan)]
+        e_copies = split_copies
+    else:
+        e_plan = [(wdev[si], k, rows, False) for si, (_, k, rows) in enumerate(SHAPES)]
+        e_copies = copies
+    xh = [torch.from_numpy(W.activations(1, lk, seed=3000 + si)).pin_memory() for si, (_, lk, _, _) in enumerate(e_plan)]
+    yh = [torch.empty(1, lr, dtype=torch.float32).pin_memory() for _, _, lr, _ in e_plan]
+    xd = [torch.empty(1, lk, dtype=torch.float32, device="cuda") for _, lk, _, _ in e_plan]
+    eq = [torch.empty(P.q8_1_bytes(lk, 1), dtype=torch.uint8, device="cuda") for _, lk, _, _ in e_plan]
+    ey = [torch.empty(1, lr, dtype=torch.float32, device="cuda") for _, _, lr, _ in e_plan]
     h2d = sum(t.numel() * 4 for t in xh)
     d2h = sum(t.numel() * 4 for t in yh)
 
     def e2e_body(c):
-        for si, (name, k, rows) in enumerate(SHAPES):
+        for si, (wl, lk, lr, ksplit) in enumerate(e_plan):
             xd[si].copy_(xh[si], non_blocking=True)
-            P.qmv_f32(W.Q4_0, wdev[si][c], rows, k, xd[si], x_q8_1=xqs[si], y=ys[si], flags=P.QMV_PDL)
-            yh[si].copy_(ys[si], non_blocking=True)
+            P.qmv_f32(W.Q4_0, wl[c], lr, lk, xd[si], x_q8_1=eq[si], y=ey[si], flags=P.QMV_PDL)
+            if ksplit:
+                tp.allreduce_sum(ey[si], stream=stream)
+            yh[si].copy_(ey[si], non_blocking=True)
 
-    e2e_graphs = [capture(torch, lambda c=c: e2e_body(c)) for c in range(copies)]
+    e2e_graphs = [capture(torch, lambda c=c: e2e_body(c)) for c in range(e_copies)]
     checksum = 0.0
 
     def e2e_run(n, eager):
@@ -720,9 +903,9 @@ def main():
         s.record(stream)
         for i in range(n):
             if eager:
-                e2e_body(i % copies)
+                e2e_body(i % e_copies)
             else:
-                e2e_graphs[i % copies].replay()
+                e2e_graphs[i % e_copies].replay()
             stream.synchronize()
             checksum += float(yh[0][0, 0])      # the host reads the step's result
         e.record(stream)
@@ -731,42 +914,56 @@ def main():
 
     e2e_run(args.warmup, False)
     e2e_run(args.warmup, True)
-    barrier()
-    e2e_ms = max_over_ranks(e2e_run(args.steps, False))
-    e2e_eager_ms = max_over_ranks(e2e_run(args.steps, True))
-    barrier()
-    e2e_value = per_step * world * args.steps / (e2e_ms / 1e3) / 1e9
-    e2e_eager = per_step * world * args.steps / (e2e_eager_ms / 1e3) / 1e9
+    e2e_rounds, e2e_eager_rounds = [], []
+    for _ in range(3):
+        barrier()
+        e2e_rounds.append(max_over_ranks(e2e_run(args.steps, False)))
+        barrier()
+        e2e_eager_rounds.append(max_over_ranks(e2e_run(args.steps, True)))
+    job_bytes = per_step * (1 if split_graphs else world) * args.steps
+    e2e_value = job_bytes / (statistics.median(e2e_rounds) / 1e3) / 1e9
+    e2e_eager = job_bytes / (statistics.median(e2e_eager_rounds) / 1e3) / 1e9
     del e2e_graphs
     fa = fa_section(torch, P, stream) if rank == 0 else None
     h16 = h16_section(torch, P, stream) if rank == 0 else None
     kvq = kv_quant_section(torch, P, stream) if rank == 0 else None
     kq = ktypes_section(torch, P, stream) if rank == 0 else None
     P.check(P.device_error())
-    decode = decode_section(torch, P, stream, rank, world, dist, max_over_ranks) if not args.no_decode else None
+    decode = decode_section(torch, P, stream, rank, world, dist, max_over_ranks, tp) if not args.no_decode else None
+    collective = collective_section(torch, P, tp, stream, world) if tp is not None else None
 
     peak, peak_kind = peak_gbs()
     target_bytes = W.qmv_algorithmic_bytes(W.Q4_0, TARGET[2], TARGET[1], 1)
     achieved = target_bytes / (target_us / 1e6) / 1e9
+    split_desc = ("TP=%d: q/o and down split along k (partial sums, an NCCL all-reduce of 16 KB each in the timed "
+                  "region), k/v and gate/up split by rows" % world)
     result = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True,
+        "scaling": "strong" if split_graphs else "weak",
         "vs_baseline": None, "dtype": "int8/fp32", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "global_batch": world, "seq_len": 1,
-                   "parallelism": f"row-split shards x{world}, no data-path collective" if world > 1 else "1 GPU",
-                   "l2": f"inputs larger than L2: {copies} rotating weight copies ({copies * per_copy / 1e6:.0f} MB)",
+        "rounds": dict(stats(head_gbs), window_s=round(window_s, 3), steps_per_round=args.steps),
+        "config": {"workload": WORKLOAD, "global_batch": 1, "seq_len": 1,
+                   "parallelism": split_desc if split_graphs else "1 GPU",
+                   "l2": f"inputs larger than L2: {split_copies if split_graphs else copies} rotating weight copies",
                    "launch": "one p100_qmv_f32 call per shape (Q8_1 quantiser + mat-vec, PDL-chained), captured into one CUDA graph per weight copy, replayed per step"},
         "roofline": {"bound": "hbm", "kernel": "qmv_team_kernel<Q4_0> gate/up 4096x14336",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_source": peak_kind,
                      "traffic": ncu_traffic("qmv_q4_0_4096x14336"), "algorithmic_bytes": target_bytes,
                      "us_per_launch": round(target_us, 3),
-                     "timing": "CUDA events over graph replays of back-to-back launches chained with PDL",
+                     "us_rounds": stats(chained_us),
+                     "frac_rounds": stats([target_bytes / (u / 1e6) / 1e9 / peak for u in chained_us]),
+                     "timing": "CUDA events over graph replays of back-to-back launches chained with PDL, "
+                               "interleaved with the headline's rounds",
                      "isolated_us_per_launch": round(target_us_isolated, 3),
                      "isolated_frac": round(target_bytes / (target_us_isolated / 1e6) / 1e9 / peak, 4)},
         "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "form": "graph replay + stream sync + host read per step", "eager_value": round(e2e_eager, 2)},
-        "gpu_launches": launches_per_step * args.steps,
+                "form": "graph replay + stream sync + host read per step (median of 3 rounds)",
+                "eager_value": round(e2e_eager, 2)},
+        "gpu_launches": (split_launches if split_graphs else launches_per_step) * args.steps * len(head_ms),
+        "gpu_launches_note": "the library's kernels in the headline's timed rounds (NCCL kernels not counted)",
+        "replicated": replicated,
         "shapes": shape_gbs,
         "batch_sweep": batch_sweep,
         "fa_decode": fa,
@@ -774,6 +971,7 @@ def main():
         "quantised_kv": kvq,
         "ktypes_qmv": kq,
         "decode": decode,
+        "collective": collective,
         "clocks": clocks.summary(),
         "checksum": round(checksum, 3),
     }
@@ -781,7 +979,10 @@ def main():
         result["cpu_baseline"] = cpu_baseline_sample()
     if rank == 0:
         print(json.dumps(result), flush=True)
-    del graphs
+    del graphs, split_graphs   # their NCCL calls go before the communicator
+    torch.cuda.synchronize()
+    if tp is not None:
+        tp.close()
     if dist is not None:
         dist.destroy_process_group()
     return 0

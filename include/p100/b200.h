@@ -279,6 +279,22 @@ p100_status p100_swiglu_q8_1(const float* gate_up, int n, int batch, void* x_q8_
  * index among equal maxima; NaN never wins. */
 p100_status p100_argmax(const float* x, int n, int batch, int* idx, float* val, p100_stream_t stream);
 
+/* One rank's reduce of the one-shot peer all-reduce, fused with RMSNorm +
+ * Q8_1 (the graph decoder's exchange; no reference counterpart).  slots is
+ * this rank's arena of [2][world][k] fp32 partials, into which every rank's
+ * push stores its partial sum at [e & 1][that rank], e = *epoch + 1; each
+ * pushing CTA then adds 1 to every rank's counter.  The kernel waits until
+ * *count >= *done + arrivals — for at most wait_ns nanoseconds (0: about a
+ * second) — then x += the world slots added in rank order, RMSNorm * w into
+ * x_q8_1 (p100_rmsnorm_q8_1's arithmetic), *epoch = e, *done += arrivals.
+ * A wait that runs out raises P100_ERR_TIMEOUT in p100_device_error() and the
+ * kernel returns normally (the sums then hold whatever the slots held); the
+ * exchange state is then undefined.  k % 32 == 0, k <= 16384; x, w and slots
+ * 16-byte aligned. */
+p100_status p100_peer_reduce_rmsnorm(float* x, const float* w, float eps, int k, void* x_q8_1, float* slots, int world,
+                                     int rank, int* epoch, unsigned long long* count, unsigned long long* done,
+                                     unsigned long long arrivals, unsigned long long wait_ns, p100_stream_t stream);
+
 /* --------------------------------------------------- batch-1 decoder */
 /* A Llama-3-shaped model with synthetic weights, decoded one token per
  * p100_decoder_step.  No reference counterpart (see above).  Every linear
@@ -356,7 +372,9 @@ p100_status p100_decoder_init_random(p100_decoder* d, unsigned long long seed);
 /* KV rows [0, n_pos) of every layer: N(0,1) * scale as fp16. */
 p100_status p100_decoder_fill_kv(p100_decoder* d, int n_pos, unsigned long long seed, float scale);
 p100_status p100_decoder_set_state(p100_decoder* d, int pos, int token);
-/* Synchronises the device, then reads the position and the last token. */
+/* Synchronises the device, then reads the position and the last token.
+ * Returns P100_ERR_TIMEOUT if a device-side wait ran out (the device flag of
+ * p100_device_error, left set): the decoder must then be recreated. */
 p100_status p100_decoder_state(p100_decoder* d, int* pos, int* token);
 /* n_steps tokens on stream.  On the step path (p100_decoder_path) each token
  * is one cooperative launch of the persistent step kernel.  On the graph path

@@ -118,6 +118,8 @@ def _bind(lib):
         "p100_peer_link_copy": (ip, [vp, vp, vp, sz, st]),
         "p100_peer_link_destroy": (ip, [vp]),
         "p100_rmsnorm_q8_1": (ip, [vp, vp, vp, C.c_float, ip, ip, vp, vp, st]),
+        "p100_peer_reduce_rmsnorm": (ip, [vp, vp, C.c_float, ip, vp, vp, ip, ip, vp, vp, vp, C.c_ulonglong,
+                                          C.c_ulonglong, st]),
         "p100_qmv_rmsnorm": (ip, [ip, vp, ip, ip, vp, vp, vp, vp, C.c_float, vp, C.c_uint, st]),
         "p100_rope_table": (None, [vp, ip, ip, C.c_float]),
         "p100_rope_kv_append": (ip, [vp, ip, ip, ip, vp, ip, vp, vp, vp, C.c_longlong, st]),

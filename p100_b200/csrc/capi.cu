@@ -232,9 +232,9 @@ bool plan_team(int type, const void* w, const void* xq, int rows, int k, int bat
     return true;
 }
 
-template <int TYPE, int NG>
+template <int TYPE, int NG, bool PUSH = false>
 p100_status launch_team_t(const TeamPlan& plan, bool pdl, cudaStream_t stream) {
-    auto kern = qmvt::qmv_team_kernel<TYPE, NG>;
+    auto kern = qmvt::qmv_team_kernel<TYPE, NG, PUSH>;
     static thread_local int configured[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -258,15 +258,15 @@ p100_status launch_team_t(const TeamPlan& plan, bool pdl, cudaStream_t stream) {
 
 // Kernels compiled for the hidden sizes of the Llama-3 8B/70B decode shapes
 // (k = 4096, 8192, 14336, 28672); any other k % 256 == 0 takes NG = 0.
-template <int TYPE>
+template <int TYPE, bool PUSH = false>
 p100_status launch_team_type(const TeamPlan& plan, int batch, bool pdl, cudaStream_t s) {
     (void)batch;   // the team kernel serves one column
     switch (plan.p.ngroups) {
-        case 16: return launch_team_t<TYPE, 16>(plan, pdl, s);
-        case 32: return launch_team_t<TYPE, 32>(plan, pdl, s);
-        case 56: return launch_team_t<TYPE, 56>(plan, pdl, s);
-        case 112: return launch_team_t<TYPE, 112>(plan, pdl, s);
-        default: return launch_team_t<TYPE, 0>(plan, pdl, s);
+        case 16: return launch_team_t<TYPE, 16, PUSH>(plan, pdl, s);
+        case 32: return launch_team_t<TYPE, 32, PUSH>(plan, pdl, s);
+        case 56: return launch_team_t<TYPE, 56, PUSH>(plan, pdl, s);
+        case 112: return launch_team_t<TYPE, 112, PUSH>(plan, pdl, s);
+        default: return launch_team_t<TYPE, 0, PUSH>(plan, pdl, s);
     }
 }
 
@@ -540,6 +540,34 @@ p100_status run_qmv(int type, const void* w, int rows, int k, const void* xq, in
         default: qmv::qmv_generic_kernel<P100_Q6_K><<<grid, 256, 0, stream>>>(wb, xb, y, rows, k, batch, row_bytes); break;
     }
     return launch_status("qmv_generic_kernel launch");
+}
+
+// Batch-1 mat-vec of a row-parallel matrix whose partial sums go straight
+// into every rank's peer slots (the team kernel's push epilogue); *ctas_out
+// = the CTAs that arrive on the counters.  False when the team kernel does
+// not take the shape (the caller then writes y and pushes separately).
+// ar: the exchange's PeerAr in device memory (ar_host: the same, on the host).
+bool run_qmv_push(int type, const void* w, int rows, int k, const void* xq, const dec::PeerAr* ar,
+                  const dec::PeerAr& ar_host, int* ctas_out, cudaStream_t stream, p100_status* st) {
+    int sms = 0;
+    *st = P100_OK;
+    if (require_sm100(nullptr, &sms) || !known_type(type) || rows != ar_host.n) return false;
+    TeamPlan tplan;
+    if (!plan_team(type, w, xq, rows, k, 1, sms, tplan)) return false;
+    tplan.p.w = static_cast<const uint8_t*>(w);
+    tplan.p.xq = static_cast<const uint8_t*>(xq);
+    tplan.p.y = nullptr;
+    tplan.p.col0 = 0;
+    tplan.p.ar = ar;
+    *ctas_out = tplan.grid;
+    switch (type) {
+        case P100_Q4_0: *st = launch_team_type<P100_Q4_0, true>(tplan, 1, true, stream); break;
+        case P100_Q8_0: *st = launch_team_type<P100_Q8_0, true>(tplan, 1, true, stream); break;
+        case P100_Q4_K: *st = launch_team_type<P100_Q4_K, true>(tplan, 1, true, stream); break;
+        case P100_Q5_K: *st = launch_team_type<P100_Q5_K, true>(tplan, 1, true, stream); break;
+        default: *st = launch_team_type<P100_Q6_K, true>(tplan, 1, true, stream); break;
+    }
+    return true;
 }
 
 // Batch-1 mat-vec whose Q8_1 row is rmsnorm(x_in + delta) * norm_w (the

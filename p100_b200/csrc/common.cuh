@@ -141,8 +141,13 @@ __device__ __forceinline__ float half_hi(uint32_t w) {
 __device__ __forceinline__ uint32_t shift2(uint32_t lo, uint32_t hi) { return __byte_perm(lo, hi, 0x5432); }
 
 // fp16 of v (nearest even) into the 2-byte aligned p with one 16-bit store.
-// (Writing its two bytes as two 8-bit stores lost the low byte in this
-// sm_100a build, measured: every scale came out with a zero low byte.)
+// The scale of a K/V block appended inside the attention kernel is written
+// while other CTAs of the same head read neighbouring rows with bulk copies
+// (async proxy); written as two 8-bit stores, its low byte read back as 0
+// (reproduced: the quantised-cache decoder test fails with the two-store
+// form and passes with this one, while the same two-store form is exact in
+// init_kv_quant_kernel, where no copy reads the rows).  One store keeps the
+// two bytes together.
 __device__ __forceinline__ void store_half_bits(uint8_t* p, float v) {
     *reinterpret_cast<unsigned short*>(p) = __half_as_ushort(__float2half_rn(v));
 }

@@ -33,36 +33,41 @@ constexpr int kArgmaxThreads = 1024;
 // ------------------------------------------------- one-shot peer all-reduce
 // Tensor-parallel sum of an n-float partial vector over `world` GPUs of one
 // box through NVLink peer memory (CUDA IPC mappings).  Every rank owns an
-// arena of slots [2][world][n] fp32 and flags [2][world][nblk] u32; slot and
-// flag pointers of every rank (own and peers') are in PeerAr.
-//   push (ar_push_kernel, after the producing mat-vec): block b stores its
-//     n/nblk chunk of the partial into slot [e&1][rank] of every rank, makes
-//     the stores visible system-wide, then sets flag [e&1][rank][b] = e on
-//     every rank (release store);
-//   reduce (rmsnorm_q8_1_kernel with ar.world > 0): waits, bounded, until all
-//     world*nblk flags of epoch e in its own arena read e (acquire loads),
-//     sums the world slots in rank order (the same order on every rank, so
-//     every rank holds the same bits), then stores e as the completed epoch.
+// arena of slots [2][world][n] fp32 and a 64-bit arrival counter; the slot
+// and counter pointers of every rank (own and peers') are in PeerAr.
+//   push (the row-parallel mat-vec's epilogue, qmv_team_kernel with its push
+//     fields, or ar_push_kernel after any other producer): the partial goes
+//     into slot [e&1][rank] of every rank; each pushing CTA then fences at
+//     system scope and adds 1 to every rank's counter (release);
+//   reduce (rmsnorm_q8_1_kernel with ar.world > 0): waits, bounded, until its
+//     own counter reaches *done + add (add = world x the pushing grid's
+//     CTAs, fixed when the step is recorded), sums the world slots in rank
+//     order (the same order on every rank, so every rank holds the same
+//     bits), then stores the new *done and e as the completed epoch.
 // e = completed epoch + 1, read from a device counter, so a replayed graph
 // uses a new epoch every call.  Slots are double-buffered by e & 1: a rank
-// writes epoch e+2 into a peer only after seeing every rank's e+1 flags, and
-// a rank raises e+1 only after its reduce of e finished reading.
+// writes epoch e+2 into a peer only after its own reduce of e+1, which
+// waited for every rank's push of e+1, which each rank made after its reduce
+// of e had finished reading.
 constexpr int kArMaxRanks = 8;
 constexpr int kArBlocks = 8;
 struct PeerAr {
     float* slots[kArMaxRanks];
-    unsigned* flags[kArMaxRanks];
+    unsigned long long* count[kArMaxRanks];
     int world, rank, n;
-    int* epoch;   // this rank's completed-epoch counter
+    int* epoch;                 // this rank's completed-epoch counter
+    unsigned long long* done;   // this rank's counter value when the last reduce finished
+    unsigned long long add;     // arrivals one exchange brings (world x pushing CTAs)
+    unsigned long long wait_ns; // the reduce's wait limit (0: kWaitLimitNs)
 };
 
-__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
-    unsigned v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
+}
+__device__ __forceinline__ void red_release_sys_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
 // Grid kArBlocks x 256; n % (4 * kArBlocks) == 0.
@@ -78,10 +83,9 @@ __global__ void __launch_bounds__(256) ar_push_kernel(const float* __restrict__ 
         for (int r = 0; r < ar.world; ++r)
             reinterpret_cast<float4*>(ar.slots[r] + (size_t(par) * ar.world + ar.rank) * ar.n)[blockIdx.x * per + i] = v;
     }
-    __threadfence_system();   // this thread's stores, system scope, before the block's flags
+    __threadfence_system();   // this thread's stores, system scope, before the block's arrival
     __syncthreads();
-    if (threadIdx.x < ar.world)
-        st_release_sys(ar.flags[threadIdx.x] + (size_t(par) * ar.world + ar.rank) * kArBlocks + blockIdx.x, e);
+    if (threadIdx.x < ar.world) red_release_sys_u64(ar.count[threadIdx.x], 1ull);
 }
 
 // ------------------------------------------------------------------ RMSNorm
@@ -160,12 +164,13 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_q8_1_kernel(float* __res
         // delta = the peer all-reduce of this epoch (batch 1, n = k)
         const unsigned e = unsigned(*ar.epoch) + 1u;
         const int par = int(e & 1u);
+        const unsigned long long target = *ar.done + ar.add;
         bool ok = true;
-        if (tid < ar.world * kArBlocks) {
-            const unsigned* f = ar.flags[ar.rank] + size_t(par) * ar.world * kArBlocks + tid;
+        if (tid == 0) {
             const unsigned long long start = globaltimer_ns();
-            while (ld_acquire_sys(f) != e) {
-                if (globaltimer_ns() - start > kWaitLimitNs) {
+            const unsigned long long limit = ar.wait_ns ? ar.wait_ns : kWaitLimitNs;
+            while (ld_acquire_sys_u64(ar.count[ar.rank]) < target) {
+                if (globaltimer_ns() - start > limit) {
                     ok = false;
                     break;
                 }
@@ -188,7 +193,10 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_q8_1_kernel(float* __res
                 xr[c] = v[i];
             }
         }
-        if (tid == 0) *ar.epoch = int(e);   // read by the next push, which starts after this kernel ends
+        if (tid == 0) {   // read by the next push and reduce, which start after this kernel ends
+            *ar.epoch = int(e);
+            *ar.done = target;
+        }
     }
     float s = 0.f;
 #pragma unroll

@@ -73,6 +73,8 @@ struct Decoder {
     void* ar_peer[dec::kArMaxRanks] = {};    // IPC mappings of the other ranks' arenas
     int* ar_epoch = nullptr;                 // completed-epoch counter (in the arena above)
     dec::PeerAr ar{};
+    unsigned long long ar_pending = 0;       // arrivals the last recorded push brings
+    dec::PeerAr* ar_dev = nullptr;           // a device copy of ar (read by the push epilogue)
     // the persistent step kernel (step.cuh): one cooperative launch a token
     bool step_region = false;   // the arena holds its buffers (the config allows it)
     bool use_step = false;      // p100_decoder_step launches it
@@ -399,12 +401,14 @@ p100_status dec_qmv(const DecTensor& w, int k, const uint8_t* xq, float* y, cuda
     return P100_OK;
 }
 
-// x += delta (or, with peer_reduce, += the peer all-reduce of this epoch),
-// then RMSNorm * w and Q8_1 into d.xq.
+// x += delta (or, with peer_reduce, += the peer all-reduce of this epoch,
+// whose pushes bring d.ar_pending arrivals), then RMSNorm * w and Q8_1 into
+// d.xq.
 p100_status dec_rmsnorm(Decoder& d, const float* delta, const DecTensor& w, cudaStream_t s, bool peer_reduce = false) {
     dec::PeerAr ar{};
     if (peer_reduce) {
         ar = d.ar;
+        ar.add = d.ar_pending;
         delta = nullptr;
     }
     return launch_glue(dec::rmsnorm_q8_1_kernel, dim3(1), dim3(dec::kNormThreads), s, "rmsnorm_q8_1_kernel launch",
@@ -412,11 +416,25 @@ p100_status dec_rmsnorm(Decoder& d, const float* delta, const DecTensor& w, cuda
                        static_cast<float*>(nullptr), ar);
 }
 
-// The partial sums in d.delta to every rank: NCCL all-reduce, or the push of
-// the one-shot peer all-reduce (whose reduce runs in the next RMSNorm).
-p100_status dec_allreduce(Decoder& d, cudaStream_t s) {
+// The row-parallel mat-vec delta = w . xq (k inputs) and its all-reduce.
+// One rank: the mat-vec alone.  NCCL: the mat-vec, then an all-reduce of
+// d.delta.  Peer memory: where the team kernel takes the matrix, its
+// epilogue pushes the rows into every rank's slots (no separate kernel);
+// else the mat-vec writes d.delta and ar_push_kernel pushes it.  The reduce
+// runs in the next RMSNorm, which waits for d.ar_pending arrivals.
+p100_status dec_qmv_allreduce(Decoder& d, const DecTensor& w, int k, cudaStream_t s) {
+    if (d.peer_ar && w.nparts == 1) {
+        int ctas = 0;
+        p100_status st = P100_OK;
+        if (run_qmv_push(w.ptype[0], w.ptr, w.prows[0], k, d.xq, d.ar_dev, d.ar, &ctas, s, &st)) {
+            d.ar_pending = static_cast<unsigned long long>(d.nranks) * ctas;
+            return st;
+        }
+    }
+    if (p100_status st = dec_qmv(w, k, d.xq, d.delta, s)) return st;
     if (!d.tp) return P100_OK;
     if (!d.peer_ar) return p100_tp_allreduce_sum(d.tp, d.delta, size_t(d.cfg.hidden), s);
+    d.ar_pending = static_cast<unsigned long long>(d.nranks) * dec::kArBlocks;
     return launch_glue(dec::ar_push_kernel, dim3(dec::kArBlocks), dim3(256), s, "ar_push_kernel launch",
                        static_cast<const float*>(d.delta), d.ar);
 }
@@ -505,14 +523,12 @@ p100_status dec_record_step(Decoder& d, cudaStream_t s) {
                                  "q8_1_quantize_kernel launch", static_cast<const float*>(d.attn), d.xq, k_o, k_o / 32);
             }
         }
-        if (!st) st = dec_qmv(d.wo[l], d.nq * hd, d.xq, d.delta, s);
-        if (!st) st = dec_allreduce(d, s);
+        if (!st) st = dec_qmv_allreduce(d, d.wo[l], d.nq * hd, s);
         if (!st) st = norm_qmv(d.delta, d.ffn_norm[l], d.wgu[l], 2 * d.ffn, d.gu);
         if (!st)
             st = launch_glue(dec::swiglu_q8_1_kernel, dim3((d.ffn / 32 + 7) / 8, 1), dim3(256), s,
                              "swiglu_q8_1_kernel launch", static_cast<const float*>(d.gu), d.ffn, d.xq);
-        if (!st) st = dec_qmv(d.wdown[l], d.ffn, d.xq, d.delta, s);
-        if (!st) st = dec_allreduce(d, s);
+        if (!st) st = dec_qmv_allreduce(d, d.wdown[l], d.ffn, s);
     }
     if (!st) st = norm_qmv(d.delta, d.out_norm, d.lm_head, d.vocab_n, d.logits);
     if (st) return st;
@@ -632,10 +648,11 @@ struct SetupComm {
 // arena, the IPC handles go round an all-gather, and every rank maps the
 // others'.  Used only if every pair of ranks' GPUs has peer access and
 // P100_TP_ALLREDUCE is not "nccl", all ranks having agreed.  The arena holds
-//   [2][world][hidden] fp32 slots (the one-shot all-reduce of the graph
-//   decoder and the step kernel's exchange), [2][world][kArBlocks] flags,
-//   the graph decoder's epoch, the step kernel's argmax candidates
-//   [world][2] and its 64-bit exchange counter.
+//   [2][world][hidden] fp32 slots (the one-shot all-reduce of either
+//   decoder path), then in 256-byte cells: the graph decoder's epoch, the
+//   step kernel's argmax candidates [world][2], and the 64-bit arrival
+//   counter (at +512; the graph decoder keeps its reduce's `done` value at
+//   +520 of its own arena).
 // Collective: every rank calls it.  Returns an error only when the ranks
 // agree that one of them failed; a declined or failed peer path leaves
 // d.peer_ar false on every rank (NCCL carries the exchanges then).
@@ -664,8 +681,7 @@ p100_status dec_setup_peer_ar(Decoder& d) {
     if (v.declines) return P100_OK;
     // 2. arenas and their IPC handles
     const size_t slot_bytes = size_t(2) * world * n * 4;
-    const size_t flag_bytes = size_t(2) * world * dec::kArBlocks * 4;
-    const size_t arena_bytes = slot_bytes + flag_bytes + 768;   // epoch | candidates | counter, 256 B each
+    const size_t arena_bytes = slot_bytes + 768 + 512;   // epoch | candidates | counter (+ done), 256 B each | ar copy
     cudaIpcMemHandle_t h{};
     p100_status st = cuda_status(cudaMalloc(&d.ar_arena, arena_bytes), "cudaMalloc(ar arena)");
     if (!st) st = cuda_status(cudaMemset(d.ar_arena, 0, arena_bytes), "cudaMemset(ar arena)");
@@ -706,11 +722,23 @@ p100_status dec_setup_peer_ar(Decoder& d) {
         }
         if (!st) {
             d.ar.slots[r] = reinterpret_cast<float*>(base);
-            d.ar.flags[r] = reinterpret_cast<unsigned*>(base + slot_bytes);
+            d.ar.count[r] = reinterpret_cast<unsigned long long*>(base + slot_bytes + 512);
             d.sp.slots[r] = reinterpret_cast<float*>(base);
-            d.sp.cslots[r] = reinterpret_cast<float*>(base + slot_bytes + flag_bytes + 256);
-            d.sp.xcount[r] = reinterpret_cast<unsigned long long*>(base + slot_bytes + flag_bytes + 512);
+            d.sp.cslots[r] = reinterpret_cast<float*>(base + slot_bytes + 256);
+            d.sp.xcount[r] = reinterpret_cast<unsigned long long*>(base + slot_bytes + 512);
         }
+    }
+    // the push epilogue reads this rank's exchange descriptor from device memory
+    if (!st) {
+        d.ar_epoch = reinterpret_cast<int*>(d.ar_arena + slot_bytes);
+        d.ar.done = reinterpret_cast<unsigned long long*>(d.ar_arena + slot_bytes + 520);
+        d.ar.world = world;
+        d.ar.rank = d.rank;
+        d.ar.n = n;
+        d.ar.epoch = d.ar_epoch;
+        static_assert(sizeof(dec::PeerAr) <= 512, "PeerAr copy");
+        d.ar_dev = reinterpret_cast<dec::PeerAr*>(d.ar_arena + slot_bytes + 768);
+        st = cuda_status(cudaMemcpy(d.ar_dev, &d.ar, sizeof d.ar, cudaMemcpyHostToDevice), "copy exchange descriptor");
     }
     // 4. every rank's arena is zeroed and mapped before any rank pushes
     sc.note(st);
@@ -719,11 +747,6 @@ p100_status dec_setup_peer_ar(Decoder& d) {
         release();
         return sc.fail("peer exchange setup");
     }
-    d.ar_epoch = reinterpret_cast<int*>(d.ar_arena + slot_bytes + flag_bytes);
-    d.ar.world = world;
-    d.ar.rank = d.rank;
-    d.ar.n = n;
-    d.ar.epoch = d.ar_epoch;
     d.peer_ar = true;
     return P100_OK;
 }
@@ -923,6 +946,35 @@ p100_status p100_rmsnorm_q8_1(float* x, const float* delta, const float* w, floa
     return launch_status("rmsnorm_q8_1_kernel launch");
 }
 
+p100_status p100_peer_reduce_rmsnorm(float* x, const float* w, float eps, int k, void* x_q8_1, float* slots, int world,
+                                     int rank, int* epoch, unsigned long long* count, unsigned long long* done,
+                                     unsigned long long arrivals, unsigned long long wait_ns, p100_stream_t stream) {
+    clear_error();
+    if (k <= 0 || k % 32 || k % (4 * dec::kArBlocks)) return set_error(P100_ERR_INVALID, "k must be a positive multiple of 32");
+    if (k > dec::kNormMaxK) return set_error(P100_ERR_UNSUPPORTED, "k above %d", dec::kNormMaxK);
+    if (world < 1 || world > dec::kArMaxRanks || rank < 0 || rank >= world)
+        return set_error(P100_ERR_INVALID, "rank %d of %d (at most %d ranks)", rank, world, dec::kArMaxRanks);
+    if (!x || !w || !x_q8_1 || !slots || !epoch || !count || !done) return set_error(P100_ERR_INVALID, "null buffer");
+    if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(w) % 16 ||
+        reinterpret_cast<uintptr_t>(slots) % 16 || reinterpret_cast<uintptr_t>(count) % 8 ||
+        reinterpret_cast<uintptr_t>(done) % 8)
+        return set_error(P100_ERR_INVALID, "x, w and slots 16-byte aligned, count and done 8-byte aligned");
+    if (p100_status st = require_sm100(nullptr, nullptr)) return st;
+    dec::PeerAr ar{};
+    ar.slots[rank] = slots;
+    ar.count[rank] = count;
+    ar.world = world;
+    ar.rank = rank;
+    ar.n = k;
+    ar.epoch = epoch;
+    ar.done = done;
+    ar.add = arrivals;
+    ar.wait_ns = wait_ns;
+    dec::rmsnorm_q8_1_kernel<<<1, dec::kNormThreads, 0, stream>>>(x, nullptr, w, eps, k, static_cast<uint8_t*>(x_q8_1),
+                                                                    nullptr, ar);
+    return launch_status("rmsnorm_q8_1_kernel launch");
+}
+
 p100_status p100_qmv_rmsnorm(int type, const void* w, int rows, int k, const float* x_in, const float* delta,
                              float* x_out, const float* norm_w, float eps, float* y, unsigned flags,
                              p100_stream_t stream) {
@@ -1079,6 +1131,12 @@ p100_status p100_decoder_state(p100_decoder* h, int* pos, int* token) {
     if (!st) st = cuda_status(cudaMemcpy(&v[1], h->d.token, 4, cudaMemcpyDeviceToHost), "read token");
     if (pos) *pos = v[0];
     if (token) *token = v[1];
+    // a bounded wait that ran out (a peer that never pushed, say) leaves the
+    // decode state undefined: report it here, where the loop synchronises
+    int flag = 0;
+    if (!st) st = cuda_status(cudaMemcpyFromSymbol(&flag, g_device_error, sizeof flag), "read device flag");
+    if (!st && flag == kDevErrTimeout)
+        st = set_error(P100_ERR_TIMEOUT, "a device-side wait ran out during a step; recreate the decoder");
     return st;
 }
 

@@ -108,6 +108,12 @@ struct Params {
     // Fused quantisation (x_f32 not null, norm_w null): the Q8_1 row is
     // built from these fp32 activations (16-byte aligned) instead of read.
     const float* x_f32;
+    // Tensor-parallel push (the PUSH kernels, batch 1): the rows are a
+    // partial sum of a row-parallel matrix; instead of y they go into slot
+    // [e & 1][rank] of every rank's peer arena, and the CTA then fences at
+    // system scope and arrives on every rank's counter (the dec::PeerAr in
+    // device memory that ar points to; its reduce runs in the next RMSNorm).
+    const dec::PeerAr* ar;
 };
 
 // The Q8_1 row of p.x_f32 into xs by the 8 consumer warps: float4 chunk c
@@ -402,7 +408,8 @@ __device__ __forceinline__ uint32_t stage_span(const Params& p, int first, int n
 }
 
 // NG = k / 256 when compiled for one hidden size, 0 for any (runtime shape).
-template <int TYPE, int NG>
+// PUSH: the tensor-parallel push epilogue (Params::ar) instead of y.
+template <int TYPE, int NG, bool PUSH = false>
 __global__ void __launch_bounds__(kThreads, 1) qmv_team_kernel(const Params p) {
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
@@ -497,6 +504,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_team_kernel(const Params p) {
         pdl_wait_prior_grid();   // x may come from an earlier kernel
         quantize_row(p, smem + p.act_off);
     }
+    bool failed = false;   // a bounded wait ran out (the push then signals nothing)
     if (!p.norm_w && !p.x_f32) {
         const bool ok = mbar_wait(act_bar, 0);
         int any_timeout;
@@ -512,8 +520,26 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_team_kernel(const Params p) {
                 : "r"(static_cast<unsigned>(ok)), "r"(kConsumers * 32)
                 : "memory");
         }
-        if (any_timeout) return;
+        if (any_timeout) {
+            if constexpr (!PUSH) return;
+            failed = true;
+        }
     }
+    // push: the slot parity of this exchange (the epoch was advanced by the
+    // previous RMSNorm, complete once the previous kernel is)
+    int par = 0;
+    if constexpr (PUSH) {
+        pdl_wait_prior_grid();
+        par = int((unsigned(*p.ar->epoch) + 1u) & 1u);
+    }
+    auto put = [&](int row, float v) {
+        if constexpr (PUSH) {
+            const dec::PeerAr& ar = *p.ar;
+            for (int r = 0; r < ar.world; ++r) ar.slots[r][(size_t(par) * ar.world + ar.rank) * ar.n + row] = v;
+        } else {
+            p.y[size_t(p.col0) * p.rows + row] = v;
+        }
+    };
     if (has_group) {
         load_group_act<TYPE>(smem + p.act_off, tl, act);
     } else {
@@ -523,7 +549,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_team_kernel(const Params p) {
         for (int i = 0; i < 8; ++i) act.dx[i] = act.m[i] = 0.f;
     }
 
-    for (int s = 0; s < nst; ++s) {
+    for (int s = 0; s < nst && (!PUSH || !failed); ++s) {
         const int slot = s % p.nslot;
         const bool timed_out = !mbar_wait(&full[slot], (s / p.nslot) & 1);
         int any_timeout;
@@ -542,7 +568,10 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_team_kernel(const Params p) {
                 : "r"(static_cast<unsigned>(timed_out)), "r"(kConsumers * 32)
                 : "memory");
         }
-        if (any_timeout) break;
+        if (any_timeout) {
+            failed = true;
+            break;
+        }
         const uint8_t* stage = ring + size_t(slot) * p.slot_bytes;
         const int first = r0 + s * teams;
         const int nr = min(teams, r1 - first);
@@ -556,7 +585,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_team_kernel(const Params p) {
         if (team_size <= 32) {
             // teams are aligned lane ranges of one warp: butterfly inside them
             for (int off = team_size >> 1; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-            if (tl == 0 && team < nr) p.y[size_t(p.col0) * p.rows + first + team] = acc;
+            if (tl == 0 && team < nr) put(first + team, acc);
         } else {
             const int wpt = team_size >> 5, wit = tl >> 5;
             float* part = partial + (size_t(s & 1) * teams + team) * wpt;
@@ -566,9 +595,25 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_team_kernel(const Params p) {
             if (tl == 0 && team < nr) {
                 float sum = 0.f;
                 for (int i = 0; i < wpt; ++i) sum += part[i];
-                p.y[size_t(p.col0) * p.rows + first + team] = sum;
+                put(first + team, sum);
             }
         }
+    }
+    if constexpr (PUSH) {
+        // every consumer's peer stores, then one arrival per CTA on every
+        // rank (none if a wait ran out: the reduce then times out and flags)
+        __threadfence_system();
+        int any_failed;
+        asm volatile(
+            "{\n\t.reg .pred p, q;\n\t"
+            "setp.ne.u32 p, %1, 0;\n\t"
+            "bar.red.or.pred q, 15, %2, p;\n\t"
+            "selp.u32 %0, 1, 0, q;\n\t}"
+            : "=r"(any_failed)
+            : "r"(static_cast<unsigned>(failed)), "r"(kConsumers * 32)
+            : "memory");
+        if (!any_failed && tid == 0)
+            for (int r = 0; r < p.ar->world; ++r) dec::red_release_sys_u64(p.ar->count[r], 1ull);
     }
 }
 

@@ -112,3 +112,16 @@ def test_cpp_caller_builds_and_gets_reference_errors():
     r = subprocess.run([str(exe), "errors"], capture_output=True, text=True, env=env)
     assert r.returncode == 0, r.stdout + r.stderr
     assert "PASS errors" in r.stdout
+
+
+@pytest.mark.gpu
+def test_cpp_caller_gpu_path():
+    """The C++ caller (tests/cpp/contract_check.cpp) on the B200: Q8_1
+    prepare bit-exact, a Q4_K mat-vec and a split FA decode against the
+    oracle, through include/p100/b200.hpp."""
+    subprocess.run(["make", "-s", "-C", str(ROOT / "tests" / "cpp")], check=True)
+    exe = ROOT / "tests" / "cpp" / "bin" / "contract_check"
+    r = subprocess.run([str(exe), "gpu"], capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "FAIL" not in r.stdout, r.stdout
+    assert "PASS" in r.stdout, r.stdout

@@ -1,14 +1,17 @@
-"""Tensor-parallel decoder (row split over 2 GPUs, NCCL all-reduce after o and
-down, all-gathered argmax) against the same model at TP=1.
+"""Tensor-parallel decoder (row split over 2, 4 or 8 GPUs, all-reduce after o
+and down, the ranks' argmax candidates compared) against the same model at
+TP=1.
 
-Both all-reduce paths are checked: the one-shot all-reduce over NVLink peer
-memory and NCCL.  Each rank initialises its own slices from global
-coordinates, so TP=2 holds
-the TP=1 model exactly; the steps differ only in the summation order of the
-row-split partial sums, so logits agree within the decoder bounds of
+Every exchange path is checked: the one-shot all-reduce over NVLink peer
+memory (pushed from the o/down mat-vec's epilogue, or by a separate push
+kernel where the mat-vec is not the team kernel), NCCL, and the persistent
+step kernel (P100_DEC_STEP) with its own exchange.  Each rank initialises
+its own slices from global coordinates, so TP=N holds the TP=1 model
+exactly; the steps differ only in the summation order of the row-split
+partial sums, so logits agree within the decoder bounds of
 test_decode_gpu.py and the tokens agree where the top two logits are further
-apart than the logit error.  Two ranks, one process per GPU; skipped with
-fewer than two GPUs."""
+apart than the logit error.  One process per GPU; a case is skipped when the
+box has fewer GPUs than ranks."""
 import os
 import socket
 
@@ -25,7 +28,10 @@ SEED, NPOS, STEPS, TOKEN = 99, 100, 3, 7
 # 420 bytes, off the 16-byte grid) on a shape whose TP=2 slices are whole
 # 256-value blocks.
 SHAPES = {"tiny": TINY,
-          "mixed": dict(TINY, hidden=512, n_head=8, n_head_kv=4, ffn=1024, tensor_types=mixed_types())}
+          "mixed": dict(TINY, hidden=512, n_head=8, n_head_kv=4, ffn=1024, tensor_types=mixed_types()),
+          # splits 2, 4 and 8 ways: at TP=8 the o slice (k = 128) is not a team
+          # mat-vec, so its exchange takes the separate push kernel
+          "wide": dict(TINY, hidden=512, n_head=16, n_head_kv=8, ffn=2048)}
 
 
 def _free_port():
@@ -48,7 +54,7 @@ def _run(dec):
     return out
 
 
-def _rank(rank, world, port, q, allreduce, shape):
+def _rank(rank, world, port, q, allreduce, shape, flags):
     import datetime
     import torch
     import torch.distributed as dist
@@ -61,7 +67,9 @@ def _rank(rank, world, port, q, allreduce, shape):
         box = [P.tp_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(box, src=0)
         tp = P.TP(box[0], world, rank, rank)
-        dec = P.Decoder(P.LlamaConfig(**SHAPES[shape]), tp)
+        dec = P.Decoder(P.LlamaConfig(**SHAPES[shape], flags=flags), tp)
+        if flags == P.DEC_STEP:
+            assert dec.path == P.DEC_PATH_STEP
         out = _run(dec)
         q.put((rank, dec.vocab_offset, [(p, t, l.tolist()) for p, t, l in out]))
     except Exception as e:  # noqa: BLE001
@@ -74,21 +82,27 @@ def _rank(rank, world, port, q, allreduce, shape):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("shape", ["tiny", "mixed"])
-@pytest.mark.parametrize("allreduce", ["peer", "nccl"])
-def test_tp2_matches_tp1(cuda, allreduce, shape):
+CASES = [(2, "tiny", "peer", 0), (2, "tiny", "nccl", 0), (2, "mixed", "peer", 0), (2, "mixed", "nccl", 0),
+         (2, "wide", "peer", 0), (4, "wide", "peer", 0), (4, "wide", "nccl", 0), (8, "wide", "peer", 0),
+         (8, "wide", "nccl", 0), (2, "wide", "peer", P.DEC_STEP), (4, "wide", "peer", P.DEC_STEP)]
+
+
+@pytest.mark.parametrize("world,shape,allreduce,flags", CASES,
+                         ids=[f"tp{w}-{s}-{a}{'-step' if f else ''}" for w, s, a, f in CASES])
+def test_tpn_matches_tp1(cuda, world, shape, allreduce, flags):
     """allreduce: 'peer' = the one-shot all-reduce over NVLink peer memory
-    (push kernel + reduce inside the next RMSNorm), 'nccl' = ncclAllReduce."""
-    if cuda.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
+    (reduce inside the next RMSNorm), 'nccl' = ncclAllReduce; flags
+    P100_DEC_STEP = the persistent step kernel."""
+    if cuda.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, 2, port, q, allreduce, shape)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, world, port, q, allreduce, shape, flags)) for r in range(world)]
     for p in procs:
         p.start()
-    res = sorted([q.get(timeout=300) for _ in range(2)], key=lambda r: r[0])
+    res = sorted([q.get(timeout=300) for _ in range(world)], key=lambda r: r[0])
     for p in procs:
         p.join(timeout=120)
         assert not p.is_alive()
@@ -107,7 +121,7 @@ def test_tp2_matches_tp1(cuda, allreduce, shape):
             pos, tok, logits = out[step]
             assert pos == pos1
             full[off:off + len(logits)] = logits
-        assert res[0][2][step][1] == res[1][2][step][1]   # every rank picks the same token
+        assert all(r[2][step][1] == res[0][2][step][1] for r in res)   # every rank picks the same token
         err = np.max(np.abs(full - logits1))
         assert err <= DECODE_LOGIT_TOL * np.max(np.abs(logits1)), (step, err)
         top2 = np.sort(logits1)[-2:]
