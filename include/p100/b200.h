@@ -115,6 +115,10 @@ p100_status p100_qmv(int type, const void* w, int rows, int k, const void* x_q8_
                             kernel in the stream: weights are prefetched before
                             that kernel finishes, so they must not be written
                             by it.  Activations are read only after it ends. */
+#define P100_QMV_TC 2u   /* batch 2..16 of Q4_0 / Q8_0 / Q4_K (16-byte aligned rows,
+                            k % 256 == 0): the 5th-generation tensor-core kernel
+                            (tcgen05.mma kind::i8, accumulators in tensor memory,
+                            weights by TMA) instead of the mma.sync kernel. */
 p100_status p100_qmv_ex(int type, const void* w, int rows, int k, const void* x_q8_1,
                         int batch, float* y, unsigned flags, p100_stream_t stream);
 /* p100_q8_1_quantize with P100_QMV_PDL available: the quantiser launched as
@@ -281,19 +285,18 @@ p100_status p100_argmax(const float* x, int n, int batch, int* idx, float* val, 
 
 /* One rank's reduce of the one-shot peer all-reduce, fused with RMSNorm +
  * Q8_1 (the graph decoder's exchange; no reference counterpart).  slots is
- * this rank's arena of [2][world][k] fp32 partials, into which every rank's
- * push stores its partial sum at [e & 1][that rank], e = *epoch + 1; each
- * pushing CTA then adds 1 to every rank's counter.  The kernel waits until
- * *count >= *done + arrivals — for at most wait_ns nanoseconds (0: about a
- * second) — then x += the world slots added in rank order, RMSNorm * w into
- * x_q8_1 (p100_rmsnorm_q8_1's arithmetic), *epoch = e, *done += arrivals.
- * A wait that runs out raises P100_ERR_TIMEOUT in p100_device_error() and the
- * kernel returns normally (the sums then hold whatever the slots held); the
- * exchange state is then undefined.  k % 32 == 0, k <= 16384; x, w and slots
- * 16-byte aligned. */
-p100_status p100_peer_reduce_rmsnorm(float* x, const float* w, float eps, int k, void* x_q8_1, float* slots, int world,
-                                     int rank, int* epoch, unsigned long long* count, unsigned long long* done,
-                                     unsigned long long arrivals, unsigned long long wait_ns, p100_stream_t stream);
+ * this rank's arena of [2][world][k] 64-bit words into which every rank's
+ * push stores its partial sum, row i of rank r at [e & 1][r][i] as
+ * (e << 32) | (the fp32 bits of the value), e = *epoch + 1.  The kernel
+ * waits until every word it reads carries e — for at most wait_ns
+ * nanoseconds (0: about a second) — then x += the world values added in
+ * rank order, RMSNorm * w into x_q8_1 (p100_rmsnorm_q8_1's arithmetic), and
+ * *epoch = e.  A wait that runs out raises P100_ERR_TIMEOUT in
+ * p100_device_error() and the kernel returns normally (the sums then hold
+ * whatever the slots held); the exchange state is then undefined.  k % 32 ==
+ * 0, k <= 16384; x, w and slots 16-byte aligned. */
+p100_status p100_peer_reduce_rmsnorm(float* x, const float* w, float eps, int k, void* x_q8_1, void* slots, int world,
+                                     int rank, int* epoch, unsigned long long wait_ns, p100_stream_t stream);
 
 /* --------------------------------------------------- batch-1 decoder */
 /* A Llama-3-shaped model with synthetic weights, decoded one token per

@@ -32,6 +32,7 @@ KV_F16, KV_Q8_0, KV_Q4_0 = 0, 1, 2
 KV_BLOCK_BYTES = {KV_Q8_0: 34, KV_Q4_0: 18}
 Q8_1_BLOCK_BYTES = 36
 QMV_PDL = 1
+QMV_TC = 2   # P100_QMV_TC: batch 2..16 on the tcgen05 kernel
 
 STATUS = {0: "P100_OK", 1: "P100_ERR_INVALID", 2: "P100_ERR_CUDA", 3: "P100_ERR_NCCL",
           4: "P100_ERR_TIMEOUT", 5: "P100_ERR_UNSUPPORTED"}
@@ -118,8 +119,7 @@ def _bind(lib):
         "p100_peer_link_copy": (ip, [vp, vp, vp, sz, st]),
         "p100_peer_link_destroy": (ip, [vp]),
         "p100_rmsnorm_q8_1": (ip, [vp, vp, vp, C.c_float, ip, ip, vp, vp, st]),
-        "p100_peer_reduce_rmsnorm": (ip, [vp, vp, C.c_float, ip, vp, vp, ip, ip, vp, vp, vp, C.c_ulonglong,
-                                          C.c_ulonglong, st]),
+        "p100_peer_reduce_rmsnorm": (ip, [vp, vp, C.c_float, ip, vp, vp, ip, ip, vp, C.c_ulonglong, st]),
         "p100_qmv_rmsnorm": (ip, [ip, vp, ip, ip, vp, vp, vp, vp, C.c_float, vp, C.c_uint, st]),
         "p100_rope_table": (None, [vp, ip, ip, C.c_float]),
         "p100_rope_kv_append": (ip, [vp, ip, ip, ip, vp, ip, vp, vp, vp, C.c_longlong, st]),

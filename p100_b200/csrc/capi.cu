@@ -22,6 +22,7 @@
 #include "h16.cuh"
 #include "qmv.cuh"
 #include "qmv_mma.cuh"
+#include "qmv_tc.cuh"
 #include "qmv_team.cuh"
 #include "quant.cuh"
 
@@ -456,6 +457,116 @@ p100_status launch_mma(const MmaPlan& plan, bool pdl, cudaStream_t stream) {
     return cuda_status(cudaLaunchKernelEx(&cfg, plan.kern, plan.p), "qmv_mma_kernel launch");
 }
 
+// ------------------------------------------------------------------ tensor-core (tcgen05) batched plan
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
+
+struct TcPlan {
+    qmvtc::Params p{};
+    int grid = 0;
+    size_t smem = 0;
+};
+
+// Batch 2..16 of Q4_0, Q8_0 or Q4_K with 16-byte aligned rows of whole
+// 256-value groups: row tiles of 128, the K split over a cluster of up to 8
+// CTAs while the grid stays within the SMs, raw stages in the ring as shared
+// memory allows.
+bool plan_tc(int type, const void* w, const void* xq, int rows, int k, int batch, int sms, TcPlan& plan) {
+    if (!ref_type(type) || batch < 2 || batch > qmvtc::kCols || k % 256 || rows <= 0) return false;
+    const size_t row_bytes = size_t(k / elems_of(type)) * bytes_of(type);
+    if (reinterpret_cast<uintptr_t>(w) % 16 || row_bytes % 16 || reinterpret_cast<uintptr_t>(xq) % 16) return false;
+    const int groups = k / 256;
+    const int group_bytes = static_cast<int>(row_bytes / size_t(groups));
+    const int tiles = (rows + qmvtc::kRows - 1) / qmvtc::kRows;
+    int slices = 1;
+    while (slices < 8 && tiles * slices * 2 <= sms && groups / (slices * 2) >= 2) slices *= 2;
+    const int raw_bytes = qmvtc::kRows * group_bytes;
+    const int slot_all = qmvtc::raw_stride(raw_bytes) + qmvtc::kActBytes;   // weights + activations of a stage
+    const int slots = std::min(qmvtc::kMaxRaw, (qmvtc::kSmemLimit - qmvtc::kRawOff) / slot_all);
+    if (slots < 2) return false;
+    PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+    if (!encode) return false;
+    const cuuint64_t dims[2] = {cuuint64_t(row_bytes / 2), cuuint64_t(rows)};
+    const cuuint64_t strides[1] = {cuuint64_t(row_bytes)};
+    const cuuint32_t box[2] = {cuuint32_t(group_bytes / 2), cuuint32_t(qmvtc::kRows)};
+    const cuuint32_t elem[2] = {1, 1};
+    if (encode(&plan.p.tmw, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(w), dims, strides, box, elem,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return false;
+    // the Q8_1 rows: a stage's eight blocks of the batch's columns per box
+    const size_t xrow = size_t(k / 32) * 36;
+    const cuuint64_t xdims[2] = {cuuint64_t(xrow / 2), cuuint64_t(batch)};
+    const cuuint64_t xstrides[1] = {cuuint64_t(xrow)};
+    const cuuint32_t xbox[2] = {cuuint32_t(qmvtc::kActRow / 2), cuuint32_t(batch)};
+    if (encode(&plan.p.tmx, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(xq), xdims, xstrides, xbox, elem,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return false;
+    plan.p.xq = static_cast<const uint8_t*>(xq);
+    plan.p.rows = rows;
+    plan.p.k = k;
+    plan.p.batch = batch;
+    plan.p.slices = slices;
+    plan.p.raw_slots = slots;
+    plan.p.raw_bytes = raw_bytes;
+    plan.p.group_bytes = group_bytes;
+    plan.grid = tiles * slices;
+    plan.smem = size_t(qmvtc::kRawOff) + size_t(slots) * slot_all;
+    return true;
+}
+
+template <int TYPE, int NC>
+p100_status launch_tc_t(const TcPlan& plan, bool pdl, cudaStream_t stream) {
+    auto kern = qmvtc::qmv_tc_kernel<TYPE, NC>;
+    static thread_local int configured[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!configured[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, qmvtc::kSmemLimit);
+        if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(qmv_tc)");
+        configured[dev] = 1;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(plan.grid);
+    cfg.blockDim = dim3(qmvtc::kThreads);
+    cfg.dynamicSmemBytes = plan.smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    int n = 0;
+    if (pdl) {
+        attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[n].val.programmaticStreamSerializationAllowed = 1;
+        ++n;
+    }
+    if (plan.p.slices > 1) {
+        attr[n].id = cudaLaunchAttributeClusterDimension;
+        attr[n].val.clusterDim.x = plan.p.slices;
+        attr[n].val.clusterDim.y = 1;
+        attr[n].val.clusterDim.z = 1;
+        ++n;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = n;
+    return cuda_status(cudaLaunchKernelEx(&cfg, kern, plan.p), "qmv_tc_kernel launch");
+}
+
+// The epilogue reads 4, 8 or 16 of the 16 accumulator columns: the fewest
+// that hold the batch.
+template <int TYPE>
+p100_status launch_tc_cols(const TcPlan& plan, bool pdl, cudaStream_t s) {
+    if (plan.p.batch <= 4) return launch_tc_t<TYPE, 4>(plan, pdl, s);
+    if (plan.p.batch <= 8) return launch_tc_t<TYPE, 8>(plan, pdl, s);
+    return launch_tc_t<TYPE, 16>(plan, pdl, s);
+}
+
+p100_status launch_tc(int type, const TcPlan& plan, bool pdl, cudaStream_t s) {
+    switch (type) {
+        case P100_Q4_0: return launch_tc_cols<P100_Q4_0>(plan, pdl, s);
+        case P100_Q8_0: return launch_tc_cols<P100_Q8_0>(plan, pdl, s);
+        default: return launch_tc_cols<P100_Q4_K>(plan, pdl, s);
+    }
+}
+
 p100_status run_qmv(int type, const void* w, int rows, int k, const void* xq, int batch, float* y, unsigned flags,
                     cudaStream_t stream) {
     if (!known_type(type)) return set_error(P100_ERR_INVALID, "unknown weight type %d", type);
@@ -482,6 +593,11 @@ p100_status run_qmv(int type, const void* w, int rows, int k, const void* xq, in
             case P100_Q5_K: return launch_team_type<P100_Q5_K>(tplan, batch, pdl, stream);
             default: return launch_team_type<P100_Q6_K>(tplan, batch, pdl, stream);
         }
+    }
+    TcPlan tc;
+    if ((flags & P100_QMV_TC) && plan_tc(type, w, xq, rows, k, batch, sms, tc)) {
+        tc.p.y = y;
+        return launch_tc(type, tc, pdl, stream);
     }
     MmaPlan mplan;
     if (plan_mma(type, w, xq, rows, k, batch, sms, mplan)) {
@@ -543,12 +659,12 @@ p100_status run_qmv(int type, const void* w, int rows, int k, const void* xq, in
 }
 
 // Batch-1 mat-vec of a row-parallel matrix whose partial sums go straight
-// into every rank's peer slots (the team kernel's push epilogue); *ctas_out
-// = the CTAs that arrive on the counters.  False when the team kernel does
-// not take the shape (the caller then writes y and pushes separately).
-// ar: the exchange's PeerAr in device memory (ar_host: the same, on the host).
+// into every rank's peer slots (the team kernel's push epilogue).  False
+// when the team kernel does not take the shape (the caller then writes y and
+// pushes separately).  ar: the exchange's PeerAr in device memory (ar_host:
+// the same, on the host).
 bool run_qmv_push(int type, const void* w, int rows, int k, const void* xq, const dec::PeerAr* ar,
-                  const dec::PeerAr& ar_host, int* ctas_out, cudaStream_t stream, p100_status* st) {
+                  const dec::PeerAr& ar_host, cudaStream_t stream, p100_status* st) {
     int sms = 0;
     *st = P100_OK;
     if (require_sm100(nullptr, &sms) || !known_type(type) || rows != ar_host.n) return false;
@@ -559,7 +675,6 @@ bool run_qmv_push(int type, const void* w, int rows, int k, const void* xq, cons
     tplan.p.y = nullptr;
     tplan.p.col0 = 0;
     tplan.p.ar = ar;
-    *ctas_out = tplan.grid;
     switch (type) {
         case P100_Q4_0: *st = launch_team_type<P100_Q4_0, true>(tplan, 1, true, stream); break;
         case P100_Q8_0: *st = launch_team_type<P100_Q8_0, true>(tplan, 1, true, stream); break;
@@ -1097,7 +1212,7 @@ p100_status p100_qmv_f32(int type, const void* w, int rows, int k, const float* 
 p100_status p100_qmv_ex(int type, const void* w, int rows, int k, const void* x_q8_1, int batch, float* y,
                         unsigned flags, p100_stream_t stream) {
     clear_error();
-    if (flags & ~P100_QMV_PDL) return set_error(P100_ERR_INVALID, "unknown flags 0x%x", flags);
+    if (flags & ~(P100_QMV_PDL | P100_QMV_TC)) return set_error(P100_ERR_INVALID, "unknown flags 0x%x", flags);
     return run_qmv(type, w, rows, k, x_q8_1, batch, y, flags, stream);
 }
 

@@ -33,41 +33,41 @@ constexpr int kArgmaxThreads = 1024;
 // ------------------------------------------------- one-shot peer all-reduce
 // Tensor-parallel sum of an n-float partial vector over `world` GPUs of one
 // box through NVLink peer memory (CUDA IPC mappings).  Every rank owns an
-// arena of slots [2][world][n] fp32 and a 64-bit arrival counter; the slot
-// and counter pointers of every rank (own and peers') are in PeerAr.
-//   push (the row-parallel mat-vec's epilogue, qmv_team_kernel with its push
-//     fields, or ar_push_kernel after any other producer): the partial goes
-//     into slot [e&1][rank] of every rank; each pushing CTA then fences at
-//     system scope and adds 1 to every rank's counter (release);
-//   reduce (rmsnorm_q8_1_kernel with ar.world > 0): waits, bounded, until its
-//     own counter reaches *done + add (add = world x the pushing grid's
-//     CTAs, fixed when the step is recorded), sums the world slots in rank
+// arena of tagged slots [2][world][n]: 64-bit words holding a value (low 32
+// bits) and the epoch that wrote it (high 32 bits).  One 8-byte store is
+// single-copy atomic, so a reader that sees the epoch it waits for also sees
+// that store's value: no fence and no arrival counter between the push and
+// the reduce (an earlier form fenced every pushing thread at system scope
+// and counted arrivals; the fences cost about 14 us an exchange).
+//   push (the row-parallel mat-vec's epilogue, qmv_team_kernel's PUSH
+//     kernels, or ar_push_kernel after any other producer): value v of row i
+//     goes to word [e&1][rank][i] of every rank as (e << 32) | bits(v);
+//   reduce (rmsnorm_q8_1_kernel with ar.world > 0): polls, bounded, until
+//     every word it needs carries epoch e, adds the world values in rank
 //     order (the same order on every rank, so every rank holds the same
-//     bits), then stores the new *done and e as the completed epoch.
-// e = completed epoch + 1, read from a device counter, so a replayed graph
-// uses a new epoch every call.  Slots are double-buffered by e & 1: a rank
-// writes epoch e+2 into a peer only after its own reduce of e+1, which
-// waited for every rank's push of e+1, which each rank made after its reduce
-// of e had finished reading.
+//     bits), then stores e as the completed epoch.
+// e = completed epoch + 1 (so never 0, the tag of a zeroed arena), read from
+// a device counter, so a replayed graph uses a new epoch every call.  Slots
+// are double-buffered by e & 1: a rank writes epoch e+2 into a peer only
+// after its own reduce of e+1, which saw every rank's push of e+1, which each
+// rank made after its reduce of e had finished reading.
 constexpr int kArMaxRanks = 8;
 constexpr int kArBlocks = 8;
 struct PeerAr {
-    float* slots[kArMaxRanks];
-    unsigned long long* count[kArMaxRanks];
+    unsigned long long* slots[kArMaxRanks];   // rank r's tagged words [2][world][n]
     int world, rank, n;
     int* epoch;                 // this rank's completed-epoch counter
-    unsigned long long* done;   // this rank's counter value when the last reduce finished
-    unsigned long long add;     // arrivals one exchange brings (world x pushing CTAs)
     unsigned long long wait_ns; // the reduce's wait limit (0: kWaitLimitNs)
 };
 
-__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
-    unsigned long long v;
-    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-    return v;
+__device__ __forceinline__ unsigned long long tag_word(unsigned e, float v) {
+    return (static_cast<unsigned long long>(e) << 32) | __float_as_uint(v);
 }
-__device__ __forceinline__ void red_release_sys_u64(unsigned long long* p, unsigned long long v) {
-    asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+__device__ __forceinline__ void st_word(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ void ld_words2(const unsigned long long* p, unsigned long long& a, unsigned long long& b) {
+    asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
 }
 
 // Grid kArBlocks x 256; n % (4 * kArBlocks) == 0.
@@ -76,16 +76,12 @@ __global__ void __launch_bounds__(256) ar_push_kernel(const float* __restrict__ 
     pdl_wait_prior_grid();
     const unsigned e = unsigned(*ar.epoch) + 1u;
     const int par = int(e & 1u);
-    const int n4 = ar.n / 4, per = n4 / kArBlocks;
-    const float4* src = reinterpret_cast<const float4*>(y) + blockIdx.x * per;
+    const int per = ar.n / kArBlocks;
     for (int i = threadIdx.x; i < per; i += blockDim.x) {
-        const float4 v = src[i];
-        for (int r = 0; r < ar.world; ++r)
-            reinterpret_cast<float4*>(ar.slots[r] + (size_t(par) * ar.world + ar.rank) * ar.n)[blockIdx.x * per + i] = v;
+        const int row = blockIdx.x * per + i;
+        const unsigned long long w = tag_word(e, y[row]);
+        for (int r = 0; r < ar.world; ++r) st_word(ar.slots[r] + (size_t(par) * ar.world + ar.rank) * ar.n + row, w);
     }
-    __threadfence_system();   // this thread's stores, system scope, before the block's arrival
-    __syncthreads();
-    if (threadIdx.x < ar.world) red_release_sys_u64(ar.count[threadIdx.x], 1ull);
 }
 
 // ------------------------------------------------------------------ RMSNorm
@@ -161,42 +157,46 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_q8_1_kernel(float* __res
             }
         }
     } else if (ar.world > 0) {
-        // delta = the peer all-reduce of this epoch (batch 1, n = k)
+        // delta = the peer all-reduce of this epoch (batch 1, n = k): every
+        // thread polls the tagged words of its own chunks (rows 4c..4c+3 of
+        // every rank), bounded, then adds the ranks in order
         const unsigned e = unsigned(*ar.epoch) + 1u;
         const int par = int(e & 1u);
-        const unsigned long long target = *ar.done + ar.add;
+        const unsigned long long* base = ar.slots[ar.rank] + size_t(par) * ar.world * ar.n;
+        const unsigned long long limit = ar.wait_ns ? ar.wait_ns : kWaitLimitNs;
+        const unsigned long long start = globaltimer_ns();
         bool ok = true;
-        if (tid == 0) {
-            const unsigned long long start = globaltimer_ns();
-            const unsigned long long limit = ar.wait_ns ? ar.wait_ns : kWaitLimitNs;
-            while (ld_acquire_sys_u64(ar.count[ar.rank]) < target) {
-                if (globaltimer_ns() - start > limit) {
-                    ok = false;
-                    break;
-                }
-            }
-        }
-        if (!__syncthreads_and(ok) && tid == 0) atomicExch(&g_device_error, kDevErrTimeout);
-        const float* base = ar.slots[ar.rank] + size_t(par) * ar.world * ar.n;
 #pragma unroll
         for (int i = 0; i < kNormChunks; ++i) {
             const int c = tid + i * kNormThreads;
-            if (c < nc) {
-                float4 d4 = reinterpret_cast<const float4*>(base)[c];
-                for (int r = 1; r < ar.world; ++r) {
-                    const float4 o = reinterpret_cast<const float4*>(base + size_t(r) * ar.n)[c];
-                    d4 = make_float4(__fadd_rn(d4.x, o.x), __fadd_rn(d4.y, o.y), __fadd_rn(d4.z, o.z),
-                                     __fadd_rn(d4.w, o.w));
+            if (c >= nc) continue;
+            float4 d4 = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int r = 0; r < ar.world; ++r) {
+                const unsigned long long* wp = base + size_t(r) * ar.n + 4 * c;
+                unsigned long long w0, w1, w2, w3;
+                for (;;) {
+                    ld_words2(wp, w0, w1);
+                    ld_words2(wp + 2, w2, w3);
+                    if (unsigned(w0 >> 32) == e && unsigned(w1 >> 32) == e && unsigned(w2 >> 32) == e &&
+                        unsigned(w3 >> 32) == e)
+                        break;
+                    if (!ok || globaltimer_ns() - start > limit) {
+                        ok = false;
+                        break;
+                    }
                 }
-                v[i] = make_float4(__fadd_rn(v[i].x, d4.x), __fadd_rn(v[i].y, d4.y), __fadd_rn(v[i].z, d4.z),
-                                   __fadd_rn(v[i].w, d4.w));
-                xr[c] = v[i];
+                const float4 o = make_float4(__uint_as_float(unsigned(w0)), __uint_as_float(unsigned(w1)),
+                                             __uint_as_float(unsigned(w2)), __uint_as_float(unsigned(w3)));
+                d4 = r == 0 ? o
+                            : make_float4(__fadd_rn(d4.x, o.x), __fadd_rn(d4.y, o.y), __fadd_rn(d4.z, o.z),
+                                          __fadd_rn(d4.w, o.w));
             }
+            v[i] = make_float4(__fadd_rn(v[i].x, d4.x), __fadd_rn(v[i].y, d4.y), __fadd_rn(v[i].z, d4.z),
+                               __fadd_rn(v[i].w, d4.w));
+            xr[c] = v[i];
         }
-        if (tid == 0) {   // read by the next push and reduce, which start after this kernel ends
-            *ar.epoch = int(e);
-            *ar.done = target;
-        }
+        if (!__syncthreads_and(ok) && tid == 0) atomicExch(&g_device_error, kDevErrTimeout);
+        if (tid == 0) *ar.epoch = int(e);   // read by the next push and reduce, which start after this kernel ends
     }
     float s = 0.f;
 #pragma unroll

@@ -73,7 +73,6 @@ struct Decoder {
     void* ar_peer[dec::kArMaxRanks] = {};    // IPC mappings of the other ranks' arenas
     int* ar_epoch = nullptr;                 // completed-epoch counter (in the arena above)
     dec::PeerAr ar{};
-    unsigned long long ar_pending = 0;       // arrivals the last recorded push brings
     dec::PeerAr* ar_dev = nullptr;           // a device copy of ar (read by the push epilogue)
     // the persistent step kernel (step.cuh): one cooperative launch a token
     bool step_region = false;   // the arena holds its buffers (the config allows it)
@@ -401,14 +400,12 @@ p100_status dec_qmv(const DecTensor& w, int k, const uint8_t* xq, float* y, cuda
     return P100_OK;
 }
 
-// x += delta (or, with peer_reduce, += the peer all-reduce of this epoch,
-// whose pushes bring d.ar_pending arrivals), then RMSNorm * w and Q8_1 into
-// d.xq.
+// x += delta (or, with peer_reduce, += the peer all-reduce of this epoch),
+// then RMSNorm * w and Q8_1 into d.xq.
 p100_status dec_rmsnorm(Decoder& d, const float* delta, const DecTensor& w, cudaStream_t s, bool peer_reduce = false) {
     dec::PeerAr ar{};
     if (peer_reduce) {
         ar = d.ar;
-        ar.add = d.ar_pending;
         delta = nullptr;
     }
     return launch_glue(dec::rmsnorm_q8_1_kernel, dim3(1), dim3(dec::kNormThreads), s, "rmsnorm_q8_1_kernel launch",
@@ -421,20 +418,15 @@ p100_status dec_rmsnorm(Decoder& d, const float* delta, const DecTensor& w, cuda
 // d.delta.  Peer memory: where the team kernel takes the matrix, its
 // epilogue pushes the rows into every rank's slots (no separate kernel);
 // else the mat-vec writes d.delta and ar_push_kernel pushes it.  The reduce
-// runs in the next RMSNorm, which waits for d.ar_pending arrivals.
+// runs in the next RMSNorm.
 p100_status dec_qmv_allreduce(Decoder& d, const DecTensor& w, int k, cudaStream_t s) {
     if (d.peer_ar && w.nparts == 1) {
-        int ctas = 0;
         p100_status st = P100_OK;
-        if (run_qmv_push(w.ptype[0], w.ptr, w.prows[0], k, d.xq, d.ar_dev, d.ar, &ctas, s, &st)) {
-            d.ar_pending = static_cast<unsigned long long>(d.nranks) * ctas;
-            return st;
-        }
+        if (run_qmv_push(w.ptype[0], w.ptr, w.prows[0], k, d.xq, d.ar_dev, d.ar, s, &st)) return st;
     }
     if (p100_status st = dec_qmv(w, k, d.xq, d.delta, s)) return st;
     if (!d.tp) return P100_OK;
     if (!d.peer_ar) return p100_tp_allreduce_sum(d.tp, d.delta, size_t(d.cfg.hidden), s);
-    d.ar_pending = static_cast<unsigned long long>(d.nranks) * dec::kArBlocks;
     return launch_glue(dec::ar_push_kernel, dim3(dec::kArBlocks), dim3(256), s, "ar_push_kernel launch",
                        static_cast<const float*>(d.delta), d.ar);
 }
@@ -648,11 +640,11 @@ struct SetupComm {
 // arena, the IPC handles go round an all-gather, and every rank maps the
 // others'.  Used only if every pair of ranks' GPUs has peer access and
 // P100_TP_ALLREDUCE is not "nccl", all ranks having agreed.  The arena holds
-//   [2][world][hidden] fp32 slots (the one-shot all-reduce of either
-//   decoder path), then in 256-byte cells: the graph decoder's epoch, the
-//   step kernel's argmax candidates [world][2], and the 64-bit arrival
-//   counter (at +512; the graph decoder keeps its reduce's `done` value at
-//   +520 of its own arena).
+//   [2][world][hidden] 64-bit slots (the graph decoder's tagged words; the
+//   step kernel uses their first half as fp32 slots of the same shape), then
+//   in 256-byte cells: the graph decoder's epoch, the step kernel's argmax
+//   candidates [world][2] and its 64-bit exchange counter, and a device copy
+//   of this rank's exchange descriptor (read by the push epilogue).
 // Collective: every rank calls it.  Returns an error only when the ranks
 // agree that one of them failed; a declined or failed peer path leaves
 // d.peer_ar false on every rank (NCCL carries the exchanges then).
@@ -680,8 +672,8 @@ p100_status dec_setup_peer_ar(Decoder& d) {
     if (v.errors) return sc.fail("peer exchange setup");
     if (v.declines) return P100_OK;
     // 2. arenas and their IPC handles
-    const size_t slot_bytes = size_t(2) * world * n * 4;
-    const size_t arena_bytes = slot_bytes + 768 + 512;   // epoch | candidates | counter (+ done), 256 B each | ar copy
+    const size_t slot_bytes = size_t(2) * world * n * 8;
+    const size_t arena_bytes = slot_bytes + 768 + 512;   // epoch | candidates | counter, 256 B each | descriptor
     cudaIpcMemHandle_t h{};
     p100_status st = cuda_status(cudaMalloc(&d.ar_arena, arena_bytes), "cudaMalloc(ar arena)");
     if (!st) st = cuda_status(cudaMemset(d.ar_arena, 0, arena_bytes), "cudaMemset(ar arena)");
@@ -721,8 +713,7 @@ p100_status dec_setup_peer_ar(Decoder& d) {
             base = static_cast<uint8_t*>(p);
         }
         if (!st) {
-            d.ar.slots[r] = reinterpret_cast<float*>(base);
-            d.ar.count[r] = reinterpret_cast<unsigned long long*>(base + slot_bytes + 512);
+            d.ar.slots[r] = reinterpret_cast<unsigned long long*>(base);
             d.sp.slots[r] = reinterpret_cast<float*>(base);
             d.sp.cslots[r] = reinterpret_cast<float*>(base + slot_bytes + 256);
             d.sp.xcount[r] = reinterpret_cast<unsigned long long*>(base + slot_bytes + 512);
@@ -731,7 +722,6 @@ p100_status dec_setup_peer_ar(Decoder& d) {
     // the push epilogue reads this rank's exchange descriptor from device memory
     if (!st) {
         d.ar_epoch = reinterpret_cast<int*>(d.ar_arena + slot_bytes);
-        d.ar.done = reinterpret_cast<unsigned long long*>(d.ar_arena + slot_bytes + 520);
         d.ar.world = world;
         d.ar.rank = d.rank;
         d.ar.n = n;
@@ -946,29 +936,24 @@ p100_status p100_rmsnorm_q8_1(float* x, const float* delta, const float* w, floa
     return launch_status("rmsnorm_q8_1_kernel launch");
 }
 
-p100_status p100_peer_reduce_rmsnorm(float* x, const float* w, float eps, int k, void* x_q8_1, float* slots, int world,
-                                     int rank, int* epoch, unsigned long long* count, unsigned long long* done,
-                                     unsigned long long arrivals, unsigned long long wait_ns, p100_stream_t stream) {
+p100_status p100_peer_reduce_rmsnorm(float* x, const float* w, float eps, int k, void* x_q8_1, void* slots, int world,
+                                     int rank, int* epoch, unsigned long long wait_ns, p100_stream_t stream) {
     clear_error();
     if (k <= 0 || k % 32 || k % (4 * dec::kArBlocks)) return set_error(P100_ERR_INVALID, "k must be a positive multiple of 32");
     if (k > dec::kNormMaxK) return set_error(P100_ERR_UNSUPPORTED, "k above %d", dec::kNormMaxK);
     if (world < 1 || world > dec::kArMaxRanks || rank < 0 || rank >= world)
         return set_error(P100_ERR_INVALID, "rank %d of %d (at most %d ranks)", rank, world, dec::kArMaxRanks);
-    if (!x || !w || !x_q8_1 || !slots || !epoch || !count || !done) return set_error(P100_ERR_INVALID, "null buffer");
+    if (!x || !w || !x_q8_1 || !slots || !epoch) return set_error(P100_ERR_INVALID, "null buffer");
     if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(w) % 16 ||
-        reinterpret_cast<uintptr_t>(slots) % 16 || reinterpret_cast<uintptr_t>(count) % 8 ||
-        reinterpret_cast<uintptr_t>(done) % 8)
-        return set_error(P100_ERR_INVALID, "x, w and slots 16-byte aligned, count and done 8-byte aligned");
+        reinterpret_cast<uintptr_t>(slots) % 16)
+        return set_error(P100_ERR_INVALID, "x, w and slots must be 16-byte aligned");
     if (p100_status st = require_sm100(nullptr, nullptr)) return st;
     dec::PeerAr ar{};
-    ar.slots[rank] = slots;
-    ar.count[rank] = count;
+    ar.slots[rank] = static_cast<unsigned long long*>(slots);
     ar.world = world;
     ar.rank = rank;
     ar.n = k;
     ar.epoch = epoch;
-    ar.done = done;
-    ar.add = arrivals;
     ar.wait_ns = wait_ns;
     dec::rmsnorm_q8_1_kernel<<<1, dec::kNormThreads, 0, stream>>>(x, nullptr, w, eps, k, static_cast<uint8_t*>(x_q8_1),
                                                                     nullptr, ar);

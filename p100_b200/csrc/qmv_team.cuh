@@ -109,10 +109,10 @@ struct Params {
     // built from these fp32 activations (16-byte aligned) instead of read.
     const float* x_f32;
     // Tensor-parallel push (the PUSH kernels, batch 1): the rows are a
-    // partial sum of a row-parallel matrix; instead of y they go into slot
-    // [e & 1][rank] of every rank's peer arena, and the CTA then fences at
-    // system scope and arrives on every rank's counter (the dec::PeerAr in
-    // device memory that ar points to; its reduce runs in the next RMSNorm).
+    // partial sum of a row-parallel matrix; instead of y they go, tagged with
+    // the exchange's epoch e, into slot [e & 1][rank] of every rank's peer
+    // arena (the dec::PeerAr in device memory that ar points to; the reduce
+    // runs in the next RMSNorm).
     const dec::PeerAr* ar;
 };
 
@@ -504,7 +504,6 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_team_kernel(const Params p) {
         pdl_wait_prior_grid();   // x may come from an earlier kernel
         quantize_row(p, smem + p.act_off);
     }
-    bool failed = false;   // a bounded wait ran out (the push then signals nothing)
     if (!p.norm_w && !p.x_f32) {
         const bool ok = mbar_wait(act_bar, 0);
         int any_timeout;
@@ -520,22 +519,21 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_team_kernel(const Params p) {
                 : "r"(static_cast<unsigned>(ok)), "r"(kConsumers * 32)
                 : "memory");
         }
-        if (any_timeout) {
-            if constexpr (!PUSH) return;
-            failed = true;
-        }
+        if (any_timeout) return;
     }
-    // push: the slot parity of this exchange (the epoch was advanced by the
-    // previous RMSNorm, complete once the previous kernel is)
-    int par = 0;
+    // push: the epoch of this exchange (advanced by the previous RMSNorm,
+    // complete once the previous kernel is)
+    unsigned epoch = 0;
     if constexpr (PUSH) {
         pdl_wait_prior_grid();
-        par = int((unsigned(*p.ar->epoch) + 1u) & 1u);
+        epoch = unsigned(*p.ar->epoch) + 1u;
     }
     auto put = [&](int row, float v) {
         if constexpr (PUSH) {
             const dec::PeerAr& ar = *p.ar;
-            for (int r = 0; r < ar.world; ++r) ar.slots[r][(size_t(par) * ar.world + ar.rank) * ar.n + row] = v;
+            const unsigned long long w = dec::tag_word(epoch, v);
+            for (int r = 0; r < ar.world; ++r)
+                dec::st_word(ar.slots[r] + (size_t(epoch & 1u) * ar.world + ar.rank) * ar.n + row, w);
         } else {
             p.y[size_t(p.col0) * p.rows + row] = v;
         }
@@ -549,7 +547,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_team_kernel(const Params p) {
         for (int i = 0; i < 8; ++i) act.dx[i] = act.m[i] = 0.f;
     }
 
-    for (int s = 0; s < nst && (!PUSH || !failed); ++s) {
+    for (int s = 0; s < nst; ++s) {
         const int slot = s % p.nslot;
         const bool timed_out = !mbar_wait(&full[slot], (s / p.nslot) & 1);
         int any_timeout;
@@ -568,10 +566,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_team_kernel(const Params p) {
                 : "r"(static_cast<unsigned>(timed_out)), "r"(kConsumers * 32)
                 : "memory");
         }
-        if (any_timeout) {
-            failed = true;
-            break;
-        }
+        if (any_timeout) break;
         const uint8_t* stage = ring + size_t(slot) * p.slot_bytes;
         const int first = r0 + s * teams;
         const int nr = min(teams, r1 - first);
@@ -598,22 +593,6 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_team_kernel(const Params p) {
                 put(first + team, sum);
             }
         }
-    }
-    if constexpr (PUSH) {
-        // every consumer's peer stores, then one arrival per CTA on every
-        // rank (none if a wait ran out: the reduce then times out and flags)
-        __threadfence_system();
-        int any_failed;
-        asm volatile(
-            "{\n\t.reg .pred p, q;\n\t"
-            "setp.ne.u32 p, %1, 0;\n\t"
-            "bar.red.or.pred q, 15, %2, p;\n\t"
-            "selp.u32 %0, 1, 0, q;\n\t}"
-            : "=r"(any_failed)
-            : "r"(static_cast<unsigned>(failed)), "r"(kConsumers * 32)
-            : "memory");
-        if (!any_failed && tid == 0)
-            for (int r = 0; r < p.ar->world; ++r) dec::red_release_sys_u64(p.ar->count[r], 1ull);
     }
 }
 
