@@ -662,6 +662,17 @@ def kernel_only(args):
         P.check(P.device_error())
         print(json.dumps({"kernel_only": f"qmv_h16 Q4_0 {k}x{rows} chain 16", "launches": args.warmup + args.steps}))
         return 0
+    if args.kernel_only == "qmvtc":
+        # the tcgen05 batched kernel: Q4_K on the target shape at batch 8, 5 copies (165 MB > L2)
+        ws = [torch.from_numpy(W.weights(W.Q4_K, rows, k, seed=s_)).cuda() for s_ in range(5)]
+        xq = P.q8_1_quantize(torch.from_numpy(W.activations(8, k, seed=2)).cuda())
+        y = torch.empty(8, rows, device="cuda")
+        for i in range(args.warmup + args.steps):
+            P.qmv(W.Q4_K, ws[i % 5], rows, k, xq, 8, y=y, flags=P.QMV_TC)
+        torch.cuda.synchronize()
+        P.check(P.device_error())
+        print(json.dumps({"kernel_only": f"qmv_tc Q4_K {k}x{rows} batch 8", "launches": args.warmup + args.steps}))
+        return 0
     if args.kernel_only == "qmv6k":
         # the Q6_K LM head of a Q4_K_M 8B model: 4096 x 128256, 431 MB > L2
         k, rows = 4096, 128256
@@ -694,8 +705,10 @@ def main():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the 8B/70B decode section")
-    ap.add_argument("--kernel-only", choices=["qmv", "qmvb", "qmv6k", "h16", "fa", "fa4096", "faq8", "faq4", "decode"],
+    ap.add_argument("--kernel-only",
+                    choices=["qmv", "qmvb", "qmvtc", "qmv6k", "h16", "fa", "fa4096", "faq8", "faq4", "decode"],
                     help="one kernel's launches only (ncu cases); qmvb = the target shape at batch 16, "
+                         "qmvtc = the target shape in Q4_K at batch 8 on the tcgen05 kernel, "
                          "h16 = the target shape on the h16 path, "
                          "qmv6k = a Q6_K 4096x128256 LM head at batch 1, "
                          "fa = 32768 keys, fa4096 = 4096 keys, faq8 / faq4 = 32768 keys of q8_0 / q4_0 K/V")

@@ -117,8 +117,14 @@ p100_status p100_qmv(int type, const void* w, int rows, int k, const void* x_q8_
                             by it.  Activations are read only after it ends. */
 #define P100_QMV_TC 2u   /* batch 2..16 of Q4_0 / Q8_0 / Q4_K (16-byte aligned rows,
                             k % 256 == 0): the 5th-generation tensor-core kernel
-                            (tcgen05.mma kind::i8, accumulators in tensor memory,
-                            weights by TMA) instead of the mma.sync kernel. */
+                            (tcgen05.mma kind::i8, operands and accumulators in
+                            tensor memory, weights by TMA) wherever it fits. */
+#define P100_QMV_MMA 4u  /* batch 2..16: never the tcgen05 kernel (the mma.sync
+                            kernel where it fits).  Without either flag, Q8_0 and
+                            Q4_K matrices of rows x k >= 2^25 take the tcgen05
+                            kernel (faster there: 1.2-1.5x on the Llama-3 FFN
+                            shapes), everything else the mma.sync kernel.  The
+                            two may not be combined. */
 p100_status p100_qmv_ex(int type, const void* w, int rows, int k, const void* x_q8_1,
                         int batch, float* y, unsigned flags, p100_stream_t stream);
 /* p100_q8_1_quantize with P100_QMV_PDL available: the quantiser launched as

@@ -32,7 +32,8 @@ KV_F16, KV_Q8_0, KV_Q4_0 = 0, 1, 2
 KV_BLOCK_BYTES = {KV_Q8_0: 34, KV_Q4_0: 18}
 Q8_1_BLOCK_BYTES = 36
 QMV_PDL = 1
-QMV_TC = 2   # P100_QMV_TC: batch 2..16 on the tcgen05 kernel
+QMV_TC = 2   # P100_QMV_TC: batch 2..16 on the tcgen05 kernel wherever it fits
+QMV_MMA = 4  # P100_QMV_MMA: batch 2..16 never on the tcgen05 kernel
 
 STATUS = {0: "P100_OK", 1: "P100_ERR_INVALID", 2: "P100_ERR_CUDA", 3: "P100_ERR_NCCL",
           4: "P100_ERR_TIMEOUT", 5: "P100_ERR_UNSUPPORTED"}

@@ -483,6 +483,10 @@ bool plan_tc(int type, const void* w, const void* xq, int rows, int k, int batch
     const int slot_all = qmvtc::raw_stride(raw_bytes) + qmvtc::kActBytes;   // weights + activations of a stage
     const int slots = std::min(qmvtc::kMaxRaw, (qmvtc::kSmemLimit - qmvtc::kRawOff) / slot_all);
     if (slots < 2) return false;
+    // slice 0 receives the other slices' partial sums in its raw ring
+    while (slices > 1 && size_t(slices - 1) * qmvtc::kCols * qmvtc::kRows * 4 >
+                             size_t(slots) * size_t(qmvtc::raw_stride(raw_bytes)))
+        slices /= 2;
     PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
     if (!encode) return false;
     const cuuint64_t dims[2] = {cuuint64_t(row_bytes / 2), cuuint64_t(rows)};
@@ -594,8 +598,13 @@ p100_status run_qmv(int type, const void* w, int rows, int k, const void* xq, in
             default: return launch_team_type<P100_Q6_K>(tplan, batch, pdl, stream);
         }
     }
+    // the tcgen05 kernel by default where it measured faster than mma.sync:
+    // Q8_0 / Q4_K on large matrices (its fixed cost loses on small ones, and
+    // Q4_0's nibble unpacking keeps it behind mma.sync at every size)
+    const bool tc_default = (type == P100_Q8_0 || type == P100_Q4_K) && size_t(rows) * size_t(k) >= (size_t(1) << 25);
+    const bool want_tc = (flags & P100_QMV_TC) || (tc_default && !(flags & P100_QMV_MMA));
     TcPlan tc;
-    if ((flags & P100_QMV_TC) && plan_tc(type, w, xq, rows, k, batch, sms, tc)) {
+    if (want_tc && plan_tc(type, w, xq, rows, k, batch, sms, tc)) {
         tc.p.y = y;
         return launch_tc(type, tc, pdl, stream);
     }
@@ -1212,7 +1221,10 @@ p100_status p100_qmv_f32(int type, const void* w, int rows, int k, const float* 
 p100_status p100_qmv_ex(int type, const void* w, int rows, int k, const void* x_q8_1, int batch, float* y,
                         unsigned flags, p100_stream_t stream) {
     clear_error();
-    if (flags & ~(P100_QMV_PDL | P100_QMV_TC)) return set_error(P100_ERR_INVALID, "unknown flags 0x%x", flags);
+    if (flags & ~(P100_QMV_PDL | P100_QMV_TC | P100_QMV_MMA))
+        return set_error(P100_ERR_INVALID, "unknown flags 0x%x", flags);
+    if ((flags & P100_QMV_TC) && (flags & P100_QMV_MMA))
+        return set_error(P100_ERR_INVALID, "P100_QMV_TC and P100_QMV_MMA exclude each other");
     return run_qmv(type, w, rows, k, x_q8_1, batch, y, flags, stream);
 }
 

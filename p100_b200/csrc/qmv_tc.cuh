@@ -39,9 +39,10 @@
 //               columns the batch uses, the bias written back, each block's
 //               scaling in packed f32x2 arithmetic; the two warpgroups' sums
 //               are added at the end in a fixed order.
-// Tensor memory holds two stages of A operands and two of accumulators; the
-// shared-memory operand slots (B tiles and scales) are four deep, so the
-// converters wait only for the MMA two stages back, not for the epilogue.
+// Operands are four stages deep (A in tensor memory, B tiles and scales in
+// shared memory), freed together when the epilogue is done with a stage, so
+// the converters run up to four stages ahead of it; the accumulators are two
+// stages deep.
 //
 // Every wait is bounded (kWaitLimitNs); a role that gives up raises the
 // device flag and the CTA's abort word, the others see it and leave, and the
@@ -58,8 +59,8 @@ namespace qmvtc {
 constexpr int kRows = 128;            // M: rows per CTA (tensor-memory lanes)
 constexpr int kCols = 16;             // N: activation columns (batch <= 16, zero-padded)
 constexpr int kBlocks = 8;            // 32-value blocks per stage (one 256-value group)
-constexpr int kTmemStages = 2;        // accumulator and A stages in tensor memory
-constexpr int kOpSlots = 4;           // shared-memory operand slots (B tiles, scales)
+constexpr int kTmemStages = 2;        // accumulator stages in tensor memory
+constexpr int kOpSlots = 4;           // operand stages: A in tensor memory, B tiles and scales in shared memory
 constexpr int kTmemCols = 512;        // the allocation (a power of two)
 constexpr int kACol = kTmemStages * kBlocks * kCols;   // 256: A operands after the accumulators
 constexpr int kAColsPerStage = kBlocks * 8;           // 32 int8 values of 128 rows = 8 columns a block
@@ -72,7 +73,7 @@ constexpr int kActRow = kBlocks * 36;            // one column's Q8_1 blocks of 
 constexpr int kActBytes = kCols * kActRow;       // activation slot: 4608 B
 constexpr uint32_t kBias = 0x4B400000u;          // the bits of 1.5 * 2^23
 
-static_assert(kACol + kTmemStages * kAColsPerStage <= kTmemCols, "tensor memory layout");
+static_assert(kACol + kOpSlots * kAColsPerStage <= kTmemCols, "tensor memory layout");
 
 // Per shared-memory operand slot: B tiles [kBlocks][512 B], then FP32
 // scales: weight [kBlocks][2][kRows] (scale and, for Q4_K, min term),
@@ -341,9 +342,9 @@ __device__ __forceinline__ void convert_weights(const uint8_t* raw, float* ws, u
 
 // The batch's activation blocks of one stage (act: a 288-byte row of eight
 // Q8_1 blocks per column) into the B tiles (column c of block j at canon(c,
-// .) of tile j) and the activation scales (xs: [kBlocks][2][kCols]).  Thread
-// t < batch x 8 converts column t / 8's block t % 8; the tiles' rows past the
-// batch stay zero from the kernel's start.
+// .) of tile j) and the activation scales (xs: [kBlocks][2][kCols]).  Item
+// t < batch x 8 is column t / 8's block t % 8; the tiles' rows past the batch
+// stay zero from the kernel's start.
 template <int TYPE>
 __device__ __forceinline__ void convert_activations(const uint8_t* act, uint8_t* B, float* xs, int batch, int t) {
     const int c = t >> 3, j = t & 7;
@@ -374,7 +375,7 @@ __device__ __forceinline__ void convert_activations(const uint8_t* act, uint8_t*
 }
 
 // ------------------------------------------------------------ the kernel
-// Shared memory: mbarriers and two words at 0, the warpgroup / split-K
+// Shared memory: mbarriers at 0, two words at 240, the warpgroup / split-K
 // exchange area [kCols][kRows] floats at kRedOff, the operand slots at kOpOff,
 // the raw weight ring after them (slots raw_stride bytes apart), then the
 // activation ring (raw_slots x kActBytes).
@@ -387,6 +388,13 @@ __device__ __forceinline__ uint32_t cluster_rank() {
     uint32_t r;
     asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
     return r;
+}
+// v into the shared-memory word of cluster CTA `rank` that corresponds to
+// this CTA's `local` (a store: no round trip).
+__device__ __forceinline__ void st_cluster_f32(float* local, uint32_t rank, float v) {
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_addr(local)), "r"(rank));
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(remote), "f"(v) : "memory");
 }
 
 // Columns 0..NC-1 of NB consecutive blocks of a warpgroup's tile in one
@@ -415,10 +423,12 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_tc_kernel(const __grid_consta
     uint64_t* raw_full = reinterpret_cast<uint64_t*>(smem);
     uint64_t* raw_empty = raw_full + kMaxRaw;
     uint64_t* op_full = raw_empty + kMaxRaw;
-    uint64_t* mma_done = op_full + kTmemStages;
+    uint64_t* op_free = op_full + kOpSlots;
+    uint64_t* mma_done = op_free + kOpSlots;
     uint64_t* tmem_free = mma_done + kTmemStages;
-    uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + 192);
-    volatile int* s_abort = reinterpret_cast<volatile int*>(smem + 196);
+    uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + 240);
+    volatile int* s_abort = reinterpret_cast<volatile int*>(smem + 244);
+    static_assert((2 * kMaxRaw + 2 * kOpSlots + 2 * kTmemStages) * 8 <= 240, "barrier area");
     float* red = reinterpret_cast<float*>(smem + kRedOff);
     uint8_t* ops = smem + kOpOff;
     uint8_t* raws = smem + kRawOff;
@@ -436,8 +446,11 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_tc_kernel(const __grid_consta
             mbar_init(&raw_full[i], 1);
             mbar_init(&raw_empty[i], kConvWarps);
         }
-        for (int i = 0; i < kTmemStages; ++i) {
+        for (int i = 0; i < kOpSlots; ++i) {
             mbar_init(&op_full[i], kConvWarps);
+            mbar_init(&op_free[i], kEpiWarps);
+        }
+        for (int i = 0; i < kTmemStages; ++i) {
             mbar_init(&mma_done[i], 1);
             mbar_init(&tmem_free[i], kEpiWarps);
         }
@@ -504,26 +517,26 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_tc_kernel(const __grid_consta
         }
     } else if (warp < kConvWarps) {
         for (int s = 0; s < nst; ++s) {
-            const int rs = s % R, pp = s & 1;
-            uint8_t* op = ops + size_t(s % kOpSlots) * kOpBytes;
+            const int rs = s % R, os = s % kOpSlots;
+            uint8_t* op = ops + size_t(os) * kOpBytes;
             bool ok = tc_wait(&raw_full[rs], (s / R) & 1, s_abort);
-            // tensor-memory A stage pp is free once the MMAs of stage s - 2
-            // have completed; those ran after the epilogue of stage s - 4 had
-            // released its accumulators, so operand slot s % 4 is free too
-            if (ok && s >= 2) ok = tc_wait(&mma_done[pp], ((s >> 1) - 1) & 1, s_abort);
+            // operand stage os (A, B tiles, scales) is free once the epilogue
+            // is done with stage s - 4
+            if (ok && s >= kOpSlots) ok = tc_wait(&op_free[os], ((s / kOpSlots) - 1) & 1, s_abort);
             if (__any_sync(0xffffffffu, !ok)) break;
             tc_fence_after();
             convert_weights<TYPE>(raws + size_t(rs) * stride, reinterpret_cast<float*>(op + kOpWs),
-                                  tmem + lanes + uint32_t(kACol + pp * kAColsPerStage), r);
+                                  tmem + lanes + uint32_t(kACol + os * kAColsPerStage), r);
+            // activation items spread over the four warps' first lanes
             convert_activations<TYPE>(acts + size_t(rs) * kActBytes, op + kOpB, reinterpret_cast<float*>(op + kOpXs),
-                                      p.batch, tid);
+                                      p.batch, lane * kConvWarps + warp);
             tmem_wait_st();
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // B tiles, for the tensor core's reads
             tc_fence_before();
             __syncwarp();
             if (lane == 0) {
                 mbar_arrive(&raw_empty[rs]);
-                mbar_arrive(&op_full[pp]);
+                mbar_arrive(&op_full[os]);
             }
         }
     } else if (warp == kMmaWarp) {
@@ -531,18 +544,18 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_tc_kernel(const __grid_consta
             constexpr uint32_t idesc = idesc_i8(TYPE == P100_Q8_0, true);
             int issued = 0;
             for (int s = 0; s < nst; ++s) {
-                const int pp = s & 1;
-                bool ok = tc_wait(&op_full[pp], (s >> 1) & 1, s_abort);
+                const int pp = s & 1, os = s % kOpSlots;
+                bool ok = tc_wait(&op_full[os], (s / kOpSlots) & 1, s_abort);
                 // accumulator stage pp biased: initially, then by the
                 // epilogue of stage s - 2 after reading it
                 if (ok) ok = tc_wait(&tmem_free[pp], (s >> 1) & 1, s_abort);
                 if (!ok) break;
                 tc_fence_after();
-                const uint32_t bsm = smem_addr(ops + size_t(s % kOpSlots) * kOpBytes + kOpB);
+                const uint32_t bsm = smem_addr(ops + size_t(os) * kOpBytes + kOpB);
 #pragma unroll
                 for (int j = 0; j < kBlocks; ++j)
                     mma_i8_ts(tmem + uint32_t((pp * kBlocks + j) * kCols),
-                              tmem + uint32_t(kACol + pp * kAColsPerStage + j * 8), umma_desc(bsm + j * kBTile, 128, 256),
+                              tmem + uint32_t(kACol + os * kAColsPerStage + j * 8), umma_desc(bsm + j * kBTile, 128, 256),
                               idesc);
                 mma_commit(&mma_done[pp]);
                 issued = s + 1;
@@ -624,7 +637,10 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_tc_kernel(const __grid_consta
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&tmem_free[pp]);
+            if (lane == 0) {
+                mbar_arrive(&tmem_free[pp]);
+                mbar_arrive(&op_free[s % kOpSlots]);
+            }
         }
 #pragma unroll
         for (int c2 = 0; c2 < NC / 2; ++c2) {
@@ -635,8 +651,10 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_tc_kernel(const __grid_consta
     }
 
     // the two epilogue warpgroups' sums: the second's into the first's (in
-    // the exchange area), then the split K's slice partials in slice order
-    // through distributed shared memory
+    // the exchange area), then the split K's slice partials in slice order:
+    // once every CTA of the cluster is done with its ring, slices 1.. store
+    // their partials into slice 0's raw ring (distributed shared memory,
+    // stores only), and slice 0 adds them after the second cluster barrier
     __syncthreads();
     if (epi && wg == 1)
 #pragma unroll
@@ -647,16 +665,16 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_tc_kernel(const __grid_consta
 #pragma unroll
         for (int c = 0; c < NC; ++c) y[c] += red[c * kRows + r];
     if (p.slices > 1) {
-        __syncthreads();
-        if (lead)
+        float* recv = reinterpret_cast<float*>(raws);   // [slices - 1][NC][kRows]
+        qmvm::cluster_sync_all();
+        if (lead && slice > 0)
 #pragma unroll
-            for (int c = 0; c < NC; ++c) red[c * kRows + r] = y[c];
+            for (int c = 0; c < NC; ++c) st_cluster_f32(recv + ((slice - 1) * NC + c) * kRows + r, 0u, y[c]);
         qmvm::cluster_sync_all();
         if (lead && slice == 0)
             for (int sl = 1; sl < p.slices; ++sl)
 #pragma unroll
-                for (int c = 0; c < NC; ++c) y[c] += qmvm::ld_cluster_f32(red + c * kRows + r, sl);
-        qmvm::cluster_sync_all();   // no block leaves while its partials are read
+                for (int c = 0; c < NC; ++c) y[c] += recv[((sl - 1) * NC + c) * kRows + r];
     }
     if (lead && slice == 0 && row0 + r < p.rows && !*s_abort)
 #pragma unroll

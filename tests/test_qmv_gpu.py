@@ -102,15 +102,17 @@ SHAPES = [(k, rows) for _, k, rows in W.LLAMA3_8B_SHAPES]
 @pytest.mark.parametrize("qtype", [P.Q4_0, P.Q8_0, P.Q4_K])
 @pytest.mark.parametrize("k,rows", SHAPES)
 def test_qmv_llama_shapes(cuda, orc, qtype, k, rows):
-    """Config-2 shapes at batch 1 and 4 against the sequential CPU model."""
+    """Config-2 shapes at batch 1 and 4 against the sequential CPU model
+    (batch 4: the default kernel choice, and the mma.sync kernel forced)."""
     w = W.weights(qtype, rows, k, seed=1000 + k + rows + qtype)
     x = W.activations(4, k, seed=77 + k)
     wd = dev(cuda, w)
     wn = row_norms(orc, qtype, w, rows, k)
     yref = q81_reference(orc, qtype, w, rows, k, x).astype(np.float64)
     xq = P.q8_1_quantize(dev(cuda, x))
-    y4 = P.qmv(qtype, wd, rows, k, xq, batch=4).cpu().numpy()
-    assert_qmv_close(y4, yref, wn, x)
+    for flags in (0, P.QMV_MMA):
+        y4 = P.qmv(qtype, wd, rows, k, xq, batch=4, flags=flags).cpu().numpy()
+        assert_qmv_close(y4, yref, wn, x)
     y1 = P.qmv(qtype, wd, rows, k, xq[: k // 32 * 36], batch=1).cpu().numpy()
     assert_qmv_close(y1, yref[:1], wn, x[:1])
 
@@ -219,6 +221,8 @@ def test_qmv_invalid_arguments(cuda):
         P.qmv(P.Q4_0, w, 1, 32, xq, 17)
     with pytest.raises(P.InvalidArgument, match="unknown weight type"):
         P.qmv(7, w, 1, 32, xq, 1)
+    with pytest.raises(P.InvalidArgument, match="exclude each other"):
+        P.qmv(P.Q4_0, w, 1, 32, xq, 2, flags=P.QMV_TC | P.QMV_MMA)
 
 
 # ------------------------------------------------- fp32 activations

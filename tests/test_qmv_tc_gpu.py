@@ -1,6 +1,6 @@
 """The batched mat-vec on the 5th-generation tensor cores (P100_QMV_TC:
-tcgen05.mma kind::i8, one tensor-memory accumulator per 32-value block,
-weights by TMA), through the C-ABI.
+tcgen05.mma kind::i8, operands and one accumulator per 32-value block in
+tensor memory, weights by TMA), through the C-ABI.
 
 Bar: within 1e-3 * ||w|| * ||x|| of prepare()+evaluate().q81 (the integer
 block dots are exact; only the FP32 scaling order differs from the CPU
@@ -32,7 +32,7 @@ def test_tc_matches_q81_model(cuda, orc, qtype, k, rows, batch):
     if rows * k <= 4096 * 4096:
         assert_qmv_close(y, q81_reference(orc, qtype, w, rows, k, x).astype(np.float64), wn, x)
     # against the mma.sync kernel (itself checked against the model elsewhere)
-    y_mma = P.qmv(qtype, wd, rows, k, xq, batch).cpu().numpy()
+    y_mma = P.qmv(qtype, wd, rows, k, xq, batch, flags=P.QMV_MMA).cpu().numpy()
     assert_qmv_close(y, y_mma.astype(np.float64), wn, x)
     assert P.device_error() == P.OK
 
