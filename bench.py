@@ -562,7 +562,8 @@ def collective_section(torch, P, tp, stream, world):
     out = {}
     for nbytes in (16384, 32768, 65536):
         buf = torch.ones(nbytes // 4, device="cuda")
-        g = capture(torch, lambda: [tp.allreduce_sum(buf, stream=stream) for _ in range(64)])
+        # the current stream: inside capture that is the capturing stream
+        g = capture(torch, lambda: [tp.allreduce_sum(buf) for _ in range(64)])
         time_graphs(torch, [g], 3, stream)
         per = [time_graphs(torch, [g], 5, stream) / (5 * 64) * 1e3 for _ in range(3)]
         us = statistics.median(per)
@@ -801,7 +802,7 @@ def main():
             for si, (ksplit, lk, lr) in enumerate(plan):
                 P.qmv_f32(W.Q4_0, sw[si][c], lr, lk, sx[si], x_q8_1=sq[si], y=sy[si], flags=P.QMV_PDL)
                 if ksplit:
-                    tp.allreduce_sum(sy[si], stream=stream)
+                    tp.allreduce_sum(sy[si])   # the current (capturing) stream
 
         split_graphs = [capture(torch, lambda c=c: split_body(c)) for c in range(split_copies)]
         split_launches = 2 * len(SHAPES)
@@ -904,7 +905,7 @@ def main():
             xd[si].copy_(xh[si], non_blocking=True)
             P.qmv_f32(W.Q4_0, wl[c], lr, lk, xd[si], x_q8_1=eq[si], y=ey[si], flags=P.QMV_PDL)
             if ksplit:
-                tp.allreduce_sum(ey[si], stream=stream)
+                tp.allreduce_sum(ey[si])   # the current (capturing) stream
             yh[si].copy_(ey[si], non_blocking=True)
 
     e2e_graphs = [capture(torch, lambda c=c: e2e_body(c)) for c in range(e_copies)]
