@@ -993,7 +993,11 @@ def main():
         result["cpu_baseline"] = cpu_baseline_sample()
     if rank == 0:
         print(json.dumps(result), flush=True)
-    del graphs, split_graphs   # their NCCL calls go before the communicator
+    # every graph that holds NCCL calls goes before the communicator (its
+    # destroy waits for them): head_graphs aliases split_graphs
+    del graphs, split_graphs, head_graphs
+    import gc
+    gc.collect()
     torch.cuda.synchronize()
     if tp is not None:
         tp.close()
