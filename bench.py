@@ -17,8 +17,10 @@ value   = algorithmic bytes of the step (weights + fp32 x + fp32 y,
           rounds repeated until they span at least a second (`rounds`).
           N = 1: the whole step on one GPU.  N > 1 (torchrun, one rank per
           GPU): the same layer step split over the ranks, strong scaling —
-          q/o and down along k (partial sums, an NCCL all-reduce each inside
-          the timed region), k/v and gate/up by rows; `replicated` keeps the
+          q/o and down along k (partial sums, each all-reduced with
+          p100_tp_allreduce_sum inside the timed region: one kernel over NVLink
+          peer memory where the GPUs reach each other, else NCCL), k/v and
+          gate/up by rows; `replicated` keeps the
           weak-scaling figure (every rank the whole shapes, no collective).
 e2e     = the headline's step through the C-ABI with host buffers: each step
           copies its activations from pinned host memory, runs, copies y back
@@ -33,8 +35,9 @@ decode  = configs 4/5: batch-1 decode tokens/s of the Llama-3 8B and 70B
           shapes (random-init Q4_0, KV prefilled to 4096 / 8192), split over
           the ranks (TP = N), with each GPU's bytes per token against the HBM
           roofline; at N > 1 the 8B model's tp_parity against the unsplit
-          model and the exchange's cost per layer, and `collective` (NCCL
-          all-reduce latency and bus bandwidth at the exchange sizes).
+          model and the exchange's cost per layer, and `collective`
+          (p100_tp_allreduce_sum and ncclAllReduce latency and bus bandwidth
+          at the exchange sizes).
 """
 from __future__ import annotations
 
@@ -554,23 +557,45 @@ def exchange_cost(torch, P, m, ms_tp, stream, world, max_over_ranks):
             "us_per_layer": round((ms_tp - ms_slice) * 1e3 / m["n_layer"], 3)}
 
 
-def collective_section(torch, P, tp, stream, world):
-    """NCCL all-reduce (p100_tp_allreduce_sum, fp32 sum) of the per-layer
-    exchange sizes, 64 calls captured in a graph: latency per call and bus
-    bandwidth 2 (N-1)/N x bytes / time (the analogue of the reference's
-    p2p_bandwidth benchmark for this layout's only collective)."""
-    out = {}
-    for nbytes in (16384, 32768, 65536):
-        buf = torch.ones(nbytes // 4, device="cuda")
-        # the current stream: inside capture that is the capturing stream
-        g = capture(torch, lambda: [tp.allreduce_sum(buf) for _ in range(64)])
-        time_graphs(torch, [g], 3, stream)
-        per = [time_graphs(torch, [g], 5, stream) / (5 * 64) * 1e3 for _ in range(3)]
-        us = statistics.median(per)
-        out[f"{nbytes // 1024}KB"] = {"us": round(us, 3), "busbw_GBs": round(2 * (world - 1) / world * nbytes / us / 1e3, 3),
-                                      "us_rounds": stats(per)}
-        del g
-    return {"nccl_allreduce": out}
+def collective_section(torch, P, tp, stream, world, dist):
+    """All-reduce latency at the per-layer exchange sizes (fp32 sum of 16, 32
+    and 64 KB), 64 calls captured in a graph: the library's
+    p100_tp_allreduce_sum as the headline uses it (one kernel over NVLink peer
+    memory where tp.peer) and ncclAllReduce (a second communicator joined with
+    P100_TP_ALLREDUCE=nccl, closed here).  Bus bandwidth 2 (N-1)/N x bytes /
+    time, the analogue of the reference's p2p_bandwidth benchmark for this
+    layout's only collective."""
+    box = [P.tp_unique_id() if dist.get_rank() == 0 else None]
+    dist.broadcast_object_list(box, src=0)
+    saved = os.environ.get("P100_TP_ALLREDUCE")
+    os.environ["P100_TP_ALLREDUCE"] = "nccl"
+    try:
+        nccl_tp = P.TP(box[0], world, tp.rank, torch.cuda.current_device())
+    finally:
+        if saved is None:
+            del os.environ["P100_TP_ALLREDUCE"]
+        else:
+            os.environ["P100_TP_ALLREDUCE"] = saved
+    out = {"p100_tp_path": "peer memory" if tp.peer else "nccl"}
+    try:
+        for label, h in (("p100_tp_allreduce", tp), ("nccl_allreduce", nccl_tp)):
+            per_size = {}
+            for nbytes in (16384, 32768, 65536):
+                buf = torch.ones(nbytes // 4, device="cuda")
+                # the current stream: inside capture that is the capturing stream
+                g = capture(torch, lambda h=h, buf=buf: [h.allreduce_sum(buf) for _ in range(64)])
+                time_graphs(torch, [g], 3, stream)
+                per = [time_graphs(torch, [g], 5, stream) / (5 * 64) * 1e3 for _ in range(3)]
+                us = statistics.median(per)
+                per_size[f"{nbytes // 1024}KB"] = {
+                    "us": round(us, 3), "busbw_GBs": round(2 * (world - 1) / world * nbytes / us / 1e3, 3),
+                    "us_rounds": stats(per)}
+                del g   # before the communicator closes
+            out[label] = per_size
+        torch.cuda.synchronize()
+    finally:
+        nccl_tp.close()
+    return out
 
 
 def c2_grid(torch, P, stream):
@@ -944,13 +969,14 @@ def main():
     kq = ktypes_section(torch, P, stream) if rank == 0 else None
     P.check(P.device_error())
     decode = decode_section(torch, P, stream, rank, world, dist, max_over_ranks, tp) if not args.no_decode else None
-    collective = collective_section(torch, P, tp, stream, world) if tp is not None else None
+    collective = collective_section(torch, P, tp, stream, world, dist) if tp is not None else None
 
     peak, peak_kind = peak_gbs()
     target_bytes = W.qmv_algorithmic_bytes(W.Q4_0, TARGET[2], TARGET[1], 1)
     achieved = target_bytes / (target_us / 1e6) / 1e9
-    split_desc = ("TP=%d: q/o and down split along k (partial sums, an NCCL all-reduce of 16 KB each in the timed "
-                  "region), k/v and gate/up split by rows" % world)
+    split_desc = ("TP=%d: q/o and down split along k (partial sums, each all-reduced with p100_tp_allreduce_sum "
+                  "(%s) in the timed region), k/v and gate/up split by rows"
+                  % (world, "one kernel over NVLink peer memory" if tp is not None and tp.peer else "ncclAllReduce"))
     result = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True,
@@ -976,7 +1002,8 @@ def main():
                 "form": "graph replay + stream sync + host read per step (median of 3 rounds)",
                 "eager_value": round(e2e_eager, 2)},
         "gpu_launches": (split_launches if split_graphs else launches_per_step) * args.steps * len(head_ms),
-        "gpu_launches_note": "the library's kernels in the headline's timed rounds (NCCL kernels not counted)",
+        "gpu_launches_note": "the library's mat-vec and quantiser kernels in the headline's timed rounds (all-reduce "
+                             "kernels not counted)",
         "replicated": replicated,
         "shapes": shape_gbs,
         "batch_sweep": batch_sweep,

@@ -431,8 +431,21 @@ int p100_tp_rank(const p100_tp* tp);
 int p100_tp_size(const p100_tp* tp);
 int p100_tp_device(const p100_tp* tp);
 /* In-place fp32 sum over ranks, ordered on stream (which belongs to the
- * rank's device). */
+ * rank's device).  In a group joined with p100_tp_init_rank whose GPUs all
+ * have peer access to each other (the ranks agree while joining), counts up
+ * to P100_TP_PEER_MAX run as one kernel over NVLink peer memory: every rank
+ * gets the values added in rank order, the same bits on every rank; larger
+ * counts, P100_TP_ALLREDUCE=nccl in the environment and p100_tp_create groups
+ * use ncclAllReduce.  Every rank passes the same count (the path depends on
+ * it).  A peer all-reduce waits up to 30 s for the other ranks (ranks may
+ * reach it far apart, as with NCCL); a wait that runs out leaves buf
+ * unchanged, raises P100_ERR_TIMEOUT in p100_device_error() and breaks the
+ * group's peer path: later all-reduces return at once with the same flag. */
+#define P100_TP_PEER_MAX 65536
 p100_status p100_tp_allreduce_sum(p100_tp* tp, float* buf, size_t count, p100_stream_t stream);
+/* 1 when this rank's all-reduces of up to P100_TP_PEER_MAX values run over
+ * peer memory, else 0. */
+int p100_tp_peer(const p100_tp* tp);
 /* The same for every rank of a single-process group, as one NCCL group call. */
 p100_status p100_tp_allreduce_sum_group(p100_tp* const* tps, int n, float* const* bufs,
                                         size_t count, const p100_stream_t* streams);

@@ -34,6 +34,7 @@ Q8_1_BLOCK_BYTES = 36
 QMV_PDL = 1
 QMV_TC = 2   # P100_QMV_TC: batch 2..16 on the tcgen05 kernel wherever it fits
 QMV_MMA = 4  # P100_QMV_MMA: batch 2..16 never on the tcgen05 kernel
+TP_PEER_MAX = 65536   # P100_TP_PEER_MAX: all-reduces up to this count may run over peer memory
 
 STATUS = {0: "P100_OK", 1: "P100_ERR_INVALID", 2: "P100_ERR_CUDA", 3: "P100_ERR_NCCL",
           4: "P100_ERR_TIMEOUT", 5: "P100_ERR_UNSUPPORTED"}
@@ -109,6 +110,7 @@ def _bind(lib):
         "p100_tp_rank": (ip, [vp]),
         "p100_tp_size": (ip, [vp]),
         "p100_tp_device": (ip, [vp]),
+        "p100_tp_peer": (ip, [vp]),
         "p100_tp_allreduce_sum": (ip, [vp, vp, sz, st]),
         "p100_tp_allreduce_sum_group": (ip, [C.POINTER(vp), ip, C.POINTER(vp), sz, C.POINTER(vp)]),
         "p100_tp_allgather": (ip, [vp, vp, vp, sz, st]),
@@ -351,6 +353,11 @@ class TP:
     @property
     def size(self):
         return lib().p100_tp_size(self.handle)
+
+    @property
+    def peer(self):
+        """True when all-reduces of up to TP_PEER_MAX values run over peer memory."""
+        return bool(lib().p100_tp_peer(self.handle))
 
     def allreduce_sum(self, buf, stream=None):
         check(lib().p100_tp_allreduce_sum(self.handle, _ptr(buf), buf.numel(), _stream(stream)))

@@ -1462,3 +1462,41 @@ extern "C" p100_status p100_fa_decode_static(const p100_attn_desc* desc, const f
 
 // The batch-1 decoder and the decode-step glue entry points.
 #include "decoder.cuh"
+
+// ------------------------------------------------ peer all-reduce (tp.cpp)
+// The launch behind p100_tp_allreduce_sum's peer path: tp.cpp is host-only
+// C++, so it reaches the kernel through this function of plain types.
+// slots[r] = rank r's arena of [2][world][n_cap] tagged words (this rank's
+// own at slots[rank]); epoch, ticket and broken are this rank's device ints;
+// wait_ns bounds each wait for another rank.
+namespace p100b {
+p100_status peer_allreduce(float* buf, size_t count, unsigned long long* const* slots, int world, int rank, int n_cap,
+                           int* epoch, int* ticket, int* broken, unsigned long long wait_ns, cudaStream_t stream) {
+    if (world < 1 || world > dec::kArMaxRanks || count > size_t(n_cap) || n_cap % 4)
+        return set_error(P100_ERR_INVALID, "peer all-reduce: %zu values, %d ranks, room for %d", count, world, n_cap);
+    if (count == 0) return P100_OK;
+    dec::PeerAr ar{};
+    for (int r = 0; r < world; ++r) ar.slots[r] = slots[r];
+    ar.world = world;
+    ar.rank = rank;
+    ar.n = n_cap;
+    ar.epoch = epoch;
+    ar.wait_ns = wait_ns;
+    const int grid = static_cast<int>((count + 4 * dec::kArThreads - 1) / (4 * dec::kArThreads));
+    dec::peer_allreduce_kernel<<<grid, dec::kArThreads, 0, stream>>>(buf, static_cast<int>(count), ar, ticket, broken);
+    return cuda_status(cudaGetLastError(), "peer_allreduce_kernel launch");
+}
+
+// Device scratch of the peer path's set-up exchanges in p100_tp_init_rank (a
+// gather's input and output and an agreement word).  A static array, so
+// every rank has it and enters every collective of the set-up.
+static __device__ float g_tp_setup_scratch[16 + 16 * dec::kArMaxRanks + 4];
+float* tp_setup_scratch() {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_tp_setup_scratch) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return nullptr;
+    }
+    return static_cast<float*>(p);
+}
+}  // namespace p100b

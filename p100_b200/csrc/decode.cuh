@@ -84,6 +84,80 @@ __global__ void __launch_bounds__(256) ar_push_kernel(const float* __restrict__ 
     }
 }
 
+// The same exchange as a plain in-place all-reduce of count fp32 values
+// (p100_tp_allreduce_sum over peer memory): thread t of CTA b owns values
+// 4 (256 b + t) .. +3.  It pushes them to every rank as tagged words, waits
+// (bounded) until its own arena holds every rank's words of this epoch, and
+// writes their sum in rank order (every rank gets the same bits).  The CTAs
+// read the epoch when they start; the last one to finish (ticket) advances
+// it.  A wait that runs out (ar.wait_ns: ranks may reach a collective far
+// apart, so the caller gives a long limit) marks the exchange broken in
+// *broken, and every later call gives up at once instead of waiting again
+// (its epochs no longer match the other ranks').  Grid ceil(count / 1024) x
+// 256 with count <= ar.n.  Every thread pushes before it waits, so no wait
+// depends on a CTA of this grid that has not started.
+constexpr int kArThreads = 256;
+__device__ __forceinline__ void st_words2(unsigned long long* p, unsigned long long a, unsigned long long b) {
+    asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(a), "l"(b) : "memory");
+}
+__global__ void __launch_bounds__(kArThreads) peer_allreduce_kernel(float* __restrict__ buf, int count, const PeerAr ar,
+                                                                    int* __restrict__ ticket, int* __restrict__ broken) {
+    const unsigned e = unsigned(*ar.epoch) + 1u;
+    const int par = int(e & 1u);
+    const int i0 = (blockIdx.x * kArThreads + threadIdx.x) * 4;
+    bool timed_out = *reinterpret_cast<volatile int*>(broken) != 0;
+    if (i0 < count) {
+        const int m = min(4, count - i0);
+        unsigned long long w[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) w[j] = tag_word(e, j < m ? buf[i0 + j] : 0.f);
+        for (int r = 0; r < ar.world; ++r) {
+            unsigned long long* dst = ar.slots[r] + (size_t(par) * ar.world + ar.rank) * ar.n + i0;
+            st_words2(dst, w[0], w[1]);
+            st_words2(dst + 2, w[2], w[3]);
+        }
+        const unsigned long long* base = ar.slots[ar.rank] + size_t(par) * ar.world * ar.n + i0;
+        const unsigned long long limit = ar.wait_ns ? ar.wait_ns : kWaitLimitNs;
+        unsigned long long start = 0;
+        float s[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int r = 0; r < ar.world && !timed_out; ++r) {
+            unsigned long long a, b, c, d;
+            for (;;) {
+                ld_words2(base + size_t(r) * ar.n, a, b);
+                ld_words2(base + size_t(r) * ar.n + 2, c, d);
+                if (unsigned(a >> 32) == e && unsigned(b >> 32) == e && unsigned(c >> 32) == e &&
+                    unsigned(d >> 32) == e)
+                    break;
+                const unsigned long long now = globaltimer_ns();
+                if (!start) {
+                    start = now;
+                } else if (now - start > limit) {
+                    timed_out = true;
+                    break;
+                }
+            }
+            const float f[4] = {__uint_as_float(uint32_t(a)), __uint_as_float(uint32_t(b)), __uint_as_float(uint32_t(c)),
+                                __uint_as_float(uint32_t(d))};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) s[j] = r == 0 ? f[j] : __fadd_rn(s[j], f[j]);
+        }
+        if (!timed_out)
+            for (int j = 0; j < m; ++j) buf[i0 + j] = s[j];
+    }
+    if (timed_out) {
+        atomicExch(&g_device_error, kDevErrTimeout);
+        atomicExch(broken, 1);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        if (atomicAdd(ticket, 1) == int(gridDim.x) - 1) {
+            *ticket = 0;
+            *ar.epoch = int(e);   // read by the next call, which starts after this kernel ends
+        }
+    }
+}
+
 // ------------------------------------------------------------------ RMSNorm
 // Q8_1 block of 32 values held four per lane by 8 consecutive lanes (lane j
 // of the octet holds elements 4j..4j+3 in v[0..3]).  Same bytes as

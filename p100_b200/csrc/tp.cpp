@@ -7,6 +7,14 @@
 // partial-sum all-reduce of the hidden vector, issued here through NCCL over
 // NVLink/NVSwitch, one communicator rank per GPU.
 //
+// All-reduces of up to P100_TP_PEER_MAX values run over NVLink peer memory
+// instead of NCCL when every pair of the group's GPUs has peer access (the
+// ranks agree while joining; P100_TP_ALLREDUCE=nccl keeps NCCL): one kernel
+// pushes each rank's values into every rank's slot arena (CUDA IPC mappings)
+// as 64-bit words tagged with the call's epoch and sums them in rank order,
+// the decoder's exchange as a plain collective (dec::peer_allreduce_kernel).
+// At these sizes NCCL's all-reduce measured about 21 us a call.
+//
 // Failure handling: every NCCL call's status becomes P100_ERR_NCCL with
 // ncclGetErrorString text; destroy aborts a communicator that reports an
 // asynchronous error instead of waiting on it.  P100_FAULT=tp_init makes
@@ -20,6 +28,7 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <algorithm>
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
@@ -36,11 +45,34 @@ p100_status cuda_status(cudaError_t err, const char* what);
 void clear_error();
 p100_status require_sm100(int* device_out, int* sm_count_out);
 bool fault_injected(const char* name);
+// In capi.cu (the CUDA translation unit).
+p100_status peer_allreduce(float* buf, size_t count, unsigned long long* const* slots, int world, int rank, int n_cap,
+                           int* epoch, int* ticket, int* broken, unsigned long long wait_ns, cudaStream_t stream);
+float* tp_setup_scratch();
 }  // namespace p100b
+
+namespace {
+constexpr int kPeerMaxRanks = 8;
+constexpr int kPeerCap = P100_TP_PEER_MAX;
+constexpr size_t kPeerSlotBytes(int world) { return size_t(2) * size_t(world) * kPeerCap * 8; }
+// How long a peer all-reduce waits for the other ranks: ranks may reach a
+// collective seconds apart (as NCCL allows), so far longer than a kernel's
+// own waits; a wait that runs out marks the exchange broken, and later calls
+// give up at once.
+constexpr unsigned long long kPeerWaitNs = 30ull * 1000 * 1000 * 1000;
+}  // namespace
 
 struct p100_tp {
     ncclComm_t comm = nullptr;
     int rank = 0, size = 1, device = 0;
+    // the peer path (multi-process groups whose GPUs all reach each other)
+    bool peer = false;
+    unsigned char* arena = nullptr;           // this rank's [2][size][kPeerCap] words, then epoch, ticket, broken
+    void* mapped[kPeerMaxRanks] = {};         // the other ranks' arenas (IPC mappings)
+    unsigned long long* slots[kPeerMaxRanks] = {};
+    int* epoch = nullptr;
+    int* ticket = nullptr;
+    int* broken = nullptr;
 };
 
 using namespace p100b;
@@ -134,6 +166,141 @@ struct DeviceScope {
         if (saved >= 0) cudaSetDevice(saved);
     }
 };
+
+// The set-up exchanges of the peer path.  Every rank calls every exchange,
+// in the same order, whatever its local state: a local failure is carried
+// into the next agreement (an all-reduce of failure counts) instead of
+// skipping a collective, so no rank is left waiting in one.
+struct PeerSetup {
+    p100_tp* tp;
+    cudaStream_t s = nullptr;
+    float* buf = nullptr;
+    p100_status err = P100_OK;   // the first local error of an exchange
+    explicit PeerSetup(p100_tp* t) : tp(t) {
+        note(cuda_status(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "peer set-up stream"));
+        buf = tp_setup_scratch();
+        if (!buf) note(set_error(P100_ERR_CUDA, "peer set-up scratch"));
+    }
+    ~PeerSetup() {
+        if (s) cudaStreamDestroy(s);
+    }
+    void note(p100_status st) {
+        if (st && !err) err = st;
+    }
+    bool usable() const { return s && buf; }
+    // every rank's `count` floats (count <= 16) into out, rank-major
+    void gather(const float* mine, int count, float* out) {
+        if (!usable()) {
+            std::fill(out, out + size_t(count) * tp->size, 0.f);
+            return;
+        }
+        note(cuda_status(cudaMemcpyAsync(buf, mine, sizeof(float) * count, cudaMemcpyHostToDevice, s), "gather in"));
+        note(nccl_status(nccl().allGather(buf, buf + 16, size_t(count), ncclFloat32, tp->comm, s), "ncclAllGather"));
+        note(cuda_status(cudaMemcpyAsync(out, buf + 16, sizeof(float) * count * tp->size, cudaMemcpyDeviceToHost, s),
+                         "gather out"));
+        note(cuda_status(cudaStreamSynchronize(s), "gather sync"));
+    }
+    // Over all ranks: 1000 x (ranks with an exchange error so far) + (ranks
+    // that passed ok = false).  Every rank gets the same number.
+    int agree(bool ok) {
+        const float mine = (err ? 1000.f : 0.f) + (ok ? 0.f : 1.f);
+        float all = 1000.f * tp->size;
+        if (usable()) {
+            float* at = buf + 16 + 16 * kPeerMaxRanks;
+            note(cuda_status(cudaMemcpyAsync(at, &mine, sizeof(float), cudaMemcpyHostToDevice, s), "agree in"));
+            note(nccl_status(nccl().allReduce(at, at, 1, ncclFloat32, ncclSum, tp->comm, s), "ncclAllReduce"));
+            note(cuda_status(cudaMemcpyAsync(&all, at, sizeof(float), cudaMemcpyDeviceToHost, s), "agree out"));
+            note(cuda_status(cudaStreamSynchronize(s), "agree sync"));
+        }
+        return static_cast<int>(all + 0.5f);
+    }
+    p100_status fail() {
+        return err ? err : set_error(P100_ERR_CUDA, "peer all-reduce set-up: another rank failed");
+    }
+};
+
+void release_peer(p100_tp* tp) {
+    for (int r = 0; r < kPeerMaxRanks; ++r)
+        if (tp->mapped[r]) {
+            cudaIpcCloseMemHandle(tp->mapped[r]);
+            tp->mapped[r] = nullptr;
+        }
+    if (tp->arena) cudaFree(tp->arena);
+    tp->arena = nullptr;
+    tp->peer = false;
+    for (auto& p : tp->slots) p = nullptr;
+    tp->epoch = tp->ticket = tp->broken = nullptr;
+}
+
+// Collective, right after the group is joined (tp->device current): decides,
+// every rank agreeing, whether all-reduces of up to kPeerCap values go over
+// peer memory, and maps every rank's slot arena.  A rank that declines (no
+// peer access to some rank, P100_TP_ALLREDUCE=nccl, an arena or IPC mapping
+// that fails: ranks in one process cannot map each other's arenas) leaves
+// every rank on NCCL; only a failure of the set-up's own exchanges is an
+// error, on every rank.
+p100_status setup_peer(p100_tp* tp) {
+    const int world = tp->size;
+    if (world < 2 || world > kPeerMaxRanks) return P100_OK;   // the same decision on every rank
+    PeerSetup ps(tp);
+    // 1. every rank's device -> peer access to all of them
+    std::vector<float> devs(size_t(world), 0.f);
+    const float me = float(tp->device);
+    ps.gather(&me, 1, devs.data());
+    const char* mode = std::getenv("P100_TP_ALLREDUCE");
+    bool ok = !(mode && std::strcmp(mode, "nccl") == 0);
+    for (int r = 0; r < world && ok; ++r) {
+        if (r == tp->rank) continue;
+        int can = 0;
+        if (cudaDeviceCanAccessPeer(&can, tp->device, int(devs[size_t(r)])) != cudaSuccess || !can) ok = false;
+    }
+    (void)cudaGetLastError();
+    int v = ps.agree(ok);
+    if (v >= 1000) return ps.fail();
+    if (v) return P100_OK;
+    // 2. this rank's arena and its IPC handle
+    const size_t bytes = kPeerSlotBytes(world) + 256;   // slots | epoch, ticket, broken
+    cudaIpcMemHandle_t h{};
+    ok = cudaMalloc(&tp->arena, bytes) == cudaSuccess;
+    if (!ok) tp->arena = nullptr;
+    ok = ok && cudaMemset(tp->arena, 0, bytes) == cudaSuccess && cudaDeviceSynchronize() == cudaSuccess &&
+         cudaIpcGetMemHandle(&h, tp->arena) == cudaSuccess;
+    (void)cudaGetLastError();
+    v = ps.agree(ok);
+    if (v) {
+        release_peer(tp);
+        return v >= 1000 ? ps.fail() : P100_OK;
+    }
+    // 3. every rank's handle; map the others' arenas
+    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+    std::vector<float> hmine(16), hall(size_t(world) * 16);
+    std::memcpy(hmine.data(), &h, 64);
+    ps.gather(hmine.data(), 16, hall.data());
+    for (int r = 0; r < world && ok; ++r) {
+        if (r == tp->rank) {
+            tp->slots[r] = reinterpret_cast<unsigned long long*>(tp->arena);
+            continue;
+        }
+        cudaIpcMemHandle_t hr;
+        std::memcpy(&hr, hall.data() + size_t(r) * 16, 64);
+        void* p = nullptr;
+        ok = cudaIpcOpenMemHandle(&p, hr, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess;
+        tp->mapped[r] = ok ? p : nullptr;
+        tp->slots[r] = static_cast<unsigned long long*>(p);
+    }
+    (void)cudaGetLastError();
+    // 4. every rank's arena is zeroed and mapped before any rank pushes
+    v = ps.agree(ok);
+    if (v) {
+        release_peer(tp);
+        return v >= 1000 ? ps.fail() : P100_OK;
+    }
+    tp->epoch = reinterpret_cast<int*>(tp->arena + kPeerSlotBytes(world));
+    tp->ticket = reinterpret_cast<int*>(tp->arena + kPeerSlotBytes(world) + 128);
+    tp->broken = reinterpret_cast<int*>(tp->arena + kPeerSlotBytes(world) + 192);
+    tp->peer = true;
+    return P100_OK;
+}
 }  // namespace
 
 extern "C" {
@@ -170,6 +337,12 @@ p100_status p100_tp_init_rank(const void* id, int nranks, int rank, int device, 
     tp->rank = rank;
     tp->size = nranks;
     tp->device = device;
+    if (p100_status st = setup_peer(tp)) {
+        release_peer(tp);
+        nccl().commDestroy(tp->comm);
+        delete tp;
+        return st;
+    }
     *out = tp;
     return P100_OK;
 }
@@ -199,6 +372,7 @@ p100_status p100_tp_create(int ngpu, const int* devs, p100_tp** out) {
 int p100_tp_rank(const p100_tp* tp) { return tp ? tp->rank : -1; }
 int p100_tp_size(const p100_tp* tp) { return tp ? tp->size : -1; }
 int p100_tp_device(const p100_tp* tp) { return tp ? tp->device : -1; }
+int p100_tp_peer(const p100_tp* tp) { return tp && tp->peer ? 1 : 0; }
 
 p100_status p100_tp_allreduce_sum(p100_tp* tp, float* buf, size_t count, p100_stream_t stream) {
     clear_error();
@@ -206,6 +380,10 @@ p100_status p100_tp_allreduce_sum(p100_tp* tp, float* buf, size_t count, p100_st
     if (count == 0) return P100_OK;
     DeviceScope scope;
     if (p100_status st = cuda_status(cudaSetDevice(tp->device), "cudaSetDevice")) return st;
+    // the path depends only on count, which every rank passes the same
+    if (tp->peer && count <= size_t(kPeerCap))
+        return peer_allreduce(buf, count, tp->slots, tp->size, tp->rank, kPeerCap, tp->epoch, tp->ticket, tp->broken,
+                              kPeerWaitNs, stream);
     return nccl_status(nccl().allReduce(buf, buf, count, ncclFloat32, ncclSum, tp->comm, stream), "ncclAllReduce");
 }
 
@@ -242,6 +420,10 @@ p100_status p100_tp_destroy(p100_tp* tp) {
     DeviceScope scope;
     cudaSetDevice(tp->device);
     p100_status st = P100_OK;
+    if (tp->arena) {
+        cudaDeviceSynchronize();   // no peer all-reduce of this rank still reads or writes the arenas
+        release_peer(tp);
+    }
     if (tp->comm) {
         ncclResult_t async = ncclSuccess;
         nccl().commGetAsyncError(tp->comm, &async);
