@@ -1482,9 +1482,19 @@ p100_status peer_allreduce(float* buf, size_t count, unsigned long long* const* 
     ar.n = n_cap;
     ar.epoch = epoch;
     ar.wait_ns = wait_ns;
-    const int grid = static_cast<int>((count + 4 * dec::kArThreads - 1) / (4 * dec::kArThreads));
-    dec::peer_allreduce_kernel<<<grid, dec::kArThreads, 0, stream>>>(buf, static_cast<int>(count), ar, ticket, broken);
-    return cuda_status(cudaGetLastError(), "peer_allreduce_kernel launch");
+    // a programmatic dependent of the previous kernel: its launch overlaps
+    // that kernel's tail, and it reads nothing before griddepcontrol.wait
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>((count + 4 * dec::kArThreads - 1) / (4 * dec::kArThreads)));
+    cfg.blockDim = dim3(dec::kArThreads);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cuda_status(cudaLaunchKernelEx(&cfg, dec::peer_allreduce_kernel, buf, static_cast<int>(count), ar, ticket, broken),
+                       "peer_allreduce_kernel launch");
 }
 
 // Device scratch of the peer path's set-up exchanges in p100_tp_init_rank (a

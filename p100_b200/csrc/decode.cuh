@@ -102,6 +102,10 @@ __device__ __forceinline__ void st_words2(unsigned long long* p, unsigned long l
 }
 __global__ void __launch_bounds__(kArThreads) peer_allreduce_kernel(float* __restrict__ buf, int count, const PeerAr ar,
                                                                     int* __restrict__ ticket, int* __restrict__ broken) {
+    // launched as a programmatic dependent: buf (and the epoch) are read
+    // only after the previous kernel has ended
+    pdl_allow_dependents();
+    pdl_wait_prior_grid();
     const unsigned e = unsigned(*ar.epoch) + 1u;
     const int par = int(e & 1u);
     const int i0 = (blockIdx.x * kArThreads + threadIdx.x) * 4;
