@@ -123,6 +123,12 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* tmap, int 
         : "memory");
 }
 
+// Starts fetching a TMA tensor map (a __grid_constant__ kernel parameter) so
+// that the first copy through it does not wait for the descriptor.
+__device__ __forceinline__ void prefetch_tensormap(const void* map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
+}
+
 // ------------------------------------------------------------ programmatic dependent launch
 // Both are no-ops for a kernel launched without the PDL attribute.
 __device__ __forceinline__ void pdl_wait_prior_grid() { asm volatile("griddepcontrol.wait;" ::: "memory"); }

@@ -188,6 +188,10 @@ __global__ void __launch_bounds__(NW * 32, ctas_per_sm<NW>(KV)) fa_mma_kernel(co
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, t = lane & 3;
     const int bk = blockIdx.y, part = blockIdx.x;
+    if (!QUANT && tid == 0) {   // the descriptors load while the query and barriers are set up
+        prefetch_tensormap(&p.tmk);
+        prefetch_tensormap(&p.tmv);
+    }
     const int b = bk / p.nkv, kvh = bk % p.nkv;
     int seq = p.seq, pos = -1;
     if (p.rope_cs) {   // fused decode step: keys [0, pos], pos device-resident

@@ -433,6 +433,10 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_tc_kernel(const __grid_consta
     uint8_t* ops = smem + kOpOff;
     uint8_t* raws = smem + kRawOff;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (warp == kProducerWarp && lane == 0) {   // the descriptors load while the block sets up
+        prefetch_tensormap(&p.tmw);
+        prefetch_tensormap(&p.tmx);
+    }
     const int slice = p.slices > 1 ? static_cast<int>(cluster_rank()) : 0;
     const int row0 = static_cast<int>(blockIdx.x / p.slices) * kRows;
     const int groups = p.k / 256;
